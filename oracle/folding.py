@@ -1,0 +1,85 @@
+"""Folded verification semantics restated in numpy (TEST INFRASTRUCTURE).
+
+Follows actfold/core/folded_transformer.py:60-203 for a layer whose parent
+activations are cached:
+
+  * parent pass (parent_branch_id None, :100-104): run the layer, store
+    ``hidden_states`` (layer input) and ``ffn_out`` (layer output);
+  * child pass: gate the child's layer input against the parent's cached
+    layer input (:124-148); all stable -> the parent's ``ffn_out`` (:162-179);
+    none stable -> recompute (:183-186); otherwise the layer is recomputed on
+    the FULL child sequence and merged row-wise with the parent output
+    (:190-196).
+
+The cache is assumed large enough to hold every parent entry (the plain
+ActivationCache with max_entries_per_layer >= 2 T), so the KeyError fallbacks
+of :135-141 never fire.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import numpy as np
+
+from oracle import llada as L
+from oracle.gate import gate as gate_fn
+from oracle.rows import merge
+
+
+def folded_layer(
+    layer: Callable[[np.ndarray], np.ndarray],
+    h_child: np.ndarray,
+    parent_in: np.ndarray,
+    parent_out: np.ndarray,
+    tau: float,
+    dtype: str,
+) -> tuple[np.ndarray, np.ndarray]:
+    """One folded layer for a [B, T, H] child batch; parent tensors broadcast over B.
+
+    Returns (output, stable_mask [B, T]).
+    """
+    B = h_child.shape[0]
+    pin = np.broadcast_to(parent_in, h_child.shape)
+    pout = np.broadcast_to(parent_out, h_child.shape)
+    stable = gate_fn(h_child, pin, tau, "cosine", 1e-8, dtype).mask
+    if stable.all():
+        return np.array(pout), stable
+    full = np.stack([layer(h_child[b]) for b in range(B)])
+    if not stable.any():
+        return full, stable
+    return merge(pout, full, stable), stable
+
+
+def llada_parent(tokens: np.ndarray, weights: dict, dims: L.LLaDADims) -> dict:
+    """Parent pass: per-layer inputs [L+1, T, H], K/V [L, T, Hkv] and logits [T, V]."""
+    return L.dense_forward(tokens, weights, dims)
+
+
+def llada_folded_children(
+    children: np.ndarray,
+    parent: dict,
+    weights: dict,
+    dims: L.LLaDADims,
+    tau: float,
+) -> dict:
+    """Verify each child [C, T] against the cached parent, sequentially (as the reference does).
+
+    Returns masks [L, C, T] (True = stable), per-layer child states
+    [L+1, C, T, H] and logits [C, T, V].
+    """
+    C, T = children.shape
+    cos, sin = L.rope_tables(T, dims.head_dim, dims.rope_theta)
+    masks = np.zeros((dims.n_layers, C, T), bool)
+    states = np.zeros((dims.n_layers + 1, C, T, dims.hidden), np.float32)
+    logits = np.zeros((C, T, dims.vocab), np.float32)
+    for c in range(C):
+        h = weights["embed"][children[c]][None]
+        states[0, c] = h[0]
+        for li, lw in enumerate(weights["layers"]):
+            layer = lambda x, lw=lw: L.block(x, lw, dims, cos, sin)  # noqa: E731
+            h, m = folded_layer(layer, h, parent["layer_in"][li][None], parent["layer_in"][li + 1][None], tau, "bf16")
+            masks[li, c] = m[0]
+            states[li + 1, c] = h[0]
+        logits[c] = L.lm_head(h[0], weights, dims)
+    return {"masks": masks, "states": states, "logits": logits}

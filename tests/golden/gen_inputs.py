@@ -1,0 +1,64 @@
+"""Deterministic inputs shared by the golden-vector generator and the tests.
+
+Everything is drawn from numpy's PCG64 generator, so the same seed gives the
+same bits here and on any other machine with the same numpy.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+from oracle.numerics import round_to
+
+# (name, seed, B, T, H, dtype, tau, metric)
+GATE_CASES = [
+    ("bf16_cos_t095", 1, 4, 256, 1024, "bf16", 0.95, "cosine"),
+    ("bf16_cos_t090", 2, 4, 256, 1024, "bf16", 0.90, "cosine"),
+    ("bf16_cos_t098", 3, 4, 256, 1024, "bf16", 0.98, "cosine"),
+    ("bf16_cos_h4096", 4, 2, 128, 4096, "bf16", 0.95, "cosine"),
+    ("bf16_cos_h3584", 5, 2, 64, 3584, "bf16", 0.95, "cosine"),
+    ("f32_cos_t095", 6, 4, 256, 512, "f32", 0.95, "cosine"),
+    ("f16_cos_t095", 7, 2, 256, 1024, "f16", 0.95, "cosine"),
+    ("bf16_l2_t050", 8, 2, 128, 256, "bf16", 0.5, "l2"),
+    ("bf16_pearson_t095", 9, 2, 128, 1024, "bf16", 0.95, "pearson"),
+    ("f32_l2_t050", 10, 2, 128, 256, "f32", 0.5, "l2"),
+    ("f32_pearson_t095", 11, 2, 128, 512, "f32", 0.95, "pearson"),
+]
+
+
+def gate_inputs(seed: int, B: int, T: int, H: int, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """Parent/child rows whose cosine spreads over [0.85, 1] plus edge rows.
+
+    Row (0,0) identical, (0,1) both zero, (0,2) negated, (0,3) child zero,
+    (0,4) tiny-magnitude copy, (0,5) large-magnitude rows.
+    """
+    rng = np.random.default_rng(seed)
+    parent = rng.standard_normal((B, T, H), dtype=np.float32)
+    noise = rng.standard_normal((B, T, H), dtype=np.float32)
+    target = rng.uniform(0.85, 1.0, size=(B, T, 1)).astype(np.float32)
+    s = np.sqrt(1.0 / (target * target) - 1.0).astype(np.float32)
+    child = parent + s * noise
+    child[0, 0] = parent[0, 0]
+    child[0, 1] = 0.0
+    parent[0, 1] = 0.0
+    child[0, 2] = -parent[0, 2]
+    child[0, 3] = 0.0
+    child[0, 4] = parent[0, 4] * np.float32(1e-3)
+    parent[0, 5] *= np.float32(64.0)
+    child[0, 5] = parent[0, 5] + np.float32(8.0) * noise[0, 5]
+    return round_to(child, dtype), round_to(parent, dtype)
+
+
+def digest(*arrays: np.ndarray) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()[:16]
+
+
+# Tiny LLaDA-shaped folded workload: dims, token layout and tau.
+TINY_LLADA = dict(T=64, n_prompt=16, mask_frac=0.5, n_children=4, d=4, tau=0.95, weight_seed=7, token_seed=42)
+TINY_DREAM = dict(T=64, n_prompt=16, mask_frac=0.75, n_children=3, d=3, tau=0.95, weight_seed=11, token_seed=43)
+DEMO = dict(T=16, n_children=2, tau=0.95, weight_seed=42, token_seed=42)

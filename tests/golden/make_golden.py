@@ -1,0 +1,290 @@
+"""Generate the golden vectors under tests/golden/ by running the REFERENCE itself.
+
+Run from the repository root in a container where the reference checkout is
+mounted at /root/reference (read-only):
+
+    python tests/golden/make_golden.py
+
+The reference is pure Python/PyTorch. Importing ``actfold.core`` pulls
+``actfold/profiler/visualization.py``, which imports matplotlib (absent here),
+so a throw-away stub package for matplotlib/seaborn is written to a temporary
+directory and put on ``sys.path`` before the reference. Nothing is written
+into the reference tree.
+
+Outputs (all small, compressed):
+  gate.npz       reference SimilarityGate masks + similarity bits per GATE_CASE
+  merge.npz      reference merge_stable_divergent outputs (fp32/fp16/bf16)
+  cache.npz      reference ActivationCache op log (puts, gets, LRU, KeyErrors)
+  demo.npz       reference folded pass of demo.py's synthetic model (config 1)
+  llada_tiny.npz reference FoldedModel over the restated tiny LLaDA block (bf16)
+  dream_tiny.npz same, GQA (Dream-shaped) tiny model
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = "/root/reference"
+sys.path.insert(0, ROOT)
+sys.path.insert(0, HERE)
+
+import torch  # noqa: E402
+
+from actfold_b200 import workloads as W  # noqa: E402
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, digest, gate_inputs  # noqa: E402
+from oracle import llada as OL  # noqa: E402
+from oracle.llada_torch import TorchLLaDA  # noqa: E402
+
+
+def _import_reference():
+    shim = tempfile.mkdtemp(prefix="af_mpl_shim_")
+    os.makedirs(os.path.join(shim, "matplotlib"))
+    with open(os.path.join(shim, "matplotlib", "__init__.py"), "w") as f:
+        f.write("def use(*a, **k):\n    pass\n")
+    with open(os.path.join(shim, "matplotlib", "pyplot.py"), "w") as f:
+        f.write("def __getattr__(name):\n    raise AttributeError(name)\n")
+    os.makedirs(os.path.join(shim, "seaborn"))
+    with open(os.path.join(shim, "seaborn", "__init__.py"), "w") as f:
+        f.write("")
+    sys.path.insert(0, REF)
+    sys.path.insert(0, shim)
+    import actfold.core as core  # noqa: F401
+
+    return core
+
+
+TORCH_DT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+
+
+def make_gate(core) -> None:
+    out = {}
+    for name, seed, B, T, H, dt, tau, metric in GATE_CASES:
+        c, p = gate_inputs(seed, B, T, H, dt)
+        tc = torch.from_numpy(c).to(TORCH_DT[dt])
+        tp = torch.from_numpy(p).to(TORCH_DT[dt])
+        g = core.SimilarityGate(tau=tau, metric=metric)
+        with torch.no_grad():
+            mask = g(tc, tp)
+            sim = g._compute_similarity(tc, tp)
+        out[f"{name}/mask"] = mask.numpy()
+        if dt == "f32":
+            out[f"{name}/sim"] = sim.numpy()
+        else:
+            out[f"{name}/sim_bits"] = sim.view(torch.int16).numpy().view(np.uint16)
+        out[f"{name}/digest"] = np.array(digest(c, p))
+    np.savez_compressed(os.path.join(HERE, "gate.npz"), **out)
+
+
+def make_merge(core) -> None:
+    from actfold.core.fused_ops import merge_stable_divergent
+
+    out = {}
+    g = torch.Generator().manual_seed(5)
+    for dt in ("f32", "f16", "bf16"):
+        p = torch.randn(2, 8, 64, generator=g).to(TORCH_DT[dt])
+        c = torch.randn(2, 8, 64, generator=g).to(TORCH_DT[dt])
+        m = torch.rand(2, 8, generator=g) > 0.5
+        o = merge_stable_divergent(p, c, m)
+        out[f"{dt}/parent"] = p.float().numpy()
+        out[f"{dt}/child"] = c.float().numpy()
+        out[f"{dt}/mask"] = m.numpy()
+        out[f"{dt}/out"] = o.float().numpy()
+    np.savez_compressed(os.path.join(HERE, "merge.npz"), **out)
+
+
+def cache_script():
+    """A fixed op sequence exercising put/get/LRU/touch/clear/step keys (shared with the tests)."""
+    g = torch.Generator().manual_seed(9)
+    ops = []
+
+    def acts(B, T, H, names=("ffn_out", "hidden_states")):
+        return {n: torch.randn(B, T, H, generator=g) for n in names}
+
+    ops.append(("put", "p", 0, acts(1, 6, 8), 0))
+    ops.append(("get", "p", 0, torch.tensor([[True, False, True, True, False, True]]), 0))
+    ops.append(("put", "c1", 0, acts(1, 6, 8), 0))
+    ops.append(("get", "p", 0, torch.ones(2, 6, dtype=torch.bool), 0))  # batch broadcast
+    ops.append(("put", "c2", 0, acts(1, 6, 8), 0))  # evicts c1's oldest tokens (p was touched)
+    ops.append(("get", "c1", 0, torch.ones(1, 6, dtype=torch.bool), 0))
+    ops.append(("get", "p", 0, torch.tensor([[False, True, False, False, True, False]]), 0))
+    ops.append(("put", "c3", 0, acts(1, 4, 8), 0))  # evicts p's untouched tokens
+    ops.append(("get", "p", 0, torch.ones(1, 6, dtype=torch.bool), 0))
+    ops.append(("get", "c2", 0, torch.tensor([[True, True, False, True, True, True]]), 0))
+    ops.append(("put", "s", 1, acts(2, 5, 4), 3))
+    ops.append(("get", "s", 1, torch.tensor([[True, False, True, False, True], [False, True, True, True, False]]), 3))
+    ops.append(("get", "s", 1, torch.ones(2, 5, dtype=torch.bool), 0))  # wrong step -> KeyError
+    ops.append(("clear_branch", "c2"))
+    ops.append(("get", "c2", 0, torch.ones(1, 6, dtype=torch.bool), 0))
+    ops.append(("clear_layer", 1))
+    ops.append(("put", "s", 1, {"ffn_out": torch.randn(1, 3, 4, generator=g)}, 0))
+    ops.append(("get", "s", 1, torch.ones(1, 3, dtype=torch.bool), 0))
+    return ops
+
+
+def make_cache(core) -> None:
+    cache = core.ActivationCache(max_entries_per_layer=14, device="cpu")
+    out = {}
+    log = []
+    for i, op in enumerate(cache_script()):
+        kind = op[0]
+        rec = {"i": i, "kind": kind}
+        if kind == "put":
+            _, b, l, a, s = op
+            rec.update(branch=b, layer=l, step=s, names=list(a))
+            cache.put(b, l, a, step_idx=s)
+            for n, t in a.items():
+                out[f"{i}/in/{n}"] = t.numpy()
+        elif kind == "get":
+            _, b, l, m, s = op
+            rec.update(branch=b, layer=l, step=s)
+            out[f"{i}/mask"] = m.numpy()
+            try:
+                r = cache.get(b, l, m, step_idx=s)
+                rec["out_names"] = sorted(r)
+                for n, t in r.items():
+                    out[f"{i}/out/{n}"] = t.numpy()
+            except KeyError:
+                rec["keyerror"] = True
+        elif kind == "clear_branch":
+            rec["branch"] = op[1]
+            cache.clear_branch(op[1])
+        elif kind == "clear_layer":
+            rec["layer"] = op[1]
+            cache.clear_layer(op[1])
+        rec["num_entries"] = cache.num_entries()
+        rec["num_entries_l0"] = cache.num_entries(0)
+        log.append(rec)
+    out["log"] = np.array(json.dumps(log))
+    np.savez_compressed(os.path.join(HERE, "cache.npz"), **out)
+
+
+def make_demo(core) -> None:
+    sys.path.insert(0, REF)
+    import demo  # reference demo.py
+
+    from actfold.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER
+
+    w = W.demo_weights(seed=DEMO["weight_seed"])
+    parent, children = W.demo_tokens(seed=DEMO["token_seed"], T=DEMO["T"], n_children=DEMO["n_children"])
+    cache = core.ActivationCache(max_entries_per_layer=1024, device="cpu")
+    gate = core.SimilarityGate(tau=DEMO["tau"], metric="cosine")
+    model = demo.FoldedSyntheticTransformer(1000, 128, 4, 8, cache, gate)
+    base = demo.SyntheticTransformer(1000, 128, 4, 8)
+    with torch.no_grad():
+        for m in (model, base):
+            m.embedding.weight.copy_(torch.from_numpy(w["embedding"]))
+            m.lm_head.weight.copy_(torch.from_numpy(w["lm_head"]))
+        for lw, fl, bl in zip(w["layers"], model.layers, base.layers):
+            for tgt in (fl.original_layer, bl):
+                tgt.attn.in_proj_weight.copy_(torch.from_numpy(lw["in_proj_weight"]))
+                tgt.attn.in_proj_bias.copy_(torch.from_numpy(lw["in_proj_bias"]))
+                tgt.attn.out_proj.weight.copy_(torch.from_numpy(lw["out_proj_weight"]))
+                tgt.attn.out_proj.bias.copy_(torch.from_numpy(lw["out_proj_bias"]))
+                tgt.norm1.weight.copy_(torch.from_numpy(lw["norm1_weight"]))
+                tgt.norm1.bias.copy_(torch.from_numpy(lw["norm1_bias"]))
+                tgt.ffn[0].weight.copy_(torch.from_numpy(lw["ffn0_weight"]))
+                tgt.ffn[0].bias.copy_(torch.from_numpy(lw["ffn0_bias"]))
+                tgt.ffn[2].weight.copy_(torch.from_numpy(lw["ffn2_weight"]))
+                tgt.ffn[2].bias.copy_(torch.from_numpy(lw["ffn2_bias"]))
+                tgt.norm2.weight.copy_(torch.from_numpy(lw["norm2_weight"]))
+                tgt.norm2.bias.copy_(torch.from_numpy(lw["norm2_bias"]))
+    model.eval()
+    base.eval()
+    GLOBAL_STABILITY_PROFILER.reset()
+    out = {}
+    with torch.no_grad():
+        pl = model(torch.from_numpy(parent)[None], branch_id="parent")
+        out["parent_logits"] = pl[0].numpy()
+        masks, logits, base_logits = [], [], []
+        for c in range(children.shape[0]):
+            ct = torch.from_numpy(children[c])[None]
+            lg = model(ct, branch_id=f"child{c}", parent_branch_id="parent")
+            prof = GLOBAL_STABILITY_PROFILER.get_profile(f"child{c}")
+            m = np.ones((4, DEMO["T"]), bool)
+            for st in prof.layer_stats:
+                if st.divergence_positions is not None:
+                    for _, t in st.divergence_positions.tolist():
+                        m[st.layer_idx, t] = False
+            masks.append(m)
+            logits.append(lg[0].numpy())
+            base_logits.append(base(ct)[0].numpy())
+    out["masks"] = np.stack(masks, axis=1)  # [L, C, T]
+    out["logits"] = np.stack(logits)
+    out["base_logits"] = np.stack(base_logits)
+    out["parent"] = parent
+    out["children"] = children
+    np.savez_compressed(os.path.join(HERE, "demo.npz"), **out)
+
+
+def make_llada(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
+    from actfold.core.model_wrapper import FoldedModel
+
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    T = spec["T"]
+    parent, children = W.llada_tokens(T, spec["n_prompt"], spec["mask_frac"], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"])
+    C = children.shape[0]
+    model = TorchLLaDA(w, od, T)
+    cache = core.ActivationCache(max_entries_per_layer=(C + 2) * T, device="cpu")
+    gate = core.SimilarityGate(tau=spec["tau"], metric="cosine")
+    folded = FoldedModel(model, cache, gate)
+    assert folded.folding_applied
+    recorded: list = []
+    orig_forward = gate.forward
+
+    def rec_forward(hc, hp):
+        m = orig_forward(hc, hp)
+        recorded.append(m.clone())
+        return m
+
+    gate.forward = rec_forward  # instance attribute; nn.Module.__call__ dispatches to it
+    states: list = []
+    hooks = [layer.register_forward_hook(lambda mod, inp, outp: states.append(outp.clone())) for layer in folded.wrapped_model.layers]
+    out = {}
+    with torch.no_grad():
+        pl = folded(torch.from_numpy(parent)[None], branch_id="parent")
+        out["parent_logits_bits"] = pl[0].view(torch.int16).numpy().view(np.uint16)
+        parent_states = [s[0] for s in states]
+        states.clear()
+        masks, logits, child_states = [], [], []
+        for c in range(C):
+            recorded.clear()
+            states.clear()
+            lg = folded(torch.from_numpy(children[c])[None], branch_id=f"child{c}", parent_branch_id="parent")
+            masks.append(torch.stack([m[0] for m in recorded]).numpy())
+            logits.append(lg[0].view(torch.int16).numpy().view(np.uint16))
+            child_states.append(torch.stack([s[0] for s in states]).view(torch.int16).numpy().view(np.uint16))
+    for h in hooks:
+        h.remove()
+    out["masks"] = np.stack(masks, axis=1)  # [L, C, T]
+    out["logits_bits"] = np.stack(logits)  # [C, T, V]
+    out["state_bits"] = np.stack(child_states, axis=1)  # [L, C, T, H] layer outputs
+    out["parent_state_bits"] = torch.stack(parent_states).view(torch.int16).numpy().view(np.uint16)
+    out["parent"] = parent
+    out["children"] = children
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
+def main() -> None:
+    torch.manual_seed(42)
+    core = _import_reference()
+    make_gate(core)
+    make_merge(core)
+    make_cache(core)
+    make_demo(core)
+    make_llada(core, W.LLADA_TINY, TINY_LLADA, "llada_tiny.npz")
+    make_llada(core, W.DREAM_TINY, TINY_DREAM, "dream_tiny.npz")
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()

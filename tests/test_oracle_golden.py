@@ -1,0 +1,142 @@
+"""Pin the CPU oracle to golden vectors produced by the reference itself (CPU only).
+
+The golden files come from tests/golden/make_golden.py, which imports the
+reference ActFold package and records what its own code computes.
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from actfold_b200 import workloads as W
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, digest, gate_inputs
+from oracle import demo as OD
+from oracle import folding as OF
+from oracle import llada as OL
+from oracle.cache import OracleActivationCache
+from oracle.gate import compact, exempt_rows, gate
+from oracle.numerics import from_bf16_bits, round_f16
+from oracle.rows import merge
+
+
+@pytest.mark.parametrize("case", GATE_CASES, ids=[c[0] for c in GATE_CASES])
+def test_gate_oracle_matches_reference(golden, case):
+    name, seed, B, T, H, dt, tau, metric = case
+    g = golden("gate")
+    c, p = gate_inputs(seed, B, T, H, dt)
+    assert str(g[f"{name}/digest"]) == digest(c, p), "input generator drifted"
+    res = gate(c, p, tau, metric, 1e-8, dt)
+    ref_mask = g[f"{name}/mask"]
+    mism = res.mask != ref_mask
+    if metric == "cosine":
+        # Order-dependent f32 accumulation may only flip rows next to the boundary.
+        assert not (mism & ~exempt_rows(res)).any(), f"{mism.sum()} mask mismatches outside the exemption window"
+    else:
+        assert mism.mean() <= 0.01
+    if dt == "f32":
+        np.testing.assert_allclose(res.sim, g[f"{name}/sim"], rtol=1e-5, atol=1e-5)
+    else:
+        bits = g[f"{name}/sim_bits"]
+        ref_sim = from_bf16_bits(bits) if dt == "bf16" else bits.view(np.float16).astype(np.float32)
+        agree = np.isclose(res.sim, ref_sim, rtol=0, atol=0) | (np.isnan(res.sim) & np.isnan(ref_sim))
+        # Allow one-ulp disagreements from accumulation order on a few rows.
+        assert agree.mean() >= 0.99, agree.mean()
+
+
+def test_gate_bf16_threshold_is_compared_in_bf16():
+    # sim 0.98046875 is bf16(0.98); the reference compares in bf16 so it is NOT > 0.98.
+    x = np.ones((1, 1, 4), np.float32)
+    r = gate(x, x, 0.98, "cosine", 1e-8, "bf16")
+    assert r.sim[0, 0] == 1.0 and r.mask[0, 0]
+    assert gate(x, x, 1.0, "cosine", 1e-8, "bf16").mask[0, 0] == False  # noqa: E712
+
+
+def test_compaction_oracle_orders_indices():
+    m = np.array([[True, False, True, False], [False, False, True, True]])
+    st, dv, cnt = compact(m)
+    assert st[0].tolist() == [0, 2] and dv[0].tolist() == [1, 3]
+    assert dv[1].tolist() == [0, 1] and cnt.tolist() == [2, 2]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_merge_oracle_matches_reference(golden, dt):
+    g = golden("merge")
+    out = merge(g[f"{dt}/parent"], g[f"{dt}/child"], g[f"{dt}/mask"])
+    np.testing.assert_array_equal(out, g[f"{dt}/out"])
+
+
+def test_cache_oracle_replays_reference_log(golden):
+    g = golden("cache")
+    log = json.loads(str(g["log"]))
+    cache = OracleActivationCache(max_entries_per_layer=14)
+    for rec in log:
+        i = rec["i"]
+        if rec["kind"] == "put":
+            acts = {n: g[f"{i}/in/{n}"] for n in rec["names"]}
+            cache.put(rec["branch"], rec["layer"], acts, rec["step"])
+        elif rec["kind"] == "get":
+            m = g[f"{i}/mask"]
+            if rec.get("keyerror"):
+                with pytest.raises(KeyError):
+                    cache.get(rec["branch"], rec["layer"], m, rec["step"])
+            else:
+                out = cache.get(rec["branch"], rec["layer"], m, rec["step"])
+                assert sorted(out) == rec["out_names"]
+                for n in rec["out_names"]:
+                    np.testing.assert_array_equal(out[n], g[f"{i}/out/{n}"])
+        elif rec["kind"] == "clear_branch":
+            cache.clear_branch(rec["branch"])
+        elif rec["kind"] == "clear_layer":
+            cache.clear_layer(rec["layer"])
+        assert cache.num_entries() == rec["num_entries"], i
+        assert cache.num_entries(0) == rec["num_entries_l0"], i
+
+
+def test_demo_oracle_matches_reference(golden):
+    g = golden("demo")
+    w = W.demo_weights(seed=DEMO["weight_seed"])
+    parent, children = W.demo_tokens(seed=DEMO["token_seed"], T=DEMO["T"], n_children=DEMO["n_children"])
+    np.testing.assert_array_equal(parent, g["parent"])
+    np.testing.assert_array_equal(children, g["children"])
+    par = OD.forward(parent, w, 8)
+    np.testing.assert_allclose(par["logits"], g["parent_logits"], rtol=1e-4, atol=1e-5)
+    res = OD.folded_children(children, par, w, 8, DEMO["tau"])
+    np.testing.assert_array_equal(res["masks"], g["masks"])
+    np.testing.assert_allclose(res["logits"], g["logits"], rtol=1e-4, atol=1e-5)
+
+
+def _llada_case(dims, spec, name, golden):
+    g = golden(name)
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    parent, children = W.llada_tokens(spec["T"], spec["n_prompt"], spec["mask_frac"], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"])
+    np.testing.assert_array_equal(parent, g["parent"])
+    np.testing.assert_array_equal(children, g["children"])
+    par = OF.llada_parent(parent, w, od)
+    res = OF.llada_folded_children(children, par, w, od, spec["tau"])
+    return g, par, res
+
+
+def _bf16_close(a, b):
+    """Tolerance of the workload: max relative error <= 2e-2 (relative to the tensor's scale)."""
+    err = np.abs(a - b).max() / max(np.abs(b).max(), 1e-6)
+    return err
+
+
+@pytest.mark.parametrize("which", ["llada", "dream"])
+def test_llada_oracle_matches_reference(golden, which):
+    dims, spec, name = (W.LLADA_TINY, TINY_LLADA, "llada_tiny") if which == "llada" else (W.DREAM_TINY, TINY_DREAM, "dream_tiny")
+    g, par, res = _llada_case(dims, spec, name, golden)
+    np.testing.assert_array_equal(res["masks"], g["masks"])
+    ref_logits = from_bf16_bits(g["logits_bits"])
+    assert _bf16_close(res["logits"], ref_logits) <= 2e-2
+    ref_states = from_bf16_bits(g["state_bits"])
+    assert _bf16_close(res["states"][1:], ref_states) <= 2e-2
+    ref_parent = from_bf16_bits(g["parent_logits_bits"])
+    assert _bf16_close(par["logits"], ref_parent) <= 2e-2
+    # Divergent rows are exactly the unmasked (edited) positions in this workload.
+    edited = g["children"] != g["parent"][None]
+    assert ((~g["masks"][0]) == edited).all()
