@@ -1,0 +1,196 @@
+// Similarity gate with fused stream compaction (sm_100a).
+//
+// One warp per token row. The row is loaded once with 128-bit non-coherent
+// loads into registers (up to 16 vectors per lane: H <= 4096 bf16 or 2048 f32),
+// then reduced twice from registers (norms, then normalized products) with
+// warp-shuffle sums in fp32. Larger or unaligned rows use a scalar path that
+// re-reads the row.
+//
+// Numerics follow the reference gate (actfold/core/similarity_gate.py:76-103
+// -> ATen cosine_similarity): for reduced-precision inputs every elementwise
+// op is evaluated in fp32 and rounded to the input dtype, reductions
+// accumulate in fp32 and round once. The per-element quotient bf16(x / n)
+// is formed as x * (1/n) and recomputed with a true IEEE division whenever the
+// fp32 product lies within 4 ulp of a bf16 rounding midpoint, so the bf16
+// result equals bf16(fp32(x / n)) exactly.
+#include "gate_row.cuh"
+
+namespace af {
+
+struct GateParams {
+  const char* child;
+  const char* parent;
+  int64_t c_bs, c_ts, p_bs, p_ts;
+  int64_t rows, T;
+  int H, nvec;
+  GateConsts k;
+  uint8_t* mask;
+  int64_t m_bs;
+  float* sim;
+};
+
+template <int DT, int METRIC, int NV>
+__global__ void __launch_bounds__(256) k_gate_vec(const GateParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int64_t b = row / p.T, t = row - b * p.T;
+  const char* c = p.child + b * p.c_bs + t * p.c_ts;
+  const char* q = p.parent + b * p.p_bs + t * p.p_ts;
+  GateOut r = gate_row_vec<DT, METRIC, NV>(c, q, p.nvec, p.H, p.k, lane);
+  if (lane == 0) {
+    p.mask[b * p.m_bs + t] = r.stable;
+    if (p.sim) p.sim[row] = r.sim;
+  }
+}
+
+template <int DT, int METRIC>
+__global__ void __launch_bounds__(256) k_gate_scalar(const GateParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const int64_t b = row / p.T, t = row - b * p.T;
+  const char* c = p.child + b * p.c_bs + t * p.c_ts;
+  const char* q = p.parent + b * p.p_bs + t * p.p_ts;
+  GateOut r = gate_row_scalar<DT, METRIC>(c, q, p.H, p.k, lane);
+  if (lane == 0) {
+    p.mask[b * p.m_bs + t] = r.stable;
+    if (p.sim) p.sim[row] = r.sim;
+  }
+}
+
+// Order-preserving compaction of one batch row's mask into stable / divergent
+// index lists. One CTA per batch row, chunks of blockDim.x tokens.
+__global__ void __launch_bounds__(1024) k_compact(const uint8_t* __restrict__ mask, int64_t m_bs, int64_t T,
+                                                  int32_t* __restrict__ stable_idx, int32_t* __restrict__ div_idx,
+                                                  int64_t idx_bs, int32_t* __restrict__ div_count) {
+  __shared__ int warp_tot[32];
+  __shared__ int chunk_base[2];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  int base_d = 0, base_s = 0;
+  for (int64_t t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int64_t t = t0 + tid;
+    const bool valid = t < T;
+    const bool st = valid && mask[b * m_bs + t] != 0;
+    const bool dv = valid && !st;
+    // packed counts: divergent in the low 16 bits, stable in the high 16 bits
+    const unsigned bd = __ballot_sync(0xffffffffu, dv), bs = __ballot_sync(0xffffffffu, st);
+    const unsigned lt = (1u << lane) - 1u;
+    const int pre = __popc(bd & lt) | (__popc(bs & lt) << 16);
+    if (lane == 0) warp_tot[warp] = __popc(bd) | (__popc(bs) << 16);
+    __syncthreads();
+    if (warp == 0) {
+      int v = lane < nwarps ? warp_tot[lane] : 0;
+      // inclusive scan across warps
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      int excl = __shfl_up_sync(0xffffffffu, v, 1);
+      if (lane == 0) excl = 0;
+      if (lane < nwarps) warp_tot[lane] = excl;
+      if (lane == 31) {
+        chunk_base[0] = v & 0xffff;
+        chunk_base[1] = v >> 16;
+      }
+    }
+    __syncthreads();
+    const int off = warp_tot[warp] + pre;
+    if (dv) div_idx[b * idx_bs + base_d + (off & 0xffff)] = (int32_t)t;
+    if (st && stable_idx) stable_idx[b * idx_bs + base_s + (off >> 16)] = (int32_t)t;
+    base_d += chunk_base[0];
+    base_s += chunk_base[1];
+    __syncthreads();
+  }
+  // -1 padding past each list
+  for (int64_t i = base_d + tid; i < T; i += blockDim.x) div_idx[b * idx_bs + i] = -1;
+  if (stable_idx)
+    for (int64_t i = base_s + tid; i < T; i += blockDim.x) stable_idx[b * idx_bs + i] = -1;
+  if (tid == 0) div_count[b] = base_d;
+}
+
+template <int DT, int METRIC>
+static int launch_gate(const GateParams& p, bool vec, cudaStream_t s) {
+  const int threads = 256, rows_per_block = threads / 32;
+  const int64_t blocks = ceil_div(p.rows, rows_per_block);
+  if (blocks > 0x7fffffff) return fail(AF_ERR_ARG, "af_gate: too many rows");
+  if (!vec) {
+    k_gate_scalar<DT, METRIC><<<(unsigned)blocks, threads, 0, s>>>(p);
+    return check_launch("af_gate(scalar)");
+  }
+  const int nv = (p.nvec + 31) / 32;
+  if (nv <= 1) k_gate_vec<DT, METRIC, 1><<<(unsigned)blocks, threads, 0, s>>>(p);
+  else if (nv <= 2) k_gate_vec<DT, METRIC, 2><<<(unsigned)blocks, threads, 0, s>>>(p);
+  else if (nv <= 4) k_gate_vec<DT, METRIC, 4><<<(unsigned)blocks, threads, 0, s>>>(p);
+  else if (nv <= 8) k_gate_vec<DT, METRIC, 8><<<(unsigned)blocks, threads, 0, s>>>(p);
+  else k_gate_vec<DT, METRIC, 16><<<(unsigned)blocks, threads, 0, s>>>(p);
+  return check_launch("af_gate(vec)");
+}
+
+template <int DT>
+static int dispatch_metric(int metric, const GateParams& p, bool vec, cudaStream_t s) {
+  switch (metric) {
+    case AF_METRIC_COSINE: return launch_gate<DT, AF_METRIC_COSINE>(p, vec, s);
+    case AF_METRIC_L2: return launch_gate<DT, AF_METRIC_L2>(p, vec, s);
+    case AF_METRIC_PEARSON: return launch_gate<DT, AF_METRIC_PEARSON>(p, vec, s);
+    default: return fail(AF_ERR_ARG, "af_gate: unsupported metric");
+  }
+}
+
+int gate_launch(const GateParams& p, int dtype, int metric, bool vec, cudaStream_t s) {
+  switch (dtype) {
+    case AF_DTYPE_BF16: return dispatch_metric<AF_DTYPE_BF16>(metric, p, vec, s);
+    case AF_DTYPE_F16: return dispatch_metric<AF_DTYPE_F16>(metric, p, vec, s);
+    case AF_DTYPE_F32: return dispatch_metric<AF_DTYPE_F32>(metric, p, vec, s);
+    default: return fail(AF_ERR_ARG, "af_gate: unsupported dtype");
+  }
+}
+
+}  // namespace af
+
+using namespace af;
+
+extern "C" int af_gate(const void* child, int64_t child_bstride, int64_t child_tstride, const void* parent,
+                       int64_t parent_bstride, int64_t parent_tstride, int64_t batch, int64_t seq, int64_t hidden,
+                       int dtype, int metric, float tau, float eps, float l2_denom, uint8_t* stable_mask,
+                       int64_t mask_bstride, float* sim, int32_t* stable_idx, int32_t* div_idx, int64_t idx_bstride,
+                       int32_t* div_count, void* stream) {
+  AF_REQUIRE(batch >= 0 && seq >= 0 && hidden > 0, "af_gate: bad shape");
+  if (batch == 0 || seq == 0) return AF_OK;
+  AF_REQUIRE(child && parent && stable_mask, "af_gate: null pointer");
+  AF_REQUIRE(hidden <= (1 << 24), "af_gate: hidden too large");
+  AF_REQUIRE(dtype == AF_DTYPE_F32 || dtype == AF_DTYPE_F16 || dtype == AF_DTYPE_BF16, "af_gate: bad dtype");
+  AF_REQUIRE(!div_idx || div_count, "af_gate: div_idx needs div_count");
+  AF_REQUIRE(!stable_idx || div_idx, "af_gate: stable_idx needs div_idx");
+  AF_REQUIRE(!div_idx || seq < (1 << 16) * 1024, "af_gate: seq too large for compaction");
+  AF_REQUIRE(!div_idx || idx_bstride >= seq, "af_gate: idx_bstride < seq");
+  cudaStream_t s = as_stream(stream);
+  const int esize = dtype == AF_DTYPE_F32 ? 4 : 2;
+  const int64_t row_bytes = hidden * esize;
+  GateParams p;
+  p.child = static_cast<const char*>(child);
+  p.parent = static_cast<const char*>(parent);
+  p.c_bs = child_bstride;
+  p.c_ts = child_tstride;
+  p.p_bs = parent_bstride;
+  p.p_ts = parent_tstride;
+  p.rows = batch * seq;
+  p.T = seq;
+  p.H = (int)hidden;
+  p.nvec = (int)(row_bytes / 16);
+  p.k = make_gate_consts(dtype, tau, eps, l2_denom);
+  p.mask = stable_mask;
+  p.m_bs = mask_bstride;
+  p.sim = sim;
+  const uintptr_t align = reinterpret_cast<uintptr_t>(child) | reinterpret_cast<uintptr_t>(parent) |
+                          (uintptr_t)child_bstride | (uintptr_t)child_tstride | (uintptr_t)parent_bstride |
+                          (uintptr_t)parent_tstride | (uintptr_t)row_bytes;
+  const bool vec = (align % 16) == 0 && p.nvec <= 16 * 32;
+  int st = gate_launch(p, dtype, metric, vec, s);
+  if (st != AF_OK || !div_idx) return st;
+  k_compact<<<(unsigned)batch, 1024, 0, s>>>(stable_mask, mask_bstride, seq, stable_idx, div_idx, idx_bstride,
+                                              div_count);
+  return check_launch("af_gate(compact)");
+}

@@ -1,0 +1,238 @@
+// Per-row similarity device functions shared by the dense gate (af_gate) and
+// the packed-row gate inside the native folded pass.
+#pragma once
+
+#include "common.cuh"
+
+namespace af {
+
+struct GateConsts {
+  float tau_r;     // tau rounded to the input dtype
+  float eps_r;     // eps rounded to the input dtype (cosine norm clamp)
+  float eps;       // eps as f32 (pearson denominator)
+  float l2_denom;  // sqrt(H) + eps evaluated in double, as f32
+};
+
+struct GateOut {
+  uint8_t stable;
+  float sim;
+};
+
+// Host-side rounding to a storage dtype (round to nearest even).
+inline float host_round(float x, int dtype) {
+  if (dtype == AF_DTYPE_BF16) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return x;  // NaN
+    u = (u + (((u >> 16) & 1u) + 0x7fffu)) & 0xffff0000u;
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+  }
+  if (dtype == AF_DTYPE_F16) return __half2float(__float2half_rn(x));
+  return x;
+}
+
+inline GateConsts make_gate_consts(int dtype, float tau, float eps, float l2_denom) {
+  GateConsts k;
+  k.tau_r = host_round(tau, dtype);
+  k.eps_r = host_round(eps, dtype);
+  k.eps = eps;
+  k.l2_denom = l2_denom;
+  return k;
+}
+
+// rnd<DT>(fp32(x / n)) with n already rounded; r = 1 / n (correctly rounded).
+template <int DT>
+__device__ __forceinline__ float quot(float x, float n, float r) {
+  if constexpr (DT == AF_DTYPE_BF16) {
+    float y = __fmul_rn(x, r);
+    const int low = (int)(__float_as_uint(y) & 0xffffu) - 0x8000;
+    if (low >= -4 && low <= 4) y = __fdiv_rn(x, n);  // near a bf16 midpoint: exact quotient
+    return rnd<DT>(y);
+  } else {
+    return rnd<DT>(__fdiv_rn(x, n));
+  }
+}
+
+template <int DT, int METRIC>
+__device__ __forceinline__ float finish_cos(float sc, float sp, const GateConsts& k, float& nc, float& np) {
+  nc = rnd<DT>(__fsqrt_rn(sc));
+  np = rnd<DT>(__fsqrt_rn(sp));
+  nc = nc < k.eps_r ? k.eps_r : nc;  // clamp_min keeps NaN
+  np = np < k.eps_r ? k.eps_r : np;
+  return 0.f;
+}
+
+template <int DT, int METRIC, int NV>
+__device__ __forceinline__ GateOut gate_row_vec(const char* c, const char* q, int nvec, int H, const GateConsts& k,
+                                                int lane) {
+  constexpr int E = Elt<DT>::kPerVec;
+  uint4 cv[NV], pv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = i * 32 + lane;
+    if (v < nvec) {
+      cv[i] = ldg16(c + 16 * (int64_t)v);
+      pv[i] = ldg16(q + 16 * (int64_t)v);
+    } else {
+      cv[i] = make_uint4(0u, 0u, 0u, 0u);
+      pv[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  float presum;
+  if constexpr (METRIC == AF_METRIC_COSINE) {
+    float sc = 0.f, sp = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float fc[E], fp[E];
+      unpack<DT>(cv[i], fc);
+      unpack<DT>(pv[i], fp);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        sc = fmaf(fc[e], fc[e], sc);
+        sp = fmaf(fp[e], fp[e], sp);
+      }
+    }
+    sc = warp_sum(sc);
+    sp = warp_sum(sp);
+    float nc, np;
+    finish_cos<DT, METRIC>(sc, sp, k, nc, np);
+    const float rc = __frcp_rn(nc), rp = __frcp_rn(np);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i * 32 + lane >= nvec) continue;
+      float fc[E], fp[E];
+      unpack<DT>(cv[i], fc);
+      unpack<DT>(pv[i], fp);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float yc = quot<DT>(fc[e], nc, rc);
+        const float yp = quot<DT>(fp[e], np, rp);
+        s = __fadd_rn(s, rnd<DT>(__fmul_rn(yc, yp)));
+      }
+    }
+    presum = warp_sum(s);
+  } else if constexpr (METRIC == AF_METRIC_L2) {
+    float sd = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i * 32 + lane >= nvec) continue;
+      float fc[E], fp[E];
+      unpack<DT>(cv[i], fc);
+      unpack<DT>(pv[i], fp);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float d = rnd<DT>(__fsub_rn(fc[e], fp[e]));
+        sd = fmaf(d, d, sd);
+      }
+    }
+    sd = warp_sum(sd);
+    const float l2 = rnd<DT>(__fsqrt_rn(sd));
+    presum = __fsub_rn(1.f, rnd<DT>(__fdiv_rn(l2, k.l2_denom)));
+  } else {  // pearson
+    float mc = 0.f, mp = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i * 32 + lane >= nvec) continue;
+      float fc[E], fp[E];
+      unpack<DT>(cv[i], fc);
+      unpack<DT>(pv[i], fp);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        mc = __fadd_rn(mc, fc[e]);
+        mp = __fadd_rn(mp, fp[e]);
+      }
+    }
+    mc = rnd<DT>(__fdiv_rn(warp_sum(mc), (float)H));
+    mp = rnd<DT>(__fdiv_rn(warp_sum(mp), (float)H));
+    float num = 0.f, scc = 0.f, spp = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i * 32 + lane >= nvec) continue;
+      float fc[E], fp[E];
+      unpack<DT>(cv[i], fc);
+      unpack<DT>(pv[i], fp);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float cc = rnd<DT>(__fsub_rn(fc[e], mc));
+        const float pc = rnd<DT>(__fsub_rn(fp[e], mp));
+        num = __fadd_rn(num, rnd<DT>(__fmul_rn(cc, pc)));
+        scc = fmaf(cc, cc, scc);
+        spp = fmaf(pc, pc, spp);
+      }
+    }
+    const float numr = rnd<DT>(warp_sum(num));
+    const float nc = rnd<DT>(__fsqrt_rn(warp_sum(scc)));
+    const float np = rnd<DT>(__fsqrt_rn(warp_sum(spp)));
+    const float den = rnd<DT>(__fadd_rn(rnd<DT>(__fmul_rn(nc, np)), k.eps));
+    presum = __fdiv_rn(numr, den);
+  }
+  GateOut o;
+  o.sim = rnd<DT>(presum);
+  o.stable = o.sim > k.tau_r ? 1 : 0;
+  return o;
+}
+
+// Scalar fallback: any H and alignment; re-reads the row for each pass.
+template <int DT, int METRIC>
+__device__ __forceinline__ GateOut gate_row_scalar(const char* c, const char* q, int H, const GateConsts& k,
+                                                   int lane) {
+  float presum;
+  if constexpr (METRIC == AF_METRIC_COSINE) {
+    float sc = 0.f, sp = 0.f;
+    for (int i = lane; i < H; i += 32) {
+      const float a = load_scalar<DT>(c, i), b = load_scalar<DT>(q, i);
+      sc = fmaf(a, a, sc);
+      sp = fmaf(b, b, sp);
+    }
+    sc = warp_sum(sc);
+    sp = warp_sum(sp);
+    float nc, np;
+    finish_cos<DT, METRIC>(sc, sp, k, nc, np);
+    const float rc = __frcp_rn(nc), rp = __frcp_rn(np);
+    float s = 0.f;
+    for (int i = lane; i < H; i += 32) {
+      const float yc = quot<DT>(load_scalar<DT>(c, i), nc, rc);
+      const float yp = quot<DT>(load_scalar<DT>(q, i), np, rp);
+      s = __fadd_rn(s, rnd<DT>(__fmul_rn(yc, yp)));
+    }
+    presum = warp_sum(s);
+  } else if constexpr (METRIC == AF_METRIC_L2) {
+    float sd = 0.f;
+    for (int i = lane; i < H; i += 32) {
+      const float d = rnd<DT>(__fsub_rn(load_scalar<DT>(c, i), load_scalar<DT>(q, i)));
+      sd = fmaf(d, d, sd);
+    }
+    const float l2 = rnd<DT>(__fsqrt_rn(warp_sum(sd)));
+    presum = __fsub_rn(1.f, rnd<DT>(__fdiv_rn(l2, k.l2_denom)));
+  } else {
+    float mc = 0.f, mp = 0.f;
+    for (int i = lane; i < H; i += 32) {
+      mc = __fadd_rn(mc, load_scalar<DT>(c, i));
+      mp = __fadd_rn(mp, load_scalar<DT>(q, i));
+    }
+    mc = rnd<DT>(__fdiv_rn(warp_sum(mc), (float)H));
+    mp = rnd<DT>(__fdiv_rn(warp_sum(mp), (float)H));
+    float num = 0.f, scc = 0.f, spp = 0.f;
+    for (int i = lane; i < H; i += 32) {
+      const float cc = rnd<DT>(__fsub_rn(load_scalar<DT>(c, i), mc));
+      const float pc = rnd<DT>(__fsub_rn(load_scalar<DT>(q, i), mp));
+      num = __fadd_rn(num, rnd<DT>(__fmul_rn(cc, pc)));
+      scc = fmaf(cc, cc, scc);
+      spp = fmaf(pc, pc, spp);
+    }
+    const float numr = rnd<DT>(warp_sum(num));
+    const float nc = rnd<DT>(__fsqrt_rn(warp_sum(scc)));
+    const float np = rnd<DT>(__fsqrt_rn(warp_sum(spp)));
+    const float den = rnd<DT>(__fadd_rn(rnd<DT>(__fmul_rn(nc, np)), k.eps));
+    presum = __fdiv_rn(numr, den);
+  }
+  GateOut o;
+  o.sim = rnd<DT>(presum);
+  o.stable = o.sim > k.tau_r ? 1 : 0;
+  return o;
+}
+
+}  // namespace af

@@ -1,0 +1,117 @@
+/*
+ * libactfold_b200 -- C ABI of the B200 (sm_100a) Branch Folding verification path.
+ *
+ * Conventions
+ *   - Every function returns an af_status; on failure af_last_error_string()
+ *     returns a message for the calling thread.
+ *   - All device pointers are caller-owned; no entry point allocates device
+ *     memory. Work that needs scratch takes it as an argument and reports its
+ *     size through a *_workspace_size() query.
+ *   - `stream` is a cudaStream_t (CUstream) handle; every launch is ordered on
+ *     it and no entry point synchronizes the device.
+ *   - Strides are in BYTES unless stated otherwise; the innermost (hidden)
+ *     dimension is contiguous.
+ *
+ * The reference (ShaneLiu04/ActFold) is pure Python/PyTorch; the functions
+ * below replace the tensor work of the Python calls cited beside each one.
+ * Paths are relative to the reference checkout.
+ */
+#ifndef ACTFOLD_B200_H_
+#define ACTFOLD_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  AF_OK = 0,
+  AF_ERR_ARG = 1,      /* bad argument (ValueError on the Python side)        */
+  AF_ERR_CAPACITY = 2, /* a size exceeds a buffer capacity                    */
+  AF_ERR_DEVICE = 3,   /* a device-side check failed (status word set)       */
+  AF_ERR_TIMEOUT = 4,  /* a bounded device wait ran out                       */
+  AF_ERR_CUDA = 5      /* a CUDA runtime call failed                          */
+} af_status;
+
+typedef enum { AF_DTYPE_F32 = 0, AF_DTYPE_F16 = 1, AF_DTYPE_BF16 = 2 } af_dtype;
+
+typedef enum { AF_METRIC_COSINE = 0, AF_METRIC_L2 = 1, AF_METRIC_PEARSON = 2 } af_metric;
+
+/* Library version string, e.g. "actfold_b200 0.1.0 sm_100a". */
+const char* af_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* af_last_error_string(void);
+
+/*
+ * af_gate -- per-token similarity gate with fused stream compaction.
+ *
+ * Replaces SimilarityGate.forward / _compute_similarity
+ * (actfold/core/similarity_gate.py:43-103) and the host-side statistics of
+ * GLOBAL_STABILITY_PROFILER.record (actfold/profiler/stability_profiler.py:106-158).
+ *
+ * For every row (b, t) of child[B, T, H] and parent[B, T, H] computes the
+ * similarity with the reference's rounding chain in `dtype` and writes
+ *   stable_mask[b * mask_bstride + t] = sim > round_dtype(tau)   (1 byte, 0/1)
+ *   sim[b * T + t]                      (optional, f32 value of the rounded sim)
+ * and, when div_idx is non-NULL, order-preserving index lists per batch row:
+ *   stable_idx[b * idx_bstride + i]  (optional) i-th stable token, -1 padded
+ *   div_idx[b * idx_bstride + i]     i-th divergent token, -1 padded
+ *   div_count[b]                     number of divergent tokens
+ * parent_bstride may be 0 to broadcast one parent row block over the batch.
+ * l2_denom = sqrt(H) + eps evaluated in double (the "l2" metric only).
+ */
+int af_gate(const void* child, int64_t child_bstride, int64_t child_tstride,
+            const void* parent, int64_t parent_bstride, int64_t parent_tstride,
+            int64_t batch, int64_t seq, int64_t hidden, int dtype, int metric,
+            float tau, float eps, float l2_denom,
+            uint8_t* stable_mask, int64_t mask_bstride, float* sim,
+            int32_t* stable_idx, int32_t* div_idx, int64_t idx_bstride,
+            int32_t* div_count, void* stream);
+
+/*
+ * af_merge_rows -- out[b, t, :] = stable[b, t] ? parent[b, t, :] : child[b, t, :].
+ *
+ * Replaces merge_stable_divergent and the Triton _merge_kernel
+ * (actfold/core/fused_ops.py:95-135, 206-253). Rows are `row_bytes` long
+ * (any element type); only the selected source row is read.
+ */
+int af_merge_rows(const void* parent, int64_t parent_bstride, int64_t parent_tstride,
+                  const void* child, int64_t child_bstride, int64_t child_tstride,
+                  const uint8_t* stable, int64_t stable_bstride,
+                  void* out, int64_t out_bstride, int64_t out_tstride,
+                  int64_t batch, int64_t seq, int64_t row_bytes, void* stream);
+
+/*
+ * af_gather_rows_masked -- zero-filled reconstruction of cached rows.
+ *
+ * Replaces gather_cached_activations (actfold/core/fused_ops.py:54-87, 256-324)
+ * for one activation tensor. src holds the cached [Bs, T, row] block
+ * (src_bstride 0 broadcasts a stored batch of 1). present[t] (nullable = all
+ * present) marks cached tokens.
+ *   mode 0 (all tokens present): out[b,t] = mask[b,t] ? src[b,t] : 0
+ *   mode 1 (some token missing): out[b,t] = present[t] && any_b' mask[b',t] ? src[b,t] : 0
+ */
+int af_gather_rows_masked(const void* src, int64_t src_bstride, int64_t src_tstride,
+                          const uint8_t* mask, int64_t mask_bstride, const uint8_t* present,
+                          int mode, void* out, int64_t out_bstride, int64_t out_tstride,
+                          int64_t batch, int64_t seq, int64_t row_bytes, void* stream);
+
+/*
+ * af_gather_rows_index -- out[b, j, :] = idx[j] >= 0 ? src[b, idx[j], :] : 0.
+ *
+ * Replaces the token-subset gather of ChunkedActivationCache.get
+ * (actfold/core/chunked_cache.py:182-225: dense[:, valid_indices]) and packs
+ * rows by index list. src_bstride 0 broadcasts one stored batch row.
+ */
+int af_gather_rows_index(const void* src, int64_t src_bstride, int64_t src_tstride,
+                         const int32_t* idx, int64_t n, int64_t batch,
+                         void* out, int64_t out_bstride, int64_t out_tstride,
+                         int64_t row_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACTFOLD_B200_H_ */
