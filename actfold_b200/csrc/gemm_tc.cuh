@@ -1,0 +1,52 @@
+// Weight-streaming tcgen05 GEMM for packed token rows (sm_100a).
+#pragma once
+
+#include "tc_common.cuh"
+
+namespace af {
+
+enum GemmEpilogue : int {
+  EPI_STORE = 0,     // out[m, n] = bf16(acc)
+  EPI_RESIDUAL = 1,  // out[m, n] = bf16(res[m, n] + bf16(acc))
+  EPI_SWIGLU = 2,    // 128-row tile = 64 gate rows + 64 up rows: out[m, f] = bf16(silu(bf16 g) * bf16 u)
+  EPI_ROPE = 3,      // QKV: rotate-half RoPE on columns [0, rope_cols), plain store after
+};
+
+struct GemmCall {
+  const void* x;       // activations [m_cap, k] bf16 (row stride ldx elements)
+  int64_t ldx;
+  int m_cap;           // activation row capacity
+  const int* m_dev;    // device-side valid row count (nullable: m_cap)
+  const void* w;       // weights [n, k] bf16, row-major
+  int n, k;
+  int epi;
+  void* out;           // bf16 output
+  int64_t ldo;         // output row stride (elements)
+  const int* out_rows; // nullable: output row of packed row m
+  const void* res;     // residual (EPI_RESIDUAL)
+  int64_t ldr;
+  const int* res_rows; // nullable
+  const float* rope_cos;  // [positions, head_dim/2]
+  const float* rope_sin;
+  const int* positions;   // position of packed row m
+  int rope_cols;          // columns [0, rope_cols) are rotated (multiple of head_dim)
+  int head_dim;           // 128
+  float* acc;          // split-K accumulator [n, m_pad] fp32, all zero on entry and exit
+  int* counters;       // split-K arrival counters [n/128 * m_tiles], zero on entry and exit
+  int64_t acc_elems;   // capacity of acc (elements)
+  int counter_elems;   // capacity of counters
+  int splits;          // 0 = choose automatically
+  unsigned* status;    // device status word (AF_STATUS_* bits)
+  // Pre-built descriptors (optional; built per call when null).
+  const CUtensorMap* tmap_w;
+  const CUtensorMap* tmap_x;
+};
+
+// Token-tile width the kernel uses for a given row capacity.
+int gemm_ntok(int m_cap);
+// Split-K workspace a call needs: accumulator elements and counters.
+void gemm_workspace(int n, int m_cap, int64_t* acc_elems, int* counter_elems);
+// Launch (stream-ordered, no synchronisation).
+int gemm_run(const GemmCall& c, cudaStream_t stream);
+
+}  // namespace af

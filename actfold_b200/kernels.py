@@ -1,0 +1,87 @@
+"""Thin torch-facing wrappers of the C-ABI kernels used by the native folded pass.
+
+Each wrapper validates shapes, takes device pointers and the current stream,
+and raises on a non-zero af_status. There is no fallback implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from actfold_b200 import _lib
+
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3
+
+class SplitKWorkspace:
+    """Zeroed split-K accumulator + tile counters + device status word.
+
+    The GEMM leaves the accumulator and counters zero when it finishes, so one
+    workspace serves every call whose (n, m_cap) fits.
+    """
+
+    def __init__(self, n_max: int, m_cap_max: int, device: torch.device | str = "cuda") -> None:
+        lib = _lib.load()
+        a, c = C.c_int64(), C.c_int64()
+        _lib.check(lib.af_linear_workspace(n_max, m_cap_max, C.byref(a), C.byref(c)))
+        self.acc = torch.zeros(int(a.value), dtype=torch.float32, device=device)
+        self.counters = torch.zeros(int(c.value), dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def check_status(self) -> None:
+        s = int(self.status.item())
+        if s:
+            self.acc.zero_()
+            self.counters.zero_()
+            self.status.zero_()
+            if s & 1:
+                raise TimeoutError(f"device wait timed out (status {s:#x})")
+            raise RuntimeError(f"device-side check failed (status {s:#x})")
+
+
+def linear(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    ws: SplitKWorkspace,
+    epilogue: int = EPI_STORE,
+    out: torch.Tensor | None = None,
+    m_dev: torch.Tensor | None = None,
+    out_rows: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    res_rows: torch.Tensor | None = None,
+    rope: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None = None,
+    splits: int = 0,
+) -> torch.Tensor:
+    """``out[m] = epilogue(x[m] . w^T)`` on the tcgen05 GEMM (bf16 in/out, fp32 accumulate).
+
+    x: [m_cap, k] bf16 (row stride may exceed k), w: [n, k] bf16 contiguous.
+    rope = (cos [P, 64] f32, sin [P, 64] f32, positions [m_cap] i32, rope_cols).
+    """
+    _lib.require_cuda(x, w, what="linear")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("linear: bf16 operands required")
+    if x.stride(1) != 1 or not w.is_contiguous():
+        raise ValueError("linear: operands must have a contiguous inner dimension")
+    m_cap, k = x.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"linear: k mismatch {x.shape} vs {w.shape}")
+    out_n = n // 2 if epilogue == EPI_SWIGLU else n
+    if out is None:
+        out = torch.empty((m_cap, out_n), dtype=torch.bfloat16, device=x.device)
+    cos = sin = pos = None
+    rope_cols = 0
+    if rope is not None:
+        cos, sin, pos, rope_cols = rope
+    with torch.cuda.device(x.device):
+        st = _lib.load().af_linear_bf16(
+            x.data_ptr(), x.stride(0), m_cap, _lib.ptr(m_dev), w.data_ptr(), n, k, epilogue,
+            out.data_ptr(), out.stride(0), _lib.ptr(out_rows),
+            _lib.ptr(residual), residual.stride(0) if residual is not None else 0, _lib.ptr(res_rows),
+            _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), rope_cols,
+            ws.acc.data_ptr(), ws.acc.numel(), ws.counters.data_ptr(), ws.counters.numel(), splits,
+            ws.status.data_ptr(), _lib.stream_ptr(x.device),
+        )
+    _lib.check(st, "linear")
+    return out

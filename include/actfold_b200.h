@@ -110,6 +110,45 @@ int af_gather_rows_index(const void* src, int64_t src_bstride, int64_t src_tstri
                          void* out, int64_t out_bstride, int64_t out_tstride,
                          int64_t row_bytes, void* stream);
 
+/* Epilogues of af_linear_bf16. */
+typedef enum {
+  AF_EPI_STORE = 0,    /* out[m, n] = bf16(acc)                                        */
+  AF_EPI_RESIDUAL = 1, /* out[m, n] = bf16(res[m, n] + bf16(acc))                      */
+  AF_EPI_SWIGLU = 2,   /* weight rows interleaved per 128: 64 gate rows then 64 up rows;
+                          out[m, f] = bf16(silu(bf16 g) * bf16 u), out width n / 2      */
+  AF_EPI_ROPE = 3      /* rotate-half RoPE (head_dim 128) on columns [0, rope_cols)    */
+} af_epilogue;
+
+/*
+ * af_linear_workspace -- split-K workspace needed by af_linear_bf16 for an
+ * (n, m_cap) problem: fp32 accumulator floats and int32 tile counters. Both
+ * must be zero before the first call; every call leaves them zero again.
+ */
+int af_linear_workspace(int64_t n, int64_t m_cap, int64_t* acc_floats, int64_t* counters);
+
+/*
+ * af_linear_bf16 -- out[row(m)] = epilogue(x[m, :] . w^T) for packed token rows.
+ *
+ * Replaces the projections inside the wrapped layer that
+ * FoldedTransformerLayer._recompute_all runs on every row
+ * (actfold/core/folded_transformer.py:224-258): here only the packed divergent
+ * rows are computed, with tcgen05 tensor cores (bf16 x bf16 -> fp32 in TMEM).
+ *   x [m_cap, k] bf16, row stride ldx (elements); valid rows = *m_dev (device
+ *   int, nullable -> m_cap); w [n, k] bf16 (n % 128 == 0, k % 64 == 0);
+ *   out rows: out_rows[m] (nullable -> m), row stride ldo; residual rows:
+ *   res_rows[m] (nullable -> m); rope tables cos/sin [P, 64] fp32 indexed by
+ *   positions[m]. splits = 0 chooses split-K automatically (needs the
+ *   workspace); status receives AF_STATUS bits (1 timeout, 2 capacity).
+ */
+int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_dev,
+                   const void* w, int64_t n, int64_t k, int epilogue,
+                   void* out, int64_t ldo, const int32_t* out_rows,
+                   const void* residual, int64_t ldr, const int32_t* res_rows,
+                   const float* rope_cos, const float* rope_sin, const int32_t* positions,
+                   int64_t rope_cols, float* acc, int64_t acc_floats,
+                   int32_t* counters, int64_t n_counters, int splits,
+                   uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,131 @@
+"""tcgen05 GEMM numerics against a plain PyTorch fp32 reference of the same op.
+
+Tolerance: bf16 outputs, so max |err| <= 1e-2 * max |ref| (a few bf16 ulps at
+the tensor's scale) and mean |err| well below that.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6))
+
+
+@pytest.fixture(scope="module")
+def ws():
+    from actfold_b200.kernels import SplitKWorkspace
+
+    return SplitKWorkspace(n_max=24576, m_cap_max=1024)
+
+
+@pytest.mark.parametrize("m", [1, 16, 40, 128, 256, 300, 1024])
+@pytest.mark.parametrize("splits", [1, 0])
+def test_linear_store(ws, m, splits):
+    from actfold_b200.kernels import linear
+
+    g = torch.Generator(device="cuda").manual_seed(m)
+    x = torch.randn(m, 4096, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(1024, 4096, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    out = linear(x, w, ws, splits=splits)
+    ref = (x.float() @ w.float().T).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    ws.check_status()
+    assert _rel(out, ref) <= 1e-2
+
+
+def test_linear_dynamic_m_and_row_maps(ws):
+    from actfold_b200.kernels import linear
+
+    m_cap, M = 256, 77
+    x = torch.randn(m_cap, 512, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(384, 512, device="cuda") * 0.05).to(torch.bfloat16)
+    m_dev = torch.tensor([M], dtype=torch.int32, device="cuda")
+    rows = torch.randperm(1000, device="cuda")[:m_cap].to(torch.int32)
+    out = torch.zeros(1000, 384, dtype=torch.bfloat16, device="cuda")
+    linear(x, w, ws, out=out, m_dev=m_dev, out_rows=rows)
+    ref = (x[:M].float() @ w.float().T).to(torch.bfloat16)
+    assert _rel(out[rows[:M].long()], ref) <= 1e-2
+    untouched = torch.ones(1000, dtype=torch.bool, device="cuda")
+    untouched[rows[:M].long()] = False
+    assert (out[untouched] == 0).all()
+    m_dev.zero_()
+    out2 = torch.zeros_like(out)
+    linear(x, w, ws, out=out2, m_dev=m_dev, out_rows=rows)
+    assert (out2 == 0).all()
+    torch.cuda.synchronize()
+    ws.check_status()
+
+
+def test_linear_residual_and_strided_input(ws):
+    from actfold_b200.kernels import EPI_RESIDUAL, linear
+
+    big = torch.randn(64, 8192, device="cuda").to(torch.bfloat16)
+    x = big[:, 1024:5120]  # row stride 8192
+    w = (torch.randn(4096, 4096, device="cuda") * 0.02).to(torch.bfloat16)
+    res = torch.randn(64, 4096, device="cuda").to(torch.bfloat16)
+    res_rows = torch.arange(63, -1, -1, device="cuda", dtype=torch.int32)
+    out = linear(x, w, ws, epilogue=EPI_RESIDUAL, residual=res, res_rows=res_rows)
+    o = (x.float() @ w.float().T).to(torch.bfloat16).float()
+    ref = (res[res_rows.long()].float() + o).to(torch.bfloat16)
+    assert _rel(out, ref) <= 1e-2
+    torch.cuda.synchronize()
+    ws.check_status()
+
+
+def test_linear_swiglu_interleaved(ws):
+    from actfold_b200.kernels import EPI_SWIGLU, linear
+
+    FF, H, m = 512, 1024, 96
+    wg = (torch.randn(FF, H, device="cuda") * 0.03).to(torch.bfloat16)
+    wu = (torch.randn(FF, H, device="cuda") * 0.03).to(torch.bfloat16)
+    w = torch.stack([wg.view(FF // 64, 64, H), wu.view(FF // 64, 64, H)], dim=1).reshape(2 * FF, H).contiguous()
+    x = torch.randn(m, H, device="cuda").to(torch.bfloat16)
+    out = linear(x, w, ws, epilogue=EPI_SWIGLU)
+    g = (x.float() @ wg.float().T).to(torch.bfloat16).float()
+    u = (x.float() @ wu.float().T).to(torch.bfloat16).float()
+    ref = (g / (1 + torch.exp(-g)) * u).to(torch.bfloat16)
+    assert out.shape == (m, FF)
+    assert _rel(out, ref) <= 1e-2
+    torch.cuda.synchronize()
+    ws.check_status()
+
+
+def test_linear_rope_matches_oracle(ws):
+    from actfold_b200.kernels import EPI_ROPE, linear
+    from oracle.llada import apply_rope, rope_tables
+    from oracle.numerics import round_bf16
+
+    H, nh, T, m = 256, 2, 64, 20
+    n = 3 * H  # q, k, v heads of 128
+    x = torch.randn(m, H, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, H, device="cuda") * 0.05).to(torch.bfloat16)
+    cos, sin = rope_tables(T, 128, 500000.0)
+    pos = torch.randint(0, T, (m,), device="cuda", dtype=torch.int32)
+    out = linear(x, w, ws, epilogue=EPI_ROPE, rope=(torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(), pos, 2 * H))
+    qkv = round_bf16((x.float() @ w.float().T).cpu().numpy())
+    p = pos.cpu().numpy()
+    q = apply_rope(qkv[:, :H].reshape(m, nh, 128), p, cos, sin).reshape(m, H)
+    k = apply_rope(qkv[:, H : 2 * H].reshape(m, nh, 128), p, cos, sin).reshape(m, H)
+    ref = np.concatenate([q, k, qkv[:, 2 * H :]], axis=1)
+    err = np.abs(out.float().cpu().numpy() - ref).max() / np.abs(ref).max()
+    assert err <= 1e-2
+    torch.cuda.synchronize()
+    ws.check_status()
+
+
+def test_linear_large_n_like_lm_head(ws):
+    from actfold_b200.kernels import linear
+
+    x = torch.randn(48, 4096, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(126464, 4096, device="cuda") * 0.02).to(torch.bfloat16)
+    out = linear(x, w, ws)
+    ref = (x.float() @ w.float().T).to(torch.bfloat16)
+    assert _rel(out, ref) <= 1e-2
+    torch.cuda.synchronize()
+    ws.check_status()
