@@ -38,6 +38,10 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _vp, _vp],
     ),
+    "af_attention_bf16": (
+        _i32,
+        [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _f32, _vp],
+    ),
 }
 
 _lib = None

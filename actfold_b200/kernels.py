@@ -85,3 +85,44 @@ def linear(
         )
     _lib.check(st, "linear")
     return out
+
+
+def attention(
+    q: torch.Tensor,
+    pk: torch.Tensor,
+    pv: torch.Tensor,
+    n_heads: int,
+    n_kv_heads: int,
+    out: torch.Tensor | None = None,
+    qsrc: torch.Tensor | None = None,
+    qchild: torch.Tensor | None = None,
+    n_q: torch.Tensor | None = None,
+    fresh_bits: torch.Tensor | None = None,
+    fk: torch.Tensor | None = None,
+    fv: torch.Tensor | None = None,
+    fchild: torch.Tensor | None = None,
+    n_f: torch.Tensor | None = None,
+    n_q_cap: int | None = None,
+) -> torch.Tensor:
+    """Non-causal attention of query rows over parent K/V with per-child fresh-key overrides.
+
+    q: rows holding n_heads x 128 query features (row i read at qsrc[i]);
+    pk/pv: [T, n_kv_heads * 128]; fk/fv: candidate K/V rows; fresh_bits:
+    [children, ceil(T/32)] int32 bitmap of fresh positions per child.
+    """
+    _lib.require_cuda(q, pk, pv, what="attention")
+    T = pk.shape[0]
+    cap = n_q_cap if n_q_cap is not None else (qsrc.shape[0] if qsrc is not None else q.shape[0])
+    if out is None:
+        out = torch.empty((cap, n_heads * 128), dtype=torch.bfloat16, device=q.device)
+    n_f_cap = fk.shape[0] if fk is not None else 0
+    with torch.cuda.device(q.device):
+        st = _lib.load().af_attention_bf16(
+            q.data_ptr(), q.stride(0), _lib.ptr(qsrc), _lib.ptr(qchild), _lib.ptr(n_q), cap,
+            pk.data_ptr(), pv.data_ptr(), pk.stride(0), T,
+            _lib.ptr(fresh_bits), fresh_bits.shape[1] if fresh_bits is not None else 0,
+            _lib.ptr(fk), _lib.ptr(fv), fk.stride(0) if fk is not None else 0, _lib.ptr(fchild), _lib.ptr(n_f), n_f_cap,
+            out.data_ptr(), out.stride(0), n_heads, n_kv_heads, 128, 128 ** -0.5, _lib.stream_ptr(q.device),
+        )
+    _lib.check(st, "attention")
+    return out

@@ -149,6 +149,27 @@ int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_d
                    int32_t* counters, int64_t n_counters, int splits,
                    uint32_t* status, void* stream);
 
+/*
+ * af_attention_bf16 -- non-causal attention of packed query rows over the
+ * parent's cached K/V, with per-child fresh-key overrides.
+ *
+ * Replaces the self-attention the wrapped layer recomputes over the FULL child
+ * context (actfold/core/folded_transformer.py:188-195): only divergent query
+ * rows are computed, and keys whose child input equals the parent's come from
+ * the parent cache. Query i (child qchild[i]) reads q + qsrc[i] * q_ld; its
+ * keys are parent rows t of pk/pv except where bit t of
+ * fresh_bits[qchild[i] * bits_ld] is set, plus candidate rows j of fk/fv with
+ * fchild[j] == qchild[i]. Valid query / candidate counts are read from
+ * n_q_dev / n_f_dev (nullable -> caps). head_dim must be 128; GQA when
+ * n_kv_heads < n_heads.
+ */
+int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsrc, const int32_t* qchild,
+                      const int32_t* n_q_dev, int64_t n_q_cap, const void* pk, const void* pv,
+                      int64_t kv_ld, int64_t T, const uint32_t* fresh_bits, int64_t bits_ld,
+                      const void* fk, const void* fv, int64_t f_ld, const int32_t* fchild,
+                      const int32_t* n_f_dev, int64_t n_f_cap, void* out, int64_t out_ld,
+                      int n_heads, int n_kv_heads, int head_dim, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

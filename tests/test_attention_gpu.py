@@ -1,0 +1,90 @@
+"""Attention kernel against a plain PyTorch fp32 reference of the same op.
+
+Tolerance: the kernel feeds bf16 probabilities to the tensor cores, so the
+max error is bounded at 2e-2 of the output scale.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, k, v, n_heads, n_kv):
+    """fp32 softmax(q k^T / sqrt(128)) v per head; q [n, nh*128], k/v [n, T, nkv*128]."""
+    n = q.shape[0]
+    grp = n_heads // n_kv
+    qh = q.float().view(n, n_heads, 128)
+    kh = k.float().view(n, -1, n_kv, 128).repeat_interleave(grp, dim=2)
+    vh = v.float().view(n, -1, n_kv, 128).repeat_interleave(grp, dim=2)
+    s = torch.einsum("nhd,nthd->nht", qh, kh) / 128 ** 0.5
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("nht,nthd->nhd", p, vh).reshape(n, -1)
+
+
+def _err(a, b):
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max())
+
+
+@pytest.mark.parametrize("T,n_q,heads,kv", [(64, 64, 2, 2), (1024, 1024, 4, 4), (200, 37, 4, 1), (512, 130, 8, 2)])
+def test_dense_attention(T, n_q, heads, kv):
+    from actfold_b200.kernels import attention
+
+    g = torch.Generator(device="cuda").manual_seed(T + n_q)
+    q = torch.randn(n_q, heads * 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(T, kv * 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(T, kv * 128, device="cuda", generator=g).to(torch.bfloat16)
+    out = attention(q, k, v, heads, kv)
+    ref = _ref(q, k[None].expand(n_q, -1, -1), v[None].expand(n_q, -1, -1), heads, kv)
+    assert _err(out, ref) <= 2e-2
+
+
+@pytest.mark.parametrize("kv", [4, 2])
+def test_fresh_key_overrides(kv):
+    from actfold_b200.kernels import attention
+
+    torch.manual_seed(0)
+    T, C, heads = 300, 3, 4
+    D = kv * 128
+    pk = torch.randn(T, D, device="cuda").to(torch.bfloat16)
+    pv = torch.randn(T, D, device="cuda").to(torch.bfloat16)
+    # candidates: sorted (child, position); each child has a few fresh positions
+    fresh = {0: [3, 77, 299], 1: [0, 150], 2: [5, 6, 7, 8, 200]}
+    cand = [(c, t) for c in range(C) for t in fresh[c]]
+    nc = len(cand)
+    fk = torch.randn(nc, D, device="cuda").to(torch.bfloat16)
+    fv = torch.randn(nc, D, device="cuda").to(torch.bfloat16)
+    fchild = torch.tensor([c for c, _ in cand], dtype=torch.int32, device="cuda")
+    bits_np = np.zeros((C, (T + 31) // 32), np.uint32)
+    for c, t in cand:
+        bits_np[c, t // 32] |= np.uint32(1 << (t % 32))
+    bits = torch.from_numpy(bits_np.view(np.int32)).cuda()
+    # queries: a subset of candidates (divergent rows) with Q rows in a packed buffer
+    qsel = [0, 2, 3, 5, 6, 9]
+    qall = torch.randn(nc, heads * 128, device="cuda").to(torch.bfloat16)
+    qsrc = torch.tensor(qsel, dtype=torch.int32, device="cuda")
+    qchild = torch.tensor([cand[i][0] for i in qsel], dtype=torch.int32, device="cuda")
+    out = attention(qall, pk, pv, heads, kv, qsrc=qsrc, qchild=qchild, fresh_bits=bits, fk=fk, fv=fv, fchild=fchild)
+    # reference: per query, parent K/V with the child's fresh rows replaced
+    ks, vs = [], []
+    for i in qsel:
+        c = cand[i][0]
+        k = pk.clone()
+        v = pv.clone()
+        for j, (cc, t) in enumerate(cand):
+            if cc == c:
+                k[t] = fk[j]
+                v[t] = fv[j]
+        ks.append(k)
+        vs.append(v)
+    ref = _ref(qall[qsrc.long()], torch.stack(ks), torch.stack(vs), heads, kv)
+    assert _err(out, ref) <= 2e-2
+    # dynamic counts: only the first 4 queries are valid
+    out2 = torch.zeros_like(out)
+    n_q = torch.tensor([4], dtype=torch.int32, device="cuda")
+    attention(qall, pk, pv, heads, kv, out=out2, qsrc=qsrc, qchild=qchild, n_q=n_q, fresh_bits=bits, fk=fk, fv=fv, fchild=fchild)
+    assert _err(out2[:4], ref[:4]) <= 2e-2
+    assert (out2[4:] == 0).all()
