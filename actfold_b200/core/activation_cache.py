@@ -139,6 +139,20 @@ class ActivationCache:
         self._stamp(layer_idx, blk, np.arange(T))
         self._evict(layer_idx)
 
+    def put_views(self, branch_id: Any, layer_idx: int, activations: dict[str, torch.Tensor], step_idx: int = 0) -> None:
+        """``put`` without copying: the cache keeps the given tensors (callers must not modify them).
+
+        Used for the native parent pass, whose per-layer activations already
+        live in one dense device buffer.
+        """
+        B, T = _validate_activations(activations)
+        _lib.require_cuda(*activations.values(), what="ActivationCache.put_views")
+        layer = self._layer(layer_idx)
+        blk = _Block({n: t.detach() for n, t in activations.items()}, B, T)
+        layer[(branch_id, step_idx)] = blk
+        self._stamp(layer_idx, blk, np.arange(T))
+        self._evict(layer_idx)
+
     def get(self, branch_id: Any, layer_idx: int, token_mask: torch.Tensor, step_idx: int = 0) -> dict[str, torch.Tensor]:
         """Zero-filled ``[B, T, ...]`` activations for tokens selected by ``token_mask``."""
         self._layer(layer_idx)

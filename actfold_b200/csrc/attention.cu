@@ -13,34 +13,9 @@
 // CTA = 4 warps, 64 query rows of one head; each warp owns 16 rows. K/V blocks
 // of 64 keys are double-buffered in XOR-swizzled shared memory with cp.async;
 // S = Q K^T and O += P V use mma.m16n8k16 (bf16 in, fp32 accumulate).
-#include "common.cuh"
+#include "attention.cuh"
 
 namespace af {
-
-struct AttnParams {
-  const __nv_bfloat16* q;  // query rows: q + qsrc[i] * q_ld + h * 128
-  int64_t q_ld;
-  const int* qsrc;         // nullable: i
-  const int* qchild;       // nullable: no masking
-  const int* n_q_dev;      // nullable: n_q_cap
-  int n_q_cap;
-  const __nv_bfloat16* pk;  // parent keys  [T, kv_ld] (head kvh at kvh * 128)
-  const __nv_bfloat16* pv;  // parent values
-  int64_t kv_ld;
-  int T;
-  const uint32_t* fresh_bits;  // [children][bits_ld] bitmap of fresh positions, nullable
-  int bits_ld;
-  const __nv_bfloat16* fk;  // candidate keys  fk + j * f_ld + kvh * 128
-  const __nv_bfloat16* fv;
-  int64_t f_ld;
-  const int* fchild;
-  const int* n_f_dev;
-  int n_f_cap;
-  __nv_bfloat16* out;  // out + i * out_ld + h * 128
-  int64_t out_ld;
-  int n_heads, n_kv_heads;
-  float scale_log2;  // softmax scale * log2(e)
-};
 
 constexpr int kHD = 128, kQB = 64, kKB = 64;
 

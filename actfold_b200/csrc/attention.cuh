@@ -1,0 +1,35 @@
+// Packed-query attention over parent K/V with fresh-key overrides (see attention.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace af {
+
+struct AttnParams {
+  const __nv_bfloat16* q;  // query rows: q + qsrc[i] * q_ld + h * 128
+  int64_t q_ld;
+  const int* qsrc;         // nullable: i
+  const int* qchild;       // nullable: no masking
+  const int* n_q_dev;      // nullable: n_q_cap
+  int n_q_cap;
+  const __nv_bfloat16* pk;  // parent keys  [T, kv_ld] (head kvh at kvh * 128)
+  const __nv_bfloat16* pv;  // parent values
+  int64_t kv_ld;
+  int T;
+  const uint32_t* fresh_bits;  // [children][bits_ld] bitmap of fresh positions, nullable
+  int bits_ld;
+  const __nv_bfloat16* fk;  // candidate keys  fk + j * f_ld + kvh * 128
+  const __nv_bfloat16* fv;
+  int64_t f_ld;
+  const int* fchild;
+  const int* n_f_dev;
+  int n_f_cap;
+  __nv_bfloat16* out;  // out + i * out_ld + h * 128
+  int64_t out_ld;
+  int n_heads, n_kv_heads;
+  float scale_log2;  // softmax scale * log2(e)
+};
+
+int attention_run(const AttnParams& p, cudaStream_t s);
+
+}  // namespace af

@@ -1,0 +1,1091 @@
+// Native batched Branch Folding pass for LLaDA/Dream-architecture blocks (sm_100a).
+//
+// All C children of one parent are verified together, with no host
+// synchronisation inside the pass. A child's layer-l input differs from the
+// parent's only on its "fresh" rows: the edited tokens at layer 0, then the
+// rows that were divergent at layer l-1 (a stable row takes the parent's
+// output, so its next input is bit-identical to the parent's). Per layer:
+//
+//   candidates  = fresh rows (+ any row the parent itself fails the gate on)
+//   k_fold_gate     gate(child row, parent row) + copy + attention RMSNorm   [warp / candidate]
+//   k_fold_compact  divergent list, fresh-key bitmap, next layer's candidates  [1 CTA]
+//   QKV GEMM (+RoPE) on candidates           (tcgen05)
+//   attention of divergent rows over parent K/V + fresh K/V
+//   O GEMM + residual, RMSNorm, gate/up GEMM + SwiGLU, down GEMM + residual
+//                                            (tcgen05) -> next layer's fresh rows
+//
+// After the last layer only the final fresh rows go through the final norm and
+// the LM head; every other logits row is the parent's (copied once per row for
+// all children). Stable rows therefore cost nothing but the copy of their
+// logits, and the per-layer cost scales with the number of divergent rows.
+//
+// The dense parent pass (af_dense_forward) runs the same kernels on all T rows
+// and fills the parent cache: layer inputs, QKV rows (K/V reused by children),
+// logits, logit row sums and the parent's self-gate results.
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "attention.cuh"
+#include "gate_row.cuh"
+#include "gemm_tc.cuh"
+
+namespace af {
+
+// ----------------------------------------------------------------------------
+// Block-wide exclusive scan (blockDim.x == 1024).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ int block_scan_1024(int v, int* warp_buf, int* total_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += n;
+  }
+  if (lane == 31) warp_buf[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_buf[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    warp_buf[lane] = w;  // inclusive per-warp totals
+  }
+  __syncthreads();
+  const int excl = x - v + (warp > 0 ? warp_buf[warp - 1] : 0);
+  *total_out = warp_buf[31];
+  __syncthreads();
+  return excl;
+}
+
+// ----------------------------------------------------------------------------
+// Candidate builder for layer 0 and for layers where the parent fails its own
+// gate on some row (one CTA of 1024 threads).
+// ----------------------------------------------------------------------------
+struct CandArgs {
+  int layer, C, T, m_cap;
+  const int64_t* ctok;           // [C*T]  (layer 0)
+  const int64_t* ptok;           // [T]    (layer 0)
+  const uint8_t* self_stable;    // [T] of this layer, nullable
+  const int* prev_div_pos;       // layer >= 1: fresh rows = previous layer's divergent rows
+  const int* prev_n_div;
+  int* slot;                     // [C*T] scratch
+  int* cand_child;
+  int* cand_pos;
+  int* cand_src;
+  int* n_cand;
+  int* fresh0_pos;               // layer 0: positions (c*T + t) of edited tokens
+  int* n_fresh0;
+  unsigned* status;
+};
+
+__global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
+  __shared__ int wbuf[32];
+  const int N = a.C * a.T;
+  int base = 0, total;
+  if (a.layer == 0) {
+    for (int i0 = 0; i0 < N; i0 += 1024) {
+      const int i = i0 + threadIdx.x;
+      const int f = (i < N && a.ctok[i] != a.ptok[i % a.T]) ? 1 : 0;
+      const int rank = base + block_scan_1024(f, wbuf, &total);
+      if (i < N) {
+        int s = -1;
+        if (f) {
+          if (rank < a.m_cap) {
+            a.fresh0_pos[rank] = i;
+            s = rank;
+          } else {
+            atomicOr(a.status, AF_STATUS_CAPACITY);
+          }
+        }
+        a.slot[i] = s;
+      }
+      base += total;
+    }
+    if (threadIdx.x == 0) *a.n_fresh0 = min(base, a.m_cap);
+  } else {
+    for (int i = threadIdx.x; i < N; i += 1024) a.slot[i] = -1;
+    __syncthreads();
+    const int nd = *a.prev_n_div;
+    for (int j = threadIdx.x; j < nd; j += 1024) a.slot[a.prev_div_pos[j]] = j;
+  }
+  __syncthreads();
+  base = 0;
+  for (int i0 = 0; i0 < N; i0 += 1024) {
+    const int i = i0 + threadIdx.x;
+    int s = -1, f = 0;
+    if (i < N) {
+      s = a.slot[i];
+      f = (s >= 0 || (a.self_stable && !a.self_stable[i % a.T])) ? 1 : 0;
+    }
+    const int rank = base + block_scan_1024(f, wbuf, &total);
+    if (f) {
+      if (rank < a.m_cap) {
+        a.cand_child[rank] = i / a.T;
+        a.cand_pos[rank] = i % a.T;
+        a.cand_src[rank] = s;
+      } else {
+        atomicOr(a.status, AF_STATUS_CAPACITY);
+      }
+    }
+    base += total;
+  }
+  if (threadIdx.x == 0) *a.n_cand = min(base, a.m_cap);
+}
+
+// ----------------------------------------------------------------------------
+// Row gathers and RMSNorm (warp per row).
+// ----------------------------------------------------------------------------
+// out[i] = embed[tokens[rows[i]]]; an id outside [0, vocab) sets AF_STATUS_BOUNDS and yields a zero row.
+__global__ void __launch_bounds__(256) k_embed_rows(const __nv_bfloat16* embed, int H, int64_t vocab,
+                                                    const int64_t* tokens, const int* rows, const int* n_dev,
+                                                    int n_cap, __nv_bfloat16* out, unsigned* status) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
+  if (i >= n) return;
+  const int64_t tok = tokens[rows ? rows[i] : i];
+  char* dst = reinterpret_cast<char*>(out + (int64_t)i * H);
+  if (tok < 0 || tok >= vocab) {
+    if (lane == 0) atomicOr(status, AF_STATUS_BOUNDS);
+    for (int v = lane; v < H / 8; v += 32) stg16(dst + 16 * v, make_uint4(0u, 0u, 0u, 0u));
+    return;
+  }
+  const char* src = reinterpret_cast<const char*>(embed + tok * H);
+  for (int v = lane; v < H / 8; v += 32) stg16(dst + 16 * v, ldg16(src + 16 * v));
+}
+
+template <int NV>
+__device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int H, const __nv_bfloat16* w, float eps,
+                                             char* out, int lane) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float f[8];
+    unpack<AF_DTYPE_BF16>(v[i], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float var = __fdiv_rn(ss, (float)H);
+  const float rinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, eps)));
+  const char* wb = reinterpret_cast<const char*>(w);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j >= nvec) continue;
+    float f[8], g[8];
+    unpack<AF_DTYPE_BF16>(v[i], f);
+    unpack<AF_DTYPE_BF16>(ldg16(wb + 16 * j), g);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float y0 = rnd<AF_DTYPE_BF16>(__fmul_rn(rnd<AF_DTYPE_BF16>(__fmul_rn(f[2 * e], rinv)), g[2 * e]));
+      const float y1 = rnd<AF_DTYPE_BF16>(__fmul_rn(rnd<AF_DTYPE_BF16>(__fmul_rn(f[2 * e + 1], rinv)), g[2 * e + 1]));
+      ow[e] = pack_bf16x2(y0, y1);
+    }
+    stg16(out + 16 * (int64_t)j, o);
+  }
+}
+
+// out[i] = rmsnorm(in[i]) * w for i < n (rows strided by H).
+template <int NV>
+__global__ void __launch_bounds__(256) k_rmsnorm_rows(const __nv_bfloat16* in, const __nv_bfloat16* w, int H,
+                                                      float eps, const int* n_dev, int n_cap, __nv_bfloat16* out) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
+  if (i >= n) return;
+  const int nvec = H / 8;
+  uint4 v[NV];
+  load_row<NV>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, lane, v);
+  rmsnorm_regs<NV>(v, nvec, H, w, eps, reinterpret_cast<char*>(out + (int64_t)i * H), lane);
+}
+
+// ----------------------------------------------------------------------------
+// Gate of candidate rows + packed copy + attention RMSNorm (warp per candidate).
+// ----------------------------------------------------------------------------
+struct FoldGateArgs {
+  const int* n_cand;
+  int m_cap, H;
+  const int* cand_pos;
+  const int* cand_src;
+  const __nv_bfloat16* x_fresh;   // fresh rows of this layer [m_cap, H]
+  const __nv_bfloat16* p_in;      // parent layer input [T, H]
+  const __nv_bfloat16* norm_w;
+  float eps;
+  GateConsts k;
+  uint8_t* stable;
+  __nv_bfloat16* xc;              // packed candidate hidden [m_cap, H]
+  __nv_bfloat16* a;               // packed normalized rows [m_cap, H]
+};
+
+template <int METRIC, int NV>
+__global__ void __launch_bounds__(256) k_fold_gate(const FoldGateArgs g) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int n = min(*g.n_cand, g.m_cap);
+  if (r >= n) return;
+  const int t = g.cand_pos[r], src = g.cand_src[r];
+  const int nvec = g.H / 8;
+  const char* prow = reinterpret_cast<const char*>(g.p_in + (int64_t)t * g.H);
+  const char* hrow = src >= 0 ? reinterpret_cast<const char*>(g.x_fresh + (int64_t)src * g.H) : prow;
+  uint4 hv[NV], pv[NV];
+  load_row<NV>(hrow, nvec, lane, hv);
+  load_row<NV>(prow, nvec, lane, pv);
+  const GateOut o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, lane);
+  if (lane == 0) g.stable[r] = o.stable;
+  char* xc = reinterpret_cast<char*>(g.xc + (int64_t)r * g.H);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j < nvec) stg16(xc + 16 * j, hv[i]);
+  }
+  rmsnorm_regs<NV>(hv, nvec, g.H, g.norm_w, g.eps, reinterpret_cast<char*>(g.a + (int64_t)r * g.H), lane);
+}
+
+// ----------------------------------------------------------------------------
+// Divergent compaction + fresh-key bitmap + next layer's candidates (1 CTA).
+// ----------------------------------------------------------------------------
+struct CompactArgs {
+  int C, T, m_cap, bits_ld;
+  const int* n_cand;
+  const uint8_t* stable;
+  const int* cand_child;
+  const int* cand_pos;
+  int* div_cand;
+  int* div_child;
+  int* div_pos;
+  int* n_div;
+  int* div_count;       // [C] divergent rows per child
+  unsigned* bits;       // [C, bits_ld] candidates of this layer (fresh keys)
+  unsigned* final_bits; // nullable: divergent rows of this layer (last layer only)
+  float* zero_f;        // nullable: buffer zeroed here (logit row sums, last layer)
+  int zero_n;
+  int write_next;
+  int* next_child;
+  int* next_pos;
+  int* next_src;
+  int* next_n_cand;
+};
+
+__global__ void __launch_bounds__(1024) k_fold_compact(const CompactArgs a) {
+  __shared__ int wbuf[32];
+  const int nb = a.C * a.bits_ld;
+  for (int i = threadIdx.x; i < nb; i += 1024) {
+    a.bits[i] = 0u;
+    if (a.final_bits) a.final_bits[i] = 0u;
+  }
+  for (int i = threadIdx.x; i < a.C; i += 1024) a.div_count[i] = 0;
+  if (a.zero_f)
+    for (int i = threadIdx.x; i < a.zero_n; i += 1024) a.zero_f[i] = 0.f;
+  __syncthreads();
+  const int n = min(*a.n_cand, a.m_cap);
+  int base = 0, total;
+  for (int r0 = 0; r0 < n || r0 == 0; r0 += 1024) {
+    const int r = r0 + threadIdx.x;
+    int c = 0, t = 0, d = 0;
+    if (r < n) {
+      c = a.cand_child[r];
+      t = a.cand_pos[r];
+      atomicOr(&a.bits[c * a.bits_ld + (t >> 5)], 1u << (t & 31));
+      d = a.stable[r] ? 0 : 1;
+    }
+    const int rank = base + block_scan_1024(d, wbuf, &total);
+    if (d) {
+      a.div_cand[rank] = r;
+      a.div_child[rank] = c;
+      a.div_pos[rank] = c * a.T + t;
+      atomicAdd(&a.div_count[c], 1);
+      if (a.final_bits) atomicOr(&a.final_bits[c * a.bits_ld + (t >> 5)], 1u << (t & 31));
+      if (a.write_next) {
+        a.next_child[rank] = c;
+        a.next_pos[rank] = t;
+        a.next_src[rank] = rank;
+      }
+    }
+    base += total;
+    if (r0 + 1024 >= n) break;
+  }
+  if (threadIdx.x == 0) {
+    *a.n_div = base;
+    if (a.write_next) *a.next_n_cand = base;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Logits of stable rows: copy the parent's row t to every child whose final
+// row t is not fresh (CTA per position; the parent row is read once).
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logits, int64_t V, int C, int T,
+                                                     const unsigned* final_bits, int bits_ld,
+                                                     __nv_bfloat16* logits) {
+  extern __shared__ int kids[];  // children that take the parent row
+  __shared__ int nk;
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) nk = 0;
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const bool fresh = (final_bits[c * bits_ld + (t >> 5)] >> (t & 31)) & 1u;
+    if (!fresh) kids[atomicAdd(&nk, 1)] = c;
+  }
+  __syncthreads();
+  const int n = nk;
+  if (n == 0) return;
+  const char* src = reinterpret_cast<const char*>(p_logits + (int64_t)t * V);
+  const int64_t nvec = V / 8;
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    const uint4 x = ldg16(src + 16 * v);
+    for (int k = 0; k < n; ++k)
+      stg16(reinterpret_cast<char*>(logits + ((int64_t)kids[k] * T + t) * V) + 16 * v, x);
+  }
+}
+
+// score[c] = mean over [T, V] of child c's logits (fp32 sums of the bf16 values).
+__global__ void __launch_bounds__(256) k_scores(const float* p_row_sums, const float* fresh_row_sums, int C, int T,
+                                                int64_t V, const unsigned* final_bits, int bits_ld, float* scores) {
+  const int c = blockIdx.x;
+  float s = 0.f;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const bool fresh = (final_bits[c * bits_ld + (t >> 5)] >> (t & 31)) & 1u;
+    s += fresh ? fresh_row_sums[(int64_t)c * T + t] : p_row_sums[t];
+  }
+  s = warp_sum(s);
+  __shared__ float ws[8];
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += ws[i];
+    scores[c] = tot / ((float)T * (float)V);
+  }
+}
+
+// Dense layer state of every child: parent rows, then fresh rows scattered over them.
+__global__ void __launch_bounds__(256) k_state_parent(const __nv_bfloat16* p_in, int H, int C, int T,
+                                                      __nv_bfloat16* out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= (int64_t)C * T) return;
+  const int t = (int)(row % T);
+  const char* s = reinterpret_cast<const char*>(p_in + (int64_t)t * H);
+  char* d = reinterpret_cast<char*>(out + row * H);
+  for (int v = lane; v < H / 8; v += 32) stg16(d + 16 * v, ldg16(s + 16 * v));
+}
+
+__global__ void __launch_bounds__(256) k_state_scatter(const __nv_bfloat16* x, int H, const int* pos, const int* n_dev,
+                                                       int n_cap, __nv_bfloat16* out) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int n = min(*n_dev, n_cap);
+  if (i >= n) return;
+  const char* s = reinterpret_cast<const char*>(x + (int64_t)i * H);
+  char* d = reinterpret_cast<char*>(out + (int64_t)pos[i] * H);
+  for (int v = lane; v < H / 8; v += 32) stg16(d + 16 * v, ldg16(s + 16 * v));
+}
+
+__global__ void k_iota(int* p, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = i;
+}
+
+__global__ void k_zero_f32(float* p, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = 0.f;
+}
+
+// Self gate of the parent rows of one layer (does the parent pass its own gate?).
+template <int NV>
+__global__ void __launch_bounds__(256) k_self_gate(const __nv_bfloat16* x, int H, int T, GateConsts k,
+                                                   uint8_t* self_stable) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int nvec = H / 8;
+  uint4 v[NV];
+  load_row<NV>(reinterpret_cast<const char*>(x + (int64_t)t * H), nvec, lane, v);
+  const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, H, k, lane);
+  if (lane == 0) self_stable[t] = o.stable;
+}
+
+// ----------------------------------------------------------------------------
+// Host side
+// ----------------------------------------------------------------------------
+struct Bump {
+  char* base;
+  int64_t off = 0, cap;
+  Bump(void* b, int64_t c) : base(static_cast<char*>(b)), cap(c) {}
+  template <class T>
+  T* take(int64_t n) {
+    off = (off + 255) & ~int64_t(255);
+    T* p = reinterpret_cast<T*>(base ? base + off : nullptr);
+    off += n * (int64_t)sizeof(T);
+    return p;
+  }
+};
+
+static int nv_for(int H) {
+  const int nvec = H / 8;
+  return (nvec + 31) / 32;
+}
+
+#define AF_DISPATCH_NV(H, KERNEL, GRID, BLOCK, SMEM, STREAM, ...)                 \
+  do {                                                                            \
+    const int _nv = nv_for(H);                                                    \
+    if (_nv <= 1) KERNEL<1><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);          \
+    else if (_nv <= 2) KERNEL<2><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);     \
+    else if (_nv <= 4) KERNEL<4><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);     \
+    else if (_nv <= 8) KERNEL<8><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);     \
+    else KERNEL<16><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);                  \
+  } while (0)
+
+static int validate_model(const af_model* m) {
+  AF_REQUIRE(m && m->layers && m->embed && m->final_norm && m->lm_head && m->rope_cos && m->rope_sin,
+             "model: null pointer");
+  const af_model_dims& d = m->dims;
+  AF_REQUIRE(d.n_layers > 0 && d.head_dim == 128, "model: head_dim must be 128");
+  AF_REQUIRE(d.n_heads > 0 && d.n_kv_heads > 0 && d.n_heads % d.n_kv_heads == 0, "model: bad head counts");
+  AF_REQUIRE(d.hidden % 128 == 0 && d.hidden <= 4096, "model: hidden must be a multiple of 128 and <= 4096");
+  AF_REQUIRE(d.ffn % 64 == 0 && (2 * d.ffn) % 128 == 0, "model: ffn must be a multiple of 64");
+  AF_REQUIRE(d.vocab % 128 == 0, "model: vocab must be a multiple of 128");
+  return AF_OK;
+}
+
+struct Sizes {
+  int H, q, kv, qkv, FF, V, L;
+};
+static Sizes sizes_of(const af_model_dims& d) {
+  Sizes s;
+  s.H = d.hidden;
+  s.q = d.n_heads * d.head_dim;
+  s.kv = d.n_kv_heads * d.head_dim;
+  s.qkv = s.q + 2 * s.kv;
+  s.FF = d.ffn;
+  s.V = d.vocab;
+  s.L = d.n_layers;
+  return s;
+}
+
+// ---------------------------------------------------------------- dense pass
+struct DenseWs {
+  __nv_bfloat16 *A, *att, *h1, *bn, *f;
+  int* pos;
+  float* acc;
+  int* counters;
+  int64_t acc_elems;
+  int counter_elems;
+};
+
+static DenseWs carve_dense(Bump& b, const Sizes& s, int T) {
+  DenseWs w;
+  w.A = b.take<__nv_bfloat16>((int64_t)T * s.H);
+  w.att = b.take<__nv_bfloat16>((int64_t)T * s.q);
+  w.h1 = b.take<__nv_bfloat16>((int64_t)T * s.H);
+  w.bn = b.take<__nv_bfloat16>((int64_t)T * s.H);
+  w.f = b.take<__nv_bfloat16>((int64_t)T * s.FF);
+  w.pos = b.take<int>(T);
+  const int nmax = std::max(std::max(s.qkv, s.H), 2 * s.FF);
+  int64_t ae;
+  int ce;
+  gemm_workspace(nmax, T, &ae, &ce);
+  // Split-K is only chosen when the tiles alone cannot fill the GPU; budget a modest accumulator.
+  ae = std::min<int64_t>(ae, (int64_t)1 << 24);
+  w.acc = b.take<float>(ae);
+  w.counters = b.take<int>(ce);
+  w.acc_elems = ae;
+  w.counter_elems = ce;
+  return w;
+}
+
+static GemmCall base_call(float* acc, int64_t acc_elems, int* counters, int counter_elems, unsigned* status) {
+  GemmCall c;
+  memset(&c, 0, sizeof(c));
+  c.acc = acc;
+  c.acc_elems = acc_elems;
+  c.counters = counters;
+  c.counter_elems = counter_elems;
+  c.status = status;
+  c.head_dim = 128;
+  return c;
+}
+
+}  // namespace af
+
+using namespace af;
+
+extern "C" int af_dense_workspace_bytes(const af_model_dims* d, int64_t T, int64_t* bytes) {
+  AF_REQUIRE(d && bytes && T > 0, "af_dense_workspace_bytes: bad argument");
+  Bump b(nullptr, 0);
+  carve_dense(b, sizes_of(*d), (int)T);
+  *bytes = b.off + 256;
+  return AF_OK;
+}
+
+extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_t T, float tau, void* layer_in,
+                                void* qkv, void* logits, uint8_t* self_stable, float* logit_row_sums, void* workspace,
+                                int64_t workspace_bytes, uint32_t* status, void* stream) {
+  int st = validate_model(m);
+  if (st) return st;
+  AF_REQUIRE(tokens && layer_in && qkv && logits && self_stable && logit_row_sums && workspace && status,
+             "af_dense_forward: null pointer");
+  AF_REQUIRE(T > 0 && T <= m->max_pos && T <= (1 << 20), "af_dense_forward: T out of range");
+  cudaStream_t s = as_stream(stream);
+  const Sizes z = sizes_of(m->dims);
+  const int Ti = (int)T;
+  Bump b(workspace, workspace_bytes);
+  DenseWs w = carve_dense(b, z, Ti);
+  AF_REQUIRE(b.off <= workspace_bytes, "af_dense_forward: workspace too small");
+  __nv_bfloat16* xin = static_cast<__nv_bfloat16*>(layer_in);
+  __nv_bfloat16* qkvb = static_cast<__nv_bfloat16*>(qkv);
+  unsigned* stw = reinterpret_cast<unsigned*>(status);
+  const float eps = m->dims.rms_eps;
+  const unsigned rows_blocks = (unsigned)((Ti + 7) / 8);
+  const GateConsts gk = make_gate_consts(AF_DTYPE_BF16, tau, 1e-8f, 0.f);
+
+  k_iota<<<(Ti + 255) / 256, 256, 0, s>>>(w.pos, Ti);
+  k_embed_rows<<<rows_blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(m->embed), z.H, z.V, tokens, nullptr,
+                                           nullptr, Ti, xin, stw);
+  for (int l = 0; l < z.L; ++l) {
+    const af_layer_weights& lw = m->layers[l];
+    const __nv_bfloat16* x = xin + (int64_t)l * Ti * z.H;
+    __nv_bfloat16* xnext = xin + (int64_t)(l + 1) * Ti * z.H;
+    __nv_bfloat16* qkv_l = qkvb + (int64_t)l * Ti * z.qkv;
+    AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, x, static_cast<const __nv_bfloat16*>(lw.attn_norm), z.H,
+                                                                eps, nullptr, Ti, w.A);
+    AF_DISPATCH_NV(z.H, k_self_gate, rows_blocks, 256, 0, s, x, z.H, Ti, gk, self_stable + (int64_t)l * Ti);
+    GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c.x = w.A;
+    c.ldx = z.H;
+    c.m_cap = Ti;
+    c.w = lw.w_qkv;
+    c.n = z.qkv;
+    c.k = z.H;
+    c.epi = EPI_ROPE;
+    c.out = qkv_l;
+    c.ldo = z.qkv;
+    c.rope_cos = m->rope_cos;
+    c.rope_sin = m->rope_sin;
+    c.positions = w.pos;
+    c.rope_cols = z.q + z.kv;
+    if ((st = gemm_run(c, s))) return st;
+    AttnParams ap;
+    memset(&ap, 0, sizeof(ap));
+    ap.q = qkv_l;
+    ap.q_ld = z.qkv;
+    ap.n_q_cap = Ti;
+    ap.pk = qkv_l + z.q;
+    ap.pv = qkv_l + z.q + z.kv;
+    ap.kv_ld = z.qkv;
+    ap.T = Ti;
+    ap.out = w.att;
+    ap.out_ld = z.q;
+    ap.n_heads = m->dims.n_heads;
+    ap.n_kv_heads = m->dims.n_kv_heads;
+    ap.scale_log2 = (1.0f / sqrtf((float)m->dims.head_dim)) * 1.4426950408889634f;
+    if ((st = attention_run(ap, s))) return st;
+    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c.x = w.att;
+    c.ldx = z.q;
+    c.m_cap = Ti;
+    c.w = lw.w_o;
+    c.n = z.H;
+    c.k = z.q;
+    c.epi = EPI_RESIDUAL;
+    c.out = w.h1;
+    c.ldo = z.H;
+    c.res = x;
+    c.ldr = z.H;
+    if ((st = gemm_run(c, s))) return st;
+    AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm),
+                                                                z.H, eps, nullptr, Ti, w.bn);
+    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c.x = w.bn;
+    c.ldx = z.H;
+    c.m_cap = Ti;
+    c.w = lw.w_gateup;
+    c.n = 2 * z.FF;
+    c.k = z.H;
+    c.epi = EPI_SWIGLU;
+    c.out = w.f;
+    c.ldo = z.FF;
+    if ((st = gemm_run(c, s))) return st;
+    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c.x = w.f;
+    c.ldx = z.FF;
+    c.m_cap = Ti;
+    c.w = lw.w_down;
+    c.n = z.H;
+    c.k = z.FF;
+    c.epi = EPI_RESIDUAL;
+    c.out = xnext;
+    c.ldo = z.H;
+    c.res = w.h1;
+    c.ldr = z.H;
+    if ((st = gemm_run(c, s))) return st;
+  }
+  const __nv_bfloat16* xl = xin + (int64_t)z.L * Ti * z.H;
+  AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, xl, static_cast<const __nv_bfloat16*>(m->final_norm),
+                                                              z.H, eps, nullptr, Ti, w.A);
+  k_zero_f32<<<(Ti + 255) / 256, 256, 0, s>>>(logit_row_sums, Ti);
+  GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+  c.x = w.A;
+  c.ldx = z.H;
+  c.m_cap = Ti;
+  c.w = m->lm_head;
+  c.n = z.V;
+  c.k = z.H;
+  c.epi = EPI_STORE;
+  c.out = logits;
+  c.ldo = z.V;
+  c.row_sums = logit_row_sums;
+  if ((st = gemm_run(c, s))) return st;
+  return check_launch("af_dense_forward");
+}
+
+// ---------------------------------------------------------------- fold plan
+namespace af {
+
+struct FoldWs {
+  int* slot;
+  int *cand_child, *cand_pos, *cand_src, *n_cand;  // [(L+1) * m_cap], [L+1]
+  int *div_cand, *div_child, *div_pos, *n_div;     // [L * m_cap], [L]
+  int *fresh0_pos, *n_fresh0;
+  uint8_t* stable;
+  unsigned *bits, *final_bits;
+  int* div_count;  // [L, C]
+  __nv_bfloat16 *x_all, *xc, *A, *qkv, *att, *h1, *bn, *f;
+  float* row_sums;  // [C*T] fresh logit row sums
+  float* acc;
+  int* counters;
+  int64_t acc_elems;
+  int counter_elems;
+  unsigned* status;
+  int bits_ld;
+};
+
+static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
+  FoldWs w;
+  const int L = z.L;
+  w.bits_ld = (T + 31) / 32;
+  w.slot = b.take<int>((int64_t)C * T);
+  w.cand_child = b.take<int>((int64_t)(L + 1) * m_cap);
+  w.cand_pos = b.take<int>((int64_t)(L + 1) * m_cap);
+  w.cand_src = b.take<int>((int64_t)(L + 1) * m_cap);
+  w.n_cand = b.take<int>(L + 1);
+  w.div_cand = b.take<int>((int64_t)L * m_cap);
+  w.div_child = b.take<int>((int64_t)L * m_cap);
+  w.div_pos = b.take<int>((int64_t)L * m_cap);
+  w.n_div = b.take<int>(L);
+  w.fresh0_pos = b.take<int>(m_cap);
+  w.n_fresh0 = b.take<int>(1);
+  w.stable = b.take<uint8_t>(m_cap);
+  w.bits = b.take<unsigned>((int64_t)C * w.bits_ld);
+  w.final_bits = b.take<unsigned>((int64_t)C * w.bits_ld);
+  w.div_count = b.take<int>((int64_t)L * C);
+  w.x_all = b.take<__nv_bfloat16>((int64_t)(L + 1) * m_cap * z.H);
+  w.xc = b.take<__nv_bfloat16>((int64_t)m_cap * z.H);
+  w.A = b.take<__nv_bfloat16>((int64_t)m_cap * z.H);
+  w.qkv = b.take<__nv_bfloat16>((int64_t)m_cap * z.qkv);
+  w.att = b.take<__nv_bfloat16>((int64_t)m_cap * z.q);
+  w.h1 = b.take<__nv_bfloat16>((int64_t)m_cap * z.H);
+  w.bn = b.take<__nv_bfloat16>((int64_t)m_cap * z.H);
+  w.f = b.take<__nv_bfloat16>((int64_t)m_cap * z.FF);
+  w.row_sums = b.take<float>((int64_t)C * T);
+  const int nmax = std::max(std::max(z.qkv, z.H), 2 * z.FF);
+  int64_t ae;
+  int ce;
+  gemm_workspace(nmax, m_cap, &ae, &ce);
+  w.acc = b.take<float>(ae);
+  w.counters = b.take<int>(ce);
+  w.acc_elems = ae;
+  w.counter_elems = ce;
+  w.status = b.take<unsigned>(1);
+  return w;
+}
+
+struct FoldPlan {
+  af_model model;
+  std::vector<af_layer_weights> layers;
+  af_parent_cache parent;
+  int C, T, m_cap;
+  float tau;
+  int metric;
+  std::vector<uint8_t> su;
+  FoldWs w;
+  int ntok;
+  std::vector<CUtensorMap> tm_qkv, tm_o, tm_gu, tm_down;
+  CUtensorMap tm_lm, tx_A, tx_att, tx_bn, tx_f;
+};
+
+static int build_maps(FoldPlan* p) {
+  const Sizes z = sizes_of(p->model.dims);
+  const int nt = gemm_ntok(p->m_cap);
+  p->ntok = nt;
+  int st;
+  p->tm_qkv.resize(z.L);
+  p->tm_o.resize(z.L);
+  p->tm_gu.resize(z.L);
+  p->tm_down.resize(z.L);
+  for (int l = 0; l < z.L; ++l) {
+    const af_layer_weights& lw = p->layers[l];
+    if ((st = make_tmap_bf16(&p->tm_qkv[l], lw.w_qkv, z.qkv, z.H, z.H, 128))) return st;
+    if ((st = make_tmap_bf16(&p->tm_o[l], lw.w_o, z.H, z.q, z.q, 128))) return st;
+    if ((st = make_tmap_bf16(&p->tm_gu[l], lw.w_gateup, 2 * z.FF, z.H, z.H, 128))) return st;
+    if ((st = make_tmap_bf16(&p->tm_down[l], lw.w_down, z.H, z.FF, z.FF, 128))) return st;
+  }
+  if ((st = make_tmap_bf16(&p->tm_lm, p->model.lm_head, z.V, z.H, z.H, 128))) return st;
+  if ((st = make_tmap_bf16(&p->tx_A, p->w.A, p->m_cap, z.H, z.H, nt))) return st;
+  if ((st = make_tmap_bf16(&p->tx_att, p->w.att, p->m_cap, z.q, z.q, nt))) return st;
+  if ((st = make_tmap_bf16(&p->tx_bn, p->w.bn, p->m_cap, z.H, z.H, nt))) return st;
+  if ((st = make_tmap_bf16(&p->tx_f, p->w.f, p->m_cap, z.FF, z.FF, nt))) return st;
+  return AF_OK;
+}
+
+template <int METRIC>
+static void launch_fold_gate(const FoldGateArgs& g, int H, unsigned blocks, cudaStream_t s) {
+  const int nv = nv_for(H);
+  if (nv <= 1) k_fold_gate<METRIC, 1><<<blocks, 256, 0, s>>>(g);
+  else if (nv <= 2) k_fold_gate<METRIC, 2><<<blocks, 256, 0, s>>>(g);
+  else if (nv <= 4) k_fold_gate<METRIC, 4><<<blocks, 256, 0, s>>>(g);
+  else if (nv <= 8) k_fold_gate<METRIC, 8><<<blocks, 256, 0, s>>>(g);
+  else k_fold_gate<METRIC, 16><<<blocks, 256, 0, s>>>(g);
+}
+
+static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, float* scores, cudaStream_t s) {
+  const Sizes z = sizes_of(p->model.dims);
+  const FoldWs& w = p->w;
+  const int C = p->C, T = p->T, M = p->m_cap, L = z.L;
+  const float eps = p->model.dims.rms_eps;
+  const unsigned mblocks = (unsigned)((M + 7) / 8);
+  const GateConsts gk = make_gate_consts(AF_DTYPE_BF16, p->tau, 1e-8f, (float)(std::sqrt((double)z.H) + 1e-8));
+  const __nv_bfloat16* p_in = static_cast<const __nv_bfloat16*>(p->parent.layer_in);
+  const __nv_bfloat16* p_qkv = static_cast<const __nv_bfloat16*>(p->parent.qkv);
+  int st;
+
+  // Layer-0 candidates: edited tokens (+ rows the parent fails its own gate on).
+  CandArgs ca;
+  memset(&ca, 0, sizeof(ca));
+  ca.layer = 0;
+  ca.C = C;
+  ca.T = T;
+  ca.m_cap = M;
+  ca.ctok = ctok;
+  ca.ptok = p->parent.tokens;
+  ca.self_stable = p->su[0] ? p->parent.self_stable : nullptr;
+  ca.slot = w.slot;
+  ca.cand_child = w.cand_child;
+  ca.cand_pos = w.cand_pos;
+  ca.cand_src = w.cand_src;
+  ca.n_cand = w.n_cand;
+  ca.fresh0_pos = w.fresh0_pos;
+  ca.n_fresh0 = w.n_fresh0;
+  ca.status = w.status;
+  k_fold_candidates<<<1, 1024, 0, s>>>(ca);
+  k_embed_rows<<<mblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V, ctok,
+                                       w.fresh0_pos, w.n_fresh0, M, w.x_all, w.status);
+
+  for (int l = 0; l < L; ++l) {
+    const af_layer_weights& lw = p->layers[l];
+    int* cc = w.cand_child + (int64_t)l * M;
+    int* cp = w.cand_pos + (int64_t)l * M;
+    int* cs = w.cand_src + (int64_t)l * M;
+    int* nc = w.n_cand + l;
+    int* dcand = w.div_cand + (int64_t)l * M;
+    int* dchild = w.div_child + (int64_t)l * M;
+    int* dpos = w.div_pos + (int64_t)l * M;
+    int* nd = w.n_div + l;
+    const __nv_bfloat16* pin_l = p_in + (int64_t)l * T * z.H;
+    const __nv_bfloat16* pqkv_l = p_qkv + (int64_t)l * T * z.qkv;
+    __nv_bfloat16* x_l = w.x_all + (int64_t)l * M * z.H;
+    __nv_bfloat16* x_next = w.x_all + (int64_t)(l + 1) * M * z.H;
+    const bool last = l == L - 1;
+    const bool next_su = !last && p->su[l + 1];
+
+    FoldGateArgs g;
+    g.n_cand = nc;
+    g.m_cap = M;
+    g.H = z.H;
+    g.cand_pos = cp;
+    g.cand_src = cs;
+    g.x_fresh = x_l;
+    g.p_in = pin_l;
+    g.norm_w = static_cast<const __nv_bfloat16*>(lw.attn_norm);
+    g.eps = eps;
+    g.k = gk;
+    g.stable = w.stable;
+    g.xc = w.xc;
+    g.a = w.A;
+    if (p->metric == AF_METRIC_COSINE) launch_fold_gate<AF_METRIC_COSINE>(g, z.H, mblocks, s);
+    else if (p->metric == AF_METRIC_L2) launch_fold_gate<AF_METRIC_L2>(g, z.H, mblocks, s);
+    else launch_fold_gate<AF_METRIC_PEARSON>(g, z.H, mblocks, s);
+
+    CompactArgs a;
+    memset(&a, 0, sizeof(a));
+    a.C = C;
+    a.T = T;
+    a.m_cap = M;
+    a.bits_ld = w.bits_ld;
+    a.n_cand = nc;
+    a.stable = w.stable;
+    a.cand_child = cc;
+    a.cand_pos = cp;
+    a.div_cand = dcand;
+    a.div_child = dchild;
+    a.div_pos = dpos;
+    a.n_div = nd;
+    a.div_count = w.div_count + (int64_t)l * C;
+    a.bits = w.bits;
+    a.final_bits = last ? w.final_bits : nullptr;
+    a.zero_f = last ? w.row_sums : nullptr;
+    a.zero_n = C * T;
+    a.write_next = !next_su;
+    a.next_child = w.cand_child + (int64_t)(l + 1) * M;
+    a.next_pos = w.cand_pos + (int64_t)(l + 1) * M;
+    a.next_src = w.cand_src + (int64_t)(l + 1) * M;
+    a.next_n_cand = w.n_cand + l + 1;
+    k_fold_compact<<<1, 1024, 0, s>>>(a);
+
+    GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    c.x = w.A;
+    c.ldx = z.H;
+    c.m_cap = M;
+    c.m_dev = nc;
+    c.w = lw.w_qkv;
+    c.n = z.qkv;
+    c.k = z.H;
+    c.epi = EPI_ROPE;
+    c.out = w.qkv;
+    c.ldo = z.qkv;
+    c.rope_cos = p->model.rope_cos;
+    c.rope_sin = p->model.rope_sin;
+    c.positions = cp;
+    c.rope_cols = z.q + z.kv;
+    c.tmap_w = &p->tm_qkv[l];
+    c.tmap_x = &p->tx_A;
+    if ((st = gemm_run(c, s))) return st;
+
+    AttnParams ap;
+    memset(&ap, 0, sizeof(ap));
+    ap.q = w.qkv;
+    ap.q_ld = z.qkv;
+    ap.qsrc = dcand;
+    ap.qchild = dchild;
+    ap.n_q_dev = nd;
+    ap.n_q_cap = M;
+    ap.pk = pqkv_l + z.q;
+    ap.pv = pqkv_l + z.q + z.kv;
+    ap.kv_ld = z.qkv;
+    ap.T = T;
+    ap.fresh_bits = w.bits;
+    ap.bits_ld = w.bits_ld;
+    ap.fk = w.qkv + z.q;
+    ap.fv = w.qkv + z.q + z.kv;
+    ap.f_ld = z.qkv;
+    ap.fchild = cc;
+    ap.n_f_dev = nc;
+    ap.n_f_cap = M;
+    ap.out = w.att;
+    ap.out_ld = z.q;
+    ap.n_heads = p->model.dims.n_heads;
+    ap.n_kv_heads = p->model.dims.n_kv_heads;
+    ap.scale_log2 = (1.0f / sqrtf(128.f)) * 1.4426950408889634f;
+    if ((st = attention_run(ap, s))) return st;
+
+    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    c.x = w.att;
+    c.ldx = z.q;
+    c.m_cap = M;
+    c.m_dev = nd;
+    c.w = lw.w_o;
+    c.n = z.H;
+    c.k = z.q;
+    c.epi = EPI_RESIDUAL;
+    c.out = w.h1;
+    c.ldo = z.H;
+    c.res = w.xc;
+    c.ldr = z.H;
+    c.res_rows = dcand;
+    c.tmap_w = &p->tm_o[l];
+    c.tmap_x = &p->tx_att;
+    if ((st = gemm_run(c, s))) return st;
+
+    AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm), z.H,
+                                                            eps, nd, M, w.bn);
+    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    c.x = w.bn;
+    c.ldx = z.H;
+    c.m_cap = M;
+    c.m_dev = nd;
+    c.w = lw.w_gateup;
+    c.n = 2 * z.FF;
+    c.k = z.H;
+    c.epi = EPI_SWIGLU;
+    c.out = w.f;
+    c.ldo = z.FF;
+    c.tmap_w = &p->tm_gu[l];
+    c.tmap_x = &p->tx_bn;
+    if ((st = gemm_run(c, s))) return st;
+
+    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    c.x = w.f;
+    c.ldx = z.FF;
+    c.m_cap = M;
+    c.m_dev = nd;
+    c.w = lw.w_down;
+    c.n = z.H;
+    c.k = z.FF;
+    c.epi = EPI_RESIDUAL;
+    c.out = x_next;
+    c.ldo = z.H;
+    c.res = w.h1;
+    c.ldr = z.H;
+    c.tmap_w = &p->tm_down[l];
+    c.tmap_x = &p->tx_f;
+    if ((st = gemm_run(c, s))) return st;
+
+    if (next_su) {
+      CandArgs cn;
+      memset(&cn, 0, sizeof(cn));
+      cn.layer = l + 1;
+      cn.C = C;
+      cn.T = T;
+      cn.m_cap = M;
+      cn.self_stable = p->parent.self_stable + (int64_t)(l + 1) * T;
+      cn.prev_div_pos = dpos;
+      cn.prev_n_div = nd;
+      cn.slot = w.slot;
+      cn.cand_child = w.cand_child + (int64_t)(l + 1) * M;
+      cn.cand_pos = w.cand_pos + (int64_t)(l + 1) * M;
+      cn.cand_src = w.cand_src + (int64_t)(l + 1) * M;
+      cn.n_cand = w.n_cand + l + 1;
+      cn.status = w.status;
+      k_fold_candidates<<<1, 1024, 0, s>>>(cn);
+    }
+  }
+
+  // Final rows: fresh after the last layer = its divergent rows.
+  int* nd_last = w.n_div + (L - 1);
+  int* pos_last = w.div_pos + (int64_t)(L - 1) * M;
+  const __nv_bfloat16* x_final = w.x_all + (int64_t)L * M * z.H;
+  AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, x_final, static_cast<const __nv_bfloat16*>(p->model.final_norm),
+                                                          z.H, eps, nd_last, M, w.A);
+  GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+  c.x = w.A;
+  c.ldx = z.H;
+  c.m_cap = M;
+  c.m_dev = nd_last;
+  c.w = p->model.lm_head;
+  c.n = z.V;
+  c.k = z.H;
+  c.epi = EPI_STORE;
+  c.out = logits;
+  c.ldo = z.V;
+  c.out_rows = pos_last;
+  c.row_sums = w.row_sums;
+  c.tmap_w = &p->tm_lm;
+  c.tmap_x = &p->tx_A;
+  if ((st = gemm_run(c, s))) return st;
+  const int smem = C * (int)sizeof(int);
+  k_logits_fill<<<T, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(p->parent.logits), z.V, C, T, w.final_bits,
+                                     w.bits_ld, logits);
+  if (scores)
+    k_scores<<<C, 256, 0, s>>>(p->parent.logit_row_sums, w.row_sums, C, T, z.V, w.final_bits, w.bits_ld, scores);
+  return check_launch("af_fold_run");
+}
+
+}  // namespace af
+
+extern "C" int af_fold_workspace_bytes(const af_model_dims* d, const af_fold_config* cfg, int64_t* bytes) {
+  AF_REQUIRE(d && cfg && bytes, "af_fold_workspace_bytes: null pointer");
+  AF_REQUIRE(cfg->n_children > 0 && cfg->seq > 0 && cfg->m_cap > 0, "af_fold_workspace_bytes: bad sizes");
+  Bump b(nullptr, 0);
+  carve_fold(b, sizes_of(*d), (int)cfg->n_children, (int)cfg->seq, (int)cfg->m_cap);
+  *bytes = b.off + 256;
+  return AF_OK;
+}
+
+extern "C" int af_fold_plan_create(const af_model* m, const af_parent_cache* parent, const af_fold_config* cfg,
+                                   void* workspace, int64_t workspace_bytes, void** plan_out) {
+  int st = validate_model(m);
+  if (st) return st;
+  AF_REQUIRE(parent && cfg && workspace && plan_out, "af_fold_plan_create: null pointer");
+  AF_REQUIRE(parent->tokens && parent->layer_in && parent->qkv && parent->logits && parent->self_stable &&
+                 parent->logit_row_sums,
+             "af_fold_plan_create: incomplete parent cache");
+  AF_REQUIRE(cfg->seq == parent->seq, "af_fold_plan_create: child length must equal the parent's");
+  AF_REQUIRE(cfg->n_children > 0 && cfg->n_children <= 4096, "af_fold_plan_create: n_children out of range");
+  AF_REQUIRE(cfg->seq > 0 && cfg->seq <= m->max_pos, "af_fold_plan_create: seq out of range");
+  AF_REQUIRE(cfg->m_cap > 0 && cfg->m_cap <= cfg->n_children * cfg->seq, "af_fold_plan_create: bad m_cap");
+  AF_REQUIRE(cfg->n_children * cfg->seq <= (1 << 24), "af_fold_plan_create: C * T too large");
+  AF_REQUIRE(cfg->metric >= AF_METRIC_COSINE && cfg->metric <= AF_METRIC_PEARSON, "af_fold_plan_create: bad metric");
+  AF_REQUIRE(cfg->su_layers, "af_fold_plan_create: su_layers required");
+  FoldPlan* p = new FoldPlan();
+  p->model = *m;
+  p->layers.assign(m->layers, m->layers + m->dims.n_layers);
+  p->model.layers = p->layers.data();
+  p->parent = *parent;
+  p->C = (int)cfg->n_children;
+  p->T = (int)cfg->seq;
+  p->m_cap = (int)cfg->m_cap;
+  p->tau = cfg->tau;
+  p->metric = cfg->metric;
+  p->su.assign(cfg->su_layers, cfg->su_layers + m->dims.n_layers);
+  Bump b(workspace, workspace_bytes);
+  p->w = carve_fold(b, sizes_of(m->dims), p->C, p->T, p->m_cap);
+  if (b.off > workspace_bytes) {
+    delete p;
+    return fail(AF_ERR_ARG, "af_fold_plan_create: workspace too small");
+  }
+  if ((st = build_maps(p))) {
+    delete p;
+    return st;
+  }
+  *plan_out = p;
+  return AF_OK;
+}
+
+extern "C" int af_fold_run(void* plan, const int64_t* child_tokens, void* logits, float* scores, void* stream) {
+  AF_REQUIRE(plan && child_tokens && logits, "af_fold_run: null pointer");
+  return fold_run(static_cast<FoldPlan*>(plan), child_tokens, static_cast<__nv_bfloat16*>(logits), scores,
+                  as_stream(stream));
+}
+
+extern "C" int af_fold_get_outputs(void* plan, af_fold_outputs* out) {
+  AF_REQUIRE(plan && out, "af_fold_get_outputs: null pointer");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  out->n_cand = p->w.n_cand;
+  out->n_div = p->w.n_div;
+  out->div_pos = p->w.div_pos;
+  out->div_count = p->w.div_count;
+  out->status = p->w.status;
+  out->m_cap = p->m_cap;
+  out->n_fresh0 = p->w.n_fresh0;
+  out->fresh0_pos = p->w.fresh0_pos;
+  return AF_OK;
+}
+
+extern "C" int af_fold_materialize(void* plan, int64_t layer, void* out, void* stream) {
+  AF_REQUIRE(plan && out, "af_fold_materialize: null pointer");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  const Sizes z = sizes_of(p->model.dims);
+  AF_REQUIRE(layer >= 0 && layer <= z.L, "af_fold_materialize: layer out of range");
+  cudaStream_t s = as_stream(stream);
+  const int64_t rows = (int64_t)p->C * p->T;
+  const __nv_bfloat16* pin = static_cast<const __nv_bfloat16*>(p->parent.layer_in) + layer * p->T * z.H;
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  k_state_parent<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(pin, z.H, p->C, p->T, o);
+  const int* pos = layer == 0 ? p->w.fresh0_pos : p->w.div_pos + (layer - 1) * p->m_cap;
+  const int* n = layer == 0 ? p->w.n_fresh0 : p->w.n_div + (layer - 1);
+  k_state_scatter<<<(unsigned)((p->m_cap + 7) / 8), 256, 0, s>>>(p->w.x_all + layer * p->m_cap * z.H, z.H, pos, n,
+                                                                  p->m_cap, o);
+  return check_launch("af_fold_materialize");
+}
+
+extern "C" int af_fold_plan_destroy(void* plan) {
+  delete static_cast<FoldPlan*>(plan);
+  return AF_OK;
+}

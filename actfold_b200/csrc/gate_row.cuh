@@ -64,22 +64,33 @@ __device__ __forceinline__ float finish_cos(float sc, float sp, const GateConsts
   return 0.f;
 }
 
+// Row held in registers: lane owns vectors v = i * 32 + lane (zero past nvec).
+template <int NV>
+__device__ __forceinline__ void load_row(const char* p, int nvec, int lane, uint4 (&v)[NV]) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    v[i] = j < nvec ? ldg16(p + 16 * (int64_t)j) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <int DT, int METRIC, int NV>
+__device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 (&pv)[NV], int nvec, int H,
+                                             const GateConsts& k, int lane);
+
 template <int DT, int METRIC, int NV>
 __device__ __forceinline__ GateOut gate_row_vec(const char* c, const char* q, int nvec, int H, const GateConsts& k,
                                                 int lane) {
-  constexpr int E = Elt<DT>::kPerVec;
   uint4 cv[NV], pv[NV];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = i * 32 + lane;
-    if (v < nvec) {
-      cv[i] = ldg16(c + 16 * (int64_t)v);
-      pv[i] = ldg16(q + 16 * (int64_t)v);
-    } else {
-      cv[i] = make_uint4(0u, 0u, 0u, 0u);
-      pv[i] = make_uint4(0u, 0u, 0u, 0u);
-    }
-  }
+  load_row<NV>(c, nvec, lane, cv);
+  load_row<NV>(q, nvec, lane, pv);
+  return gate_regs<DT, METRIC, NV>(cv, pv, nvec, H, k, lane);
+}
+
+template <int DT, int METRIC, int NV>
+__device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 (&pv)[NV], int nvec, int H,
+                                             const GateConsts& k, int lane) {
+  constexpr int E = Elt<DT>::kPerVec;
   float presum;
   if constexpr (METRIC == AF_METRIC_COSINE) {
     float sc = 0.f, sp = 0.f;

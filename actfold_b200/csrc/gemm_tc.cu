@@ -48,6 +48,7 @@ struct GemmDev {
   float* acc;
   int* counters;
   unsigned* status;
+  float* row_sums;
 };
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -201,7 +202,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
           const int64_t orow = p.out_rows ? p.out_rows[gm] : gm;
           const float a = tile[r * ld + m];
           if (p.epi == EPI_STORE) {
-            p.out[orow * p.ldo + n] = __float2bfloat16_rn(a);
+            const __nv_bfloat16 ob = __float2bfloat16_rn(a);
+            p.out[orow * p.ldo + n] = ob;
+            if (p.row_sums) {
+              const float part = warp_sum(__bfloat162float(ob));
+              if (lane == 0) atomicAdd(p.row_sums + orow, part);
+            }
           } else if (p.epi == EPI_RESIDUAL) {
             const int64_t rrow = p.res_rows ? p.res_rows[gm] : gm;
             const float rv = __bfloat162float(p.res[rrow * p.ldr + n]);
@@ -376,6 +382,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.acc = c.acc;
   d.counters = c.counters;
   d.status = c.status;
+  d.row_sums = c.epi == EPI_STORE ? c.row_sums : nullptr;
 
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {

@@ -37,6 +37,7 @@ struct GemmCall {
   int counter_elems;   // capacity of counters
   int splits;          // 0 = choose automatically
   unsigned* status;    // device status word (AF_STATUS_* bits)
+  float* row_sums;     // EPI_STORE only, nullable: row_sums[out row] += sum of the row's bf16 outputs
   // Pre-built descriptors (optional; built per call when null).
   const CUtensorMap* tmap_w;
   const CUtensorMap* tmap_x;

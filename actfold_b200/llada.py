@@ -1,0 +1,453 @@
+"""LLaDA / Dream-architecture models on the native folded pass.
+
+``LLaDAModel`` is the weight container of a pre-norm Transformer with RMSNorm,
+rotate-half RoPE, non-causal multi-head / grouped-query attention and a
+SwiGLU FFN (the LLaDA-8B and Dream-7B layouts), stored in bf16 on the GPU in
+the layouts the CUDA kernels stream:
+
+* ``w_qkv``   [q_dim + 2 kv_dim, H]: Wq rows, then Wk, then Wv
+* ``w_gateup``[2 FF, H]: per 128 rows, 64 gate rows then the 64 matching up rows
+* ``w_o`` [H, q_dim], ``w_down`` [H, FF], ``lm_head`` [V, H], norms [H]
+
+``forward(tokens)`` is the dense pass (``af_dense_forward``). Wrapped in
+``FoldedModel``, the model verifies whole batches of children with
+``native_folded_forward``: the parent pass fills a :class:`ParentCache` that is
+registered in the ActivationCache under the parent's branch id, and each child
+batch runs ``af_fold_run`` (gate, compaction, divergent-row recompute, merge,
+logits) with no host synchronisation until the caller reads a result.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass
+from typing import Any, Sequence
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from actfold_b200 import _lib
+from actfold_b200.workloads import ModelDims
+
+_vp, _i32, _i64, _f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_float
+
+
+class _Dims(C.Structure):
+    _fields_ = [
+        ("n_layers", _i32), ("hidden", _i32), ("n_heads", _i32), ("n_kv_heads", _i32),
+        ("head_dim", _i32), ("ffn", _i32), ("vocab", _i32), ("rms_eps", _f32),
+    ]
+
+
+class _Layer(C.Structure):
+    _fields_ = [("attn_norm", _vp), ("w_qkv", _vp), ("w_o", _vp), ("ffn_norm", _vp), ("w_gateup", _vp), ("w_down", _vp)]
+
+
+class _Model(C.Structure):
+    _fields_ = [
+        ("dims", _Dims), ("layers", C.POINTER(_Layer)), ("embed", _vp), ("final_norm", _vp), ("lm_head", _vp),
+        ("rope_cos", _vp), ("rope_sin", _vp), ("max_pos", _i64),
+    ]
+
+
+class _Parent(C.Structure):
+    _fields_ = [
+        ("seq", _i64), ("tokens", _vp), ("layer_in", _vp), ("qkv", _vp), ("logits", _vp),
+        ("self_stable", _vp), ("logit_row_sums", _vp),
+    ]
+
+
+class _FoldConfig(C.Structure):
+    _fields_ = [("n_children", _i64), ("seq", _i64), ("m_cap", _i64), ("tau", _f32), ("metric", _i32), ("su_layers", _vp)]
+
+
+class _FoldOutputs(C.Structure):
+    _fields_ = [
+        ("n_cand", _vp), ("n_div", _vp), ("div_pos", _vp), ("div_count", _vp), ("status", _vp), ("m_cap", _i64),
+        ("n_fresh0", _vp), ("fresh0_pos", _vp),
+    ]
+
+
+_lib.SIGNATURES.update(
+    {
+        "af_dense_workspace_bytes": (_i32, [C.POINTER(_Dims), _i64, C.POINTER(_i64)]),
+        "af_dense_forward": (_i32, [C.POINTER(_Model), _vp, _i64, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp]),
+        "af_fold_workspace_bytes": (_i32, [C.POINTER(_Dims), C.POINTER(_FoldConfig), C.POINTER(_i64)]),
+        "af_fold_plan_create": (_i32, [C.POINTER(_Model), C.POINTER(_Parent), C.POINTER(_FoldConfig), _vp, _i64, C.POINTER(_vp)]),
+        "af_fold_run": (_i32, [_vp, _vp, _vp, _vp, _vp]),
+        "af_fold_get_outputs": (_i32, [_vp, C.POINTER(_FoldOutputs)]),
+        "af_fold_materialize": (_i32, [_vp, _i64, _vp, _vp]),
+        "af_fold_plan_destroy": (_i32, [_vp]),
+    }
+)
+
+
+def _bind_late() -> C.CDLL:
+    lib = _lib.load()
+    for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
+                 "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy"):
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = _lib.SIGNATURES[name]
+    return lib
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[FF, H] x 2 -> [2 FF, H] with 64 gate rows then 64 up rows per 128-row block."""
+    FF, H = w_gate.shape
+    if FF % 64:
+        raise ValueError("ffn must be a multiple of 64")
+    return torch.stack([w_gate.view(FF // 64, 64, H), w_up.view(FF // 64, 64, H)], dim=1).reshape(2 * FF, H).contiguous()
+
+
+def rope_tables(max_pos: int, head_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [max_pos, head_dim/2]: angle t * theta^(-2i/d) in float64, rounded once to float32."""
+    i = torch.arange(0, head_dim, 2, dtype=torch.float64, device=device)
+    inv = 1.0 / (float(theta) ** (i / head_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64, device=device)[:, None] * inv[None, :]
+    return torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous()
+
+
+class LLaDABlock(nn.Module):
+    """Weights of one block (bf16 buffers in kernel layout)."""
+
+    def __init__(self, attn_norm, w_qkv, w_o, ffn_norm, w_gateup, w_down) -> None:
+        super().__init__()
+        for k, v in dict(attn_norm=attn_norm, w_qkv=w_qkv, w_o=w_o, ffn_norm=ffn_norm, w_gateup=w_gateup, w_down=w_down).items():
+            self.register_buffer(k, v.contiguous())
+
+    def forward(self, hidden_states: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        raise RuntimeError("LLaDABlock runs inside the native folded pass; call LLaDAModel or FoldedModel instead")
+
+
+@dataclass
+class ParentCache:
+    """Dense parent activations consumed by the folded pass (one per parent branch)."""
+
+    tokens: torch.Tensor        # [T] int64
+    layer_in: torch.Tensor      # [L+1, T, H] bf16
+    qkv: torch.Tensor           # [L, T, q+2kv] bf16
+    logits: torch.Tensor        # [T, V] bf16
+    self_stable: torch.Tensor   # [L, T] uint8
+    row_sums: torch.Tensor      # [T] fp32
+    tau: float
+
+    @property
+    def seq(self) -> int:
+        return int(self.tokens.shape[0])
+
+    def su_layers(self) -> np.ndarray:
+        """Host flags: layers where some parent row fails its own gate (one small copy)."""
+        return (self.self_stable == 0).any(dim=1).to(torch.uint8).cpu().numpy()
+
+    def struct(self) -> _Parent:
+        return _Parent(self.seq, self.tokens.data_ptr(), self.layer_in.data_ptr(), self.qkv.data_ptr(),
+                       self.logits.data_ptr(), self.self_stable.data_ptr(), self.row_sums.data_ptr())
+
+    def tensors(self) -> list[torch.Tensor]:
+        return [self.tokens, self.layer_in, self.qkv, self.logits, self.self_stable, self.row_sums]
+
+
+class FoldPlan:
+    """A prepared folded pass for C children of length T with m_cap candidate rows."""
+
+    def __init__(self, model: "LLaDAModel", parent: ParentCache, n_children: int, m_cap: int, tau: float, metric: str = "cosine") -> None:
+        self.lib = _bind_late()
+        self.model = model
+        self.parent = parent
+        self.C, self.T, self.m_cap, self.tau = n_children, parent.seq, m_cap, tau
+        su = parent.su_layers() if tau == parent.tau else self._su_for_tau(tau)
+        self._su = np.ascontiguousarray(su.astype(np.uint8))
+        self._cfg = _FoldConfig(n_children, self.T, m_cap, float(tau), _lib.METRIC[metric], self._su.ctypes.data)
+        nbytes = _i64()
+        _lib.check(self.lib.af_fold_workspace_bytes(C.byref(model._cmodel.dims), C.byref(self._cfg), C.byref(nbytes)))
+        self.workspace = torch.zeros(int(nbytes.value), dtype=torch.uint8, device=model.device)
+        self._pstruct = parent.struct()
+        plan = _vp()
+        _lib.check(self.lib.af_fold_plan_create(C.byref(model._cmodel), C.byref(self._pstruct), C.byref(self._cfg),
+                                                self.workspace.data_ptr(), self.workspace.numel(), C.byref(plan)))
+        self._plan = plan
+        out = _FoldOutputs()
+        _lib.check(self.lib.af_fold_get_outputs(plan, C.byref(out)))
+        L = model.dims.n_layers
+        ws = self.workspace
+        base = ws.data_ptr()
+
+        def view(ptr, n, dtype):
+            off = ptr - base
+            itemsize = torch.empty((), dtype=dtype).element_size()
+            return ws[off: off + n * itemsize].view(dtype)
+
+        self.n_cand = view(out.n_cand, L + 1, torch.int32)
+        self.n_div = view(out.n_div, L, torch.int32)
+        self.div_pos = view(out.div_pos, L * m_cap, torch.int32).view(L, m_cap)
+        self.div_count = view(out.div_count, L * n_children, torch.int32).view(L, n_children)
+        self.status = view(out.status, 1, torch.int32)
+        self.n_fresh0 = view(out.n_fresh0, 1, torch.int32)
+
+    def _su_for_tau(self, tau: float) -> np.ndarray:
+        # Self-gate results depend on tau; recompute the flags for a different tau.
+        from actfold_b200.core.similarity_gate import SimilarityGate
+
+        x = self.parent.layer_in[:-1]
+        m = SimilarityGate(tau=tau)(x, x)
+        return (~m).any(dim=1).to(torch.uint8).cpu().numpy()
+
+    def run(self, child_tokens: torch.Tensor, logits: torch.Tensor, scores: torch.Tensor | None = None) -> None:
+        if child_tokens.shape != (self.C, self.T) or child_tokens.dtype != torch.int64 or not child_tokens.is_contiguous():
+            raise ValueError(f"child_tokens must be contiguous int64 [{self.C}, {self.T}]")
+        st = self.lib.af_fold_run(self._plan, child_tokens.data_ptr(), logits.data_ptr(), _lib.ptr(scores),
+                                  _lib.stream_ptr(child_tokens.device))
+        _lib.check(st, "af_fold_run")
+
+    def materialize(self, layer: int) -> torch.Tensor:
+        out = torch.empty((self.C, self.T, self.model.dims.hidden), dtype=torch.bfloat16, device=self.model.device)
+        _lib.check(self.lib.af_fold_materialize(self._plan, layer, out.data_ptr(), _lib.stream_ptr(out.device)))
+        return out
+
+    def stable_masks(self) -> torch.Tensor:
+        """[L, C, T] bool stability masks of the last pass, rebuilt on the device from the divergent lists."""
+        L = self.model.dims.n_layers
+        masks = torch.ones((L, self.C * self.T), dtype=torch.bool, device=self.model.device)
+        idx = torch.arange(self.m_cap, device=self.model.device)[None, :]
+        valid = idx < self.n_div[:, None].long()
+        flat = (torch.arange(L, device=masks.device)[:, None] * (self.C * self.T) + self.div_pos.long())[valid]
+        masks.view(-1)[flat] = False
+        return masks.view(L, self.C, self.T)
+
+    def check_status(self) -> None:
+        s = int(self.status.item())
+        if s:
+            self.status.zero_()
+            if s & 1:
+                raise TimeoutError(f"folded pass: a device wait timed out (status {s:#x})")
+            if s & 2:
+                raise ValueError(f"folded pass: candidate rows exceeded m_cap={self.m_cap} (status {s:#x})")
+            raise RuntimeError(f"folded pass: device check failed (status {s:#x})")
+
+    def __del__(self) -> None:
+        plan = getattr(self, "_plan", None)
+        if plan is not None and plan.value:
+            try:
+                self.lib.af_fold_plan_destroy(plan)
+            except Exception:  # pragma: no cover - interpreter shutdown
+                pass
+            self._plan = None
+
+
+class LLaDAModel(nn.Module):
+    """LLaDA/Dream-architecture weights + native dense and folded passes (CUDA only)."""
+
+    def __init__(self, dims: ModelDims, embed, layers: Sequence[LLaDABlock], final_norm, lm_head, max_pos: int = 4096) -> None:
+        super().__init__()
+        self.dims = dims
+        self.register_buffer("embed", embed.contiguous())
+        self.layers = nn.ModuleList(layers)
+        self.register_buffer("final_norm", final_norm.contiguous())
+        self.register_buffer("lm_head", lm_head.contiguous())
+        cos, sin = rope_tables(max_pos, dims.head_dim, dims.rope_theta, embed.device)
+        self.register_buffer("rope_cos", cos)
+        self.register_buffer("rope_sin", sin)
+        self.max_pos = max_pos
+        self._plans: dict = {}
+        self._build_struct()
+
+    @property
+    def device(self) -> torch.device:
+        return self.embed.device
+
+    # ------------------------------------------------------------ construction
+    @classmethod
+    def from_numpy(cls, dims: ModelDims, w: dict, device="cuda", max_pos: int = 4096) -> "LLaDAModel":
+        """From float32 arrays named as in ``workloads.llada_weights_numpy`` (rounded to bf16)."""
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device=device, dtype=torch.bfloat16)  # noqa: E731
+        layers = [
+            LLaDABlock(
+                t(lw["attn_norm"]),
+                torch.cat([t(lw["wq"]), t(lw["wk"]), t(lw["wv"])], dim=0),
+                t(lw["wo"]),
+                t(lw["ffn_norm"]),
+                interleave_gate_up(t(lw["w_gate"]), t(lw["w_up"])),
+                t(lw["w_down"]),
+            )
+            for lw in w["layers"]
+        ]
+        return cls(dims, t(w["embed"]), layers, t(w["final_norm"]), t(w["lm_head"]), max_pos=max_pos)
+
+    @classmethod
+    def random(cls, dims: ModelDims, seed: int = 0, device="cuda", std: float = 0.02, max_pos: int = 4096) -> "LLaDAModel":
+        """N(0, std) weights drawn on the device (seeded), unit RMSNorm weights."""
+        g = torch.Generator(device=device).manual_seed(seed)
+        H = dims.hidden
+
+        def w(*shape):
+            out = torch.empty(shape, dtype=torch.bfloat16, device=device)
+            # draw in chunks to bound the float32 temporary
+            flat = out.view(-1)
+            step = 1 << 26
+            for i in range(0, flat.numel(), step):
+                n = min(step, flat.numel() - i)
+                flat[i: i + n] = (torch.randn(n, generator=g, device=device) * std).to(torch.bfloat16)
+            return out
+
+        ones = lambda: torch.ones(H, dtype=torch.bfloat16, device=device)  # noqa: E731
+        layers = [
+            LLaDABlock(ones(), w(dims.q_dim + 2 * dims.kv_dim, H), w(H, dims.q_dim), ones(), w(2 * dims.ffn, H), w(H, dims.ffn))
+            for _ in range(dims.n_layers)
+        ]
+        return cls(dims, w(dims.vocab, H), layers, ones(), w(dims.vocab, H), max_pos=max_pos)
+
+    def _build_struct(self) -> None:
+        d = self.dims
+        self._cdims = _Dims(d.n_layers, d.hidden, d.n_heads, d.n_kv_heads, d.head_dim, d.ffn, d.vocab, d.rms_eps)
+        arr = (_Layer * d.n_layers)()
+        for i, b in enumerate(self.layers):
+            arr[i] = _Layer(b.attn_norm.data_ptr(), b.w_qkv.data_ptr(), b.w_o.data_ptr(), b.ffn_norm.data_ptr(),
+                            b.w_gateup.data_ptr(), b.w_down.data_ptr())
+        self._clayers = arr
+        self._cmodel = _Model(self._cdims, C.cast(arr, C.POINTER(_Layer)), self.embed.data_ptr(), self.final_norm.data_ptr(),
+                              self.lm_head.data_ptr(), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), self.max_pos)
+
+    # ------------------------------------------------------------ dense pass
+    def parent_pass(self, tokens: torch.Tensor, tau: float = 0.95) -> ParentCache:
+        """Dense pass over one sequence [T] (or [1, T]); returns the parent cache."""
+        _lib.require_cuda(self.embed, what="LLaDAModel")
+        tokens = tokens.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
+        T = tokens.shape[0]
+        if T > self.max_pos:
+            raise ValueError(f"sequence {T} longer than max_pos {self.max_pos}")
+        d = self.dims
+        dev = self.device
+        lib = _bind_late()
+        layer_in = torch.empty((d.n_layers + 1, T, d.hidden), dtype=torch.bfloat16, device=dev)
+        qkv = torch.empty((d.n_layers, T, d.q_dim + 2 * d.kv_dim), dtype=torch.bfloat16, device=dev)
+        logits = torch.empty((T, d.vocab), dtype=torch.bfloat16, device=dev)
+        self_stable = torch.empty((d.n_layers, T), dtype=torch.uint8, device=dev)
+        row_sums = torch.empty((T,), dtype=torch.float32, device=dev)
+        nb = _i64()
+        _lib.check(lib.af_dense_workspace_bytes(C.byref(self._cdims), T, C.byref(nb)))
+        ws = torch.zeros(int(nb.value), dtype=torch.uint8, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            st = lib.af_dense_forward(C.byref(self._cmodel), tokens.data_ptr(), T, float(tau), layer_in.data_ptr(), qkv.data_ptr(),
+                                      logits.data_ptr(), self_stable.data_ptr(), row_sums.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      status.data_ptr(), _lib.stream_ptr(dev))
+        _lib.check(st, "af_dense_forward")
+        s = int(status.item())
+        if s:
+            raise TimeoutError(f"dense pass: device status {s:#x}") if s & 1 else RuntimeError(f"dense pass: device status {s:#x}")
+        return ParentCache(tokens, layer_in, qkv, logits, self_stable, row_sums, float(tau))
+
+    def forward(self, tokens: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """Plain (unfolded) logits [B, T, V] for tokens [B, T]: one dense pass per row."""
+        tokens = tokens.to(self.device)
+        if tokens.dim() == 1:
+            tokens = tokens[None]
+        return torch.stack([self.parent_pass(tokens[b]).logits for b in range(tokens.shape[0])])
+
+    # ------------------------------------------------------------ folded pass
+    def plan(self, parent: ParentCache, n_children: int, m_cap: int, tau: float, metric: str = "cosine") -> FoldPlan:
+        key = (id(parent), n_children, m_cap, float(tau), metric)
+        p = self._plans.get(key)
+        if p is None or p.parent is not parent:
+            p = FoldPlan(self, parent, n_children, m_cap, tau, metric)
+            self._plans = {k: v for k, v in self._plans.items() if v.parent is parent}
+            self._plans[key] = p
+        return p
+
+    @staticmethod
+    def capacity(child_tokens: torch.Tensor, parent: ParentCache, su: np.ndarray) -> int:
+        """Rows a pass can need: edited rows + every child x every row the parent fails its own gate on."""
+        C, T = child_tokens.shape
+        edited = int((child_tokens != parent.tokens[None]).sum().item())
+        su_rows = int((parent.self_stable == 0).any(dim=0).sum().item()) if su.any() else 0
+        cap = edited + C * su_rows
+        cap = max(16, ((cap + 15) // 16) * 16)
+        return min(cap, ((C * T + 15) // 16) * 16)
+
+    def verify(self, child_tokens: torch.Tensor, parent: ParentCache, tau: float, metric: str = "cosine",
+               logits: torch.Tensor | None = None, scores: torch.Tensor | None = None, m_cap: int | None = None) -> tuple[torch.Tensor, FoldPlan]:
+        """Folded verification of child_tokens [C, T] against ``parent``; returns (logits [C, T, V], plan)."""
+        child_tokens = child_tokens.to(device=self.device, dtype=torch.int64).contiguous()
+        if child_tokens.dim() != 2 or child_tokens.shape[1] != parent.seq:
+            raise ValueError(f"children must be [C, {parent.seq}], got {tuple(child_tokens.shape)}")
+        Cn = child_tokens.shape[0]
+        if m_cap is None:
+            m_cap = self.capacity(child_tokens, parent, parent.su_layers())
+        plan = self.plan(parent, Cn, m_cap, tau, metric)
+        if logits is None:
+            logits = torch.empty((Cn, parent.seq, self.dims.vocab), dtype=torch.bfloat16, device=self.device)
+        plan.run(child_tokens, logits, scores)
+        return logits, plan
+
+    def native_folded_forward(self, tokens: torch.Tensor, cache, gate, branch_id: Any, parent_branch_id: Any = None,
+                              step_idx: int = 0, scheduler=None, **kwargs: Any) -> torch.Tensor:
+        """FoldedModel.forward for this architecture (see actfold_b200.core.model_wrapper)."""
+        from actfold_b200.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER
+
+        if scheduler is not None:
+            raise NotImplementedError("the native LLaDA pass folds with one tau for every layer; use scheduler=None")
+        tokens = tokens.to(self.device)
+        if tokens.dim() == 1:
+            tokens = tokens[None]
+        parents = getattr(cache, "native_parents", None)
+        if parents is None:
+            parents = {}
+            cache.native_parents = parents
+        if parent_branch_id is None:
+            if tokens.shape[0] != 1:
+                raise ValueError("a parent pass takes one sequence [1, T]")
+            pc = self.parent_pass(tokens[0], tau=gate.tau)
+            parents[branch_id] = pc
+            register_parent_in_cache(cache, branch_id, pc)
+            return pc.logits[None]
+        pc = parents.get(parent_branch_id)
+        if pc is None or pc.seq != tokens.shape[1]:
+            # No usable parent activations: recompute (folded_transformer.py:135-141).
+            return self.forward(tokens)
+        logits, plan = self.verify(tokens, pc, gate.tau, gate.metric)
+        plan.check_status()
+        ids = list(branch_id) if isinstance(branch_id, (list, tuple)) else [branch_id] * tokens.shape[0]
+        if len(set(ids)) == len(ids):
+            GLOBAL_STABILITY_PROFILER.record_batch(ids, parent_branch_id, step_idx, plan.stable_masks(), gate.tau, gate.metric)
+        else:
+            masks = plan.stable_masks()
+            for li in range(masks.shape[0]):
+                GLOBAL_STABILITY_PROFILER.record(ids[0], parent_branch_id, li, step_idx, masks[li], gate.tau, gate.metric)
+        return logits
+
+
+def register_parent_in_cache(cache, branch_id: Any, pc: ParentCache) -> None:
+    """Expose the parent's per-layer input / output through the ActivationCache API (views, no copies)."""
+    put_views = getattr(cache, "put_views", None)
+    if put_views is None:
+        return
+    L = pc.layer_in.shape[0] - 1
+    for li in range(L):
+        put_views(branch_id, li, {"ffn_out": pc.layer_in[li + 1][None], "hidden_states": pc.layer_in[li][None]})
+
+
+def smoke_check() -> None:
+    """One tiny folded verification on cuda:0 checked against the oracle (used by smoke())."""
+    from actfold_b200 import workloads as W
+    from oracle import folding as OF
+    from oracle import llada as OL
+
+    dims = W.LLADA_TINY
+    w = W.llada_weights_numpy(dims, seed=7)
+    parent, children = W.llada_tokens(64, 16, 0.5, 4, 4, dims.mask_id, 42)
+    model = LLaDAModel.from_numpy(dims, w, device="cuda", max_pos=64)
+    pc = model.parent_pass(torch.from_numpy(parent).cuda(), tau=0.95)
+    logits, plan = model.verify(torch.from_numpy(children).cuda(), pc, 0.95)
+    plan.check_status()
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    ref_par = OF.llada_parent(parent, w, od)
+    ref = OF.llada_folded_children(children, ref_par, w, od, 0.95)
+    masks = plan.stable_masks().cpu().numpy()
+    assert (masks == ref["masks"]).mean() >= 0.999, "folded masks disagree with the oracle"
+    got = logits.float().cpu().numpy()
+    err = np.abs(got - ref["logits"]).max() / np.abs(ref["logits"]).max()
+    assert err <= 2e-2, f"folded logits rel err {err}"
+    cos = (got * ref["logits"]).sum() / math.sqrt((got * got).sum() * (ref["logits"] ** 2).sum())
+    assert cos >= 0.999, cos

@@ -170,6 +170,97 @@ int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsrc, const in
                       const int32_t* n_f_dev, int64_t n_f_cap, void* out, int64_t out_ld,
                       int n_heads, int n_kv_heads, int head_dim, float scale, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Native folded verification of LLaDA / Dream-architecture models.
+ *
+ * Replaces, for a model whose blocks are pre-norm RMSNorm -> QKV (+RoPE) ->
+ * non-causal attention -> O + residual -> RMSNorm -> SwiGLU FFN + residual,
+ * the whole per-layer loop of FoldedModel.forward / FoldedTransformerLayer
+ * (actfold/core/model_wrapper.py:137-208, actfold/core/folded_transformer.py:60-203)
+ * for a batch of children sharing one parent: gates, index compaction,
+ * recompute of divergent rows only, merge of parent rows, logits.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
+  float rms_eps;
+} af_model_dims;
+
+typedef struct {
+  const void* attn_norm; /* [hidden] bf16 */
+  const void* w_qkv;     /* [q_dim + 2 kv_dim, hidden] bf16: Wq rows, Wk rows, Wv rows */
+  const void* w_o;       /* [hidden, q_dim] */
+  const void* ffn_norm;  /* [hidden] */
+  const void* w_gateup;  /* [2 ffn, hidden]: per 128 rows, 64 gate rows then the 64 matching up rows */
+  const void* w_down;    /* [hidden, ffn] */
+} af_layer_weights;
+
+typedef struct {
+  af_model_dims dims;
+  const af_layer_weights* layers; /* host array of n_layers entries (copied by plans) */
+  const void* embed;              /* [vocab, hidden] bf16 */
+  const void* final_norm;         /* [hidden] */
+  const void* lm_head;            /* [vocab, hidden] */
+  const float* rope_cos;          /* [max_pos, head_dim / 2] fp32 */
+  const float* rope_sin;
+  int64_t max_pos;
+} af_model;
+
+/* Parent activation cache (the dense equivalent of ActivationCache entries of the parent branch). */
+typedef struct {
+  int64_t seq;                  /* T */
+  const int64_t* tokens;        /* [T] */
+  const void* layer_in;         /* [n_layers + 1, T, hidden] bf16: layer inputs; [n_layers] = final hidden */
+  const void* qkv;              /* [n_layers, T, q_dim + 2 kv_dim] bf16 (K at column q_dim, V after it) */
+  const void* logits;           /* [T, vocab] bf16 */
+  const uint8_t* self_stable;   /* [n_layers, T] gate(parent row, parent row) */
+  const float* logit_row_sums;  /* [T] fp32 sums of each logits row */
+} af_parent_cache;
+
+/* Workspace of af_dense_forward for T tokens. */
+int af_dense_workspace_bytes(const af_model_dims* dims, int64_t T, int64_t* bytes);
+
+/*
+ * af_dense_forward -- the parent pass (FoldedTransformerLayer with
+ * parent_branch_id None -> _recompute_all + _store_activations,
+ * actfold/core/folded_transformer.py:100-104): runs every layer on all T rows
+ * and writes the parent cache arrays.
+ */
+int af_dense_forward(const af_model* model, const int64_t* tokens, int64_t T, float tau,
+                     void* layer_in, void* qkv, void* logits, uint8_t* self_stable,
+                     float* logit_row_sums, void* workspace, int64_t workspace_bytes,
+                     uint32_t* status, void* stream);
+
+typedef struct {
+  int64_t n_children;          /* C */
+  int64_t seq;                 /* T (equal to the parent's) */
+  int64_t m_cap;               /* capacity for candidate / divergent rows per layer (all children) */
+  float tau;                   /* SimilarityGate tau (compared in bf16) */
+  int32_t metric;              /* af_metric */
+  const uint8_t* su_layers;    /* host [n_layers]: 1 where some parent row fails its own gate */
+} af_fold_config;
+
+typedef struct {
+  const int32_t* n_cand;       /* [n_layers + 1] candidate rows per layer (device) */
+  const int32_t* n_div;        /* [n_layers] divergent rows per layer */
+  const int32_t* div_pos;      /* [n_layers, m_cap] divergent rows as child * T + t, in that order */
+  const int32_t* div_count;    /* [n_layers, C] divergent rows per child */
+  const uint32_t* status;      /* device status word (AF_STATUS bits) */
+  int64_t m_cap;
+  const int32_t* n_fresh0;     /* edited rows at layer 0 */
+  const int32_t* fresh0_pos;   /* [m_cap] */
+} af_fold_outputs;
+
+int af_fold_workspace_bytes(const af_model_dims* dims, const af_fold_config* cfg, int64_t* bytes);
+int af_fold_plan_create(const af_model* model, const af_parent_cache* parent, const af_fold_config* cfg,
+                        void* workspace, int64_t workspace_bytes, void** plan);
+/* One verification pass of child_tokens [C, T]; writes logits [C, T, vocab] bf16 and
+ * (nullable) scores [C] = mean of each child's logits. No host synchronisation. */
+int af_fold_run(void* plan, const int64_t* child_tokens, void* logits, float* scores, void* stream);
+int af_fold_get_outputs(void* plan, af_fold_outputs* out);
+/* Dense input of layer `layer` (0..n_layers) for every child: out [C, T, hidden] bf16. */
+int af_fold_materialize(void* plan, int64_t layer, void* out, void* stream);
+int af_fold_plan_destroy(void* plan);
+
 #ifdef __cplusplus
 }
 #endif

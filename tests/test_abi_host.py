@@ -13,6 +13,8 @@ import re
 import pytest
 
 from actfold_b200 import _lib
+import actfold_b200.kernels  # noqa: F401  (registers GEMM/attention signatures)
+import actfold_b200.llada  # noqa: F401  (registers the folded-pass signatures)
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
