@@ -33,10 +33,9 @@ SIGNATURES: dict[str, tuple] = {
     "af_merge_rows": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "af_gather_rows_masked": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "af_gather_rows_index": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp]),
-    "af_linear_workspace": (_i32, [_i64, _i64, C.POINTER(_i64), C.POINTER(_i64)]),
     "af_linear_bf16": (
         _i32,
-        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _vp, _vp],
+        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _vp],
     ),
     "af_attention_bf16": (
         _i32,

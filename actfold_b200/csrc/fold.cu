@@ -474,10 +474,6 @@ static Sizes sizes_of(const af_model_dims& d) {
 struct DenseWs {
   __nv_bfloat16 *A, *att, *h1, *bn, *f;
   int* pos;
-  float* acc;
-  int* counters;
-  int64_t acc_elems;
-  int counter_elems;
 };
 
 static DenseWs carve_dense(Bump& b, const Sizes& s, int T) {
@@ -488,26 +484,12 @@ static DenseWs carve_dense(Bump& b, const Sizes& s, int T) {
   w.bn = b.take<__nv_bfloat16>((int64_t)T * s.H);
   w.f = b.take<__nv_bfloat16>((int64_t)T * s.FF);
   w.pos = b.take<int>(T);
-  const int nmax = std::max(std::max(s.qkv, s.H), 2 * s.FF);
-  int64_t ae;
-  int ce;
-  gemm_workspace(nmax, T, &ae, &ce);
-  // Split-K is only chosen when the tiles alone cannot fill the GPU; budget a modest accumulator.
-  ae = std::min<int64_t>(ae, (int64_t)1 << 24);
-  w.acc = b.take<float>(ae);
-  w.counters = b.take<int>(ce);
-  w.acc_elems = ae;
-  w.counter_elems = ce;
   return w;
 }
 
-static GemmCall base_call(float* acc, int64_t acc_elems, int* counters, int counter_elems, unsigned* status) {
+static GemmCall base_call(unsigned* status) {
   GemmCall c;
   memset(&c, 0, sizeof(c));
-  c.acc = acc;
-  c.acc_elems = acc_elems;
-  c.counters = counters;
-  c.counter_elems = counter_elems;
   c.status = status;
   c.head_dim = 128;
   return c;
@@ -557,7 +539,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, x, static_cast<const __nv_bfloat16*>(lw.attn_norm), z.H,
                                                                 eps, nullptr, Ti, w.A);
     AF_DISPATCH_NV(z.H, k_self_gate, rows_blocks, 256, 0, s, x, z.H, Ti, gk, self_stable + (int64_t)l * Ti);
-    GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    GemmCall c = base_call(stw);
     c.x = w.A;
     c.ldx = z.H;
     c.m_cap = Ti;
@@ -587,7 +569,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     ap.n_kv_heads = m->dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf((float)m->dims.head_dim)) * 1.4426950408889634f;
     if ((st = attention_run(ap, s))) return st;
-    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c = base_call(stw);
     c.x = w.att;
     c.ldx = z.q;
     c.m_cap = Ti;
@@ -602,7 +584,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     if ((st = gemm_run(c, s))) return st;
     AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm),
                                                                 z.H, eps, nullptr, Ti, w.bn);
-    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c = base_call(stw);
     c.x = w.bn;
     c.ldx = z.H;
     c.m_cap = Ti;
@@ -613,7 +595,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     c.out = w.f;
     c.ldo = z.FF;
     if ((st = gemm_run(c, s))) return st;
-    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+    c = base_call(stw);
     c.x = w.f;
     c.ldx = z.FF;
     c.m_cap = Ti;
@@ -631,7 +613,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
   AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, xl, static_cast<const __nv_bfloat16*>(m->final_norm),
                                                               z.H, eps, nullptr, Ti, w.A);
   k_zero_f32<<<(Ti + 255) / 256, 256, 0, s>>>(logit_row_sums, Ti);
-  GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, stw);
+  GemmCall c = base_call(stw);
   c.x = w.A;
   c.ldx = z.H;
   c.m_cap = Ti;
@@ -659,10 +641,6 @@ struct FoldWs {
   int* div_count;  // [L, C]
   __nv_bfloat16 *x_all, *xc, *A, *qkv, *att, *h1, *bn, *f;
   float* row_sums;  // [C*T] fresh logit row sums
-  float* acc;
-  int* counters;
-  int64_t acc_elems;
-  int counter_elems;
   unsigned* status;
   int bits_ld;
 };
@@ -695,17 +673,74 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
   w.bn = b.take<__nv_bfloat16>((int64_t)m_cap * z.H);
   w.f = b.take<__nv_bfloat16>((int64_t)m_cap * z.FF);
   w.row_sums = b.take<float>((int64_t)C * T);
-  const int nmax = std::max(std::max(z.qkv, z.H), 2 * z.FF);
-  int64_t ae;
-  int ce;
-  gemm_workspace(nmax, m_cap, &ae, &ce);
-  w.acc = b.take<float>(ae);
-  w.counters = b.take<int>(ce);
-  w.acc_elems = ae;
-  w.counter_elems = ce;
   w.status = b.take<unsigned>(1);
   return w;
 }
+
+// Kernel classes of a folded pass (per-class CUDA-event timing).
+enum FoldKind {
+  FK_SETUP = 0, FK_GATE, FK_COMPACT, FK_QKV, FK_ATTN, FK_O, FK_NORM, FK_GATEUP, FK_DOWN, FK_LM, FK_FILL, FK_SCORES,
+  FK_COUNT
+};
+
+// Optional CUDA-event brackets around each launch of a pass, on the pass's stream.
+struct KernelTimer {
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  struct Mark {
+    int kind;
+    cudaEvent_t b, e;
+  };
+  std::vector<Mark> marks;
+  double ms[FK_COUNT] = {};
+  int64_t n[FK_COUNT] = {};
+  int64_t launches = 0;
+
+  cudaEvent_t next() {
+    if (used == pool.size()) {
+      cudaEvent_t ev;
+      cudaEventCreate(&ev);
+      pool.push_back(ev);
+    }
+    return pool[used++];
+  }
+  cudaEvent_t begin(cudaStream_t s) {
+    if (!on) return nullptr;
+    cudaEvent_t b = next();
+    cudaEventRecord(b, s);
+    return b;
+  }
+  void end(int kind, cudaStream_t s, cudaEvent_t b) {
+    ++launches;
+    if (!on || !b) return;
+    cudaEvent_t e = next();
+    cudaEventRecord(e, s);
+    marks.push_back({kind, b, e});
+  }
+  void collect() {
+    if (!marks.empty()) cudaEventSynchronize(marks.back().e);
+    for (const Mark& m : marks) {
+      float t = 0.f;
+      if (cudaEventElapsedTime(&t, m.b, m.e) == cudaSuccess) {
+        ms[m.kind] += t;
+        n[m.kind] += 1;
+      }
+    }
+    marks.clear();
+    used = 0;
+  }
+  ~KernelTimer() {
+    for (cudaEvent_t e : pool) cudaEventDestroy(e);
+  }
+};
+
+#define AF_TIMED(KIND, ...)                  \
+  do {                                       \
+    cudaEvent_t _b = p->tk.begin(s);         \
+    __VA_ARGS__;                             \
+    p->tk.end(KIND, s, _b);                  \
+  } while (0)
 
 struct FoldPlan {
   af_model model;
@@ -719,6 +754,8 @@ struct FoldPlan {
   int ntok;
   std::vector<CUtensorMap> tm_qkv, tm_o, tm_gu, tm_down;
   CUtensorMap tm_lm, tx_A, tx_att, tx_bn, tx_f;
+  KernelTimer tk;
+  int64_t last_launches = 0;
 };
 
 static int build_maps(FoldPlan* p) {
@@ -765,6 +802,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   const __nv_bfloat16* p_in = static_cast<const __nv_bfloat16*>(p->parent.layer_in);
   const __nv_bfloat16* p_qkv = static_cast<const __nv_bfloat16*>(p->parent.qkv);
   int st;
+  p->tk.launches = 0;
 
   // Layer-0 candidates: edited tokens (+ rows the parent fails its own gate on).
   CandArgs ca;
@@ -784,9 +822,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   ca.fresh0_pos = w.fresh0_pos;
   ca.n_fresh0 = w.n_fresh0;
   ca.status = w.status;
-  k_fold_candidates<<<1, 1024, 0, s>>>(ca);
-  k_embed_rows<<<mblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V, ctok,
-                                       w.fresh0_pos, w.n_fresh0, M, w.x_all, w.status);
+  AF_TIMED(FK_SETUP, k_fold_candidates<<<1, 1024, 0, s>>>(ca));
+  AF_TIMED(FK_SETUP, k_embed_rows<<<mblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V,
+                                                           ctok, w.fresh0_pos, w.n_fresh0, M, w.x_all, w.status));
 
   for (int l = 0; l < L; ++l) {
     const af_layer_weights& lw = p->layers[l];
@@ -819,9 +857,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     g.stable = w.stable;
     g.xc = w.xc;
     g.a = w.A;
-    if (p->metric == AF_METRIC_COSINE) launch_fold_gate<AF_METRIC_COSINE>(g, z.H, mblocks, s);
-    else if (p->metric == AF_METRIC_L2) launch_fold_gate<AF_METRIC_L2>(g, z.H, mblocks, s);
-    else launch_fold_gate<AF_METRIC_PEARSON>(g, z.H, mblocks, s);
+    AF_TIMED(FK_GATE, if (p->metric == AF_METRIC_COSINE) launch_fold_gate<AF_METRIC_COSINE>(g, z.H, mblocks, s);
+             else if (p->metric == AF_METRIC_L2) launch_fold_gate<AF_METRIC_L2>(g, z.H, mblocks, s);
+             else launch_fold_gate<AF_METRIC_PEARSON>(g, z.H, mblocks, s));
 
     CompactArgs a;
     memset(&a, 0, sizeof(a));
@@ -847,9 +885,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     a.next_pos = w.cand_pos + (int64_t)(l + 1) * M;
     a.next_src = w.cand_src + (int64_t)(l + 1) * M;
     a.next_n_cand = w.n_cand + l + 1;
-    k_fold_compact<<<1, 1024, 0, s>>>(a);
+    AF_TIMED(FK_COMPACT, k_fold_compact<<<1, 1024, 0, s>>>(a));
 
-    GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    GemmCall c = base_call(w.status);
     c.x = w.A;
     c.ldx = z.H;
     c.m_cap = M;
@@ -866,7 +904,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.rope_cols = z.q + z.kv;
     c.tmap_w = &p->tm_qkv[l];
     c.tmap_x = &p->tx_A;
-    if ((st = gemm_run(c, s))) return st;
+    AF_TIMED(FK_QKV, if ((st = gemm_run(c, s))) return st);
 
     AttnParams ap;
     memset(&ap, 0, sizeof(ap));
@@ -893,9 +931,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.n_heads = p->model.dims.n_heads;
     ap.n_kv_heads = p->model.dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf(128.f)) * 1.4426950408889634f;
-    if ((st = attention_run(ap, s))) return st;
+    AF_TIMED(FK_ATTN, if ((st = attention_run(ap, s))) return st);
 
-    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    c = base_call(w.status);
     c.x = w.att;
     c.ldx = z.q;
     c.m_cap = M;
@@ -911,11 +949,11 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.res_rows = dcand;
     c.tmap_w = &p->tm_o[l];
     c.tmap_x = &p->tx_att;
-    if ((st = gemm_run(c, s))) return st;
+    AF_TIMED(FK_O, if ((st = gemm_run(c, s))) return st);
 
-    AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm), z.H,
-                                                            eps, nd, M, w.bn);
-    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    AF_TIMED(FK_NORM, AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, w.h1,
+                                     static_cast<const __nv_bfloat16*>(lw.ffn_norm), z.H, eps, nd, M, w.bn));
+    c = base_call(w.status);
     c.x = w.bn;
     c.ldx = z.H;
     c.m_cap = M;
@@ -928,9 +966,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.ldo = z.FF;
     c.tmap_w = &p->tm_gu[l];
     c.tmap_x = &p->tx_bn;
-    if ((st = gemm_run(c, s))) return st;
+    AF_TIMED(FK_GATEUP, if ((st = gemm_run(c, s))) return st);
 
-    c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+    c = base_call(w.status);
     c.x = w.f;
     c.ldx = z.FF;
     c.m_cap = M;
@@ -945,7 +983,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.ldr = z.H;
     c.tmap_w = &p->tm_down[l];
     c.tmap_x = &p->tx_f;
-    if ((st = gemm_run(c, s))) return st;
+    AF_TIMED(FK_DOWN, if ((st = gemm_run(c, s))) return st);
 
     if (next_su) {
       CandArgs cn;
@@ -963,7 +1001,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
       cn.cand_src = w.cand_src + (int64_t)(l + 1) * M;
       cn.n_cand = w.n_cand + l + 1;
       cn.status = w.status;
-      k_fold_candidates<<<1, 1024, 0, s>>>(cn);
+      AF_TIMED(FK_SETUP, k_fold_candidates<<<1, 1024, 0, s>>>(cn));
     }
   }
 
@@ -971,9 +1009,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   int* nd_last = w.n_div + (L - 1);
   int* pos_last = w.div_pos + (int64_t)(L - 1) * M;
   const __nv_bfloat16* x_final = w.x_all + (int64_t)L * M * z.H;
-  AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, x_final, static_cast<const __nv_bfloat16*>(p->model.final_norm),
-                                                          z.H, eps, nd_last, M, w.A);
-  GemmCall c = base_call(w.acc, w.acc_elems, w.counters, w.counter_elems, w.status);
+  AF_TIMED(FK_NORM, AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, x_final, static_cast<const __nv_bfloat16*>(p->model.final_norm),
+                                                          z.H, eps, nd_last, M, w.A));
+  GemmCall c = base_call(w.status);
   c.x = w.A;
   c.ldx = z.H;
   c.m_cap = M;
@@ -988,12 +1026,14 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   c.row_sums = w.row_sums;
   c.tmap_w = &p->tm_lm;
   c.tmap_x = &p->tx_A;
-  if ((st = gemm_run(c, s))) return st;
+  AF_TIMED(FK_LM, if ((st = gemm_run(c, s))) return st);
   const int smem = C * (int)sizeof(int);
-  k_logits_fill<<<T, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(p->parent.logits), z.V, C, T, w.final_bits,
-                                     w.bits_ld, logits);
+  AF_TIMED(FK_FILL, k_logits_fill<<<T, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(p->parent.logits), z.V, C, T,
+                                                       w.final_bits, w.bits_ld, logits));
   if (scores)
-    k_scores<<<C, 256, 0, s>>>(p->parent.logit_row_sums, w.row_sums, C, T, z.V, w.final_bits, w.bits_ld, scores);
+    AF_TIMED(FK_SCORES, k_scores<<<C, 256, 0, s>>>(p->parent.logit_row_sums, w.row_sums, C, T, z.V, w.final_bits,
+                                                    w.bits_ld, scores));
+  p->last_launches = p->tk.launches;
   return check_launch("af_fold_run");
 }
 
@@ -1083,6 +1123,28 @@ extern "C" int af_fold_materialize(void* plan, int64_t layer, void* out, void* s
   k_state_scatter<<<(unsigned)((p->m_cap + 7) / 8), 256, 0, s>>>(p->w.x_all + layer * p->m_cap * z.H, z.H, pos, n,
                                                                   p->m_cap, o);
   return check_launch("af_fold_materialize");
+}
+
+extern "C" int af_fold_set_timing(void* plan, int enabled) {
+  AF_REQUIRE(plan, "af_fold_set_timing: null plan");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  p->tk.collect();
+  p->tk.on = enabled != 0;
+  return AF_OK;
+}
+
+extern "C" int af_fold_get_timing(void* plan, double* ms, int64_t* counts, int n_kinds, int64_t* launches_per_run) {
+  AF_REQUIRE(plan && ms && counts && launches_per_run, "af_fold_get_timing: null pointer");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  p->tk.collect();
+  for (int k = 0; k < n_kinds && k < FK_COUNT; ++k) {
+    ms[k] = p->tk.ms[k];
+    counts[k] = p->tk.n[k];
+    p->tk.ms[k] = 0.0;
+    p->tk.n[k] = 0;
+  }
+  *launches_per_run = p->last_launches;
+  return AF_OK;
 }
 
 extern "C" int af_fold_plan_destroy(void* plan) {

@@ -10,16 +10,22 @@
 // 128-byte swizzle) into a multi-stage shared-memory ring; warp 1 owns the
 // TMEM accumulator (128 lanes x ntok fp32 columns) and its lane 0 issues
 // tcgen05.mma (K = 16 per instruction, 4 per k-block) and tcgen05.commit to
-// release ring slots; warps 2-5 drain TMEM (tcgen05.ld) into shared memory and
-// run the fused epilogue. When the k-range is split across CTAs (split-K, used
-// to put >= 2 CTAs on every SM for the small projections), partial tiles are
-// reduced with vector red.global.add into an fp32 accumulator and the last
-// arriving CTA (per-tile counter) runs the epilogue and re-zeroes its slice,
-// so the workspace is clean again when the kernel ends.
+// release ring slots; warps 2-5 drain TMEM (tcgen05.ld) into shared memory.
+//
+// Split-K for the narrow projections: the k-range of one output tile is split
+// over the CTAs of a thread-block cluster (up to 8, along grid y), so every SM
+// streams weights. Each CTA parks its fp32 partial tile in its own shared
+// memory; after a cluster barrier, CTA j sums rows {lo_j..hi_j} and
+// {64+lo_j..64+hi_j} over all CTAs of the cluster through distributed shared
+// memory (ld.shared::cluster) and runs the epilogue for those rows (the row
+// pairs r, r+64 keep RoPE and SwiGLU partners in one CTA). No global scratch,
+// no atomics, a deterministic summation order.
 //
 // Every mbarrier wait is bounded (about one second); on timeout the CTA sets
-// AF_STATUS_TIMEOUT in the status word, stops issuing, waits (bounded) for its
-// in-flight TMA loads, frees its TMEM and returns.
+// AF_STATUS_TIMEOUT in the status word, stops issuing, skips its stores, waits
+// (bounded) for its in-flight TMA loads, frees its TMEM and returns. Cluster
+// barriers are reached by every thread on every path.
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -30,9 +36,10 @@ namespace af {
 constexpr int kBlockK = 64;   // bf16 elements per k-block (one 128-byte swizzle row)
 constexpr int kTileN = 128;   // weight rows per CTA (MMA M)
 constexpr int kThreads = 192;
+constexpr int kMaxSplits = 8; // portable cluster size
 
 struct GemmDev {
-  int n, k, m_cap, m_pad, ntok, n_tiles, nkb, kb_per_split, splits, stages;
+  int n, k, m_cap, ntok, n_tiles, nkb, kb_per_split, splits, stages;
   const int* m_dev;
   int epi;
   __nv_bfloat16* out;
@@ -45,13 +52,60 @@ struct GemmDev {
   const float* rope_sin;
   const int* positions;
   int rope_cols, half_dim;
-  float* acc;
-  int* counters;
   unsigned* status;
   float* row_sums;
 };
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+// One output element (or SwiGLU pair) of tile row r (feature n0 + r) for token m.
+// `a` is this row's fp32 sum, `partner` the sum of row r ^ 64 (RoPE / SwiGLU).
+__device__ __forceinline__ void epi_store(const GemmDev& p, int n0, int r, int gm, float a, float partner) {
+  const int64_t orow = p.out_rows ? p.out_rows[gm] : gm;
+  const int n = n0 + r;
+  if (p.epi == EPI_STORE) {
+    p.out[orow * p.ldo + n] = __float2bfloat16_rn(a);
+  } else if (p.epi == EPI_RESIDUAL) {
+    const int64_t rrow = p.res_rows ? p.res_rows[gm] : gm;
+    const float rv = __bfloat162float(p.res[rrow * p.ldr + n]);
+    p.out[orow * p.ldo + n] = __float2bfloat16_rn(__fadd_rn(rv, bf(a)));
+  } else if (p.epi == EPI_SWIGLU) {
+    if (r < 64) {
+      const float g = bf(a), u = bf(partner);
+      const float silu = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+      p.out[orow * p.ldo + (n0 >> 1) + r] = __float2bfloat16_rn(__fmul_rn(silu, u));
+    }
+  } else {  // EPI_ROPE
+    const float x = bf(a);
+    float y = x;
+    if (n < p.rope_cols) {
+      const int i = r & (p.half_dim - 1);
+      const float other = bf(partner);
+      const int pos = p.positions[gm];
+      const float cs = p.rope_cos[(int64_t)pos * p.half_dim + i];
+      const float sn = p.rope_sin[(int64_t)pos * p.half_dim + i];
+      y = (r & p.half_dim) ? __fadd_rn(__fmul_rn(x, cs), __fmul_rn(other, sn))
+                           : __fsub_rn(__fmul_rn(x, cs), __fmul_rn(other, sn));
+    }
+    p.out[orow * p.ldo + n] = __float2bfloat16_rn(y);
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmW,
                                                           const __grid_constant__ CUtensorMap tmX, const GemmDev p) {
@@ -63,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     M = p.m_cap;
   }
   const int m0 = blockIdx.z * p.ntok;
-  if (m0 >= M) return;  // uniform: nothing to compute for this token tile
+  if (m0 >= M) return;  // uniform over a cluster (all its CTAs share blockIdx.x / z)
   const int Mv = min(p.ntok, M - m0);
   const int n0 = blockIdx.x * kTileN;
   const int kb0 = blockIdx.y * p.kb_per_split;
@@ -77,12 +131,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t bars = base + S * stage_bytes;
-  uint64_t* bar_ptr = reinterpret_cast<uint64_t*>(gbase + S * stage_bytes);
-  (void)bar_ptr;
   const uint32_t full0 = bars, empty0 = bars + 8 * S, accb = bars + 16 * S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * stage_bytes + 16 * S + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 16);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 20);
   volatile int* issued_slot = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 24);
 
   uint32_t ncols = 32;
@@ -95,7 +146,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
     mbar_init(accb, 1);
     *abort_flag = 0;
-    *last_flag = 0;
     *issued_slot = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmW);
@@ -106,6 +156,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  const int ld = p.ntok + 4;  // staging row stride (floats): 16-byte aligned, conflict-free float4 stores
+  float* tile = reinterpret_cast<float*>(gbase);  // the ring is idle once the accumulator is final
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
@@ -146,98 +199,77 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
     tc_commit(accb);
   } else if (warp >= 2) {
-    // ---------------- epilogue (128 threads) ----------------
+    // ---------------- TMEM -> shared memory (128 threads, one tile row each) ----------------
     const int q = warp & 3;
-    const int r = 32 * q + lane;  // tile row = output feature n0 + r
-    const int ld = p.ntok + 1;
-    float* tile = reinterpret_cast<float*>(gbase);  // ring memory is idle once the accumulator is final
-    const bool ok = mbar_wait(accb, 0, abort_flag);
-    if (!ok) {
+    const int r = 32 * q + lane;
+    if (!mbar_wait(accb, 0, abort_flag)) {
       atomicOr(p.status, AF_STATUS_TIMEOUT);
       *abort_flag = 1;
     }
     tc_fence_after();
-    const int nchunk = (Mv + 15) / 16;
-    if (ok && !*abort_flag) {
-      float* arow = p.acc + (int64_t)(n0 + r) * p.m_pad + m0;
+    if (!*abort_flag) {
+      const int nchunk = (Mv + 15) / 16;
       for (int c = 0; c < nchunk; ++c) {
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(16 * c), v);
-        if (p.splits > 1) {
+        float4* dst = reinterpret_cast<float4*>(tile + r * ld + 16 * c);
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) red_add_v4(arow + 16 * c + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) tile[r * ld + 16 * c + j] = v[j];
-        }
-      }
-      if (p.splits > 1) {
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 64) {
-          const int tile_id = blockIdx.z * p.n_tiles + blockIdx.x;
-          const int old = atomicAdd(&p.counters[tile_id], 1);
-          *last_flag = (old == p.splits - 1) ? 1 : 0;
-          if (old == p.splits - 1) p.counters[tile_id] = 0;
-        }
-        named_bar_sync(1, 128);
-        if (*last_flag) {
-          __threadfence();
-          for (int c = 0; c < nchunk * 16; c += 4) {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(arow + c));
-            __stcg(reinterpret_cast<float4*>(arow + c), make_float4(0.f, 0.f, 0.f, 0.f));
-            tile[r * ld + c] = a.x;
-            tile[r * ld + c + 1] = a.y;
-            tile[r * ld + c + 2] = a.z;
-            tile[r * ld + c + 3] = a.w;
-          }
-        }
-      }
-      const bool do_epi = (p.splits == 1) || *last_flag;
-      named_bar_sync(1, 128);
-      if (do_epi) {
-        const int n = n0 + r;
-        for (int m = 0; m < Mv; ++m) {
-          const int gm = m0 + m;
-          const int64_t orow = p.out_rows ? p.out_rows[gm] : gm;
-          const float a = tile[r * ld + m];
-          if (p.epi == EPI_STORE) {
-            const __nv_bfloat16 ob = __float2bfloat16_rn(a);
-            p.out[orow * p.ldo + n] = ob;
-            if (p.row_sums) {
-              const float part = warp_sum(__bfloat162float(ob));
-              if (lane == 0) atomicAdd(p.row_sums + orow, part);
-            }
-          } else if (p.epi == EPI_RESIDUAL) {
-            const int64_t rrow = p.res_rows ? p.res_rows[gm] : gm;
-            const float rv = __bfloat162float(p.res[rrow * p.ldr + n]);
-            p.out[orow * p.ldo + n] = __float2bfloat16_rn(__fadd_rn(rv, bf(a)));
-          } else if (p.epi == EPI_SWIGLU) {
-            if (r < 64) {
-              const float g = bf(a), u = bf(tile[(r + 64) * ld + m]);
-              const float silu = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
-              p.out[orow * p.ldo + (n0 >> 1) + r] = __float2bfloat16_rn(__fmul_rn(silu, u));
-            }
-          } else {  // EPI_ROPE
-            const float x = bf(a);
-            float y = x;
-            if (n < p.rope_cols) {
-              const int i = r & (p.half_dim - 1);
-              const float other = bf(tile[(r ^ p.half_dim) * ld + m]);
-              const int pos = p.positions[gm];
-              const float cs = p.rope_cos[(int64_t)pos * p.half_dim + i];
-              const float sn = p.rope_sin[(int64_t)pos * p.half_dim + i];
-              y = (r & p.half_dim) ? __fadd_rn(__fmul_rn(x, cs), __fmul_rn(other, sn))
-                                   : __fsub_rn(__fmul_rn(x, cs), __fmul_rn(other, sn));
-            }
-            p.out[orow * p.ldo + n] = __float2bfloat16_rn(y);
-          }
-        }
+        for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       }
     }
   }
-
   __syncthreads();
+  const bool ok = !*abort_flag;
+
+  if (p.splits == 1) {
+    // ---------------- epilogue over all 128 rows: thread r (< 128) owns feature n0 + r ----------------
+    if (ok && threadIdx.x < kTileN) {
+      const int r = threadIdx.x;
+      for (int m = 0; m < Mv; ++m) {
+        const float a = tile[r * ld + m];
+        const float partner = (p.epi == EPI_SWIGLU || p.epi == EPI_ROPE) ? tile[(r ^ 64) * ld + m] : 0.f;
+        epi_store(p, n0, r, m0 + m, a, partner);
+        if (p.row_sums && p.epi == EPI_STORE) {
+          const float part = warp_sum(bf(a));
+          if (lane == 0) atomicAdd(p.row_sums + (p.out_rows ? p.out_rows[m0 + m] : m0 + m), part);
+        }
+      }
+    }
+  } else {
+    // ---------------- cluster split-K reduction through distributed shared memory ----------------
+    __syncwarp();
+    cluster_sync_all();  // every partial tile of the cluster is in shared memory
+    // CTA j owns the row pairs (lo + i, 64 + lo + i), i < k: consecutive threads take
+    // consecutive pairs (adjacent output features) of the same 4-token column group.
+    const int j = blockIdx.y, Sp = p.splits;
+    const int lo = (j * 64) / Sp, hi = ((j + 1) * 64) / Sp, k = hi - lo;
+    const int nc4 = (Mv + 3) / 4;
+    if (ok) {
+      for (int f = threadIdx.x; f < k * nc4; f += kThreads) {
+        const int c4 = f / k, i = f - c4 * k;
+        const int ra = lo + i, rb = 64 + lo + i;
+        const uint32_t oa = base + (uint32_t)((ra * ld + 4 * c4) * 4);
+        const uint32_t ob = base + (uint32_t)((rb * ld + 4 * c4) * 4);
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int src = 0; src < Sp; ++src) {
+          const float4 va = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
+          const float4 vb = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
+          sa[0] += va.x; sa[1] += va.y; sa[2] += va.z; sa[3] += va.w;
+          sb[0] += vb.x; sb[1] += vb.y; sb[2] += vb.z; sb[3] += vb.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int m = 4 * c4 + e;
+          if (m >= Mv) break;
+          epi_store(p, n0, ra, m0 + m, sa[e], sb[e]);
+          epi_store(p, n0, rb, m0 + m, sb[e], sa[e]);
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // peers may still read this CTA's partial tile until here
+  }
+
   if (threadIdx.x == 0 && *abort_flag) {
     // Drain TMA loads that may still be in flight into the ring (bounded).
     const int issued = *issued_slot;
@@ -293,21 +325,36 @@ int gemm_ntok(int m_cap) {
   return nt < 16 ? 16 : nt;
 }
 
-void gemm_workspace(int n, int m_cap, int64_t* acc_elems, int* counter_elems) {
-  const int nt = gemm_ntok(m_cap);
-  const int mt = (m_cap + nt - 1) / nt;
-  *acc_elems = (int64_t)n * mt * nt;
-  *counter_elems = (n / kTileN) * mt;
-}
+struct GemmShape {
+  int ntok, m_tiles, n_tiles, nkb, splits, kb_per, stages, smem;
+};
 
-static int stages_for(int ntok) {
-  const int stage = kTileN * kBlockK * 2 + ntok * kBlockK * 2;
-  int s = (100 * 1024) / stage;  // two CTAs per SM when it fits
-  if (s < 2) s = 2;
-  if (s > 8) s = 8;
-  const int staging = kTileN * (ntok + 1) * 4;
-  while (s * stage < staging) ++s;
-  return s;
+static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_sums) {
+  GemmShape g;
+  g.ntok = gemm_ntok(m_cap);
+  g.m_tiles = (m_cap + g.ntok - 1) / g.ntok;
+  g.n_tiles = n / kTileN;
+  g.nkb = k / kBlockK;
+  const int stage = kTileN * kBlockK * 2 + g.ntok * kBlockK * 2;
+  int st = (100 * 1024) / stage;  // two CTAs per SM when it fits
+  st = std::max(2, std::min(8, st));
+  const int per_sm = (2 * (st * stage + 1024 + 256) <= 227 * 1024) ? 2 : 1;
+  int splits = want_splits;
+  if (splits <= 0) {
+    const int tiles = g.n_tiles * g.m_tiles;
+    splits = (per_sm * sm_count()) / tiles;
+    splits = std::min(splits, std::max(1, g.nkb / 4));
+    splits = std::max(1, std::min(splits, kMaxSplits));
+  }
+  if (row_sums) splits = 1;
+  splits = std::min(splits, kMaxSplits);
+  g.kb_per = (g.nkb + splits - 1) / splits;
+  g.splits = (g.nkb + g.kb_per - 1) / g.kb_per;
+  const int tile_bytes = kTileN * (g.ntok + 4) * 4;  // fp32 staging of the accumulator
+  while (st * stage < tile_bytes) ++st;
+  g.stages = st;
+  g.smem = st * stage + 1024 + 16 * st + 64;
+  return g;
 }
 
 int gemm_run(const GemmCall& c, cudaStream_t stream) {
@@ -319,28 +366,8 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.epi != EPI_RESIDUAL || c.res, "gemm: residual epilogue needs res");
   AF_REQUIRE(c.epi != EPI_ROPE || (c.rope_cos && c.rope_sin && c.positions && c.head_dim == 128 && c.rope_cols % 128 == 0),
              "gemm: rope epilogue needs cos/sin/positions and head_dim 128");
-  const int ntok = gemm_ntok(c.m_cap);
-  const int m_tiles = (c.m_cap + ntok - 1) / ntok;
-  const int n_tiles = c.n / kTileN;
-  const int nkb = c.k / kBlockK;
-  int splits = c.splits;
-  const int stages = stages_for(ntok);
-  const int stage_bytes = kTileN * kBlockK * 2 + ntok * kBlockK * 2;
-  const int smem = stages * stage_bytes + 1024 + 16 * stages + 64;
-  const int per_sm = (2 * smem <= 227 * 1024) ? 2 : 1;
-  if (splits <= 0) {
-    const int target = per_sm * sm_count();
-    splits = target / (n_tiles * m_tiles);
-    const int max_splits = nkb / 4 > 0 ? nkb / 4 : 1;
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-  }
-  int64_t need_acc;
-  int need_cnt;
-  gemm_workspace(c.n, c.m_cap, &need_acc, &need_cnt);
-  if (splits > 1 && (!c.acc || !c.counters || c.acc_elems < need_acc || c.counter_elems < need_cnt)) splits = 1;
-  const int kb_per = (nkb + splits - 1) / splits;
-  splits = (nkb + kb_per - 1) / kb_per;
+  const GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr);
+  AF_REQUIRE(g.smem <= 227 * 1024, "gemm: shared memory budget exceeded");
 
   CUtensorMap tw, tx;
   const CUtensorMap* pw = c.tmap_w;
@@ -351,7 +378,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
     pw = &tw;
   }
   if (!px) {
-    int st = make_tmap_bf16(&tx, c.x, c.m_cap, c.k, c.ldx, ntok);
+    int st = make_tmap_bf16(&tx, c.x, c.m_cap, c.k, c.ldx, g.ntok);
     if (st) return st;
     px = &tx;
   }
@@ -359,13 +386,12 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.n = c.n;
   d.k = c.k;
   d.m_cap = c.m_cap;
-  d.m_pad = m_tiles * ntok;
-  d.ntok = ntok;
-  d.n_tiles = n_tiles;
-  d.nkb = nkb;
-  d.kb_per_split = kb_per;
-  d.splits = splits;
-  d.stages = stages;
+  d.ntok = g.ntok;
+  d.n_tiles = g.n_tiles;
+  d.nkb = g.nkb;
+  d.kb_per_split = g.kb_per;
+  d.splits = g.splits;
+  d.stages = g.stages;
   d.m_dev = c.m_dev;
   d.epi = c.epi;
   d.out = static_cast<__nv_bfloat16*>(c.out);
@@ -379,8 +405,6 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.positions = c.positions;
   d.rope_cols = c.rope_cols;
   d.half_dim = c.head_dim / 2;
-  d.acc = c.acc;
-  d.counters = c.counters;
   d.status = c.status;
   d.row_sums = c.epi == EPI_STORE ? c.row_sums : nullptr;
 
@@ -388,8 +412,21 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  dim3 grid(n_tiles, splits, m_tiles);
-  k_gemm_tc<<<grid, kThreads, smem, stream>>>(*pw, *px, d);
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(g.n_tiles, g.splits, g.m_tiles);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = g.splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g.splits > 1 ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc, *pw, *px, d);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_tc launch: ") + cudaGetErrorString(e));
   return check_launch("gemm_tc");
 }
 
@@ -397,24 +434,15 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
 
 using namespace af;
 
-extern "C" int af_linear_workspace(int64_t n, int64_t m_cap, int64_t* acc_floats, int64_t* counters) {
-  AF_REQUIRE(n > 0 && m_cap > 0 && acc_floats && counters, "af_linear_workspace: bad argument");
-  int64_t a;
-  int c;
-  gemm_workspace((int)n, (int)m_cap, &a, &c);
-  *acc_floats = a;
-  *counters = c;
-  return AF_OK;
-}
-
 extern "C" int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_dev, const void* w,
                               int64_t n, int64_t k, int epilogue, void* out, int64_t ldo, const int32_t* out_rows,
                               const void* residual, int64_t ldr, const int32_t* res_rows, const float* rope_cos,
-                              const float* rope_sin, const int32_t* positions, int64_t rope_cols, float* acc,
-                              int64_t acc_floats, int32_t* counters, int64_t n_counters, int splits,
+                              const float* rope_sin, const int32_t* positions, int64_t rope_cols, int splits,
                               uint32_t* status, void* stream) {
   AF_REQUIRE(n <= (1 << 30) && k <= (1 << 30) && m_cap <= (1 << 30), "af_linear_bf16: size too large");
-  GemmCall c{};
+  AF_REQUIRE(splits >= 0 && splits <= kMaxSplits, "af_linear_bf16: splits must be in [0, 8]");
+  GemmCall c;
+  memset(&c, 0, sizeof(c));
   c.x = x;
   c.ldx = ldx;
   c.m_cap = (int)m_cap;
@@ -434,10 +462,6 @@ extern "C" int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const i
   c.positions = positions;
   c.rope_cols = (int)rope_cols;
   c.head_dim = 128;
-  c.acc = acc;
-  c.acc_elems = acc_floats;
-  c.counters = counters;
-  c.counter_elems = (int)n_counters;
   c.splits = splits;
   c.status = status;
   return gemm_run(c, as_stream(stream));

@@ -31,11 +31,7 @@ struct GemmCall {
   const int* positions;   // position of packed row m
   int rope_cols;          // columns [0, rope_cols) are rotated (multiple of head_dim)
   int head_dim;           // 128
-  float* acc;          // split-K accumulator [n, m_pad] fp32, all zero on entry and exit
-  int* counters;       // split-K arrival counters [n/128 * m_tiles], zero on entry and exit
-  int64_t acc_elems;   // capacity of acc (elements)
-  int counter_elems;   // capacity of counters
-  int splits;          // 0 = choose automatically
+  int splits;          // k-range split over a thread-block cluster (<= 8); 0 = choose automatically
   unsigned* status;    // device status word (AF_STATUS_* bits)
   float* row_sums;     // EPI_STORE only, nullable: row_sums[out row] += sum of the row's bf16 outputs
   // Pre-built descriptors (optional; built per call when null).
@@ -45,8 +41,6 @@ struct GemmCall {
 
 // Token-tile width the kernel uses for a given row capacity.
 int gemm_ntok(int m_cap);
-// Split-K workspace a call needs: accumulator elements and counters.
-void gemm_workspace(int n, int m_cap, int64_t* acc_elems, int* counter_elems);
 // Launch (stream-ordered, no synchronisation).
 int gemm_run(const GemmCall& c, cudaStream_t stream);
 

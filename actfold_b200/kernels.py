@@ -14,26 +14,15 @@ from actfold_b200 import _lib
 
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3
 
-class SplitKWorkspace:
-    """Zeroed split-K accumulator + tile counters + device status word.
+class DeviceStatus:
+    """Device status word the kernels OR their AF_STATUS bits into (1 timeout, 2 capacity, 4 bounds)."""
 
-    The GEMM leaves the accumulator and counters zero when it finishes, so one
-    workspace serves every call whose (n, m_cap) fits.
-    """
-
-    def __init__(self, n_max: int, m_cap_max: int, device: torch.device | str = "cuda") -> None:
-        lib = _lib.load()
-        a, c = C.c_int64(), C.c_int64()
-        _lib.check(lib.af_linear_workspace(n_max, m_cap_max, C.byref(a), C.byref(c)))
-        self.acc = torch.zeros(int(a.value), dtype=torch.float32, device=device)
-        self.counters = torch.zeros(int(c.value), dtype=torch.int32, device=device)
+    def __init__(self, device: torch.device | str = "cuda") -> None:
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
 
     def check_status(self) -> None:
         s = int(self.status.item())
         if s:
-            self.acc.zero_()
-            self.counters.zero_()
             self.status.zero_()
             if s & 1:
                 raise TimeoutError(f"device wait timed out (status {s:#x})")
@@ -43,7 +32,7 @@ class SplitKWorkspace:
 def linear(
     x: torch.Tensor,
     w: torch.Tensor,
-    ws: SplitKWorkspace,
+    ws: DeviceStatus,
     epilogue: int = EPI_STORE,
     out: torch.Tensor | None = None,
     m_dev: torch.Tensor | None = None,
@@ -80,8 +69,7 @@ def linear(
             out.data_ptr(), out.stride(0), _lib.ptr(out_rows),
             _lib.ptr(residual), residual.stride(0) if residual is not None else 0, _lib.ptr(res_rows),
             _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), rope_cols,
-            ws.acc.data_ptr(), ws.acc.numel(), ws.counters.data_ptr(), ws.counters.numel(), splits,
-            ws.status.data_ptr(), _lib.stream_ptr(x.device),
+            splits, ws.status.data_ptr(), _lib.stream_ptr(x.device),
         )
     _lib.check(st, "linear")
     return out

@@ -80,14 +80,20 @@ _lib.SIGNATURES.update(
         "af_fold_get_outputs": (_i32, [_vp, C.POINTER(_FoldOutputs)]),
         "af_fold_materialize": (_i32, [_vp, _i64, _vp, _vp]),
         "af_fold_plan_destroy": (_i32, [_vp]),
+        "af_fold_set_timing": (_i32, [_vp, _i32]),
+        "af_fold_get_timing": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32, C.POINTER(_i64)]),
     }
 )
+
+KERNEL_CLASSES = ("setup", "gate", "compact", "gemm_qkv", "attention", "gemm_o", "rmsnorm", "gemm_gateup",
+                  "gemm_down", "gemm_lm_head", "logits_fill", "scores")
 
 
 def _bind_late() -> C.CDLL:
     lib = _lib.load()
     for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
-                 "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy"):
+                 "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy",
+                 "af_fold_set_timing", "af_fold_get_timing"):
         fn = getattr(lib, name)
         fn.restype, fn.argtypes = _lib.SIGNATURES[name]
     return lib
@@ -215,6 +221,18 @@ class FoldPlan:
         flat = (torch.arange(L, device=masks.device)[:, None] * (self.C * self.T) + self.div_pos.long())[valid]
         masks.view(-1)[flat] = False
         return masks.view(L, self.C, self.T)
+
+    def set_timing(self, enabled: bool) -> None:
+        _lib.check(self.lib.af_fold_set_timing(self._plan, 1 if enabled else 0))
+
+    def get_timing(self) -> tuple[dict, dict, int]:
+        """(ms per kernel class, launches per class) accumulated since the last call, launches per run."""
+        n = len(KERNEL_CLASSES)
+        ms = (C.c_double * n)()
+        cnt = (_i64 * n)()
+        per_run = _i64()
+        _lib.check(self.lib.af_fold_get_timing(self._plan, ms, cnt, n, C.byref(per_run)))
+        return ({k: ms[i] for i, k in enumerate(KERNEL_CLASSES)}, {k: int(cnt[i]) for i, k in enumerate(KERNEL_CLASSES)}, int(per_run.value))
 
     def check_status(self) -> None:
         s = int(self.status.item())

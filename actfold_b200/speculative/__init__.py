@@ -1,0 +1,5 @@
+"""Speculative verification on the native folded pass (drop-in for ``actfold.speculative``'s engine)."""
+
+from actfold_b200.speculative.verification_engine import ActFoldVerificationEngine, Branch, VerificationResult
+
+__all__ = ["ActFoldVerificationEngine", "Branch", "VerificationResult"]

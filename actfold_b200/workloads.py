@@ -121,13 +121,24 @@ def llada_tokens(
     n_mask = int(round(mask_frac * gen.size))
     masked = np.sort(rng.choice(gen, size=n_mask, replace=False))
     parent[masked] = mask_id
+    return parent, _unmask_children(parent, masked, n_children, d, mask_id, rng)
+
+
+def _unmask_children(parent: np.ndarray, masked: np.ndarray, n_children: int, d: int, mask_id: int, rng) -> np.ndarray:
     children = np.repeat(parent[None], n_children, axis=0)
     if d > masked.size:
         raise ValueError(f"d={d} exceeds the {masked.size} masked positions")
     for c in range(n_children):
         pos = rng.choice(masked, size=d, replace=False)
         children[c, pos] = rng.integers(0, mask_id, size=d, dtype=np.int64)
-    return parent, children
+    return children
+
+
+def llada_children(parent: np.ndarray, n_children: int, d: int, mask_id: int, seed: int) -> np.ndarray:
+    """Children [C, T] of an existing parent: each unmasks d of its masked positions (seeded)."""
+    rng = np.random.default_rng(seed)
+    masked = np.nonzero(parent == mask_id)[0]
+    return _unmask_children(parent, masked, n_children, d, mask_id, rng)
 
 
 def demo_weights(seed: int = 42, vocab: int = 1000, hidden: int = 128, n_layers: int = 4, std: float = 0.02) -> dict:

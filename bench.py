@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Verified-tokens/s of the folded verification pass on B200.
+
+Workload (headline): LLaDA-8B architecture (32 layers, hidden 4096, 32 heads x
+128, SwiGLU 12288, vocab 126464), bf16, seeded N(0, 0.02) weights; parent of
+1024 ids (256 prompt + 768 generation positions, 50% of them the mask id);
+8 children per GPU, each unmasking 16 masked positions; tau 0.95. One step =
+one verification pass of a rank's children: gate, compaction, divergent-row
+recompute (tcgen05 GEMMs + attention), merge, full logits [C, T, V] and
+per-child scores. The parent pass runs once before timing; with N > 1 ranks
+rank 0 computes it and broadcasts the parent cache over NCCL, every rank then
+verifies its own 8 children (weak scaling, no collective inside a step).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0). ``--impl reference`` times the reference
+algorithm (full-layer recompute per child, gate, merge, LM head) restated in
+numpy on the host cores, on a bounded sample extrapolated to one pass.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "verify tokens/sec, LLaDA-8B arch, 8 branches×1024 tok; % HBM/TC roofline"
+UNIT = "verified tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--children", type=int, default=8, help="children per GPU")
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--d", type=int, default=16, help="unmasked positions per child")
+    ap.add_argument("--tau", type=float, default=0.95)
+    ap.add_argument("--layers", type=int, default=None, help="override layer count (small profiling captures only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_name(a) -> str:
+    return f"LLaDA-8B arch folded verification, {a.children} children x {a.seq} tokens per GPU, d={a.d}, tau={a.tau}"
+
+
+def config_dict(a, n):
+    return {
+        "workload": workload_name(a),
+        "model": "LLaDA-8B architecture (32 x [H 4096, 32x128 MHA, SwiGLU 12288], vocab 126464)" if a.layers is None else f"LLaDA-8B layer shapes, {a.layers} layers",
+        "children_per_gpu": a.children,
+        "global_children": a.children * n,
+        "seq_len": a.seq,
+        "prompt": 256,
+        "mask_fraction": 0.5,
+        "d_unmasked_per_child": a.d,
+        "tau": a.tau,
+        "parallelism": "children sharded across ranks, parent cache NCCL-broadcast once" if n > 1 else "single GPU",
+        "l2": "inputs larger than L2: 15 GB of weights streamed every step",
+    }
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the GEMM kernel from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "gemm_tc_llada8b_fold.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch_full_workload:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        time.sleep(0.3)
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(a, rank: int) -> None:
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import CpuSample
+    from oracle.llada import LLaDADims
+
+    from actfold_b200 import workloads as W
+
+    d = W.LLADA_8B
+    dims = LLaDADims(a.layers or d.n_layers, d.hidden, d.n_heads, d.n_kv_heads, d.head_dim, d.ffn, d.vocab, d.rms_eps, d.rope_theta)
+    s = CpuSample(dims, a.seq, a.children, a.tau)
+    for _ in range(min(max(1, a.warmup), 2)):
+        s.time_pass()
+    n_samples = min(max(1, a.steps), 10)
+    ts = [s.time_pass()[0] for _ in range(n_samples)]
+    t = statistics.median(ts)
+    value = a.children * a.seq / t
+    sample = (f"median of {n_samples} samples of one LLaDA-8B block (T={a.seq}, numpy f32 BLAS, all host threads) + gate "
+              f"+ merge + LM head on a {s.vs}-column vocabulary slice, extrapolated to {a.children} children x "
+              f"{dims.n_layers} layers per pass")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": a.gpus,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": t * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": config_dict(a, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": s.threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- our arm
+def main() -> None:
+    a = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from actfold_b200 import workloads as W
+    from actfold_b200.llada import KERNEL_CLASSES, LLaDAModel, ParentCache
+    from actfold_b200.speculative import ActFoldVerificationEngine, Branch
+    from actfold_b200.core import SimilarityGate
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    base = W.LLADA_8B
+    dims = base if a.layers is None else W.ModelDims(a.layers, base.hidden, base.n_heads, base.n_kv_heads, base.head_dim, base.ffn, base.vocab, base.rms_eps, base.rope_theta, base.mask_id)
+    model = LLaDAModel.random(dims, seed=1234, device=dev, max_pos=max(a.seq, 1024))
+    parent_np, _ = W.llada_tokens(a.seq, 256, 0.5, 1, 1, dims.mask_id, seed=42)
+    children_np = W.llada_children(parent_np, a.children, a.d, dims.mask_id, seed=1000 + rank)
+
+    # ---- parent pass (rank 0) + broadcast of the parent cache
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    if rank == 0:
+        pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)
+    else:
+        L, T, H = dims.n_layers, a.seq, dims.hidden
+        pc = ParentCache(
+            torch.empty(T, dtype=torch.int64, device=dev),
+            torch.empty((L + 1, T, H), dtype=torch.bfloat16, device=dev),
+            torch.empty((L, T, dims.q_dim + 2 * dims.kv_dim), dtype=torch.bfloat16, device=dev),
+            torch.empty((T, dims.vocab), dtype=torch.bfloat16, device=dev),
+            torch.empty((L, T), dtype=torch.uint8, device=dev),
+            torch.empty((T,), dtype=torch.float32, device=dev),
+            a.tau,
+        )
+    torch.cuda.synchronize()
+    parent_ms = (time.perf_counter() - t0) * 1e3
+    bcast_ms = 0.0
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in pc.tensors():
+            dist.broadcast(t, src=0)
+        e1.record()
+        torch.cuda.synchronize()
+        bcast_ms = e0.elapsed_time(e1)
+
+    gate = SimilarityGate(a.tau)
+    engine = ActFoldVerificationEngine(model, gate=gate)
+    pbranch = Branch("parent", None, pc.tokens)
+    engine.set_parent_cache(pbranch, pc)
+    host_children = torch.from_numpy(children_np).pin_memory()
+    ct = host_children.to(dev)
+    m_cap = engine._m_cap(host_children, pc, a.children, a.seq)
+    logits = torch.empty((a.children, a.seq, dims.vocab), dtype=torch.bfloat16, device=dev)
+    scores = torch.empty((a.children,), dtype=torch.float32, device=dev)
+    _, plan = model.verify(ct, pc, a.tau, logits=logits, scores=scores, m_cap=m_cap)
+    torch.cuda.synchronize()
+    plan.check_status()
+
+    def step():
+        plan.run(ct, logits, scores)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K device-timed steps
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    step_ms = ev0.elapsed_time(ev1) / a.steps
+    plan.check_status()
+    t_max = torch.tensor([step_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    step_ms_max = float(t_max.item())
+    value = a.children * world * a.seq / (step_ms_max / 1e3)
+
+    # ---- per-kernel-class device times (same stream, same workload)
+    plan.set_timing(True)
+    n_prof = max(3, min(a.steps, 20))
+    for _ in range(n_prof):
+        step()
+    torch.cuda.synchronize()
+    ms_by, cnt_by, launches_per_run = plan.get_timing()
+    plan.set_timing(False)
+    kernel_ms = {k: ms_by[k] / n_prof for k in KERNEL_CLASSES}
+    tot_k = sum(kernel_ms.values()) or 1.0
+
+    # ---- roofline of the dominant kernel: the tcgen05 GEMM (weights streamed from HBM)
+    H, q, kv, FF, V, L = dims.hidden, dims.q_dim, dims.kv_dim, dims.ffn, dims.vocab, dims.n_layers
+    n_div = plan.n_div.cpu().numpy().astype(np.int64)
+    n_cand = plan.n_cand.cpu().numpy().astype(np.int64)
+    gemm_bytes = 0
+    gemm_flops = 0
+    for li in range(L):
+        mc, md = int(n_cand[li]), int(n_div[li])
+        gemm_bytes += 2 * ((q + 2 * kv) * H + mc * H + mc * (q + 2 * kv))
+        gemm_bytes += 2 * (H * q + md * q + 2 * md * H)
+        gemm_bytes += 2 * (2 * FF * H + md * H + md * FF)
+        gemm_bytes += 2 * (H * FF + md * FF + 2 * md * H)
+        gemm_flops += 2 * mc * H * (q + 2 * kv) + 2 * md * (q * H + 3 * H * FF)
+    md_last = int(n_div[L - 1])
+    gemm_bytes += 2 * (V * H + md_last * H + md_last * V)
+    gemm_flops += 2 * md_last * H * V
+    gemm_launches = sum(cnt_by[k] for k in ("gemm_qkv", "gemm_o", "gemm_gateup", "gemm_down", "gemm_lm_head")) / n_prof
+    gemm_ms = sum(kernel_ms[k] for k in ("gemm_qkv", "gemm_o", "gemm_gateup", "gemm_down", "gemm_lm_head"))
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+    achieved = (gemm_bytes / gemm_launches) / ((gemm_ms / gemm_launches) / 1e3) / 1e9
+    traffic = profiled_traffic()
+    roofline = {
+        "kernel": "k_gemm_tc (tcgen05 weight-streaming GEMM, all projections + LM head)",
+        "bound": "hbm",
+        "achieved": achieved,
+        "peak": hbm_peak,
+        "unit": "GB/s",
+        "frac": achieved / hbm_peak,
+        "traffic": traffic,
+        "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback 6650 GB/s",
+        "algorithmic_bytes_per_launch": gemm_bytes / gemm_launches,
+        "avg_launch_us": gemm_ms / gemm_launches * 1e3,
+        "tensor_tflops": gemm_flops / (gemm_ms / 1e3) / 1e12,
+        "tensor_frac_of_peak": gemm_flops / (gemm_ms / 1e3) / 1e12 / tc_peak,
+        "divergent_rows_per_layer": int(n_div[0]),
+    }
+
+    # ---- end to end through the public API with host buffers
+    for _ in range(max(1, a.warmup)):
+        engine.verify_tokens(pbranch, host_children)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        res = engine.verify_tokens(pbranch, host_children)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = a.children * world * a.seq / (float(e2e_ms.item()) / 1e3)
+    h2d = host_children.numel() * host_children.element_size()
+    d2h = a.children * 4 + L * a.children * 4 + 4
+
+    # ---- CPU baseline (rank 0, single GPU runs only)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from oracle.cpu_baseline import CpuSample
+        from oracle.llada import LLaDADims
+
+        od = LLaDADims(L, H, dims.n_heads, dims.n_kv_heads, dims.head_dim, FF, V, dims.rms_eps, dims.rope_theta)
+        cs = CpuSample(od, a.seq, a.children, a.tau)
+        cs.time_pass()
+        t_cpu = min(cs.time_pass()[0] for _ in range(2))
+        cpu = {
+            "value": a.children * a.seq / t_cpu,
+            "unit": UNIT,
+            "cores": cs.threads,
+            "kind": "port",
+            "sample": f"one LLaDA-8B block on {a.seq} rows + gate + merge + LM head on a {cs.vs}-column vocab slice "
+                      f"(numpy f32 BLAS, all host threads), extrapolated to {a.children} children x {L} layers",
+        }
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": a.steps,
+            "warmup": a.warmup,
+            "ms_per_step": step_ms_max,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: seeded N(0,0.02) weights drawn on the GPU, seeded token ids",
+            "config": config_dict(a, world),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches_per_run * a.steps),
+            "clocks": clocks,
+            "kernels_ms_per_step": {k: round(v, 4) for k, v in kernel_ms.items()},
+            "kernel_share": {k: round(v / tot_k, 4) for k, v in kernel_ms.items()},
+            "parent_pass_ms": parent_ms,
+            "parent_broadcast_ms": bcast_ms,
+            "stable_ratio_mean": float(np.mean(res["stable_ratio"])),
+        }
+        print(json.dumps(line), flush=True)
+    del plan, engine
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

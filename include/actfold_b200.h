@@ -120,13 +120,6 @@ typedef enum {
 } af_epilogue;
 
 /*
- * af_linear_workspace -- split-K workspace needed by af_linear_bf16 for an
- * (n, m_cap) problem: fp32 accumulator floats and int32 tile counters. Both
- * must be zero before the first call; every call leaves them zero again.
- */
-int af_linear_workspace(int64_t n, int64_t m_cap, int64_t* acc_floats, int64_t* counters);
-
-/*
  * af_linear_bf16 -- out[row(m)] = epilogue(x[m, :] . w^T) for packed token rows.
  *
  * Replaces the projections inside the wrapped layer that
@@ -137,17 +130,17 @@ int af_linear_workspace(int64_t n, int64_t m_cap, int64_t* acc_floats, int64_t* 
  *   int, nullable -> m_cap); w [n, k] bf16 (n % 128 == 0, k % 64 == 0);
  *   out rows: out_rows[m] (nullable -> m), row stride ldo; residual rows:
  *   res_rows[m] (nullable -> m); rope tables cos/sin [P, 64] fp32 indexed by
- *   positions[m]. splits = 0 chooses split-K automatically (needs the
- *   workspace); status receives AF_STATUS bits (1 timeout, 2 capacity).
+ *   positions[m]. splits (0..8, 0 = automatic) divides the k-range over a
+ *   thread-block cluster whose partial tiles are summed in distributed shared
+ *   memory (no workspace); status receives AF_STATUS bits (1 timeout,
+ *   2 capacity).
  */
 int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_dev,
                    const void* w, int64_t n, int64_t k, int epilogue,
                    void* out, int64_t ldo, const int32_t* out_rows,
                    const void* residual, int64_t ldr, const int32_t* res_rows,
                    const float* rope_cos, const float* rope_sin, const int32_t* positions,
-                   int64_t rope_cols, float* acc, int64_t acc_floats,
-                   int32_t* counters, int64_t n_counters, int splits,
-                   uint32_t* status, void* stream);
+                   int64_t rope_cols, int splits, uint32_t* status, void* stream);
 
 /*
  * af_attention_bf16 -- non-causal attention of packed query rows over the
@@ -260,6 +253,18 @@ int af_fold_get_outputs(void* plan, af_fold_outputs* out);
 /* Dense input of layer `layer` (0..n_layers) for every child: out [C, T, hidden] bf16. */
 int af_fold_materialize(void* plan, int64_t layer, void* out, void* stream);
 int af_fold_plan_destroy(void* plan);
+
+/*
+ * Per-kernel-class CUDA-event timing of af_fold_run, recorded on the pass's
+ * stream when enabled. Classes: 0 candidates/embedding, 1 gate, 2 compaction,
+ * 3 QKV GEMM, 4 attention, 5 O GEMM, 6 RMSNorm, 7 gate/up GEMM, 8 down GEMM,
+ * 9 LM-head GEMM, 10 parent-logit fill, 11 scores. af_fold_get_timing
+ * synchronizes on the last event, returns the accumulated milliseconds and
+ * launch counts per class (then resets them) and the number of kernel
+ * launches of the last run. No counterpart in the reference (measurement).
+ */
+int af_fold_set_timing(void* plan, int enabled);
+int af_fold_get_timing(void* plan, double* ms, int64_t* counts, int n_kinds, int64_t* launches_per_run);
 
 #ifdef __cplusplus
 }

@@ -19,13 +19,13 @@ def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
 
 @pytest.fixture(scope="module")
 def ws():
-    from actfold_b200.kernels import SplitKWorkspace
+    from actfold_b200.kernels import DeviceStatus
 
-    return SplitKWorkspace(n_max=24576, m_cap_max=1024)
+    return DeviceStatus()
 
 
 @pytest.mark.parametrize("m", [1, 16, 40, 128, 256, 300, 1024])
-@pytest.mark.parametrize("splits", [1, 0])
+@pytest.mark.parametrize("splits", [1, 0, 3, 8])
 def test_linear_store(ws, m, splits):
     from actfold_b200.kernels import linear
 
@@ -62,7 +62,8 @@ def test_linear_dynamic_m_and_row_maps(ws):
     ws.check_status()
 
 
-def test_linear_residual_and_strided_input(ws):
+@pytest.mark.parametrize("splits", [1, 0])
+def test_linear_residual_and_strided_input(ws, splits):
     from actfold_b200.kernels import EPI_RESIDUAL, linear
 
     big = torch.randn(64, 8192, device="cuda").to(torch.bfloat16)
@@ -70,7 +71,7 @@ def test_linear_residual_and_strided_input(ws):
     w = (torch.randn(4096, 4096, device="cuda") * 0.02).to(torch.bfloat16)
     res = torch.randn(64, 4096, device="cuda").to(torch.bfloat16)
     res_rows = torch.arange(63, -1, -1, device="cuda", dtype=torch.int32)
-    out = linear(x, w, ws, epilogue=EPI_RESIDUAL, residual=res, res_rows=res_rows)
+    out = linear(x, w, ws, epilogue=EPI_RESIDUAL, residual=res, res_rows=res_rows, splits=splits)
     o = (x.float() @ w.float().T).to(torch.bfloat16).float()
     ref = (res[res_rows.long()].float() + o).to(torch.bfloat16)
     assert _rel(out, ref) <= 1e-2
@@ -78,7 +79,8 @@ def test_linear_residual_and_strided_input(ws):
     ws.check_status()
 
 
-def test_linear_swiglu_interleaved(ws):
+@pytest.mark.parametrize("splits", [1, 4, 5])
+def test_linear_swiglu_interleaved(ws, splits):
     from actfold_b200.kernels import EPI_SWIGLU, linear
 
     FF, H, m = 512, 1024, 96
@@ -86,7 +88,7 @@ def test_linear_swiglu_interleaved(ws):
     wu = (torch.randn(FF, H, device="cuda") * 0.03).to(torch.bfloat16)
     w = torch.stack([wg.view(FF // 64, 64, H), wu.view(FF // 64, 64, H)], dim=1).reshape(2 * FF, H).contiguous()
     x = torch.randn(m, H, device="cuda").to(torch.bfloat16)
-    out = linear(x, w, ws, epilogue=EPI_SWIGLU)
+    out = linear(x, w, ws, epilogue=EPI_SWIGLU, splits=splits)
     g = (x.float() @ wg.float().T).to(torch.bfloat16).float()
     u = (x.float() @ wu.float().T).to(torch.bfloat16).float()
     ref = (g / (1 + torch.exp(-g)) * u).to(torch.bfloat16)
@@ -96,7 +98,8 @@ def test_linear_swiglu_interleaved(ws):
     ws.check_status()
 
 
-def test_linear_rope_matches_oracle(ws):
+@pytest.mark.parametrize("splits", [1, 2])
+def test_linear_rope_matches_oracle(ws, splits):
     from actfold_b200.kernels import EPI_ROPE, linear
     from oracle.llada import apply_rope, rope_tables
     from oracle.numerics import round_bf16
@@ -107,7 +110,7 @@ def test_linear_rope_matches_oracle(ws):
     w = (torch.randn(n, H, device="cuda") * 0.05).to(torch.bfloat16)
     cos, sin = rope_tables(T, 128, 500000.0)
     pos = torch.randint(0, T, (m,), device="cuda", dtype=torch.int32)
-    out = linear(x, w, ws, epilogue=EPI_ROPE, rope=(torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(), pos, 2 * H))
+    out = linear(x, w, ws, epilogue=EPI_ROPE, rope=(torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(), pos, 2 * H), splits=splits)
     qkv = round_bf16((x.float() @ w.float().T).cpu().numpy())
     p = pos.cpu().numpy()
     q = apply_rope(qkv[:, :H].reshape(m, nh, 128), p, cos, sin).reshape(m, H)
