@@ -35,7 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "af_gather_rows_index": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp]),
     "af_linear_bf16": (
         _i32,
-        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _vp],
+        [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i32, _vp, _vp],
     ),
     "af_attention_bf16": (
         _i32,

@@ -487,10 +487,12 @@ static DenseWs carve_dense(Bump& b, const Sizes& s, int T) {
   return w;
 }
 
+// Model projections are stored tiled (see af_model in the header).
 static GemmCall base_call(unsigned* status) {
   GemmCall c;
   memset(&c, 0, sizeof(c));
   c.status = status;
+  c.w_tiled = 1;
   c.head_dim = 128;
   return c;
 }
@@ -769,12 +771,12 @@ static int build_maps(FoldPlan* p) {
   p->tm_down.resize(z.L);
   for (int l = 0; l < z.L; ++l) {
     const af_layer_weights& lw = p->layers[l];
-    if ((st = make_tmap_bf16(&p->tm_qkv[l], lw.w_qkv, z.qkv, z.H, z.H, 128))) return st;
-    if ((st = make_tmap_bf16(&p->tm_o[l], lw.w_o, z.H, z.q, z.q, 128))) return st;
-    if ((st = make_tmap_bf16(&p->tm_gu[l], lw.w_gateup, 2 * z.FF, z.H, z.H, 128))) return st;
-    if ((st = make_tmap_bf16(&p->tm_down[l], lw.w_down, z.H, z.FF, z.FF, 128))) return st;
+    if ((st = make_tmap_bf16_tiled(&p->tm_qkv[l], lw.w_qkv, z.qkv, z.H))) return st;
+    if ((st = make_tmap_bf16_tiled(&p->tm_o[l], lw.w_o, z.H, z.q))) return st;
+    if ((st = make_tmap_bf16_tiled(&p->tm_gu[l], lw.w_gateup, 2 * z.FF, z.H))) return st;
+    if ((st = make_tmap_bf16_tiled(&p->tm_down[l], lw.w_down, z.H, z.FF))) return st;
   }
-  if ((st = make_tmap_bf16(&p->tm_lm, p->model.lm_head, z.V, z.H, z.H, 128))) return st;
+  if ((st = make_tmap_bf16_tiled(&p->tm_lm, p->model.lm_head, z.V, z.H))) return st;
   if ((st = make_tmap_bf16(&p->tx_A, p->w.A, p->m_cap, z.H, z.H, nt))) return st;
   if ((st = make_tmap_bf16(&p->tx_att, p->w.att, p->m_cap, z.q, z.q, nt))) return st;
   if ((st = make_tmap_bf16(&p->tx_bn, p->w.bn, p->m_cap, z.H, z.H, nt))) return st;

@@ -40,6 +40,7 @@ constexpr int kMaxSplits = 8; // portable cluster size
 
 struct GemmDev {
   int n, k, m_cap, ntok, n_tiles, nkb, kb_per_split, splits, stages;
+  int w_tiled;  // 1: weights stored as contiguous 128 x 64 tiles (3-D descriptor)
   const int* m_dev;
   int epi;
   __nv_bfloat16* out;
@@ -162,6 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
+    // Tiles start at different k-blocks (rotation by tile index) so concurrent CTAs
+    // do not all read the same activation lines at the same time.
+    const int rot = blockIdx.x % nkb;
     int i = 0;
     for (; i < nkb; ++i) {
       const int s = i % S;
@@ -173,9 +177,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       }
       const uint32_t st = base + s * stage_bytes;
       mbar_arrive_expect_tx(full0 + 8 * s, stage_bytes);
-      const int kx = (kb0 + i) * kBlockK;
-      tma_load_2d(st, &tmW, full0 + 8 * s, kx, n0);
-      tma_load_2d(st + w_bytes, &tmX, full0 + 8 * s, kx, m0);
+      int kb = i + rot;
+      if (kb >= nkb) kb -= nkb;
+      kb += kb0;
+      if (p.w_tiled)
+        tma_load_3d(st, &tmW, full0 + 8 * s, 0, 0, blockIdx.x * p.nkb + kb);
+      else
+        tma_load_2d(st, &tmW, full0 + 8 * s, kb * kBlockK, n0);
+      tma_load_2d(st + w_bytes, &tmX, full0 + 8 * s, kb * kBlockK, m0);
     }
     *issued_slot = i;
   } else if (warp == 1 && lane == 0) {
@@ -318,6 +327,22 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
   return AF_OK;
 }
 
+int make_tmap_bf16_tiled(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (!fn) return fail(AF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || rows % 128 || cols % 64)
+    return fail(AF_ERR_ARG, "tiled weight must be 16-byte aligned with 128-row / 64-column multiples");
+  const cuuint64_t gdim[3] = {64, 128, (rows / 128) * (cols / 64)};
+  const cuuint64_t gstride[2] = {128, 128 * 128};  // bytes: tile row, tile
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gdim, gstride, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AF_ERR_CUDA, "cuTensorMapEncodeTiled (tiled) failed (" + std::to_string((int)r) + ")");
+  return AF_OK;
+}
+
 int gemm_ntok(int m_cap) {
   const int mt = (m_cap + 255) / 256;
   int nt = (m_cap + mt - 1) / mt;
@@ -337,7 +362,12 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   g.nkb = k / kBlockK;
   const int stage = kTileN * kBlockK * 2 + g.ntok * kBlockK * 2;
   int st = (100 * 1024) / stage;  // two CTAs per SM when it fits
-  st = std::max(2, std::min(8, st));
+  static const int env_stages = [] {
+    const char* e = getenv("ACTFOLD_GEMM_STAGES");  // tuning override of the ring depth
+    return e ? atoi(e) : 0;
+  }();
+  if (env_stages > 0) st = env_stages;
+  st = std::max(2, std::min(12, st));
   const int per_sm = (2 * (st * stage + 1024 + 256) <= 227 * 1024) ? 2 : 1;
   int splits = want_splits;
   if (splits <= 0) {
@@ -373,7 +403,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   const CUtensorMap* pw = c.tmap_w;
   const CUtensorMap* px = c.tmap_x;
   if (!pw) {
-    int st = make_tmap_bf16(&tw, c.w, c.n, c.k, c.k, kTileN);
+    int st = c.w_tiled ? make_tmap_bf16_tiled(&tw, c.w, c.n, c.k) : make_tmap_bf16(&tw, c.w, c.n, c.k, c.k, kTileN);
     if (st) return st;
     pw = &tw;
   }
@@ -392,6 +422,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.kb_per_split = g.kb_per;
   d.splits = g.splits;
   d.stages = g.stages;
+  d.w_tiled = c.w_tiled ? 1 : 0;
   d.m_dev = c.m_dev;
   d.epi = c.epi;
   d.out = static_cast<__nv_bfloat16*>(c.out);
@@ -435,14 +466,16 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
 using namespace af;
 
 extern "C" int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_dev, const void* w,
-                              int64_t n, int64_t k, int epilogue, void* out, int64_t ldo, const int32_t* out_rows,
-                              const void* residual, int64_t ldr, const int32_t* res_rows, const float* rope_cos,
-                              const float* rope_sin, const int32_t* positions, int64_t rope_cols, int splits,
-                              uint32_t* status, void* stream) {
+                              int64_t n, int64_t k, int w_layout, int epilogue, void* out, int64_t ldo,
+                              const int32_t* out_rows, const void* residual, int64_t ldr, const int32_t* res_rows,
+                              const float* rope_cos, const float* rope_sin, const int32_t* positions,
+                              int64_t rope_cols, int splits, uint32_t* status, void* stream) {
   AF_REQUIRE(n <= (1 << 30) && k <= (1 << 30) && m_cap <= (1 << 30), "af_linear_bf16: size too large");
   AF_REQUIRE(splits >= 0 && splits <= kMaxSplits, "af_linear_bf16: splits must be in [0, 8]");
+  AF_REQUIRE(w_layout == 0 || w_layout == 1, "af_linear_bf16: w_layout must be 0 (row-major) or 1 (tiled)");
   GemmCall c;
   memset(&c, 0, sizeof(c));
+  c.w_tiled = w_layout;
   c.x = x;
   c.ldx = ldx;
   c.m_cap = (int)m_cap;

@@ -37,6 +37,7 @@ struct GemmCall {
   // Pre-built descriptors (optional; built per call when null).
   const CUtensorMap* tmap_w;
   const CUtensorMap* tmap_x;
+  int w_tiled;         // 1: w is stored tiled [n/128][k/64][128][64] (contiguous 16 KB tiles)
 };
 
 // Token-tile width the kernel uses for a given row capacity.

@@ -65,6 +65,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -149,5 +157,10 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 // 128-byte swizzle, out-of-bounds reads zero-filled.
 int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                    uint32_t box_rows);
+
+// Host: 3-D descriptor over a TILED weight [rows/128][cols/64][128][64] bf16
+// (each 128 x 64 tile one contiguous 16 KB block): box = one tile, 128-byte
+// swizzle; tile (n_tile, k_block) sits at coordinate z = n_tile * (cols/64) + k_block.
+int make_tmap_bf16_tiled(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
 
 }  // namespace af

@@ -14,6 +14,18 @@ from actfold_b200 import _lib
 
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3
 
+
+def tile_weight(w: torch.Tensor) -> torch.Tensor:
+    """[n, k] -> [n/128, k/64, 128, 64]: every 128 x 64 GEMM tile one contiguous 16 KB block.
+
+    A one-time re-layout at model load so the GEMM streams each weight tile from
+    HBM as a single contiguous block instead of 128 strided 128-byte pieces.
+    """
+    n, k = w.shape
+    if n % 128 or k % 64:
+        raise ValueError(f"tile_weight: shape {tuple(w.shape)} is not a multiple of (128, 64)")
+    return w.reshape(n // 128, 128, k // 64, 64).permute(0, 2, 1, 3).contiguous()
+
 class DeviceStatus:
     """Device status word the kernels OR their AF_STATUS bits into (1 timeout, 2 capacity, 4 bounds)."""
 
@@ -41,10 +53,13 @@ def linear(
     res_rows: torch.Tensor | None = None,
     rope: tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None = None,
     splits: int = 0,
+    w_tiled: bool = False,
+    n: int | None = None,
 ) -> torch.Tensor:
     """``out[m] = epilogue(x[m] . w^T)`` on the tcgen05 GEMM (bf16 in/out, fp32 accumulate).
 
-    x: [m_cap, k] bf16 (row stride may exceed k), w: [n, k] bf16 contiguous.
+    x: [m_cap, k] bf16 (row stride may exceed k); w: [n, k] bf16 contiguous, or
+    with ``w_tiled`` the output of :func:`tile_weight` (pass ``n``).
     rope = (cos [P, 64] f32, sin [P, 64] f32, positions [m_cap] i32, rope_cols).
     """
     _lib.require_cuda(x, w, what="linear")
@@ -53,9 +68,13 @@ def linear(
     if x.stride(1) != 1 or not w.is_contiguous():
         raise ValueError("linear: operands must have a contiguous inner dimension")
     m_cap, k = x.shape
-    n = w.shape[0]
-    if w.shape[1] != k:
-        raise ValueError(f"linear: k mismatch {x.shape} vs {w.shape}")
+    if w_tiled:
+        if n is None or w.numel() != n * k:
+            raise ValueError("linear: a tiled weight needs n with w.numel() == n * k")
+    else:
+        n = w.shape[0]
+        if w.shape[1] != k:
+            raise ValueError(f"linear: k mismatch {x.shape} vs {w.shape}")
     out_n = n // 2 if epilogue == EPI_SWIGLU else n
     if out is None:
         out = torch.empty((m_cap, out_n), dtype=torch.bfloat16, device=x.device)
@@ -65,7 +84,7 @@ def linear(
         cos, sin, pos, rope_cols = rope
     with torch.cuda.device(x.device):
         st = _lib.load().af_linear_bf16(
-            x.data_ptr(), x.stride(0), m_cap, _lib.ptr(m_dev), w.data_ptr(), n, k, epilogue,
+            x.data_ptr(), x.stride(0), m_cap, _lib.ptr(m_dev), w.data_ptr(), n, k, 1 if w_tiled else 0, epilogue,
             out.data_ptr(), out.stride(0), _lib.ptr(out_rows),
             _lib.ptr(residual), residual.stride(0) if residual is not None else 0, _lib.ptr(res_rows),
             _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), rope_cols,

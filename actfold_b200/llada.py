@@ -29,6 +29,7 @@ import torch
 import torch.nn as nn
 
 from actfold_b200 import _lib
+from actfold_b200.kernels import tile_weight
 from actfold_b200.workloads import ModelDims
 
 _vp, _i32, _i64, _f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_float
@@ -116,12 +117,20 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, device) -> tuple[torc
 
 
 class LLaDABlock(nn.Module):
-    """Weights of one block (bf16 buffers in kernel layout)."""
+    """Weights of one block: bf16 buffers, projections tiled for the GEMM (``kernels.tile_weight``).
+
+    Takes row-major [n, k] projections and stores them tiled; ``shapes`` keeps
+    the logical [n, k] of each.
+    """
 
     def __init__(self, attn_norm, w_qkv, w_o, ffn_norm, w_gateup, w_down) -> None:
         super().__init__()
-        for k, v in dict(attn_norm=attn_norm, w_qkv=w_qkv, w_o=w_o, ffn_norm=ffn_norm, w_gateup=w_gateup, w_down=w_down).items():
-            self.register_buffer(k, v.contiguous())
+        self.register_buffer("attn_norm", attn_norm.contiguous())
+        self.register_buffer("ffn_norm", ffn_norm.contiguous())
+        self.shapes = {}
+        for k, v in dict(w_qkv=w_qkv, w_o=w_o, w_gateup=w_gateup, w_down=w_down).items():
+            self.shapes[k] = tuple(v.shape)
+            self.register_buffer(k, tile_weight(v))
 
     def forward(self, hidden_states: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
         raise RuntimeError("LLaDABlock runs inside the native folded pass; call LLaDAModel or FoldedModel instead")
@@ -263,7 +272,7 @@ class LLaDAModel(nn.Module):
         self.register_buffer("embed", embed.contiguous())
         self.layers = nn.ModuleList(layers)
         self.register_buffer("final_norm", final_norm.contiguous())
-        self.register_buffer("lm_head", lm_head.contiguous())
+        self.register_buffer("lm_head", tile_weight(lm_head))
         cos, sin = rope_tables(max_pos, dims.head_dim, dims.rope_theta, embed.device)
         self.register_buffer("rope_cos", cos)
         self.register_buffer("rope_sin", sin)

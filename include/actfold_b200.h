@@ -127,7 +127,9 @@ typedef enum {
  * (actfold/core/folded_transformer.py:224-258): here only the packed divergent
  * rows are computed, with tcgen05 tensor cores (bf16 x bf16 -> fp32 in TMEM).
  *   x [m_cap, k] bf16, row stride ldx (elements); valid rows = *m_dev (device
- *   int, nullable -> m_cap); w [n, k] bf16 (n % 128 == 0, k % 64 == 0);
+ *   int, nullable -> m_cap); w [n, k] bf16 (n % 128 == 0, k % 64 == 0),
+ *   w_layout 0 = row-major, 1 = tiled [n/128][k/64][128][64] (each 128 x 64
+ *   tile one contiguous 16 KB block; streams from HBM in whole blocks);
  *   out rows: out_rows[m] (nullable -> m), row stride ldo; residual rows:
  *   res_rows[m] (nullable -> m); rope tables cos/sin [P, 64] fp32 indexed by
  *   positions[m]. splits (0..8, 0 = automatic) divides the k-range over a
@@ -136,7 +138,7 @@ typedef enum {
  *   2 capacity).
  */
 int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_dev,
-                   const void* w, int64_t n, int64_t k, int epilogue,
+                   const void* w, int64_t n, int64_t k, int w_layout, int epilogue,
                    void* out, int64_t ldo, const int32_t* out_rows,
                    const void* residual, int64_t ldr, const int32_t* res_rows,
                    const float* rope_cos, const float* rope_sin, const int32_t* positions,
@@ -178,13 +180,15 @@ typedef struct {
   float rms_eps;
 } af_model_dims;
 
+/* Projection weights are bf16 matrices [n, k] stored TILED, i.e. as
+ * [n/128][k/64][128][64] (af_linear_bf16 w_layout 1); norms are plain [hidden]. */
 typedef struct {
   const void* attn_norm; /* [hidden] bf16 */
-  const void* w_qkv;     /* [q_dim + 2 kv_dim, hidden] bf16: Wq rows, Wk rows, Wv rows */
-  const void* w_o;       /* [hidden, q_dim] */
+  const void* w_qkv;     /* [q_dim + 2 kv_dim, hidden]: Wq rows, Wk rows, Wv rows (tiled) */
+  const void* w_o;       /* [hidden, q_dim] (tiled) */
   const void* ffn_norm;  /* [hidden] */
-  const void* w_gateup;  /* [2 ffn, hidden]: per 128 rows, 64 gate rows then the 64 matching up rows */
-  const void* w_down;    /* [hidden, ffn] */
+  const void* w_gateup;  /* [2 ffn, hidden]: per 128 rows, 64 gate rows then the 64 matching up rows (tiled) */
+  const void* w_down;    /* [hidden, ffn] (tiled) */
 } af_layer_weights;
 
 typedef struct {
@@ -192,7 +196,7 @@ typedef struct {
   const af_layer_weights* layers; /* host array of n_layers entries (copied by plans) */
   const void* embed;              /* [vocab, hidden] bf16 */
   const void* final_norm;         /* [hidden] */
-  const void* lm_head;            /* [vocab, hidden] */
+  const void* lm_head;            /* [vocab, hidden] (tiled) */
   const float* rope_cos;          /* [max_pos, head_dim / 2] fp32 */
   const float* rope_sin;
   int64_t max_pos;

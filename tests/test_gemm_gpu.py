@@ -132,3 +132,21 @@ def test_linear_large_n_like_lm_head(ws):
     assert _rel(out, ref) <= 1e-2
     torch.cuda.synchronize()
     ws.check_status()
+
+
+@pytest.mark.parametrize("splits", [1, 0])
+def test_linear_tiled_weights(ws, splits):
+    from actfold_b200.kernels import EPI_SWIGLU, linear, tile_weight
+
+    x = torch.randn(128, 4096, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(2048, 4096, device="cuda") * 0.02).to(torch.bfloat16)
+    out = linear(x, tile_weight(w), ws, splits=splits, w_tiled=True, n=2048)
+    ref = (x.float() @ w.float().T).to(torch.bfloat16)
+    assert _rel(out, ref) <= 1e-2
+    out_g = linear(x, tile_weight(w), ws, epilogue=EPI_SWIGLU, splits=splits, w_tiled=True, n=2048)
+    g = ref.float().view(128, 16, 2, 64)
+    gate, up = g[:, :, 0].reshape(128, 1024), g[:, :, 1].reshape(128, 1024)
+    ref_g = (gate / (1 + torch.exp(-gate)) * up).to(torch.bfloat16)
+    assert _rel(out_g, ref_g) <= 2e-2
+    torch.cuda.synchronize()
+    ws.check_status()
