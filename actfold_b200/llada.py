@@ -75,6 +75,7 @@ _lib.SIGNATURES.update(
     {
         "af_dense_workspace_bytes": (_i32, [C.POINTER(_Dims), _i64, C.POINTER(_i64)]),
         "af_dense_forward": (_i32, [C.POINTER(_Model), _vp, _i64, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp]),
+        "af_dense_forward_static": (_i32, [C.POINTER(_Model), _vp, _i64, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
         "af_fold_workspace_bytes": (_i32, [C.POINTER(_Dims), C.POINTER(_FoldConfig), C.POINTER(_i64)]),
         "af_fold_plan_create": (_i32, [C.POINTER(_Model), C.POINTER(_Parent), C.POINTER(_FoldConfig), _vp, _i64, C.POINTER(_vp)]),
         "af_fold_run": (_i32, [_vp, _vp, _vp, _vp, _vp]),

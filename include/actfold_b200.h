@@ -227,6 +227,31 @@ int af_dense_forward(const af_model* model, const int64_t* tokens, int64_t T, fl
                      float* logit_row_sums, void* workspace, int64_t workspace_bytes,
                      uint32_t* status, void* stream);
 
+/* Size of the file-scope device scratch array behind af_dense_forward_static. */
+#define AF_DENSE_STATIC_WORKSPACE_BYTES (32ll << 20)
+
+/*
+ * af_dense_forward_static -- af_dense_forward with its scratch in a
+ * file-scope __device__ array of AF_DENSE_STATIC_WORKSPACE_BYTES (32 MiB) per
+ * device instead of a caller workspace. It has no counterpart in the
+ * reference: it exists so a caller that must not allocate (no
+ * cudaMalloc/cudaFree, no allocating library routine) can run the parent pass.
+ *   - The outputs are bit-identical to af_dense_forward on the same inputs.
+ *   - T is rejected with AF_ERR_CAPACITY when af_dense_workspace_bytes(dims, T)
+ *     exceeds the array (LLaDA-8B dims: 585 tokens at most).
+ *   - The first call on a device looks up the array's address with
+ *     cudaGetSymbolAddress, with that device current, and caches it; make that
+ *     first call before any stream capture. The device owning `stream` must be
+ *     current on every call.
+ *   - No part of the scratch has to start at zero.
+ *   - There is one array per device: calls that overlap on the same device
+ *     (another stream or host thread before the previous call's kernels have
+ *     finished) race on it.
+ */
+int af_dense_forward_static(const af_model* model, const int64_t* tokens, int64_t T, float tau,
+                            void* layer_in, void* qkv, void* logits, uint8_t* self_stable,
+                            float* logit_row_sums, uint32_t* status, void* stream);
+
 typedef struct {
   int64_t n_children;          /* C */
   int64_t seq;                 /* T (equal to the parent's) */
