@@ -13,11 +13,23 @@
 // CTA = 4 warps, 64 query rows of one head; each warp owns 16 rows. K/V blocks
 // of 64 keys are double-buffered in XOR-swizzled shared memory with cp.async;
 // S = Q K^T and O += P V use mma.m16n8k16 (bf16 in, fp32 accumulate).
+//
+// Key split: when few query rows give few CTAs (the folded pass packs only the
+// divergent rows), the key blocks of one (query block, head) are divided over
+// the S CTAs of a thread-block cluster (grid z). Each CTA leaves its softmax
+// partials (row max m, row sum l, unnormalised O) in its own shared memory;
+// after a cluster barrier CTA z combines rows [z*64/S, (z+1)*64/S) from all S
+// partials through distributed shared memory and writes them, and a second
+// barrier keeps every CTA's partials alive until its peers have read them.
+#include <cstdlib>
+
 #include "attention.cuh"
 
 namespace af {
 
 constexpr int kHD = 128, kQB = 64, kKB = 64;
+constexpr int kSmemKV = 16384 + 2 * 32768;      // Q tile + two K/V stages
+constexpr int kSmem = kSmemKV + 2 * kKB * 4;    // + candidate-key children per stage
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [64][128] bf16 tile
   return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4));
@@ -61,6 +73,7 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
   const int q0 = blockIdx.x * kQB;
   if (q0 >= n_q) return;
   const int h = blockIdx.y;
+  const int ns = gridDim.z, split = blockIdx.z;  // key splits = cluster size along z
   const int kvh = h / (p.n_heads / p.n_kv_heads);
   const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -69,6 +82,7 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
   const uint32_t sQ = static_cast<uint32_t>(__cvta_generic_to_shared(sm));
   const uint32_t sK[2] = {sQ + 16384, sQ + 16384 + 32768};
   const uint32_t sV[2] = {sQ + 16384 + 16384, sQ + 16384 + 32768 + 16384};
+  int* sF = reinterpret_cast<int*>(sm + kSmemKV);  // [2][kKB] child of each candidate key of a block
 
   // ---- Q tile (64 rows x 128) ----
   for (int idx = tid; idx < kQB * 16; idx += 128) {
@@ -83,6 +97,7 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
   const int n_pb = (p.T + kKB - 1) / kKB;
   const int n_fb = (n_f + kKB - 1) / kKB;
   const int n_blocks = n_pb + n_fb;
+  const int b_lo = split * n_blocks / ns, b_hi = (split + 1) * n_blocks / ns;  // balanced, possibly empty
 
   auto load_block = [&](int b, int buf) {
     for (int idx = tid; idx < kKB * 16; idx += 128) {
@@ -106,9 +121,13 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
       cp_async16(sV[buf] + swz(r, c), vs, ok);
     }
     cp_commit();
+    if (b >= n_pb && tid < kKB) {
+      const int j = (b - n_pb) * kKB + tid;
+      sF[buf * kKB + tid] = j >= n_f ? -2 : (p.fchild ? p.fchild[j] : -1);
+    }
   };
 
-  load_block(0, 0);
+  if (b_lo < b_hi) load_block(b_lo, 0);
 
   // Per-thread rows: r0 = 16*warp + g, r1 = r0 + 8 (within the CTA's 64).
   const int row0 = q0 + 16 * warp + g, row1 = row0 + 8;
@@ -121,16 +140,16 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   uint32_t qa[8][4];
 
-  for (int b = 0; b < n_blocks; ++b) {
-    const int buf = b & 1;
-    if (b + 1 < n_blocks) {
+  for (int b = b_lo; b < b_hi; ++b) {
+    const int buf = (b - b_lo) & 1;
+    if (b + 1 < b_hi) {
       load_block(b + 1, buf ^ 1);
       cp_wait_1();
     } else {
       cp_wait_0();
     }
     __syncthreads();
-    if (b == 0) {
+    if (b == b_lo) {
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const int r = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
@@ -155,24 +174,50 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
       }
     }
     // ---- mask + online softmax ----
+    // Valid keys of this block as 64-bit masks for the thread's two rows:
+    // parent keys minus the row's fresh positions, or the candidate keys of
+    // the row's own child (-1 in sF: no child filter; -2: past n_f).
     const bool parent_blk = b < n_pb;
+    uint64_t v0, v1;
+    if (parent_blk) {
+      const int t0 = b * kKB;
+      const int nvalid = min(kKB, p.T - t0);
+      const uint64_t range = nvalid >= 64 ? ~0ull : ((1ull << nvalid) - 1ull);
+      uint64_t f0 = 0, f1 = 0;
+      if (p.fresh_bits) {
+        const int w = t0 >> 5;
+        if (child0 >= 0) {
+          const uint32_t* fb = p.fresh_bits + (int64_t)child0 * p.bits_ld;
+          f0 = (uint64_t)fb[w] | ((w + 1 < p.bits_ld) ? (uint64_t)fb[w + 1] << 32 : 0ull);
+        }
+        if (child1 >= 0) {
+          const uint32_t* fb = p.fresh_bits + (int64_t)child1 * p.bits_ld;
+          f1 = (uint64_t)fb[w] | ((w + 1 < p.bits_ld) ? (uint64_t)fb[w + 1] << 32 : 0ull);
+        }
+      }
+      v0 = range & ~f0;
+      v1 = range & ~f1;
+    } else {
+      v0 = v1 = 0;
+      const int* fc = sF + buf * kKB;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = 8 * j + 2 * t4 + e;
+          const int cf = fc[key];
+          if (cf == -1 || (cf >= 0 && cf == child0)) v0 |= 1ull << key;
+          if (cf == -1 || (cf >= 0 && cf == child1)) v1 |= 1ull << key;
+        }
+      }
+    }
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int key = 8 * j + 2 * t4 + (e & 1);
-        const int child = (e < 2) ? child0 : child1;
-        bool valid;
-        if (parent_blk) {
-          const int t = b * kKB + key;
-          valid = t < p.T;
-          if (valid && p.fresh_bits && child >= 0)
-            valid = ((p.fresh_bits[(int64_t)child * p.bits_ld + (t >> 5)] >> (t & 31)) & 1u) == 0;
-        } else {
-          const int jj = (b - n_pb) * kKB + key;
-          valid = jj < n_f && (p.fchild == nullptr || p.fchild[jj] == child);
-        }
+        const bool valid = (((e < 2) ? v0 : v1) >> key) & 1ull;
         const float v = valid ? s[j][e] * p.scale_log2 : -INFINITY;
         s[j][e] = v;
         if (e < 2) mx0 = fmaxf(mx0, v);
@@ -228,19 +273,99 @@ __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
     __syncthreads();
   }
   // ---- finalize ----
+  cp_wait_0();  // a split without key blocks still has its Q copy in flight
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  if (ns == 1) {
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int d = h * kHD + 8 * j + 2 * t4;
+      if (row0 < n_q)
+        *reinterpret_cast<uint32_t*>(p.out + (int64_t)row0 * p.out_ld + d) = pack2(o[j][0] * inv0, o[j][1] * inv0);
+      if (row1 < n_q)
+        *reinterpret_cast<uint32_t*>(p.out + (int64_t)row1 * p.out_ld + d) = pack2(o[j][2] * inv1, o[j][3] * inv1);
+    }
+    return;
+  }
+  // Partials into this CTA's shared memory (the K/V buffers are free after the
+  // loop's final barrier): O [64][128] f32 at sK[0], (m, l) [64] at sK[0] + 32 KB.
+  __syncthreads();
+  float* po = reinterpret_cast<float*>(sm + 16384);
+  float2* pml = reinterpret_cast<float2*>(sm + 16384 + 32768);
+  const int r0 = 16 * warp + g, r1 = r0 + 8;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const int d = h * kHD + 8 * j + 2 * t4;
-    if (row0 < n_q)
-      *reinterpret_cast<uint32_t*>(p.out + (int64_t)row0 * p.out_ld + d) = pack2(o[j][0] * inv0, o[j][1] * inv0);
-    if (row1 < n_q)
-      *reinterpret_cast<uint32_t*>(p.out + (int64_t)row1 * p.out_ld + d) = pack2(o[j][2] * inv1, o[j][3] * inv1);
+    const int d = 8 * j + 2 * t4;
+    *reinterpret_cast<float2*>(po + r0 * kHD + d) = make_float2(o[j][0], o[j][1]);
+    *reinterpret_cast<float2*>(po + r1 * kHD + d) = make_float2(o[j][2], o[j][3]);
   }
+  if (t4 == 0) {
+    pml[r0] = make_float2(m0, l0);
+    pml[r1] = make_float2(m1, l1);
+  }
+  cluster_sync_all();
+  const int rows_per = kQB / ns;
+  const uint32_t po_s = static_cast<uint32_t>(__cvta_generic_to_shared(po));
+  const uint32_t pml_s = static_cast<uint32_t>(__cvta_generic_to_shared(pml));
+  for (int idx = tid; idx < rows_per * (kHD / 4); idx += 128) {
+    const int r = split * rows_per + idx / (kHD / 4);
+    const int c4 = idx % (kHD / 4);
+    float mk[8], lk[8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < ns) {
+        const float2 v = ld_cluster_f2(cluster_map(pml_s + 8u * r, (uint32_t)k));
+        mk[k] = v.x;
+        lk[k] = v.y;
+        mx = fmaxf(mx, v.x);
+      }
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < ns && mk[k] != -INFINITY) {
+        const float f = exp2f(mk[k] - mx);
+        lsum += f * lk[k];
+        const float4 v = ld_cluster_f4(cluster_map(po_s + 4u * (r * kHD + 4 * c4), (uint32_t)k));
+        acc.x += f * v.x;
+        acc.y += f * v.y;
+        acc.z += f * v.z;
+        acc.w += f * v.w;
+      }
+    }
+    const int row = q0 + r;
+    if (row < n_q) {
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      uint2 w;
+      w.x = pack2(acc.x * inv, acc.y * inv);
+      w.y = pack2(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(p.out + (int64_t)row * p.out_ld + h * kHD + 4 * c4) = w;
+    }
+  }
+  cluster_sync_all();  // peers may read this CTA's partials until here
+}
+
+// Key splits per (query block, head): the largest of 1, 2, 4, 8 (the portable
+// cluster size) that keeps every CTA resident in one wave (two CTAs per SM,
+// bound by registers and shared memory) and leaves each split at least two
+// key blocks. ACTFOLD_ATTN_SPLITS (1, 2, 4 or 8) overrides the choice.
+static int attention_splits(const AttnParams& p) {
+  const char* env = std::getenv("ACTFOLD_ATTN_SPLITS");
+  if (env) {
+    const int v = std::atoi(env);
+    if (v == 1 || v == 2 || v == 4 || v == 8) return v;
+  }
+  const int ctas = (p.n_q_cap + kQB - 1) / kQB * p.n_heads;
+  const int n_blocks = (p.T + kKB - 1) / kKB + (p.fk ? (p.n_f_cap + kKB - 1) / kKB : 0);
+  const int resident = 2 * sm_count();
+  int ns = 1;
+  while (ns < 8 && 2 * ns * ctas <= resident && n_blocks / (2 * ns) >= 2) ns *= 2;
+  return ns;
 }
 
 int attention_run(const AttnParams& p, cudaStream_t s) {
@@ -250,16 +375,31 @@ int attention_run(const AttnParams& p, cudaStream_t s) {
   AF_REQUIRE(!p.fk || (p.fv && p.n_f_cap >= 0), "attention: fresh keys need values");
   AF_REQUIRE(((p.q_ld | p.kv_ld | p.out_ld | p.f_ld) & 7) == 0, "attention: row strides must be multiples of 8");
   if (p.n_q_cap == 0) return AF_OK;
-  const int smem = 16384 + 2 * 32768;
+  const int smem = kSmem;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_attention, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     attr = true;
   }
-  dim3 grid((p.n_q_cap + kQB - 1) / kQB, p.n_heads);
-  k_attention<<<grid, 128, smem, s>>>(p);
+  const int ns = attention_splits(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.n_q_cap + kQB - 1) / kQB, p.n_heads, ns);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr_c[1];
+  attr_c[0].id = cudaLaunchAttributeClusterDimension;
+  attr_c[0].val.clusterDim.x = 1;
+  attr_c[0].val.clusterDim.y = 1;
+  attr_c[0].val.clusterDim.z = ns;
+  cfg.attrs = attr_c;
+  cfg.numAttrs = ns > 1 ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_attention, p);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("attention: launch: ") + cudaGetErrorString(e));
   return check_launch("attention");
 }
+
 
 }  // namespace af
 

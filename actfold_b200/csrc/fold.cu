@@ -7,7 +7,7 @@
 // output, so its next input is bit-identical to the parent's). Per layer:
 //
 //   candidates  = fresh rows (+ any row the parent itself fails the gate on)
-//   k_fold_gate     gate(child row, parent row) + copy + attention RMSNorm   [warp / candidate]
+//   k_fold_gate     gate(child row, parent row) + copy + attention RMSNorm   [CTA / candidate]
 //   k_fold_compact  divergent list, fresh-key bitmap, next layer's candidates  [1 CTA]
 //   QKV GEMM (+RoPE) on candidates           (tcgen05)
 //   attention of divergent rows over parent K/V + fresh K/V
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
 }
 
 // ----------------------------------------------------------------------------
-// Row gathers and RMSNorm (warp per row).
+// Row gathers (warp per row) and RMSNorm (CTA per row).
 // ----------------------------------------------------------------------------
 // out[i] = embed[tokens[rows[i]]]; an id outside [0, vocab) sets AF_STATUS_BOUNDS and yields a zero row.
 __global__ void __launch_bounds__(256) k_embed_rows(const __nv_bfloat16* embed, int H, int64_t vocab,
@@ -158,9 +158,16 @@ __global__ void __launch_bounds__(256) k_embed_rows(const __nv_bfloat16* embed, 
   for (int v = lane; v < H / 8; v += 32) stg16(dst + 16 * v, ldg16(src + 16 * v));
 }
 
-template <int NV>
+// Rows of the per-row kernels below are spread over one CTA of kRowThreads
+// threads (H <= 4096 gives each thread at most two 16-byte vectors), so a
+// few hundred packed rows still occupy every SM.
+constexpr int kRowThreads = 256;
+using RowGroup = CtaRows<kRowThreads>;
+
+template <int NV, class Rows = WarpRows>
 __device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int H, const __nv_bfloat16* w, float eps,
-                                             char* out, int lane) {
+                                             char* out, int tid, const Rows& rows = Rows()) {
+  constexpr int G = Rows::kThreads;
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
@@ -169,13 +176,13 @@ __device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int
 #pragma unroll
     for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
   }
-  ss = warp_sum(ss);
+  ss = rows.sum(ss);
   const float var = __fdiv_rn(ss, (float)H);
   const float rinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, eps)));
   const char* wb = reinterpret_cast<const char*>(w);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
+    const int j = i * G + tid;
     if (j >= nvec) continue;
     float f[8], g[8];
     unpack<AF_DTYPE_BF16>(v[i], f);
@@ -192,18 +199,19 @@ __device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int
   }
 }
 
-// out[i] = rmsnorm(in[i]) * w for i < n (rows strided by H).
+// out[i] = rmsnorm(in[i]) * w for i < n (rows strided by H); one CTA per row.
 template <int NV>
-__global__ void __launch_bounds__(256) k_rmsnorm_rows(const __nv_bfloat16* in, const __nv_bfloat16* w, int H,
-                                                      float eps, const int* n_dev, int n_cap, __nv_bfloat16* out) {
-  const int lane = threadIdx.x & 31;
-  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat16* in, const __nv_bfloat16* w, int H,
+                                                              float eps, const int* n_dev, int n_cap,
+                                                              __nv_bfloat16* out) {
+  __shared__ float red[2 * kRowThreads / 32];
+  const int i = blockIdx.x;
   const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
   if (i >= n) return;
   const int nvec = H / 8;
   uint4 v[NV];
-  load_row<NV>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, lane, v);
-  rmsnorm_regs<NV>(v, nvec, H, w, eps, reinterpret_cast<char*>(out + (int64_t)i * H), lane);
+  load_row<NV, kRowThreads>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, threadIdx.x, v);
+  rmsnorm_regs<NV>(v, nvec, H, w, eps, reinterpret_cast<char*>(out + (int64_t)i * H), threadIdx.x, RowGroup{red});
 }
 
 // ----------------------------------------------------------------------------
@@ -225,27 +233,29 @@ struct FoldGateArgs {
 };
 
 template <int METRIC, int NV>
-__global__ void __launch_bounds__(256) k_fold_gate(const FoldGateArgs g) {
-  const int lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g) {
+  __shared__ float red[2 * kRowThreads / 32];
+  const int tid = threadIdx.x;
+  const int r = blockIdx.x;
   const int n = min(*g.n_cand, g.m_cap);
   if (r >= n) return;
   const int t = g.cand_pos[r], src = g.cand_src[r];
   const int nvec = g.H / 8;
+  const RowGroup rows{red};
   const char* prow = reinterpret_cast<const char*>(g.p_in + (int64_t)t * g.H);
   const char* hrow = src >= 0 ? reinterpret_cast<const char*>(g.x_fresh + (int64_t)src * g.H) : prow;
   uint4 hv[NV], pv[NV];
-  load_row<NV>(hrow, nvec, lane, hv);
-  load_row<NV>(prow, nvec, lane, pv);
-  const GateOut o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, lane);
-  if (lane == 0) g.stable[r] = o.stable;
+  load_row<NV, kRowThreads>(hrow, nvec, tid, hv);
+  load_row<NV, kRowThreads>(prow, nvec, tid, pv);
+  const GateOut o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, tid, rows);
+  if (tid == 0) g.stable[r] = o.stable;
   char* xc = reinterpret_cast<char*>(g.xc + (int64_t)r * g.H);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
+    const int j = i * kRowThreads + tid;
     if (j < nvec) stg16(xc + 16 * j, hv[i]);
   }
-  rmsnorm_regs<NV>(hv, nvec, g.H, g.norm_w, g.eps, reinterpret_cast<char*>(g.a + (int64_t)r * g.H), lane);
+  rmsnorm_regs<NV>(hv, nvec, g.H, g.norm_w, g.eps, reinterpret_cast<char*>(g.a + (int64_t)r * g.H), tid, rows);
 }
 
 // ----------------------------------------------------------------------------
@@ -398,18 +408,20 @@ __global__ void k_zero_f32(float* p, int64_t n) {
   if (i < n) p[i] = 0.f;
 }
 
-// Self gate of the parent rows of one layer (does the parent pass its own gate?).
+// Self gate of the parent rows of one layer (does the parent pass its own
+// gate?). Same row grouping and arithmetic as k_fold_gate, so a parent row
+// that fails here fails there too when a child carries it unchanged.
 template <int NV>
-__global__ void __launch_bounds__(256) k_self_gate(const __nv_bfloat16* x, int H, int T, GateConsts k,
-                                                   uint8_t* self_stable) {
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(kRowThreads) k_self_gate(const __nv_bfloat16* x, int H, int T, GateConsts k,
+                                                           uint8_t* self_stable) {
+  __shared__ float red[2 * kRowThreads / 32];
+  const int t = blockIdx.x;
   if (t >= T) return;
   const int nvec = H / 8;
   uint4 v[NV];
-  load_row<NV>(reinterpret_cast<const char*>(x + (int64_t)t * H), nvec, lane, v);
-  const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, H, k, lane);
-  if (lane == 0) self_stable[t] = o.stable;
+  load_row<NV, kRowThreads>(reinterpret_cast<const char*>(x + (int64_t)t * H), nvec, threadIdx.x, v);
+  const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, H, k, threadIdx.x, RowGroup{red});
+  if (threadIdx.x == 0) self_stable[t] = o.stable;
 }
 
 // ----------------------------------------------------------------------------
@@ -428,19 +440,11 @@ struct Bump {
   }
 };
 
-static int nv_for(int H) {
-  const int nvec = H / 8;
-  return (nvec + 31) / 32;
-}
-
-#define AF_DISPATCH_NV(H, KERNEL, GRID, BLOCK, SMEM, STREAM, ...)                 \
-  do {                                                                            \
-    const int _nv = nv_for(H);                                                    \
-    if (_nv <= 1) KERNEL<1><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);          \
-    else if (_nv <= 2) KERNEL<2><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);     \
-    else if (_nv <= 4) KERNEL<4><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);     \
-    else if (_nv <= 8) KERNEL<8><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);     \
-    else KERNEL<16><<<GRID, BLOCK, SMEM, STREAM>>>(__VA_ARGS__);                  \
+// Per-row kernels on one CTA of kRowThreads threads per row: H <= 4096.
+#define AF_DISPATCH_ROWS(H, KERNEL, ROWS, STREAM, ...)                                              \
+  do {                                                                                              \
+    if ((H) / 8 <= kRowThreads) KERNEL<1><<<(unsigned)(ROWS), kRowThreads, 0, STREAM>>>(__VA_ARGS__); \
+    else KERNEL<2><<<(unsigned)(ROWS), kRowThreads, 0, STREAM>>>(__VA_ARGS__);                      \
   } while (0)
 
 static int validate_model(const af_model* m) {
@@ -538,9 +542,9 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     const __nv_bfloat16* x = xin + (int64_t)l * Ti * z.H;
     __nv_bfloat16* xnext = xin + (int64_t)(l + 1) * Ti * z.H;
     __nv_bfloat16* qkv_l = qkvb + (int64_t)l * Ti * z.qkv;
-    AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, x, static_cast<const __nv_bfloat16*>(lw.attn_norm), z.H,
-                                                                eps, nullptr, Ti, w.A);
-    AF_DISPATCH_NV(z.H, k_self_gate, rows_blocks, 256, 0, s, x, z.H, Ti, gk, self_stable + (int64_t)l * Ti);
+    AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, x, static_cast<const __nv_bfloat16*>(lw.attn_norm), z.H, eps, nullptr,
+                     Ti, w.A);
+    AF_DISPATCH_ROWS(z.H, k_self_gate, Ti, s, x, z.H, Ti, gk, self_stable + (int64_t)l * Ti);
     GemmCall c = base_call(stw);
     c.x = w.A;
     c.ldx = z.H;
@@ -584,8 +588,8 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     c.res = x;
     c.ldr = z.H;
     if ((st = gemm_run(c, s))) return st;
-    AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm),
-                                                                z.H, eps, nullptr, Ti, w.bn);
+    AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm), z.H, eps,
+                     nullptr, Ti, w.bn);
     c = base_call(stw);
     c.x = w.bn;
     c.ldx = z.H;
@@ -612,8 +616,8 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     if ((st = gemm_run(c, s))) return st;
   }
   const __nv_bfloat16* xl = xin + (int64_t)z.L * Ti * z.H;
-  AF_DISPATCH_NV(z.H, k_rmsnorm_rows, rows_blocks, 256, 0, s, xl, static_cast<const __nv_bfloat16*>(m->final_norm),
-                                                              z.H, eps, nullptr, Ti, w.A);
+  AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, xl, static_cast<const __nv_bfloat16*>(m->final_norm), z.H, eps,
+                   nullptr, Ti, w.A);
   k_zero_f32<<<(Ti + 255) / 256, 256, 0, s>>>(logit_row_sums, Ti);
   GemmCall c = base_call(stw);
   c.x = w.A;
@@ -785,13 +789,9 @@ static int build_maps(FoldPlan* p) {
 }
 
 template <int METRIC>
-static void launch_fold_gate(const FoldGateArgs& g, int H, unsigned blocks, cudaStream_t s) {
-  const int nv = nv_for(H);
-  if (nv <= 1) k_fold_gate<METRIC, 1><<<blocks, 256, 0, s>>>(g);
-  else if (nv <= 2) k_fold_gate<METRIC, 2><<<blocks, 256, 0, s>>>(g);
-  else if (nv <= 4) k_fold_gate<METRIC, 4><<<blocks, 256, 0, s>>>(g);
-  else if (nv <= 8) k_fold_gate<METRIC, 8><<<blocks, 256, 0, s>>>(g);
-  else k_fold_gate<METRIC, 16><<<blocks, 256, 0, s>>>(g);
+static void launch_fold_gate(const FoldGateArgs& g, int H, int rows, cudaStream_t s) {
+  if (H / 8 <= kRowThreads) k_fold_gate<METRIC, 1><<<(unsigned)rows, kRowThreads, 0, s>>>(g);
+  else k_fold_gate<METRIC, 2><<<(unsigned)rows, kRowThreads, 0, s>>>(g);
 }
 
 static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, float* scores, cudaStream_t s) {
@@ -859,9 +859,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     g.stable = w.stable;
     g.xc = w.xc;
     g.a = w.A;
-    AF_TIMED(FK_GATE, if (p->metric == AF_METRIC_COSINE) launch_fold_gate<AF_METRIC_COSINE>(g, z.H, mblocks, s);
-             else if (p->metric == AF_METRIC_L2) launch_fold_gate<AF_METRIC_L2>(g, z.H, mblocks, s);
-             else launch_fold_gate<AF_METRIC_PEARSON>(g, z.H, mblocks, s));
+    AF_TIMED(FK_GATE, if (p->metric == AF_METRIC_COSINE) launch_fold_gate<AF_METRIC_COSINE>(g, z.H, M, s);
+             else if (p->metric == AF_METRIC_L2) launch_fold_gate<AF_METRIC_L2>(g, z.H, M, s);
+             else launch_fold_gate<AF_METRIC_PEARSON>(g, z.H, M, s));
 
     CompactArgs a;
     memset(&a, 0, sizeof(a));
@@ -953,8 +953,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.tmap_x = &p->tx_att;
     AF_TIMED(FK_O, if ((st = gemm_run(c, s))) return st);
 
-    AF_TIMED(FK_NORM, AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, w.h1,
-                                     static_cast<const __nv_bfloat16*>(lw.ffn_norm), z.H, eps, nd, M, w.bn));
+    AF_TIMED(FK_NORM, AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, M, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm),
+                                       z.H, eps, nd, M, w.bn));
     c = base_call(w.status);
     c.x = w.bn;
     c.ldx = z.H;
@@ -1011,8 +1011,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   int* nd_last = w.n_div + (L - 1);
   int* pos_last = w.div_pos + (int64_t)(L - 1) * M;
   const __nv_bfloat16* x_final = w.x_all + (int64_t)L * M * z.H;
-  AF_TIMED(FK_NORM, AF_DISPATCH_NV(z.H, k_rmsnorm_rows, mblocks, 256, 0, s, x_final, static_cast<const __nv_bfloat16*>(p->model.final_norm),
-                                                          z.H, eps, nd_last, M, w.A));
+  AF_TIMED(FK_NORM, AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, M, s, x_final,
+                                     static_cast<const __nv_bfloat16*>(p->model.final_norm), z.H, eps, nd_last, M, w.A));
   GemmCall c = base_call(w.status);
   c.x = w.A;
   c.ldx = z.H;

@@ -64,19 +64,65 @@ __device__ __forceinline__ float finish_cos(float sc, float sp, const GateConsts
   return 0.f;
 }
 
-// Row held in registers: lane owns vectors v = i * 32 + lane (zero past nvec).
-template <int NV>
-__device__ __forceinline__ void load_row(const char* p, int nvec, int lane, uint4 (&v)[NV]) {
+// Threads that share one row and how they sum across it.
+// WarpRows: one warp per row (the reduction is a shuffle tree).
+struct WarpRows {
+  static constexpr int kThreads = 32;
+  __device__ __forceinline__ float sum(float v) const { return warp_sum(v); }
+  __device__ __forceinline__ void sum2(float& a, float& b) const {
+    a = warp_sum(a);
+    b = warp_sum(b);
+  }
+};
+
+// CtaRows<NT>: one CTA of NT threads per row. Warp partials go through
+// `red` (2 * NT / 32 floats of shared memory) and every thread adds them in
+// the same fixed order, so all threads hold the same total. Every thread of
+// the CTA must call each reduction (they contain __syncthreads).
+template <int NT>
+struct CtaRows {
+  static constexpr int kThreads = NT;
+  float* red;
+  __device__ __forceinline__ void sum2(float& a, float& b) const {
+    a = warp_sum(a);
+    b = warp_sum(b);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+      red[2 * w] = a;
+      red[2 * w + 1] = b;
+    }
+    __syncthreads();
+    float x = 0.f, y = 0.f;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) {
+      x += red[2 * i];
+      y += red[2 * i + 1];
+    }
+    __syncthreads();
+    a = x;
+    b = y;
+  }
+  __device__ __forceinline__ float sum(float v) const {
+    float z = 0.f;
+    sum2(v, z);
+    return v;
+  }
+};
+
+// Row held in registers: thread `tid` of a G-thread row group owns vectors
+// v = i * G + tid (zero past nvec).
+template <int NV, int G = 32>
+__device__ __forceinline__ void load_row(const char* p, int nvec, int tid, uint4 (&v)[NV]) {
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
+    const int j = i * G + tid;
     v[i] = j < nvec ? ldg16(p + 16 * (int64_t)j) : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-template <int DT, int METRIC, int NV>
+template <int DT, int METRIC, int NV, class Rows = WarpRows>
 __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 (&pv)[NV], int nvec, int H,
-                                             const GateConsts& k, int lane);
+                                             const GateConsts& k, int tid, const Rows& rows = Rows());
 
 template <int DT, int METRIC, int NV>
 __device__ __forceinline__ GateOut gate_row_vec(const char* c, const char* q, int nvec, int H, const GateConsts& k,
@@ -87,10 +133,11 @@ __device__ __forceinline__ GateOut gate_row_vec(const char* c, const char* q, in
   return gate_regs<DT, METRIC, NV>(cv, pv, nvec, H, k, lane);
 }
 
-template <int DT, int METRIC, int NV>
+template <int DT, int METRIC, int NV, class Rows>
 __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 (&pv)[NV], int nvec, int H,
-                                             const GateConsts& k, int lane) {
+                                             const GateConsts& k, int tid, const Rows& rows) {
   constexpr int E = Elt<DT>::kPerVec;
+  constexpr int G = Rows::kThreads;
   float presum;
   if constexpr (METRIC == AF_METRIC_COSINE) {
     float sc = 0.f, sp = 0.f;
@@ -105,15 +152,14 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
         sp = fmaf(fp[e], fp[e], sp);
       }
     }
-    sc = warp_sum(sc);
-    sp = warp_sum(sp);
+    rows.sum2(sc, sp);
     float nc, np;
     finish_cos<DT, METRIC>(sc, sp, k, nc, np);
     const float rc = __frcp_rn(nc), rp = __frcp_rn(np);
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      if (i * 32 + lane >= nvec) continue;
+      if (i * G + tid >= nvec) continue;
       float fc[E], fp[E];
       unpack<DT>(cv[i], fc);
       unpack<DT>(pv[i], fp);
@@ -124,12 +170,12 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
         s = __fadd_rn(s, rnd<DT>(__fmul_rn(yc, yp)));
       }
     }
-    presum = warp_sum(s);
+    presum = rows.sum(s);
   } else if constexpr (METRIC == AF_METRIC_L2) {
     float sd = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      if (i * 32 + lane >= nvec) continue;
+      if (i * G + tid >= nvec) continue;
       float fc[E], fp[E];
       unpack<DT>(cv[i], fc);
       unpack<DT>(pv[i], fp);
@@ -139,14 +185,14 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
         sd = fmaf(d, d, sd);
       }
     }
-    sd = warp_sum(sd);
+    sd = rows.sum(sd);
     const float l2 = rnd<DT>(__fsqrt_rn(sd));
     presum = __fsub_rn(1.f, rnd<DT>(__fdiv_rn(l2, k.l2_denom)));
   } else {  // pearson
     float mc = 0.f, mp = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      if (i * 32 + lane >= nvec) continue;
+      if (i * G + tid >= nvec) continue;
       float fc[E], fp[E];
       unpack<DT>(cv[i], fc);
       unpack<DT>(pv[i], fp);
@@ -156,12 +202,13 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
         mp = __fadd_rn(mp, fp[e]);
       }
     }
-    mc = rnd<DT>(__fdiv_rn(warp_sum(mc), (float)H));
-    mp = rnd<DT>(__fdiv_rn(warp_sum(mp), (float)H));
+    rows.sum2(mc, mp);
+    mc = rnd<DT>(__fdiv_rn(mc, (float)H));
+    mp = rnd<DT>(__fdiv_rn(mp, (float)H));
     float num = 0.f, scc = 0.f, spp = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      if (i * 32 + lane >= nvec) continue;
+      if (i * G + tid >= nvec) continue;
       float fc[E], fp[E];
       unpack<DT>(cv[i], fc);
       unpack<DT>(pv[i], fp);
@@ -174,9 +221,11 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
         spp = fmaf(pc, pc, spp);
       }
     }
-    const float numr = rnd<DT>(warp_sum(num));
-    const float nc = rnd<DT>(__fsqrt_rn(warp_sum(scc)));
-    const float np = rnd<DT>(__fsqrt_rn(warp_sum(spp)));
+    rows.sum2(num, scc);
+    spp = rows.sum(spp);
+    const float numr = rnd<DT>(num);
+    const float nc = rnd<DT>(__fsqrt_rn(scc));
+    const float np = rnd<DT>(__fsqrt_rn(spp));
     const float den = rnd<DT>(__fadd_rn(rnd<DT>(__fmul_rn(nc, np)), k.eps));
     presum = __fdiv_rn(numr, den);
   }

@@ -42,32 +42,28 @@ def test_dense_attention(T, n_q, heads, kv):
     assert _err(out, ref) <= 2e-2
 
 
-@pytest.mark.parametrize("kv", [4, 2])
-def test_fresh_key_overrides(kv):
-    from actfold_b200.kernels import attention
+def _fresh_case(T, heads, kv, fresh, qsel, seed=0):
+    """Parent K/V plus per-child fresh K/V rows; queries are candidate rows qsel.
 
-    torch.manual_seed(0)
-    T, C, heads = 300, 3, 4
+    Returns the kernel inputs and the fp32 reference output of every query.
+    """
+    g = torch.Generator(device="cuda").manual_seed(seed)
     D = kv * 128
-    pk = torch.randn(T, D, device="cuda").to(torch.bfloat16)
-    pv = torch.randn(T, D, device="cuda").to(torch.bfloat16)
-    # candidates: sorted (child, position); each child has a few fresh positions
-    fresh = {0: [3, 77, 299], 1: [0, 150], 2: [5, 6, 7, 8, 200]}
-    cand = [(c, t) for c in range(C) for t in fresh[c]]
+    pk = torch.randn(T, D, device="cuda", generator=g).to(torch.bfloat16)
+    pv = torch.randn(T, D, device="cuda", generator=g).to(torch.bfloat16)
+    C = max(fresh) + 1
+    cand = [(c, t) for c in range(C) for t in fresh.get(c, [])]
     nc = len(cand)
-    fk = torch.randn(nc, D, device="cuda").to(torch.bfloat16)
-    fv = torch.randn(nc, D, device="cuda").to(torch.bfloat16)
+    fk = torch.randn(nc, D, device="cuda", generator=g).to(torch.bfloat16)
+    fv = torch.randn(nc, D, device="cuda", generator=g).to(torch.bfloat16)
     fchild = torch.tensor([c for c, _ in cand], dtype=torch.int32, device="cuda")
     bits_np = np.zeros((C, (T + 31) // 32), np.uint32)
     for c, t in cand:
         bits_np[c, t // 32] |= np.uint32(1 << (t % 32))
     bits = torch.from_numpy(bits_np.view(np.int32)).cuda()
-    # queries: a subset of candidates (divergent rows) with Q rows in a packed buffer
-    qsel = [0, 2, 3, 5, 6, 9]
-    qall = torch.randn(nc, heads * 128, device="cuda").to(torch.bfloat16)
+    qall = torch.randn(nc, heads * 128, device="cuda", generator=g).to(torch.bfloat16)
     qsrc = torch.tensor(qsel, dtype=torch.int32, device="cuda")
     qchild = torch.tensor([cand[i][0] for i in qsel], dtype=torch.int32, device="cuda")
-    out = attention(qall, pk, pv, heads, kv, qsrc=qsrc, qchild=qchild, fresh_bits=bits, fk=fk, fv=fv, fchild=fchild)
     # reference: per query, parent K/V with the child's fresh rows replaced
     ks, vs = [], []
     for i in qsel:
@@ -81,10 +77,46 @@ def test_fresh_key_overrides(kv):
         ks.append(k)
         vs.append(v)
     ref = _ref(qall[qsrc.long()], torch.stack(ks), torch.stack(vs), heads, kv)
+    args = dict(qsrc=qsrc, qchild=qchild, fresh_bits=bits, fk=fk, fv=fv, fchild=fchild)
+    return qall, pk, pv, args, ref
+
+
+@pytest.mark.parametrize("kv", [4, 2])
+def test_fresh_key_overrides(kv):
+    from actfold_b200.kernels import attention
+
+    heads = 4
+    fresh = {0: [3, 77, 299], 1: [0, 150], 2: [5, 6, 7, 8, 200]}
+    qsel = [0, 2, 3, 5, 6, 9]
+    qall, pk, pv, args, ref = _fresh_case(300, heads, kv, fresh, qsel)
+    out = attention(qall, pk, pv, heads, kv, **args)
     assert _err(out, ref) <= 2e-2
     # dynamic counts: only the first 4 queries are valid
     out2 = torch.zeros_like(out)
     n_q = torch.tensor([4], dtype=torch.int32, device="cuda")
-    attention(qall, pk, pv, heads, kv, out=out2, qsrc=qsrc, qchild=qchild, n_q=n_q, fresh_bits=bits, fk=fk, fv=fv, fchild=fchild)
+    attention(qall, pk, pv, heads, kv, out=out2, n_q=n_q, **args)
     assert _err(out2[:4], ref[:4]) <= 2e-2
     assert (out2[4:] == 0).all()
+
+
+@pytest.mark.parametrize("splits", [1, 2, 4, 8])
+@pytest.mark.parametrize("T", [300, 1024])
+def test_key_splits_over_a_cluster(splits, T, monkeypatch):
+    """Every key-split count gives the unsplit result: 8 splits of a 300-key
+    case leave some CTAs without key blocks, 70 queries leave the second query
+    block partly empty, and a dynamic query count cuts it further."""
+    from actfold_b200.kernels import attention
+
+    monkeypatch.setenv("ACTFOLD_ATTN_SPLITS", str(splits))
+    heads, kv = 4, 2
+    fresh = {0: [1, 64, T - 1], 1: [0, 127, 128], 2: list(range(10, 30)), 3: [T // 2]}
+    nc = sum(len(v) for v in fresh.values())
+    qsel = [i % nc for i in range(70)]
+    qall, pk, pv, args, ref = _fresh_case(T, heads, kv, fresh, qsel, seed=T)
+    out = attention(qall, pk, pv, heads, kv, **args)
+    assert _err(out, ref) <= 2e-2
+    out2 = torch.zeros_like(out)
+    n_q = torch.tensor([67], dtype=torch.int32, device="cuda")
+    attention(qall, pk, pv, heads, kv, out=out2, n_q=n_q, **args)
+    assert _err(out2[:67], ref[:67]) <= 2e-2
+    assert (out2[67:] == 0).all()
