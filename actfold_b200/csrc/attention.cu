@@ -68,6 +68,8 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 
 __global__ void __launch_bounds__(128) k_attention(const AttnParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t sm[];
   const int n_q = p.n_q_dev ? min(*p.n_q_dev, p.n_q_cap) : p.n_q_cap;
   const int q0 = blockIdx.x * kQB;
@@ -383,19 +385,8 @@ int attention_run(const AttnParams& p, cudaStream_t s) {
     attr = true;
   }
   const int ns = attention_splits(p);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.n_q_cap + kQB - 1) / kQB, p.n_heads, ns);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr_c[1];
-  attr_c[0].id = cudaLaunchAttributeClusterDimension;
-  attr_c[0].val.clusterDim.x = 1;
-  attr_c[0].val.clusterDim.y = 1;
-  attr_c[0].val.clusterDim.z = ns;
-  cfg.attrs = attr_c;
-  cfg.numAttrs = ns > 1 ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_attention, p);
+  cudaError_t e = launch_ex(k_attention, dim3((p.n_q_cap + kQB - 1) / kQB, p.n_heads, ns), dim3(128, 1, 1),
+                            (size_t)smem, s, p.pdl != 0, dim3(1, 1, ns), p);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("attention: launch: ") + cudaGetErrorString(e));
   return check_launch("attention");
 }
@@ -414,6 +405,7 @@ extern "C" int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsr
   AF_REQUIRE(head_dim == kHD, "af_attention_bf16: head_dim must be 128");
   AF_REQUIRE(T <= (1 << 24) && n_q_cap <= (1 << 24) && n_f_cap <= (1 << 24), "af_attention_bf16: size too large");
   AttnParams p;
+  memset(&p, 0, sizeof(p));
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_ld = q_ld;
   p.qsrc = qsrc;

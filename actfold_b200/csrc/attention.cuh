@@ -28,6 +28,7 @@ struct AttnParams {
   int64_t out_ld;
   int n_heads, n_kv_heads;
   float scale_log2;  // softmax scale * log2(e)
+  int pdl;           // 1: programmatic dependent launch (the kernel waits for its predecessor)
 };
 
 int attention_run(const AttnParams& p, cudaStream_t s);

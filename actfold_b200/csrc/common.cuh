@@ -8,6 +8,7 @@
 #include <string.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/actfold_b200.h"
 
@@ -128,6 +129,48 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Launch `kernel` on `stream` as clusters of `cluster` CTAs (none when the
+// cluster has one CTA) and, when `pdl`, with programmatic dependent launch.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             bool pdl, dim3 cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = cluster.x;
+    at[n].val.clusterDim.y = cluster.y;
+    at[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  if (pdl) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while its stream predecessor is
+// still running. pdl_wait() blocks the calling thread until the predecessor
+// grid has completed and its memory operations are visible (it returns at once
+// for a normal launch); pdl_trigger() lets this grid's own dependents begin
+// launching. Kernels of the folded and dense passes call pdl_trigger() first
+// and pdl_wait() before their first access to memory that another kernel of
+// the stream writes or reads; only read-only weights may be touched before it.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Thread-block cluster helpers: a full cluster barrier (release/acquire, so
 // shared-memory writes before it are visible to peers after it), the address

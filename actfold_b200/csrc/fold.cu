@@ -83,6 +83,8 @@ struct CandArgs {
 };
 
 __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int wbuf[32];
   const int N = a.C * a.T;
   int base = 0, total;
@@ -143,6 +145,8 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
 __global__ void __launch_bounds__(256) k_embed_rows(const __nv_bfloat16* embed, int H, int64_t vocab,
                                                     const int64_t* tokens, const int* rows, const int* n_dev,
                                                     int n_cap, __nv_bfloat16* out, unsigned* status) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
@@ -204,6 +208,8 @@ template <int NV>
 __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat16* in, const __nv_bfloat16* w, int H,
                                                               float eps, const int* n_dev, int n_cap,
                                                               __nv_bfloat16* out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
   const int i = blockIdx.x;
   const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
@@ -234,6 +240,8 @@ struct FoldGateArgs {
 
 template <int METRIC, int NV>
 __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
   const int tid = threadIdx.x;
   const int r = blockIdx.x;
@@ -284,6 +292,8 @@ struct CompactArgs {
 };
 
 __global__ void __launch_bounds__(1024) k_fold_compact(const CompactArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int wbuf[32];
   const int nb = a.C * a.bits_ld;
   for (int i = threadIdx.x; i < nb; i += 1024) {
@@ -334,6 +344,8 @@ __global__ void __launch_bounds__(1024) k_fold_compact(const CompactArgs a) {
 __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logits, int64_t V, int C, int T,
                                                      const unsigned* final_bits, int bits_ld,
                                                      __nv_bfloat16* logits) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int kids[];  // children that take the parent row
   __shared__ int nk;
   const int t = blockIdx.x;
@@ -358,6 +370,8 @@ __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logi
 // score[c] = mean over [T, V] of child c's logits (fp32 sums of the bf16 values).
 __global__ void __launch_bounds__(256) k_scores(const float* p_row_sums, const float* fresh_row_sums, int C, int T,
                                                 int64_t V, const unsigned* final_bits, int bits_ld, float* scores) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x;
   float s = 0.f;
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
@@ -378,6 +392,8 @@ __global__ void __launch_bounds__(256) k_scores(const float* p_row_sums, const f
 // Dense layer state of every child: parent rows, then fresh rows scattered over them.
 __global__ void __launch_bounds__(256) k_state_parent(const __nv_bfloat16* p_in, int H, int C, int T,
                                                       __nv_bfloat16* out) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= (int64_t)C * T) return;
@@ -389,6 +405,8 @@ __global__ void __launch_bounds__(256) k_state_parent(const __nv_bfloat16* p_in,
 
 __global__ void __launch_bounds__(256) k_state_scatter(const __nv_bfloat16* x, int H, const int* pos, const int* n_dev,
                                                        int n_cap, __nv_bfloat16* out) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int n = min(*n_dev, n_cap);
@@ -399,11 +417,15 @@ __global__ void __launch_bounds__(256) k_state_scatter(const __nv_bfloat16* x, i
 }
 
 __global__ void k_iota(int* p, int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = i;
 }
 
 __global__ void k_zero_f32(float* p, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = 0.f;
 }
@@ -414,6 +436,8 @@ __global__ void k_zero_f32(float* p, int64_t n) {
 template <int NV>
 __global__ void __launch_bounds__(kRowThreads) k_self_gate(const __nv_bfloat16* x, int H, int T, GateConsts k,
                                                            uint8_t* self_stable) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
   const int t = blockIdx.x;
   if (t >= T) return;
@@ -440,11 +464,26 @@ struct Bump {
   }
 };
 
+// Kernels of the dense and folded passes are launched with programmatic
+// dependent launch (each waits for its predecessor inside the kernel, see
+// pdl_wait), so a kernel's launch and prologue overlap the previous kernel's
+// tail. ACTFOLD_PDL=0 turns it off.
+static bool pass_pdl() {
+  static const bool on = [] {
+    const char* e = getenv("ACTFOLD_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+#define AF_LAUNCH(KERNEL, GRID, BLOCK, SMEM, STREAM, ...) \
+  launch_ex(KERNEL, dim3(GRID), dim3(BLOCK), (size_t)(SMEM), STREAM, pass_pdl(), dim3(1, 1, 1), __VA_ARGS__)
+
 // Per-row kernels on one CTA of kRowThreads threads per row: H <= 4096.
-#define AF_DISPATCH_ROWS(H, KERNEL, ROWS, STREAM, ...)                                              \
-  do {                                                                                              \
-    if ((H) / 8 <= kRowThreads) KERNEL<1><<<(unsigned)(ROWS), kRowThreads, 0, STREAM>>>(__VA_ARGS__); \
-    else KERNEL<2><<<(unsigned)(ROWS), kRowThreads, 0, STREAM>>>(__VA_ARGS__);                      \
+#define AF_DISPATCH_ROWS(H, KERNEL, ROWS, STREAM, ...)                                   \
+  do {                                                                                   \
+    if ((H) / 8 <= kRowThreads) AF_LAUNCH(KERNEL<1>, (unsigned)(ROWS), kRowThreads, 0, STREAM, __VA_ARGS__); \
+    else AF_LAUNCH(KERNEL<2>, (unsigned)(ROWS), kRowThreads, 0, STREAM, __VA_ARGS__);    \
   } while (0)
 
 static int validate_model(const af_model* m) {
@@ -498,6 +537,7 @@ static GemmCall base_call(unsigned* status) {
   c.status = status;
   c.w_tiled = 1;
   c.head_dim = 128;
+  c.pdl = pass_pdl() ? 1 : 0;
   return c;
 }
 
@@ -534,8 +574,8 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
   const unsigned rows_blocks = (unsigned)((Ti + 7) / 8);
   const GateConsts gk = make_gate_consts(AF_DTYPE_BF16, tau, 1e-8f, 0.f);
 
-  k_iota<<<(Ti + 255) / 256, 256, 0, s>>>(w.pos, Ti);
-  k_embed_rows<<<rows_blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(m->embed), z.H, z.V, tokens, nullptr,
+  AF_LAUNCH(k_iota, (Ti + 255) / 256, 256, 0, s, w.pos, Ti);
+  AF_LAUNCH(k_embed_rows, rows_blocks, 256, 0, s, static_cast<const __nv_bfloat16*>(m->embed), z.H, z.V, tokens, nullptr,
                                            nullptr, Ti, xin, stw);
   for (int l = 0; l < z.L; ++l) {
     const af_layer_weights& lw = m->layers[l];
@@ -574,6 +614,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     ap.n_heads = m->dims.n_heads;
     ap.n_kv_heads = m->dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf((float)m->dims.head_dim)) * 1.4426950408889634f;
+    ap.pdl = pass_pdl() ? 1 : 0;
     if ((st = attention_run(ap, s))) return st;
     c = base_call(stw);
     c.x = w.att;
@@ -618,7 +659,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
   const __nv_bfloat16* xl = xin + (int64_t)z.L * Ti * z.H;
   AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, xl, static_cast<const __nv_bfloat16*>(m->final_norm), z.H, eps,
                    nullptr, Ti, w.A);
-  k_zero_f32<<<(Ti + 255) / 256, 256, 0, s>>>(logit_row_sums, Ti);
+  AF_LAUNCH(k_zero_f32, (Ti + 255) / 256, 256, 0, s, logit_row_sums, (int64_t)Ti);
   GemmCall c = base_call(stw);
   c.x = w.A;
   c.ldx = z.H;
@@ -790,8 +831,8 @@ static int build_maps(FoldPlan* p) {
 
 template <int METRIC>
 static void launch_fold_gate(const FoldGateArgs& g, int H, int rows, cudaStream_t s) {
-  if (H / 8 <= kRowThreads) k_fold_gate<METRIC, 1><<<(unsigned)rows, kRowThreads, 0, s>>>(g);
-  else k_fold_gate<METRIC, 2><<<(unsigned)rows, kRowThreads, 0, s>>>(g);
+  if (H / 8 <= kRowThreads) AF_LAUNCH((k_fold_gate<METRIC, 1>), (unsigned)rows, kRowThreads, 0, s, g);
+  else AF_LAUNCH((k_fold_gate<METRIC, 2>), (unsigned)rows, kRowThreads, 0, s, g);
 }
 
 static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, float* scores, cudaStream_t s) {
@@ -824,8 +865,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   ca.fresh0_pos = w.fresh0_pos;
   ca.n_fresh0 = w.n_fresh0;
   ca.status = w.status;
-  AF_TIMED(FK_SETUP, k_fold_candidates<<<1, 1024, 0, s>>>(ca));
-  AF_TIMED(FK_SETUP, k_embed_rows<<<mblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V,
+  AF_TIMED(FK_SETUP, AF_LAUNCH(k_fold_candidates, 1, 1024, 0, s, ca));
+  AF_TIMED(FK_SETUP, AF_LAUNCH(k_embed_rows, mblocks, 256, 0, s, static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V,
                                                            ctok, w.fresh0_pos, w.n_fresh0, M, w.x_all, w.status));
 
   for (int l = 0; l < L; ++l) {
@@ -887,7 +928,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     a.next_pos = w.cand_pos + (int64_t)(l + 1) * M;
     a.next_src = w.cand_src + (int64_t)(l + 1) * M;
     a.next_n_cand = w.n_cand + l + 1;
-    AF_TIMED(FK_COMPACT, k_fold_compact<<<1, 1024, 0, s>>>(a));
+    AF_TIMED(FK_COMPACT, AF_LAUNCH(k_fold_compact, 1, 1024, 0, s, a));
 
     GemmCall c = base_call(w.status);
     c.x = w.A;
@@ -933,6 +974,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.n_heads = p->model.dims.n_heads;
     ap.n_kv_heads = p->model.dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf(128.f)) * 1.4426950408889634f;
+    ap.pdl = pass_pdl() ? 1 : 0;
     AF_TIMED(FK_ATTN, if ((st = attention_run(ap, s))) return st);
 
     c = base_call(w.status);
@@ -1003,7 +1045,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
       cn.cand_src = w.cand_src + (int64_t)(l + 1) * M;
       cn.n_cand = w.n_cand + l + 1;
       cn.status = w.status;
-      AF_TIMED(FK_SETUP, k_fold_candidates<<<1, 1024, 0, s>>>(cn));
+      AF_TIMED(FK_SETUP, AF_LAUNCH(k_fold_candidates, 1, 1024, 0, s, cn));
     }
   }
 
@@ -1030,11 +1072,12 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   c.tmap_x = &p->tx_A;
   AF_TIMED(FK_LM, if ((st = gemm_run(c, s))) return st);
   const int smem = C * (int)sizeof(int);
-  AF_TIMED(FK_FILL, k_logits_fill<<<T, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(p->parent.logits), z.V, C, T,
-                                                       w.final_bits, w.bits_ld, logits));
+  AF_TIMED(FK_FILL, AF_LAUNCH(k_logits_fill, T, 256, smem, s, static_cast<const __nv_bfloat16*>(p->parent.logits),
+                               (int64_t)z.V, C, T, (const unsigned*)w.final_bits, w.bits_ld, logits));
   if (scores)
-    AF_TIMED(FK_SCORES, k_scores<<<C, 256, 0, s>>>(p->parent.logit_row_sums, w.row_sums, C, T, z.V, w.final_bits,
-                                                    w.bits_ld, scores));
+    AF_TIMED(FK_SCORES, AF_LAUNCH(k_scores, C, 256, 0, s, (const float*)p->parent.logit_row_sums,
+                                  (const float*)w.row_sums, C, T, (int64_t)z.V, (const unsigned*)w.final_bits,
+                                  w.bits_ld, scores));
   p->last_launches = p->tk.launches;
   return check_launch("af_fold_run");
 }

@@ -59,43 +59,104 @@ struct GemmDev {
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// One output element (or SwiGLU pair) of tile row r (feature n0 + r) for token m.
-// `a` is this row's fp32 sum, `partner` the sum of row r ^ 64 (RoPE / SwiGLU).
-__device__ __forceinline__ void epi_store(const GemmDev& p, int n0, int r, int gm, float a, float partner) {
+// Staged accumulator: tile[m * kLdt + r] (fp32, token-major) for tile row r
+// (feature n0 + r) and token m; the 4-float pad keeps rows 16-byte aligned.
+constexpr int kLdt = kTileN + 4;
+
+__device__ __forceinline__ void load8(const float* s, float* v) {
+  const float4 x = *reinterpret_cast<const float4*>(s), y = *reinterpret_cast<const float4*>(s + 4);
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* y) {
+  uint4 o;
+  o.x = pack_bf16x2(y[0], y[1]);
+  o.y = pack_bf16x2(y[2], y[3]);
+  o.z = pack_bf16x2(y[4], y[5]);
+  o.w = pack_bf16x2(y[6], y[7]);
+  return o;
+}
+
+// Epilogue of 8 consecutive tile rows r0..r0+7 (r0 % 8 == 0) for token gm: `a`
+// holds their fp32 sums, `b` those of rows r0 ^ 64 (the RoPE rotation partner
+// and the SwiGLU up rows). Writes one 16-byte vector; returns the sum of the
+// bf16 outputs (EPI_STORE) for the logit row sums.
+__device__ __forceinline__ float epi_chunk(const GemmDev& p, int n0, int r0, int gm, const float* a, const float* b) {
   const int64_t orow = p.out_rows ? p.out_rows[gm] : gm;
-  const int n = n0 + r;
+  float y[8];
+  float rs = 0.f;
   if (p.epi == EPI_STORE) {
-    p.out[orow * p.ldo + n] = __float2bfloat16_rn(a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      y[i] = bf(a[i]);
+      rs += y[i];
+    }
+    stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
   } else if (p.epi == EPI_RESIDUAL) {
     const int64_t rrow = p.res_rows ? p.res_rows[gm] : gm;
-    const float rv = __bfloat162float(p.res[rrow * p.ldr + n]);
-    p.out[orow * p.ldo + n] = __float2bfloat16_rn(__fadd_rn(rv, bf(a)));
+    float rv[8];
+    unpack<AF_DTYPE_BF16>(ldg16(p.res + rrow * p.ldr + n0 + r0), rv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(rv[i], bf(a[i]));
+    stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
   } else if (p.epi == EPI_SWIGLU) {
-    if (r < 64) {
-      const float g = bf(a), u = bf(partner);
-      const float silu = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
-      p.out[orow * p.ldo + (n0 >> 1) + r] = __float2bfloat16_rn(__fmul_rn(silu, u));
+    if (r0 < 64) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float g = bf(a[i]), u = bf(b[i]);
+        const float silu = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+        y[i] = __fmul_rn(silu, u);
+      }
+      stg16(p.out + orow * p.ldo + (n0 >> 1) + r0, pack8(y));
     }
   } else {  // EPI_ROPE
-    const float x = bf(a);
-    float y = x;
+    const int n = n0 + r0;
     if (n < p.rope_cols) {
-      const int i = r & (p.half_dim - 1);
-      const float other = bf(partner);
       const int pos = p.positions[gm];
-      const float cs = p.rope_cos[(int64_t)pos * p.half_dim + i];
-      const float sn = p.rope_sin[(int64_t)pos * p.half_dim + i];
-      y = (r & p.half_dim) ? __fadd_rn(__fmul_rn(x, cs), __fmul_rn(other, sn))
-                           : __fsub_rn(__fmul_rn(x, cs), __fmul_rn(other, sn));
+      const int i0 = r0 & (p.half_dim - 1);
+      float cs[8], sn[8];
+      load8(p.rope_cos + (int64_t)pos * p.half_dim + i0, cs);
+      load8(p.rope_sin + (int64_t)pos * p.half_dim + i0, sn);
+      const bool second = (r0 & p.half_dim) != 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = bf(a[i]), other = bf(b[i]);
+        y[i] = second ? __fadd_rn(__fmul_rn(x, cs[i]), __fmul_rn(other, sn[i]))
+                      : __fsub_rn(__fmul_rn(x, cs[i]), __fmul_rn(other, sn[i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = bf(a[i]);
     }
-    p.out[orow * p.ldo + n] = __float2bfloat16_rn(y);
+    stg16(p.out + orow * p.ldo + n, pack8(y));
   }
+  return rs;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmW,
                                                           const __grid_constant__ CUtensorMap tmX, const GemmDev p) {
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    // Weights never depend on the preceding kernel: pull this CTA's first
+    // k-blocks into L2 while that kernel may still be finishing.
+    const int kb_first = blockIdx.y * p.kb_per_split;
+    const int nkb_cta = min(p.kb_per_split, p.nkb - kb_first);
+    const int rot = nkb_cta > 0 ? (int)(blockIdx.x % nkb_cta) : 0;
+    const int npf = min(nkb_cta, 2 * p.stages);
+    for (int i = 0; i < npf; ++i) {
+      int kb = i + rot;
+      if (kb >= nkb_cta) kb -= nkb_cta;
+      kb += kb_first;
+      if (p.w_tiled)
+        tma_prefetch_l2_3d(&tmW, 0, 0, blockIdx.x * p.nkb + kb);
+      else
+        tma_prefetch_l2_2d(&tmW, kb * kBlockK, blockIdx.x * kTileN);
+    }
+  }
+  pdl_wait();
   int M = p.m_dev ? *p.m_dev : p.m_cap;
   if (M > p.m_cap) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
@@ -142,8 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int ld = p.ntok + 4;  // staging row stride (floats): 16-byte aligned, conflict-free float4 stores
-  float* tile = reinterpret_cast<float*>(gbase);  // the ring is idle once the accumulator is final
+  float* tile = reinterpret_cast<float*>(gbase);  // staging (the ring is idle once the accumulator is final)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
@@ -201,30 +261,47 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
     tc_fence_after();
     if (!*abort_flag) {
+      // Thread r holds tile row r (TMEM lane) across the token columns; the
+      // token-major staging makes a warp's 32 stores one contiguous line.
       const int nchunk = (Mv + 15) / 16;
       for (int c = 0; c < nchunk; ++c) {
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(16 * c), v);
-        float4* dst = reinterpret_cast<float4*>(tile + r * ld + 16 * c);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int j = 0; j < 16; ++j) tile[(16 * c + j) * kLdt + r] = v[j];
       }
     }
   }
   __syncthreads();
   const bool ok = !*abort_flag;
 
+  const bool partner = p.epi == EPI_SWIGLU || p.epi == EPI_ROPE;
   if (p.splits == 1) {
-    // ---------------- epilogue over all 128 rows: thread r (< 128) owns feature n0 + r ----------------
-    if (ok && threadIdx.x < kTileN) {
-      const int r = threadIdx.x;
-      for (int m = 0; m < Mv; ++m) {
-        const float a = tile[r * ld + m];
-        const float partner = (p.epi == EPI_SWIGLU || p.epi == EPI_ROPE) ? tile[(r ^ 64) * ld + m] : 0.f;
-        epi_store(p, n0, r, m0 + m, a, partner);
-        if (p.row_sums && p.epi == EPI_STORE) {
-          const float part = warp_sum(bf(a));
-          if (lane == 0) atomicAdd(p.row_sums + (p.out_rows ? p.out_rows[m0 + m] : m0 + m), part);
+    // ---------------- epilogue: 16 chunks of 8 rows per token, all threads ----------------
+    // Warp-uniform loop: a warp's lanes 0-15 and 16-31 cover the 16 chunks of
+    // two tokens, so the logit row sums reduce over half-warps.
+    if (ok) {
+      const int total = Mv * (kTileN / 8);
+      for (int base_ch = warp * 32; base_ch < total; base_ch += kThreads) {
+        const int ch = base_ch + lane;
+        const bool valid = ch < total;
+        float rs = 0.f;
+        if (valid) {
+          const int m = ch >> 4, r0 = 8 * (ch & 15);
+          float a[8], b[8];
+          load8(tile + m * kLdt + r0, a);
+          if (partner) load8(tile + m * kLdt + (r0 ^ 64), b);
+          rs = epi_chunk(p, n0, r0, m0 + m, a, b);
+        }
+        if (p.row_sums) {
+          rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+          rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+          if (valid && (lane & 15) == 0) {
+            const int gm = m0 + (ch >> 4);
+            atomicAdd(p.row_sums + (p.out_rows ? p.out_rows[gm] : gm), rs);
+          }
         }
       }
     }
@@ -232,31 +309,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     // ---------------- cluster split-K reduction through distributed shared memory ----------------
     __syncwarp();
     cluster_sync_all();  // every partial tile of the cluster is in shared memory
-    // CTA j owns the row pairs (lo + i, 64 + lo + i), i < k: consecutive threads take
-    // consecutive pairs (adjacent output features) of the same 4-token column group.
+    // Units of work: (token m, chunk pair c / c + 8), i.e. rows 8c..8c+7 and
+    // their partners 64+8c..64+8c+7; CTA j of the cluster takes a contiguous
+    // share of the Mv * 8 units and sums them over all CTAs in a fixed order.
     const int j = blockIdx.y, Sp = p.splits;
-    const int lo = (j * 64) / Sp, hi = ((j + 1) * 64) / Sp, k = hi - lo;
-    const int nc4 = (Mv + 3) / 4;
+    const int units = Mv * 8;
+    const int lo = (j * units) / Sp, hi = ((j + 1) * units) / Sp;
     if (ok) {
-      for (int f = threadIdx.x; f < k * nc4; f += kThreads) {
-        const int c4 = f / k, i = f - c4 * k;
-        const int ra = lo + i, rb = 64 + lo + i;
-        const uint32_t oa = base + (uint32_t)((ra * ld + 4 * c4) * 4);
-        const uint32_t ob = base + (uint32_t)((rb * ld + 4 * c4) * 4);
-        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int u = lo + threadIdx.x; u < hi; u += kThreads) {
+        const int m = u >> 3, c = u & 7;
+        const uint32_t oa = base + (uint32_t)((m * kLdt + 8 * c) * 4);
+        const uint32_t ob = oa + 64 * 4;
+        float sa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, sb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int src = 0; src < Sp; ++src) {
-          const float4 va = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
-          const float4 vb = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
-          sa[0] += va.x; sa[1] += va.y; sa[2] += va.z; sa[3] += va.w;
-          sb[0] += vb.x; sb[1] += vb.y; sb[2] += vb.z; sb[3] += vb.w;
+          const float4 a0 = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
+          const float4 a1 = ld_cluster_f4(cluster_map(oa + 16, (uint32_t)src));
+          const float4 b0 = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
+          const float4 b1 = ld_cluster_f4(cluster_map(ob + 16, (uint32_t)src));
+          sa[0] += a0.x; sa[1] += a0.y; sa[2] += a0.z; sa[3] += a0.w;
+          sa[4] += a1.x; sa[5] += a1.y; sa[6] += a1.z; sa[7] += a1.w;
+          sb[0] += b0.x; sb[1] += b0.y; sb[2] += b0.z; sb[3] += b0.w;
+          sb[4] += b1.x; sb[5] += b1.y; sb[6] += b1.z; sb[7] += b1.w;
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int m = 4 * c4 + e;
-          if (m >= Mv) break;
-          epi_store(p, n0, ra, m0 + m, sa[e], sb[e]);
-          epi_store(p, n0, rb, m0 + m, sb[e], sa[e]);
-        }
+        epi_chunk(p, n0, 8 * c, m0 + m, sa, sb);
+        epi_chunk(p, n0, 8 * c + 64, m0 + m, sb, sa);
       }
     }
     __syncwarp();
@@ -352,19 +428,21 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   }();
   if (env_stages > 0) st = env_stages;
   st = std::max(2, std::min(12, st));
-  const int per_sm = (2 * (st * stage + 1024 + 256) <= 227 * 1024) ? 2 : 1;
   int splits = want_splits;
   if (splits <= 0) {
+    // About 4/3 CTAs per SM, at most 4 splits: measured on B200 for the
+    // LLaDA/Dream projections, more and shorter split CTAs lose more to their
+    // ramp-up and cluster reduction than they gain in parallel streams.
     const int tiles = g.n_tiles * g.m_tiles;
-    splits = (per_sm * sm_count()) / tiles;
+    splits = (4 * sm_count()) / (3 * tiles);
     splits = std::min(splits, std::max(1, g.nkb / 4));
-    splits = std::max(1, std::min(splits, kMaxSplits));
+    splits = std::max(1, std::min(splits, 4));
   }
   if (row_sums) splits = 1;
   splits = std::min(splits, kMaxSplits);
   g.kb_per = (g.nkb + splits - 1) / splits;
   g.splits = (g.nkb + g.kb_per - 1) / g.kb_per;
-  const int tile_bytes = kTileN * (g.ntok + 4) * 4;  // fp32 staging of the accumulator
+  const int tile_bytes = g.ntok * kLdt * 4;  // fp32 staging of the accumulator
   while (st * stage < tile_bytes) ++st;
   g.stages = st;
   g.smem = st * stage + 1024 + 16 * st + 64;
@@ -377,6 +455,10 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.k > 0 && c.k % kBlockK == 0, "gemm: k must be a positive multiple of 64");
   AF_REQUIRE(c.m_cap > 0, "gemm: m_cap must be positive");
   AF_REQUIRE(c.epi >= EPI_STORE && c.epi <= EPI_ROPE, "gemm: bad epilogue");
+  AF_REQUIRE(c.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(c.out) & 15u) == 0,
+             "gemm: out must be 16-byte aligned with a row stride that is a multiple of 8");
+  AF_REQUIRE(!c.res || (c.ldr % 8 == 0 && (reinterpret_cast<uintptr_t>(c.res) & 15u) == 0),
+             "gemm: residual must be 16-byte aligned with a row stride that is a multiple of 8");
   AF_REQUIRE(c.epi != EPI_RESIDUAL || c.res, "gemm: residual epilogue needs res");
   AF_REQUIRE(c.epi != EPI_ROPE || (c.rope_cos && c.rope_sin && c.positions && c.head_dim == 128 && c.rope_cols % 128 == 0),
              "gemm: rope epilogue needs cos/sin/positions and head_dim 128");
@@ -427,20 +509,8 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(g.n_tiles, g.splits, g.m_tiles);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = g.smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = g.splits;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = g.splits > 1 ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc, *pw, *px, d);
+  cudaError_t e = launch_ex(k_gemm_tc, dim3(g.n_tiles, g.splits, g.m_tiles), dim3(kThreads, 1, 1), (size_t)g.smem, stream,
+                            c.pdl != 0, dim3(1, g.splits, 1), *pw, *px, d);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_tc launch: ") + cudaGetErrorString(e));
   return check_launch("gemm_tc");
 }

@@ -38,6 +38,7 @@ struct GemmCall {
   const CUtensorMap* tmap_w;
   const CUtensorMap* tmap_x;
   int w_tiled;         // 1: w is stored tiled [n/128][k/64][128][64] (contiguous 16 KB tiles)
+  int pdl;             // 1: programmatic dependent launch (the kernel waits for its predecessor)
 };
 
 // Token-tile width the kernel uses for a given row capacity.
