@@ -210,7 +210,8 @@ def main() -> None:
     import torch.distributed as dist
 
     from actfold_b200 import workloads as W
-    from actfold_b200.llada import KERNEL_CLASSES, LLaDAModel, ParentCache
+    from actfold_b200.llada import KERNEL_CLASSES, LLaDAModel
+    from actfold_b200.sharding import broadcast_parent_cache, empty_parent_cache
     from actfold_b200.speculative import ActFoldVerificationEngine, Branch
     from actfold_b200.core import SimilarityGate
 
@@ -233,16 +234,7 @@ def main() -> None:
     if rank == 0:
         pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)
     else:
-        L, T, H = dims.n_layers, a.seq, dims.hidden
-        pc = ParentCache(
-            torch.empty(T, dtype=torch.int64, device=dev),
-            torch.empty((L + 1, T, H), dtype=torch.bfloat16, device=dev),
-            torch.empty((L, T, dims.q_dim + 2 * dims.kv_dim), dtype=torch.bfloat16, device=dev),
-            torch.empty((T, dims.vocab), dtype=torch.bfloat16, device=dev),
-            torch.empty((L, T), dtype=torch.uint8, device=dev),
-            torch.empty((T,), dtype=torch.float32, device=dev),
-            a.tau,
-        )
+        pc = empty_parent_cache(dims, a.seq, a.tau, dev)
     torch.cuda.synchronize()
     parent_ms = (time.perf_counter() - t0) * 1e3
     bcast_ms = 0.0
@@ -251,8 +243,7 @@ def main() -> None:
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for t in pc.tensors():
-            dist.broadcast(t, src=0)
+        broadcast_parent_cache(pc, src=0)
         e1.record()
         torch.cuda.synchronize()
         bcast_ms = e0.elapsed_time(e1)
