@@ -220,6 +220,8 @@ def main() -> None:
     if world > 1:
         from datetime import timedelta
 
+        # stdout carries only the JSON line: NCCL's own log lines go to stderr.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     base = W.LLADA_8B
@@ -242,8 +244,11 @@ def main() -> None:
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        broadcast_parent_cache(pc, src=0)  # first transfer also sets up the NCCL channels
+        dist.barrier()
+        torch.cuda.synchronize()
         e0.record()
-        broadcast_parent_cache(pc, src=0)
+        broadcast_parent_cache(pc, src=0)  # steady-state cost of moving the cache over NVLink
         e1.record()
         torch.cuda.synchronize()
         bcast_ms = e0.elapsed_time(e1)
@@ -401,6 +406,7 @@ def main() -> None:
             "kernel_share": {k: round(v / tot_k, 4) for k, v in kernel_ms.items()},
             "parent_pass_ms": parent_ms,
             "parent_broadcast_ms": bcast_ms,
+            "parent_broadcast_bytes": sum(t.numel() * t.element_size() for t in pc.tensors()),
             "stable_ratio_mean": float(np.mean(res["stable_ratio"])),
         }
         print(json.dumps(line), flush=True)
