@@ -39,7 +39,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "af_attention_bf16": (
         _i32,
-        [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _f32, _vp],
+        [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _f32,
+         _vp, _vp],
     ),
 }
 

@@ -377,6 +377,13 @@ int attention_run(const AttnParams& p, cudaStream_t s) {
   AF_REQUIRE(!p.fk || (p.fv && p.n_f_cap >= 0), "attention: fresh keys need values");
   AF_REQUIRE(((p.q_ld | p.kv_ld | p.out_ld | p.f_ld) & 7) == 0, "attention: row strides must be multiples of 8");
   if (p.n_q_cap == 0) return AF_OK;
+  // The tcgen05 kernel covers up to 24 key blocks of 128 (an 8-CTA cluster of
+  // 3 blocks each); ACTFOLD_ATTN_IMPL=mma selects this mma.sync kernel instead.
+  const char* impl = std::getenv("ACTFOLD_ATTN_IMPL");
+  if (!(impl && impl[0] == 'm')) {
+    const int ns_tc = attention_tc_splits(p);
+    if (ns_tc > 0) return attention_tc_run(p, ns_tc, s);
+  }
   const int smem = kSmem;
   static bool attr = false;
   if (!attr) {
@@ -401,7 +408,7 @@ extern "C" int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsr
                                  int64_t kv_ld, int64_t T, const uint32_t* fresh_bits, int64_t bits_ld,
                                  const void* fk, const void* fv, int64_t f_ld, const int32_t* fchild,
                                  const int32_t* n_f_dev, int64_t n_f_cap, void* out, int64_t out_ld, int n_heads,
-                                 int n_kv_heads, int head_dim, float scale, void* stream) {
+                                 int n_kv_heads, int head_dim, float scale, uint32_t* status, void* stream) {
   AF_REQUIRE(head_dim == kHD, "af_attention_bf16: head_dim must be 128");
   AF_REQUIRE(T <= (1 << 24) && n_q_cap <= (1 << 24) && n_f_cap <= (1 << 24), "af_attention_bf16: size too large");
   AttnParams p;
@@ -429,5 +436,6 @@ extern "C" int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsr
   p.n_heads = n_heads;
   p.n_kv_heads = n_kv_heads;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = reinterpret_cast<unsigned*>(status);
   return attention_run(p, as_stream(stream));
 }

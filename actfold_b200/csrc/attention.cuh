@@ -29,8 +29,12 @@ struct AttnParams {
   int n_heads, n_kv_heads;
   float scale_log2;  // softmax scale * log2(e)
   int pdl;           // 1: programmatic dependent launch (the kernel waits for its predecessor)
+  unsigned* status;  // nullable: AF_STATUS_TIMEOUT is ORed in when a bounded wait runs out
 };
 
 int attention_run(const AttnParams& p, cudaStream_t s);
+// tcgen05 kernel (attention_tc.cu): key splits for `p` (0: shape not supported) and launch.
+int attention_tc_splits(const AttnParams& p);
+int attention_tc_run(const AttnParams& p, int splits, cudaStream_t s);
 
 }  // namespace af

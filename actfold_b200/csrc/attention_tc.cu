@@ -1,0 +1,354 @@
+// tcgen05 attention of packed query rows over the parent's K/V with per-child
+// fresh-key overrides (sm_100a). Same semantics as k_attention (attention.cu):
+// query row i (child qchild[i]) attends to every parent position t except the
+// fresh positions of its child, and to its child's candidate keys.
+//
+// CTA = 4 warps = 128 query rows of one head (MMA M = 128; thread r owns query
+// row r, i.e. TMEM lane r) and at most three 128-key blocks (a key split of a
+// thread-block cluster along grid z). All S tiles fit in TMEM at once
+// (3 x 128 columns, plus 128 for O = the whole 512-column TMEM), so the
+// softmax is exact in two sweeps per row (max, then exp / sum) and O is never
+// rescaled:
+//   1. cp.async Q, K_j, V_j into 128-byte-swizzled shared tiles;
+//   2. S_j = Q K_j^T (tcgen05.mma, bf16 -> fp32 TMEM, K-major operands);
+//   3. each thread masks its row, finds the max over its blocks, writes
+//      P_j = exp2(S_j - max) in bf16 over K_j's tiles and sums the row;
+//   4. O = sum_j P_j V_j (A = P K-major, B = V MN-major: V rows stay [key][dim]);
+//   5. one split: O / l is written; several: the (max, sum, O) partials are
+//      combined across the cluster through distributed shared memory.
+// Every mbarrier wait is bounded; a timeout sets AF_STATUS_TIMEOUT.
+#include <cstdlib>
+
+#include "attention.cuh"
+#include "tc_common.cuh"
+
+namespace af {
+
+namespace {
+
+constexpr int kTQ = 128;            // query rows per CTA (MMA M)
+constexpr int kThreads = 512;       // 16 warps: 4 per TMEM lane quadrant, one 32-column group each
+constexpr int kTK = 128;            // keys per block
+constexpr int kMaxBlk = 3;          // key blocks per CTA
+constexpr int kTileB = 128 * 64 * 2;  // [128 rows][64 cols] bf16 tile = 16 KB
+constexpr int kOpB = 2 * kTileB;      // a 128 x 128 operand: columns 0-63, then 64-127
+constexpr int kOffQ = 0;
+constexpr int kOffKP = kOffQ + kOpB;              // K_j, overwritten by P_j
+constexpr int kOffV = kOffKP + kMaxBlk * kOpB;
+constexpr int kOffF = kOffV + kMaxBlk * kOpB;      // child of each candidate key [3][128]
+constexpr int kOffBar = kOffF + kMaxBlk * kTK * 4;  // barS, barO, fail flag
+constexpr int kSmemTc = kOffBar + 64 + 1024;        // + alignment slack
+
+// Byte offset of 16-byte chunk `ch` (0..7) of row `row` in a swizzled tile.
+__device__ __forceinline__ uint32_t sw_off(int row, int ch) { return (uint32_t)(row * 128 + ((ch ^ (row & 7)) << 4)); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// 128 rows x 128 bf16 columns from global rows into two swizzled tiles; a
+// null row is zero-filled (its copy reads nothing from `dummy`).
+template <class RowPtr>
+__device__ __forceinline__ void load_op(uint32_t dst, RowPtr row_ptr, const void* dummy, int tid) {
+  for (int idx = tid; idx < 128 * 16; idx += kThreads) {
+    const int r = idx >> 4, c16 = idx & 15;
+    const __nv_bfloat16* src = row_ptr(r);
+    cp_async16(dst + (c16 >> 3) * kTileB + sw_off(r, c16 & 7), src ? (const void*)(src + c16 * 8) : dummy,
+               src != nullptr);
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
+  pdl_wait();
+  const int n_q = p.n_q_dev ? min(*p.n_q_dev, p.n_q_cap) : p.n_q_cap;
+  const int q0 = blockIdx.x * kTQ;
+  if (q0 >= n_q) return;  // uniform over a cluster (its CTAs share blockIdx.x)
+  const int h = blockIdx.y;
+  const int ns = gridDim.z, split = blockIdx.z;
+  const int kvh = h / (p.n_heads / p.n_kv_heads);
+  const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, cg = warp >> 2;  // TMEM lane quadrant, 32-column group
+  const int r = 32 * qd + lane;             // this thread's query row (TMEM lane)
+  const int c0 = 32 * cg;                   // its 32 key (then head-dim) columns
+  const int n_pb = (p.T + kTK - 1) / kTK, n_fb = (n_f + kTK - 1) / kTK, nb = n_pb + n_fb;
+  const int b_lo = split * nb / ns, b_hi = (split + 1) * nb / ns;  // balanced, at most kMaxBlk
+  const int nbl = b_hi - b_lo;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gb = smem_raw + (base - raw);
+  const uint32_t sQ = base + kOffQ, sKP = base + kOffKP, sV = base + kOffV;
+  int* sF = reinterpret_cast<int*>(gb + kOffF);
+  float* red = reinterpret_cast<float*>(gb + kOffQ);  // [2][4][128] row max / sum partials, after S is done
+  const uint32_t barS = base + kOffBar, barO = barS + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + kOffBar + 16);
+  volatile int* fail = reinterpret_cast<volatile int*>(gb + kOffBar + 24);
+
+  if (tid == 0) {
+    mbar_init(barS, 1);
+    mbar_init(barO, 1);
+    *fail = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tmem_slot), 512);
+
+  // ---- operands ----
+  load_op(sQ, [&](int rr) -> const __nv_bfloat16* {
+    const int qi = q0 + rr;
+    if (qi >= n_q) return nullptr;
+    return p.q + (int64_t)(p.qsrc ? p.qsrc[qi] : qi) * p.q_ld + h * 128;
+  }, p.q, tid);
+  for (int j = 0; j < nbl; ++j) {
+    const int b = b_lo + j;
+    const bool parent_blk = b < n_pb;
+    const int r0 = (parent_blk ? b : b - n_pb) * kTK;
+    const int lim = parent_blk ? p.T : n_f;
+    const __nv_bfloat16* kb = parent_blk ? p.pk : p.fk;
+    const __nv_bfloat16* vb = parent_blk ? p.pv : p.fv;
+    const int64_t ld = parent_blk ? p.kv_ld : p.f_ld;
+    load_op(sKP + j * kOpB, [&](int rr) -> const __nv_bfloat16* {
+      return r0 + rr < lim ? kb + (int64_t)(r0 + rr) * ld + kvh * 128 : nullptr;
+    }, p.q, tid);
+    load_op(sV + j * kOpB, [&](int rr) -> const __nv_bfloat16* {
+      return r0 + rr < lim ? vb + (int64_t)(r0 + rr) * ld + kvh * 128 : nullptr;
+    }, p.q, tid);
+    if (!parent_blk && tid < kTK) {
+      const int jj = r0 + tid;
+      sF[j * kTK + tid] = jj >= n_f ? -2 : (p.fchild ? p.fchild[jj] : -1);
+    }
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
+
+  // ---- S_j = Q K_j^T ----
+  if (tid == 0 && nbl > 0) {
+    const uint32_t idesc = idesc_bf16(kTQ, kTK);
+    for (int j = 0; j < nbl; ++j)
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t half = (uint32_t)(kk >> 2) * kTileB;
+        tc_mma_bf16(tmem + (uint32_t)(j * kTK), sw128_desc(sQ + half) + 2 * (kk & 3),
+                    sw128_desc(sKP + j * kOpB + half) + 2 * (kk & 3), idesc, kk > 0 ? 1u : 0u);
+      }
+    tc_commit(barS);
+  }
+
+  // ---- masked softmax: row r, key columns c0..c0+31 of every block ----
+  const bool row_ok = q0 + r < n_q;
+  const int child = (p.qchild && row_ok) ? p.qchild[q0 + r] : -1;
+  if (nbl > 0) {
+    volatile int no_abort = 0;
+    if (!mbar_wait(barS, 0, &no_abort)) *fail = 1;
+  }
+  const bool s_bad = __syncthreads_or(*fail);  // also: S is complete, Q's tiles are free for `red`
+  tc_fence_after();
+  float m = -INFINITY, l = 0.f;
+  uint32_t vm[kMaxBlk];  // valid keys among this thread's 32 columns of each block
+  const float sc = p.scale_log2;
+  if (!s_bad) {
+    for (int j = 0; j < nbl; ++j) {
+      const int b = b_lo + j;
+      uint32_t v = 0;
+      if (b < n_pb) {
+        const int tw = b * kTK + c0;
+        const int nv = min(32, max(0, p.T - tw));
+        v = nv >= 32 ? 0xffffffffu : ((1u << nv) - 1u);
+        if (p.fresh_bits && child >= 0 && nv > 0) v &= ~p.fresh_bits[(int64_t)child * p.bits_ld + (tw >> 5)];
+      } else {
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+          const int cf = sF[j * kTK + c0 + k];
+          if (cf == -1 || (cf >= 0 && cf == child)) v |= 1u << k;
+        }
+      }
+      vm[j] = v;
+      uint32_t sv[32];
+      tmem_ld32_nowait(lane_base + (uint32_t)(j * kTK + c0), sv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if ((v >> i) & 1u) m = fmaxf(m, __uint_as_float(sv[i]) * sc);
+    }
+  }
+  red[cg * kTQ + r] = m;
+  __syncthreads();
+  m = fmaxf(fmaxf(red[r], red[kTQ + r]), fmaxf(red[2 * kTQ + r], red[3 * kTQ + r]));
+  if (!s_bad) {
+    for (int j = 0; j < nbl; ++j) {
+      uint32_t sv[32];
+      tmem_ld32_nowait(lane_base + (uint32_t)(j * kTK + c0), sv);
+      tmem_wait_ld();
+      const uint32_t v = vm[j];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {  // 8-key groups of the thread's 32 keys
+        float pv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const bool ok = ((v >> (8 * g + i)) & 1u) && m != -INFINITY;
+          pv[i] = ok ? exp2f(__uint_as_float(sv[8 * g + i]) * sc - m) : 0.f;
+          l += pv[i];
+        }
+        const int key8 = (c0 >> 3) + g;
+        const uint32_t dst = sKP + j * kOpB + (key8 >> 3) * kTileB + sw_off(r, key8 & 7);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(pack2(pv[0], pv[1])),
+                     "r"(pack2(pv[2], pv[3])), "r"(pack2(pv[4], pv[5])), "r"(pack2(pv[6], pv[7]))
+                     : "memory");
+      }
+    }
+  }
+  red[4 * kTQ + cg * kTQ + r] = l;
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  l = (red[4 * kTQ + r] + red[5 * kTQ + r]) + (red[6 * kTQ + r] + red[7 * kTQ + r]);
+
+  // ---- O = sum_j P_j V_j ----
+  const bool have_o = nbl > 0 && !s_bad;
+  if (tid == 0 && have_o) {
+    const uint32_t idesc = idesc_bf16_bmn(kTQ, 128);
+    for (int j = 0; j < nbl; ++j)
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t a = sw128_desc(sKP + j * kOpB + (uint32_t)(kk >> 2) * kTileB) + 2 * (kk & 3);
+        const uint64_t bdesc = sw128_desc_mn(sV + j * kOpB + (uint32_t)kk * 2048u, kTileB, 1024);
+        tc_mma_bf16(tmem + 3 * kTK, a, bdesc, idesc, (j | kk) != 0 ? 1u : 0u);
+      }
+    tc_commit(barO);
+  }
+  if (have_o) {
+    volatile int no_abort = 0;
+    if (!mbar_wait(barO, 0, &no_abort)) *fail = 1;
+  }
+  const bool bad = __syncthreads_or(*fail);
+  if (bad && tid == 0 && p.status) atomicOr(p.status, AF_STATUS_TIMEOUT);
+  tc_fence_after();
+
+  // This thread's 32 head-dim columns of row r of O.
+  uint32_t o[32];
+  if (have_o && !bad) {
+    tmem_ld32_nowait(lane_base + (uint32_t)(3 * kTK + c0), o);
+    tmem_wait_ld();
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = 0u;
+  }
+  if (ns == 1) {
+    if (row_ok && !bad) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)(q0 + r) * p.out_ld + h * 128 + c0);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 w;
+        w.x = pack2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+        w.y = pack2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+        w.z = pack2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+        w.w = pack2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+        dst[c] = w;
+      }
+    }
+  } else {
+    // Partials into the (now idle) V region: O rows [128][kPoLd] f32, then (m, l) [128].
+    constexpr int kPoLd = 132;  // padded row: conflict-free 16-byte stores
+    float* po = reinterpret_cast<float*>(gb + kOffV);
+    float2* pml = reinterpret_cast<float2*>(gb + kOffV + 128 * kPoLd * 4);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      *reinterpret_cast<float4*>(po + r * kPoLd + c0 + i) = make_float4(
+          __uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]), __uint_as_float(o[i + 3]));
+    if (cg == 0) pml[r] = make_float2(bad ? -INFINITY : m, bad ? 0.f : l);
+    cluster_sync_all();
+    const int rows_per = (kTQ + ns - 1) / ns;
+    const int rlo = split * rows_per, rhi = min(kTQ, rlo + rows_per);
+    const uint32_t po_s = smem_u32(po), pml_s = smem_u32(pml);
+    for (int idx = tid; idx < (rhi - rlo) * 32; idx += kThreads) {
+      const int rr = rlo + idx / 32, c4 = idx % 32;
+      float mk[8], lk[8];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < ns) {
+          const float2 v = ld_cluster_f2(cluster_map(pml_s + 8u * rr, (uint32_t)k));
+          mk[k] = v.x;
+          lk[k] = v.y;
+          mx = fmaxf(mx, v.x);
+        }
+      }
+      float4 vk[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < ns) vk[k] = ld_cluster_f4(cluster_map(po_s + 4u * (rr * kPoLd + 4 * c4), (uint32_t)k));
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float lsum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < ns && mk[k] != -INFINITY) {
+          const float f = exp2f(mk[k] - mx);
+          lsum += f * lk[k];
+          acc.x += f * vk[k].x;
+          acc.y += f * vk[k].y;
+          acc.z += f * vk[k].z;
+          acc.w += f * vk[k].w;
+        }
+      }
+      if (q0 + rr < n_q && !bad) {
+        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+        uint2 w;
+        w.x = pack2(acc.x * inv, acc.y * inv);
+        w.y = pack2(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(p.out + (int64_t)(q0 + rr) * p.out_ld + h * 128 + 4 * c4) = w;
+      }
+    }
+    cluster_sync_all();  // peers may read this CTA's partials until here
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Key splits for the tcgen05 kernel, or 0 when the shape needs more than
+// kMaxBlk blocks per split in an 8-CTA cluster.
+int attention_tc_splits(const AttnParams& p) {
+  const int nb = (p.T + kTK - 1) / kTK + (p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0);
+  const int need = (nb + kMaxBlk - 1) / kMaxBlk;
+  if (need > 8) return 0;
+  const int ctas = (p.n_q_cap + kTQ - 1) / kTQ * p.n_heads;
+  int ns = need;
+  while (ns < 8 && ns < nb && (ns + 1) * ctas <= sm_count()) ++ns;
+  return ns;
+}
+
+int attention_tc_run(const AttnParams& p, int ns, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+    attr = true;
+  }
+  cudaError_t e = launch_ex(k_attention_tc, dim3((p.n_q_cap + kTQ - 1) / kTQ, p.n_heads, ns), dim3(kThreads, 1, 1),
+                            (size_t)kSmemTc, s, p.pdl != 0, dim3(1, 1, ns), p);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("attention_tc: launch: ") + cudaGetErrorString(e));
+  return check_launch("attention_tc");
+}
+
+}  // namespace af

@@ -615,6 +615,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     ap.n_kv_heads = m->dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf((float)m->dims.head_dim)) * 1.4426950408889634f;
     ap.pdl = pass_pdl() ? 1 : 0;
+    ap.status = stw;
     if ((st = attention_run(ap, s))) return st;
     c = base_call(stw);
     c.x = w.att;
@@ -975,6 +976,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.n_kv_heads = p->model.dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf(128.f)) * 1.4426950408889634f;
     ap.pdl = pass_pdl() ? 1 : 0;
+    ap.status = w.status;
     AF_TIMED(FK_ATTN, if ((st = attention_run(ap, s))) return st);
 
     c = base_call(w.status);

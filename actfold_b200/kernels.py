@@ -110,6 +110,7 @@ def attention(
     fchild: torch.Tensor | None = None,
     n_f: torch.Tensor | None = None,
     n_q_cap: int | None = None,
+    status: DeviceStatus | None = None,
 ) -> torch.Tensor:
     """Non-causal attention of query rows over parent K/V with per-child fresh-key overrides.
 
@@ -129,7 +130,8 @@ def attention(
             pk.data_ptr(), pv.data_ptr(), pk.stride(0), T,
             _lib.ptr(fresh_bits), fresh_bits.shape[1] if fresh_bits is not None else 0,
             _lib.ptr(fk), _lib.ptr(fv), fk.stride(0) if fk is not None else 0, _lib.ptr(fchild), _lib.ptr(n_f), n_f_cap,
-            out.data_ptr(), out.stride(0), n_heads, n_kv_heads, 128, 128 ** -0.5, _lib.stream_ptr(q.device),
+            out.data_ptr(), out.stride(0), n_heads, n_kv_heads, 128, 128 ** -0.5,
+            status.status.data_ptr() if status is not None else None, _lib.stream_ptr(q.device),
         )
     _lib.check(st, "attention")
     return out

@@ -156,14 +156,18 @@ int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_d
  * fresh_bits[qchild[i] * bits_ld] is set, plus candidate rows j of fk/fv with
  * fchild[j] == qchild[i]. Valid query / candidate counts are read from
  * n_q_dev / n_f_dev (nullable -> caps). head_dim must be 128; GQA when
- * n_kv_heads < n_heads.
+ * n_kv_heads < n_heads. Up to 24 blocks of 128 keys (parent + candidates) run
+ * on tcgen05 tensor cores (128 query rows per CTA, key splits combined in a
+ * thread-block cluster); larger shapes use an mma.sync kernel. status
+ * (nullable) receives AF_STATUS_TIMEOUT if a bounded wait ran out.
  */
 int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsrc, const int32_t* qchild,
                       const int32_t* n_q_dev, int64_t n_q_cap, const void* pk, const void* pv,
                       int64_t kv_ld, int64_t T, const uint32_t* fresh_bits, int64_t bits_ld,
                       const void* fk, const void* fv, int64_t f_ld, const int32_t* fchild,
                       const int32_t* n_f_dev, int64_t n_f_cap, void* out, int64_t out_ld,
-                      int n_heads, int n_kv_heads, int head_dim, float scale, void* stream);
+                      int n_heads, int n_kv_heads, int head_dim, float scale, uint32_t* status,
+                      void* stream);
 
 /* ------------------------------------------------------------------------
  * Native folded verification of LLaDA / Dream-architecture models.

@@ -1,7 +1,9 @@
 """Attention kernel against a plain PyTorch fp32 reference of the same op.
 
 Tolerance: the kernel feeds bf16 probabilities to the tensor cores, so the
-max error is bounded at 2e-2 of the output scale.
+max error is bounded at 2e-2 of the output scale. Each case runs on the
+tcgen05 kernel (the default for up to 24 key blocks) and on the mma.sync
+kernel (ACTFOLD_ATTN_IMPL=mma).
 """
 
 from __future__ import annotations
@@ -29,8 +31,15 @@ def _err(a, b):
     return float((a.float() - b.float()).abs().max() / b.float().abs().max())
 
 
-@pytest.mark.parametrize("T,n_q,heads,kv", [(64, 64, 2, 2), (1024, 1024, 4, 4), (200, 37, 4, 1), (512, 130, 8, 2)])
-def test_dense_attention(T, n_q, heads, kv):
+@pytest.fixture(params=["tc", "mma"])
+def impl(request, monkeypatch):
+    monkeypatch.setenv("ACTFOLD_ATTN_IMPL", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("T,n_q,heads,kv", [(64, 64, 2, 2), (1024, 1024, 4, 4), (200, 37, 4, 1), (512, 130, 8, 2),
+                                            (3000, 200, 2, 2), (130, 129, 32, 32)])
+def test_dense_attention(T, n_q, heads, kv, impl):
     from actfold_b200.kernels import attention
 
     g = torch.Generator(device="cuda").manual_seed(T + n_q)
@@ -82,7 +91,7 @@ def _fresh_case(T, heads, kv, fresh, qsel, seed=0):
 
 
 @pytest.mark.parametrize("kv", [4, 2])
-def test_fresh_key_overrides(kv):
+def test_fresh_key_overrides(kv, impl):
     from actfold_b200.kernels import attention
 
     heads = 4
@@ -101,13 +110,13 @@ def test_fresh_key_overrides(kv):
 
 @pytest.mark.parametrize("splits", [1, 2, 4, 8])
 @pytest.mark.parametrize("T", [300, 1024])
-def test_key_splits_over_a_cluster(splits, T, monkeypatch):
+def test_key_splits_over_a_cluster(splits, T, monkeypatch, impl):
     """Every key-split count gives the unsplit result: 8 splits of a 300-key
     case leave some CTAs without key blocks, 70 queries leave the second query
     block partly empty, and a dynamic query count cuts it further."""
     from actfold_b200.kernels import attention
 
-    monkeypatch.setenv("ACTFOLD_ATTN_SPLITS", str(splits))
+    monkeypatch.setenv("ACTFOLD_ATTN_SPLITS", str(splits))  # mma.sync kernel; tcgen05 picks its own
     heads, kv = 4, 2
     fresh = {0: [1, 64, T - 1], 1: [0, 127, 128], 2: list(range(10, 30)), 3: [T // 2]}
     nc = sum(len(v) for v in fresh.values())
@@ -120,3 +129,20 @@ def test_key_splits_over_a_cluster(splits, T, monkeypatch):
     attention(qall, pk, pv, heads, kv, out=out2, n_q=n_q, **args)
     assert _err(out2[:67], ref[:67]) <= 2e-2
     assert (out2[67:] == 0).all()
+
+
+def test_fold_shape_many_children_and_timeout_status(impl):
+    """The folded pass's shape (128 packed queries, 1024 parent keys, 128 candidate keys of 8
+    children, 32 heads) against the reference, with a status word that stays clear."""
+    from actfold_b200.kernels import DeviceStatus, attention
+
+    heads, kv, T = 32, 32, 1024
+    g = torch.Generator().manual_seed(5)
+    fresh = {c: sorted(torch.randperm(T, generator=g)[:16].tolist()) for c in range(8)}
+    qsel = list(range(128))
+    qall, pk, pv, args, ref = _fresh_case(T, heads, kv, fresh, qsel, seed=11)
+    st = DeviceStatus()
+    out = attention(qall, pk, pv, heads, kv, status=st, **args)
+    torch.cuda.synchronize()
+    st.check_status()
+    assert _err(out, ref) <= 2e-2
