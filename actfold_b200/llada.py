@@ -217,6 +217,21 @@ class FoldPlan:
                                   _lib.stream_ptr(child_tokens.device))
         _lib.check(st, "af_fold_run")
 
+    def capture(self, child_tokens: torch.Tensor, logits: torch.Tensor, scores: torch.Tensor | None = None
+                ) -> torch.cuda.CUDAGraph:
+        """Record one pass over these buffers as a CUDA graph; ``graph.replay()`` reruns it.
+
+        The pass has no host synchronisation, so the whole launch sequence
+        (with its programmatic-dependency edges) goes into one graph. New
+        tokens are passed by copying them into ``child_tokens`` before a replay.
+        """
+        self.run(child_tokens, logits, scores)  # first run: kernel attributes, flag words
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.run(child_tokens, logits, scores)
+        return g
+
     def materialize(self, layer: int) -> torch.Tensor:
         out = torch.empty((self.C, self.T, self.model.dims.hidden), dtype=torch.bfloat16, device=self.model.device)
         _lib.check(self.lib.af_fold_materialize(self._plan, layer, out.data_ptr(), _lib.stream_ptr(out.device)))

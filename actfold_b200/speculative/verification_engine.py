@@ -50,7 +50,8 @@ class VerificationResult:
 
 
 class ActFoldVerificationEngine:
-    def __init__(self, model: LLaDAModel, cache=None, gate: SimilarityGate | None = None, scheduler=None, acceptance_threshold: float = 0.0) -> None:
+    def __init__(self, model: LLaDAModel, cache=None, gate: SimilarityGate | None = None, scheduler=None,
+                 acceptance_threshold: float = 0.0, use_graphs: bool = True) -> None:
         if not 0.0 <= acceptance_threshold <= 1.0:
             raise ValueError(f"acceptance_threshold must be in [0, 1], got {acceptance_threshold}")
         if scheduler is not None:
@@ -61,15 +62,28 @@ class ActFoldVerificationEngine:
         self.acceptance_threshold = acceptance_threshold
         self._parents: dict = {}
         self._host: dict = {}
+        # verify_tokens replays each plan's pass from a CUDA graph captured over
+        # the engine's fixed token / logits / score buffers (use_graphs=False: launch eagerly).
+        self.use_graphs = use_graphs
+        self._graphs: dict = {}
 
     # ----------------------------------------------------------------- parent
     def parent_cache(self, parent_branch: Branch) -> ParentCache:
         toks = parent_branch.tokens.reshape(-1)
         key = parent_branch.branch_id
         pc = self._parents.get(key)
-        if pc is None or pc.seq != toks.numel() or not torch.equal(pc.tokens, toks.to(pc.tokens.device)) or pc.tau != self.gate.tau:
-            pc = self.model.parent_pass(toks.to(self.model.device), tau=self.gate.tau)
-            self._parents = {key: pc}
+        if pc is not None and pc.seq == toks.numel() and pc.tau == self.gate.tau:
+            # Same tokens: the cached buffer itself, equal host ids, or (last) a device compare.
+            if toks.device == pc.tokens.device and toks.data_ptr() == pc.tokens.data_ptr():
+                return pc
+            if toks.device.type == "cpu":
+                if np.array_equal(toks.numpy(), self._parent_host_tokens(pc)):
+                    return pc
+            elif torch.equal(pc.tokens, toks.to(pc.tokens.device)):
+                return pc
+        pc = self.model.parent_pass(toks.to(self.model.device), tau=self.gate.tau)
+        self._parents = {key: pc}
+        self._graphs = {}
         return pc
 
     def set_parent_cache(self, parent_branch: Branch, pc: ParentCache) -> None:
@@ -111,8 +125,19 @@ class ActFoldVerificationEngine:
             }
             self._host = {key: bufs}
         bufs["tok"].copy_(child_tokens_host, non_blocking=True)
-        _, plan = self.model.verify(bufs["tok"], pc, self.gate.tau, self.gate.metric, logits=bufs["logits"], scores=bufs["scores"],
-                                    m_cap=self._m_cap(child_tokens_host, pc, Cn, T))
+        m_cap = self._m_cap(child_tokens_host, pc, Cn, T)
+        if self.use_graphs:
+            plan = self.model.plan(pc, Cn, m_cap, self.gate.tau, self.gate.metric)
+            entry = self._graphs.get(id(plan))
+            if entry is None or entry[1] is not plan or entry[2] is not bufs:
+                if len(self._graphs) >= 8:
+                    self._graphs = {}
+                entry = (plan.capture(bufs["tok"], bufs["logits"], bufs["scores"]), plan, bufs)
+                self._graphs[id(plan)] = entry
+            entry[0].replay()
+        else:
+            _, plan = self.model.verify(bufs["tok"], pc, self.gate.tau, self.gate.metric, logits=bufs["logits"],
+                                        scores=bufs["scores"], m_cap=m_cap)
         bufs["h_scores"].copy_(bufs["scores"], non_blocking=True)
         bufs["h_div"].copy_(plan.div_count, non_blocking=True)
         bufs["h_status"].copy_(plan.status, non_blocking=True)
@@ -132,8 +157,10 @@ class ActFoldVerificationEngine:
         # Capacity from the host copy of the tokens (no device round trip).
         ptok = self._parent_host_tokens(pc)
         edited = int((child_tokens_host.numpy() != ptok[None]).sum())
-        su = pc.su_layers()
-        su_rows = int((pc.self_stable == 0).any(dim=0).sum().item()) if su.any() else 0
+        su_rows = getattr(pc, "_su_rows", None)
+        if su_rows is None:  # rows the parent fails its own gate on (one device read per parent)
+            su_rows = int((pc.self_stable == 0).any(dim=0).sum().item())
+            pc._su_rows = su_rows
         cap = edited + Cn * su_rows
         cap = max(16, ((cap + 15) // 16) * 16)
         return min(cap, ((Cn * T + 15) // 16) * 16)

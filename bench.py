@@ -51,6 +51,7 @@ def parse_args():
     ap.add_argument("--tau", type=float, default=0.95)
     ap.add_argument("--layers", type=int, default=None, help="override layer count (small profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch the pass kernel by kernel instead of replaying its CUDA graph")
     return ap.parse_args()
 
 
@@ -70,6 +71,7 @@ def config_dict(a, n):
         "d_unmasked_per_child": a.d,
         "tau": a.tau,
         "parallelism": "children sharded across ranks, parent cache NCCL-broadcast once" if n > 1 else "single GPU",
+        "launch": "eager kernel launches" if a.eager else "CUDA graph replay of the pass",
         "l2": "inputs larger than L2: 15 GB of weights streamed every step",
     }
 
@@ -238,7 +240,14 @@ def main() -> None:
     else:
         pc = empty_parent_cache(dims, a.seq, a.tau, dev)
     torch.cuda.synchronize()
-    parent_ms = (time.perf_counter() - t0) * 1e3
+    parent_first_ms = (time.perf_counter() - t0) * 1e3
+    parent_ms = parent_first_ms
+    if rank == 0:
+        # A second dense pass: the first includes one-time module loading and kernel set-up.
+        t0 = time.perf_counter()
+        pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)
+        torch.cuda.synchronize()
+        parent_ms = (time.perf_counter() - t0) * 1e3
     bcast_ms = 0.0
     if world > 1:
         dist.barrier()
@@ -254,7 +263,7 @@ def main() -> None:
         bcast_ms = e0.elapsed_time(e1)
 
     gate = SimilarityGate(a.tau)
-    engine = ActFoldVerificationEngine(model, gate=gate)
+    engine = ActFoldVerificationEngine(model, gate=gate, use_graphs=not a.eager)
     pbranch = Branch("parent", None, pc.tokens)
     engine.set_parent_cache(pbranch, pc)
     host_children = torch.from_numpy(children_np).pin_memory()
@@ -266,8 +275,14 @@ def main() -> None:
     torch.cuda.synchronize()
     plan.check_status()
 
-    def step():
-        plan.run(ct, logits, scores)
+    if not a.eager:
+        graph = plan.capture(ct, logits, scores)
+
+        def step():
+            graph.replay()
+    else:
+        def step():
+            plan.run(ct, logits, scores)
 
     for _ in range(a.warmup):
         step()
@@ -297,10 +312,10 @@ def main() -> None:
     value = a.children * world * a.seq / (step_ms_max / 1e3)
 
     # ---- per-kernel-class device times (same stream, same workload)
-    plan.set_timing(True)
+    plan.set_timing(True)  # events around every launch class: always the eager launch sequence
     n_prof = max(3, min(a.steps, 20))
     for _ in range(n_prof):
-        step()
+        plan.run(ct, logits, scores)
     torch.cuda.synchronize()
     ms_by, cnt_by, launches_per_run = plan.get_timing()
     plan.set_timing(False)
@@ -405,6 +420,7 @@ def main() -> None:
             "kernels_ms_per_step": {k: round(v, 4) for k, v in kernel_ms.items()},
             "kernel_share": {k: round(v / tot_k, 4) for k, v in kernel_ms.items()},
             "parent_pass_ms": parent_ms,
+            "parent_pass_first_ms": parent_first_ms,
             "parent_broadcast_ms": bcast_ms,
             "parent_broadcast_bytes": sum(t.numel() * t.element_size() for t in pc.tensors()),
             "stable_ratio_mean": float(np.mean(res["stable_ratio"])),

@@ -188,3 +188,26 @@ def test_folded_model_api_on_llada(tiny):
 def test_gate_boundary_exemption_documented():
     # bf16 decision boundary at tau=0.95 is the midpoint between bf16(0.95) and the next bf16 value.
     assert decision_boundary(0.95, "bf16") == pytest.approx((0.94921875 + 0.953125) / 2)
+
+
+def test_engine_graph_replay_matches_eager_launches(tiny):
+    """verify_tokens replays a CUDA graph of the pass: for two different child batches in a row it
+    must return exactly what the kernel-by-kernel launch returns (scores, divergent counts, logits)."""
+    from actfold_b200.core import SimilarityGate
+    from actfold_b200.speculative import ActFoldVerificationEngine, Branch
+
+    model, spec, dims = tiny["model"], tiny["spec"], tiny["dims"]
+    parent = torch.from_numpy(tiny["parent"])
+    kids = tiny["children"]
+    others = W.llada_children(tiny["parent"], kids.shape[0], spec["d"] + 1, dims.mask_id, seed=77)
+    eng_g = ActFoldVerificationEngine(model, gate=SimilarityGate(spec["tau"]), use_graphs=True)
+    eng_e = ActFoldVerificationEngine(model, gate=SimilarityGate(spec["tau"]), use_graphs=False)
+    pb = Branch("parent", None, parent)
+    for batch in (kids, others, kids):
+        host = torch.from_numpy(np.ascontiguousarray(batch)).pin_memory()
+        rg = eng_g.verify_tokens(pb, host)
+        rg_logits = rg["logits"].clone()
+        re = eng_e.verify_tokens(pb, host)
+        np.testing.assert_array_equal(rg["div_count"], re["div_count"])
+        np.testing.assert_allclose(rg["scores"], re["scores"], rtol=1e-5, atol=1e-6)
+        assert torch.equal(rg_logits.view(torch.int16), re["logits"].view(torch.int16))
