@@ -1,8 +1,11 @@
 """Native batched folded pass (LLaDA / Dream architectures) against the oracle and the golden vectors.
 
 Tolerances (bf16 hidden states and logits): max relative error <= 2e-2 of the
-tensor's scale, logit cosine >= 0.999, argmax agreement >= 99.9%. Masks are
-compared bit-exactly except for rows the oracle places on the gate boundary.
+tensor's scale, logit cosine >= 0.999, argmax agreement >= 99.9% over the rows
+whose oracle argmax is defined (top-2 margin above two bf16 ulps of the row's
+scale: random-init tiny models have exact bf16 ties, which any summation order
+may break either way). Masks are compared bit-exactly except for rows the
+oracle places on the gate boundary.
 """
 
 from __future__ import annotations
@@ -35,6 +38,19 @@ def _cos(a, b):
     a = a.astype(np.float64).ravel()
     b = b.astype(np.float64).ravel()
     return float(a @ b / math.sqrt((a @ a) * (b @ b)))
+
+
+def _argmax_agreement(got, ref):
+    """Fraction of rows with equal argmax, over rows whose reference top-2 margin exceeds
+    two bf16 ulps of the row's largest magnitude (ties and near-ties have no defined argmax)."""
+    got = got.reshape(-1, got.shape[-1]).astype(np.float64)
+    ref = ref.reshape(-1, ref.shape[-1]).astype(np.float64)
+    top2 = np.sort(ref, axis=-1)[:, -2:]
+    scale = np.abs(ref).max(-1)
+    ulp = np.exp2(np.floor(np.log2(np.maximum(scale, 1e-30))) - 7)
+    defined = (top2[:, 1] - top2[:, 0]) > 2 * ulp
+    assert defined.mean() >= 0.75, "too few rows with a defined argmax to judge"
+    return float((got.argmax(-1) == ref.argmax(-1))[defined].mean())
 
 
 def _case(which):
@@ -90,7 +106,7 @@ def test_folded_children_match_oracle_and_reference(tiny, golden):
     got = logits.float().cpu().numpy()
     assert _rel(got, ref["logits"]) <= 2e-2
     assert _cos(got, ref["logits"]) >= 0.999
-    assert (got.argmax(-1) == ref["logits"].argmax(-1)).mean() >= 0.999
+    assert _argmax_agreement(got, ref["logits"]) >= 0.999
     ref_g = from_bf16_bits(g["logits_bits"])
     assert _rel(got, ref_g) <= 2e-2 and _cos(got, ref_g) >= 0.999
     # per-layer child states through the merge/scatter materialisation
