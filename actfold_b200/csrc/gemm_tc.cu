@@ -421,27 +421,32 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   g.n_tiles = n / kTileN;
   g.nkb = k / kBlockK;
   const int stage = kTileN * kBlockK * 2 + g.ntok * kBlockK * 2;
-  int st = (100 * 1024) / stage;  // two CTAs per SM when it fits
   static const int env_stages = [] {
     const char* e = getenv("ACTFOLD_GEMM_STAGES");  // tuning override of the ring depth
     return e ? atoi(e) : 0;
   }();
-  if (env_stages > 0) st = env_stages;
-  st = std::max(2, std::min(12, st));
+  const int tiles = g.n_tiles * g.m_tiles;
   int splits = want_splits;
   if (splits <= 0) {
     // About 4/3 CTAs per SM, at most 4 splits: measured on B200 for the
     // LLaDA/Dream projections, more and shorter split CTAs lose more to their
     // ramp-up and cluster reduction than they gain in parallel streams.
-    const int tiles = g.n_tiles * g.m_tiles;
     splits = (4 * sm_count()) / (3 * tiles);
-    splits = std::min(splits, std::max(1, g.nkb / 4));
     splits = std::max(1, std::min(splits, 4));
+    splits = std::min(splits, std::max(1, g.nkb / 4));
   }
   if (row_sums) splits = 1;
   splits = std::min(splits, kMaxSplits);
   g.kb_per = (g.nkb + splits - 1) / splits;
   g.splits = (g.nkb + g.kb_per - 1) / g.kb_per;
+  // A CTA streams at most (bytes its ring keeps in flight) / (load latency):
+  // a launch whose CTAs all fit one per SM and stream long k-ranges (the down
+  // projection) gets the deepest ring that fits; otherwise ~100 KB rings let
+  // two CTAs share an SM.
+  const bool one_per_sm = tiles * g.splits <= sm_count() && g.kb_per >= 24;
+  int st = (one_per_sm ? 220 * 1024 : 100 * 1024) / stage;
+  if (env_stages > 0) st = env_stages;
+  st = std::max(2, std::min(16, st));
   const int tile_bytes = g.ntok * kLdt * 4;  // fp32 staging of the accumulator
   while (st * stage < tile_bytes) ++st;
   g.stages = st;
