@@ -34,6 +34,21 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "verify tokens/sec, LLaDA-8B arch, 8 branches×1024 tok; % HBM/TC roofline"
+# The Dream-7B workload (28 layers, hidden 3584, 28 q / 4 kv heads, SwiGLU 18944,
+# vocab 152064): 1024 ids, 75% of the 768 generation positions masked, 16
+# children per GPU differing at 8 positions. Reported under its own metric.
+METRIC_DREAM = "verify tokens/sec, Dream-7B arch, 16 branches×1024 tok; % HBM/TC roofline"
+MODEL_DEFAULTS = {"llada8b": dict(children=8, d=16, mask_fraction=0.5), "dream7b": dict(children=16, d=8, mask_fraction=0.75)}
+
+
+def metric_of(a) -> str:
+    return METRIC if a.model == "llada8b" else METRIC_DREAM
+
+
+def base_dims(a):
+    from actfold_b200 import workloads as W
+
+    return W.LLADA_8B if a.model == "llada8b" else W.DREAM_7B
 UNIT = "verified tokens/s"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
@@ -45,35 +60,56 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--children", type=int, default=8, help="children per GPU")
+    ap.add_argument("--model", choices=sorted(MODEL_DEFAULTS), default="llada8b")
+    ap.add_argument("--children", type=int, default=None, help="children per GPU (model default)")
     ap.add_argument("--seq", type=int, default=1024)
-    ap.add_argument("--d", type=int, default=16, help="unmasked positions per child")
+    ap.add_argument("--d", type=int, default=None, help="unmasked positions per child (model default)")
     ap.add_argument("--tau", type=float, default=0.95)
     ap.add_argument("--layers", type=int, default=None, help="override layer count (small profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch the pass kernel by kernel instead of replaying its CUDA graph")
-    return ap.parse_args()
+    a = ap.parse_args()
+    for k, v in MODEL_DEFAULTS[a.model].items():
+        if getattr(a, k, None) is None:
+            setattr(a, k, v)
+    return a
 
 
 def workload_name(a) -> str:
-    return f"LLaDA-8B arch folded verification, {a.children} children x {a.seq} tokens per GPU, d={a.d}, tau={a.tau}"
+    arch = "LLaDA-8B" if a.model == "llada8b" else "Dream-7B"
+    return f"{arch} arch folded verification, {a.children} children x {a.seq} tokens per GPU, d={a.d}, tau={a.tau}"
+
+
+def model_desc(a) -> str:
+    d = base_dims(a)
+    heads = f"{d.n_heads}x{d.head_dim} MHA" if d.n_heads == d.n_kv_heads else f"{d.n_heads} q / {d.n_kv_heads} kv heads x {d.head_dim}"
+    arch = "LLaDA-8B" if a.model == "llada8b" else "Dream-7B"
+    if a.layers is not None:
+        return f"{arch} layer shapes, {a.layers} layers"
+    return f"{arch} architecture ({d.n_layers} x [H {d.hidden}, {heads}, SwiGLU {d.ffn}], vocab {d.vocab})"
 
 
 def config_dict(a, n):
     return {
         "workload": workload_name(a),
-        "model": "LLaDA-8B architecture (32 x [H 4096, 32x128 MHA, SwiGLU 12288], vocab 126464)" if a.layers is None else f"LLaDA-8B layer shapes, {a.layers} layers",
+        "model": model_desc(a),
         "children_per_gpu": a.children,
         "global_children": a.children * n,
         "seq_len": a.seq,
         "prompt": 256,
-        "mask_fraction": 0.5,
+        "mask_fraction": MODEL_DEFAULTS[a.model]["mask_fraction"],
         "d_unmasked_per_child": a.d,
         "tau": a.tau,
         "parallelism": "children sharded across ranks, parent cache NCCL-broadcast once" if n > 1 else "single GPU",
         "launch": "eager kernel launches" if a.eager else "CUDA graph replay of the pass",
-        "l2": "inputs larger than L2: 15 GB of weights streamed every step",
+        "l2": f"inputs larger than L2: {weight_gb(a):.1f} GB of weights streamed every step",
     }
+
+
+def weight_gb(a) -> float:
+    d = base_dims(a)
+    L = a.layers or d.n_layers
+    return (L * d.params_per_layer + d.vocab * d.hidden) * 2 / 1e9
 
 
 def measured_peaks():
@@ -164,7 +200,7 @@ def run_reference(a, rank: int) -> None:
 
     from actfold_b200 import workloads as W
 
-    d = W.LLADA_8B
+    d = base_dims(a)
     dims = LLaDADims(a.layers or d.n_layers, d.hidden, d.n_heads, d.n_kv_heads, d.head_dim, d.ffn, d.vocab, d.rms_eps, d.rope_theta)
     s = CpuSample(dims, a.seq, a.children, a.tau)
     for _ in range(min(max(1, a.warmup), 2)):
@@ -173,12 +209,13 @@ def run_reference(a, rank: int) -> None:
     ts = [s.time_pass()[0] for _ in range(n_samples)]
     t = statistics.median(ts)
     value = a.children * a.seq / t
-    sample = (f"median of {n_samples} samples of one LLaDA-8B block (T={a.seq}, numpy f32 BLAS, all host threads) + gate "
+    arch = "LLaDA-8B" if a.model == "llada8b" else "Dream-7B"
+    sample = (f"median of {n_samples} samples of one {arch} block (T={a.seq}, numpy f32 BLAS, all host threads) + gate "
               f"+ merge + LM head on a {s.vs}-column vocabulary slice, extrapolated to {a.children} children x "
               f"{dims.n_layers} layers per pass")
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": metric_of(a),
         "value": value,
         "unit": UNIT,
         "n_gpus": a.gpus,
@@ -226,10 +263,10 @@ def main() -> None:
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    base = W.LLADA_8B
+    base = base_dims(a)
     dims = base if a.layers is None else W.ModelDims(a.layers, base.hidden, base.n_heads, base.n_kv_heads, base.head_dim, base.ffn, base.vocab, base.rms_eps, base.rope_theta, base.mask_id)
     model = LLaDAModel.random(dims, seed=1234, device=dev, max_pos=max(a.seq, 1024))
-    parent_np, _ = W.llada_tokens(a.seq, 256, 0.5, 1, 1, dims.mask_id, seed=42)
+    parent_np, _ = W.llada_tokens(a.seq, 256, MODEL_DEFAULTS[a.model]["mask_fraction"], 1, 1, dims.mask_id, seed=42)
     children_np = W.llada_children(parent_np, a.children, a.d, dims.mask_id, seed=1000 + rank)
 
     # ---- parent pass (rank 0) + broadcast of the parent cache
@@ -393,13 +430,13 @@ def main() -> None:
             "unit": UNIT,
             "cores": cs.threads,
             "kind": "port",
-            "sample": f"one LLaDA-8B block on {a.seq} rows + gate + merge + LM head on a {cs.vs}-column vocab slice "
+            "sample": f"one {'LLaDA-8B' if a.model == 'llada8b' else 'Dream-7B'} block on {a.seq} rows + gate + merge + LM head on a {cs.vs}-column vocab slice "
                       f"(numpy f32 BLAS, all host threads), extrapolated to {a.children} children x {L} layers",
         }
 
     if rank == 0:
         line = {
-            "metric": METRIC,
+            "metric": metric_of(a),
             "value": value,
             "unit": UNIT,
             "n_gpus": world,
