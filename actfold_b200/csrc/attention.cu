@@ -437,5 +437,9 @@ extern "C" int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsr
   p.n_kv_heads = n_kv_heads;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = reinterpret_cast<unsigned*>(status);
+  // A plain stream-ordered launch (no programmatic dependency): every earlier
+  // kernel of the stream has finished when it starts, so the parent K/V may be
+  // loaded at kernel entry.
+  p.kv_static = 1;
   return attention_run(p, as_stream(stream));
 }

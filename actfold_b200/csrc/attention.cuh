@@ -29,6 +29,8 @@ struct AttnParams {
   int n_heads, n_kv_heads;
   float scale_log2;  // softmax scale * log2(e)
   int pdl;           // 1: programmatic dependent launch (the kernel waits for its predecessor)
+  int kv_static;     // 1: pk / pv are not written by the preceding kernels (a cached parent), so the
+                     //    tcgen05 kernel loads them by TMA before it waits for its predecessor
   unsigned* status;  // nullable: AF_STATUS_TIMEOUT is ORed in when a bounded wait runs out
 };
 

@@ -9,7 +9,9 @@
 // (3 x 128 columns, plus 128 for O = the whole 512-column TMEM), so the
 // softmax is exact in two sweeps per row (max, then exp / sum) and O is never
 // rescaled:
-//   1. cp.async Q, K_j, V_j into 128-byte-swizzled shared tiles;
+//   1. Q, K_j, V_j into 128-byte-swizzled shared tiles: a cached parent's
+//      K / V blocks by TMA, issued before the programmatic-dependency wait
+//      (they do not depend on the preceding kernel), the rest by cp.async;
 //   2. S_j = Q K_j^T (tcgen05.mma, bf16 -> fp32 TMEM, K-major operands);
 //   3. each thread masks its row, finds the max over its blocks, writes
 //      P_j = exp2(S_j - max) in bf16 over K_j's tiles and sums the row;
@@ -18,6 +20,9 @@
 //      combined across the cluster through distributed shared memory.
 // Every mbarrier wait is bounded; a timeout sets AF_STATUS_TIMEOUT.
 #include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "attention.cuh"
 #include "tc_common.cuh"
@@ -36,7 +41,7 @@ constexpr int kOffQ = 0;
 constexpr int kOffKP = kOffQ + kOpB;              // K_j, overwritten by P_j
 constexpr int kOffV = kOffKP + kMaxBlk * kOpB;
 constexpr int kOffF = kOffV + kMaxBlk * kOpB;      // child of each candidate key [3][128]
-constexpr int kOffBar = kOffF + kMaxBlk * kTK * 4;  // barS, barO, fail flag
+constexpr int kOffBar = kOffF + kMaxBlk * kTK * 4;  // barS, barO, TMEM slot, fail flag, barK, barV
 constexpr int kSmemTc = kOffBar + 64 + 1024;        // + alignment slack
 
 // Byte offset of 16-byte chunk `ch` (0..7) of row `row` in a swizzled tile.
@@ -68,24 +73,28 @@ __device__ __forceinline__ void load_op(uint32_t dst, RowPtr row_ptr, const void
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const AttnParams p) {
+__global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_constant__ CUtensorMap tmK,
+                                                              const __grid_constant__ CUtensorMap tmV,
+                                                              const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   pdl_trigger();
-  pdl_wait();
-  const int n_q = p.n_q_dev ? min(*p.n_q_dev, p.n_q_cap) : p.n_q_cap;
   const int q0 = blockIdx.x * kTQ;
-  if (q0 >= n_q) return;  // uniform over a cluster (its CTAs share blockIdx.x)
   const int h = blockIdx.y;
   const int ns = gridDim.z, split = blockIdx.z;
   const int kvh = h / (p.n_heads / p.n_kv_heads);
-  const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = warp & 3, cg = warp >> 2;  // TMEM lane quadrant, 32-column group
   const int r = 32 * qd + lane;             // this thread's query row (TMEM lane)
   const int c0 = 32 * cg;                   // its 32 key (then head-dim) columns
-  const int n_pb = (p.T + kTK - 1) / kTK, n_fb = (n_f + kTK - 1) / kTK, nb = n_pb + n_fb;
+  // Key blocks: the T parent keys, then the candidate keys. The split over the
+  // cluster counts candidate blocks by capacity, so every CTA knows its parent
+  // blocks (the first n_par of its blocks) before its predecessor finishes.
+  const int n_pb = (p.T + kTK - 1) / kTK;
+  const int n_fb = p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0, nb = n_pb + n_fb;
   const int b_lo = split * nb / ns, b_hi = (split + 1) * nb / ns;  // balanced, at most kMaxBlk
   const int nbl = b_hi - b_lo;
+  const int n_par = max(0, min(b_hi, n_pb) - b_lo);
+  const bool kv_tma = p.kv_static != 0 && n_par > 0;
 
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -93,19 +102,48 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const AttnParams p
   const uint32_t sQ = base + kOffQ, sKP = base + kOffKP, sV = base + kOffV;
   int* sF = reinterpret_cast<int*>(gb + kOffF);
   float* red = reinterpret_cast<float*>(gb + kOffQ);  // [2][4][128] row max / sum partials, after S is done
-  const uint32_t barS = base + kOffBar, barO = barS + 8;
+  const uint32_t barS = base + kOffBar, barO = barS + 8, barK = barS + 32, barV = barS + 40;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + kOffBar + 16);
   volatile int* fail = reinterpret_cast<volatile int*>(gb + kOffBar + 24);
 
   if (tid == 0) {
     mbar_init(barS, 1);
     mbar_init(barO, 1);
+    mbar_init(barK, 1);
+    mbar_init(barV, 1);
     *fail = 0;
     fence_barrier_init();
+    if (kv_tma) {
+      // Parent K / V blocks: two 64-column boxes of 128 keys each, swizzled
+      // like the cp.async tiles; rows past T are zero-filled by the TMA unit.
+      const uint32_t bytes = (uint32_t)n_par * kOpB;
+      mbar_arrive_expect_tx(barK, bytes);
+      mbar_arrive_expect_tx(barV, bytes);
+      for (int j = 0; j < n_par; ++j) {
+        const int y = (b_lo + j) * kTK;
+        for (int hf = 0; hf < 2; ++hf) {
+          tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmK, barK, kvh * 128 + 64 * hf, y);
+          tma_load_2d(sV + j * kOpB + hf * kTileB, &tmV, barV, kvh * 128 + 64 * hf, y);
+        }
+      }
+    }
   }
+  pdl_wait();
+  const int n_q = p.n_q_dev ? min(*p.n_q_dev, p.n_q_cap) : p.n_q_cap;
+  if (q0 >= n_q) {  // uniform over a cluster (its CTAs share blockIdx.x)
+    // Nothing to compute; TMA writes into this CTA's shared memory land before it exits.
+    if (tid == 0 && kv_tma) {
+      volatile int no_abort = 0;
+      mbar_wait(barK, 0, &no_abort);
+      mbar_wait(barV, 0, &no_abort);
+    }
+    __syncthreads();
+    return;
+  }
+  const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
   if (warp == 0) tmem_alloc(smem_u32(tmem_slot), 512);
 
-  // ---- operands ----
+  // ---- operands (cp.async): Q rows, candidate blocks, and parent blocks without TMA ----
   load_op(sQ, [&](int rr) -> const __nv_bfloat16* {
     const int qi = q0 + rr;
     if (qi >= n_q) return nullptr;
@@ -114,6 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const AttnParams p
   for (int j = 0; j < nbl; ++j) {
     const int b = b_lo + j;
     const bool parent_blk = b < n_pb;
+    if (parent_blk && kv_tma) continue;
     const int r0 = (parent_blk ? b : b - n_pb) * kTK;
     const int lim = parent_blk ? p.T : n_f;
     const __nv_bfloat16* kb = parent_blk ? p.pk : p.fk;
@@ -140,15 +179,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const AttnParams p
 
   // ---- S_j = Q K_j^T ----
   if (tid == 0 && nbl > 0) {
+    bool k_ok = true;
+    if (kv_tma) {
+      volatile int no_abort = 0;
+      k_ok = mbar_wait(barK, 0, &no_abort);
+      if (!k_ok) *fail = 1;
+      tc_fence_after();
+    }
     const uint32_t idesc = idesc_bf16(kTQ, kTK);
-    for (int j = 0; j < nbl; ++j)
+    for (int j = 0; j < nbl && k_ok; ++j)
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t half = (uint32_t)(kk >> 2) * kTileB;
         tc_mma_bf16(tmem + (uint32_t)(j * kTK), sw128_desc(sQ + half) + 2 * (kk & 3),
                     sw128_desc(sKP + j * kOpB + half) + 2 * (kk & 3), idesc, kk > 0 ? 1u : 0u);
       }
-    tc_commit(barS);
+    tc_commit(barS);  // also when nothing was issued, so the waits below end
   }
 
   // ---- masked softmax: row r, key columns c0..c0+31 of every block ----
@@ -223,9 +269,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const AttnParams p
 
   // ---- O = sum_j P_j V_j ----
   const bool have_o = nbl > 0 && !s_bad;
+  bool v_ok = true;
+  if (tid == 0 && kv_tma) {  // also on the failure paths: the V loads land before the CTA moves on
+    volatile int no_abort = 0;
+    v_ok = mbar_wait(barV, 0, &no_abort);
+    if (!v_ok) *fail = 1;
+    tc_fence_after();
+  }
   if (tid == 0 && have_o) {
     const uint32_t idesc = idesc_bf16_bmn(kTQ, 128);
-    for (int j = 0; j < nbl; ++j)
+    for (int j = 0; j < nbl && v_ok; ++j)
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint64_t a = sw128_desc(sKP + j * kOpB + (uint32_t)(kk >> 2) * kTileB) + 2 * (kk & 3);
@@ -333,10 +386,42 @@ int attention_tc_splits(const AttnParams& p) {
   const int nb = (p.T + kTK - 1) / kTK + (p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0);
   const int need = (nb + kMaxBlk - 1) / kMaxBlk;
   if (need > 8) return 0;
+  // The slowest CTA (most key blocks) sets the time; among the split counts
+  // that fit one wave, take the fewest that reach the smallest per-CTA block
+  // count: more splits at the same maximum only add CTAs to wait on and
+  // partials to combine.
   const int ctas = (p.n_q_cap + kTQ - 1) / kTQ * p.n_heads;
   int ns = need;
   while (ns < 8 && ns < nb && (ns + 1) * ctas <= sm_count()) ++ns;
+  const int most = (nb + ns - 1) / ns;
+  while (ns > need && (nb + ns - 2) / (ns - 1) == most) --ns;
   return ns;
+}
+
+// Tensor maps of a cached parent's K or V ([T keys, n_kv_heads * 128] columns
+// of a row-major buffer with row stride ld), reused across passes: the parent
+// cache keeps its buffers for its lifetime.
+static int kv_tmap(CUtensorMap* map, const __nv_bfloat16* base, int T, int cols, int64_t ld) {
+  struct Entry {
+    const void* base;
+    int T, cols;
+    int64_t ld;
+    CUtensorMap map;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : cache)
+    if (e.base == base && e.T == T && e.cols == cols && e.ld == ld) {
+      *map = e.map;
+      return AF_OK;
+    }
+  Entry e{base, T, cols, ld, {}};
+  if (int st = make_tmap_bf16(&e.map, base, (uint64_t)T, (uint64_t)cols, (uint64_t)ld, 128)) return st;
+  if (cache.size() >= 512) cache.erase(cache.begin());
+  cache.push_back(e);
+  *map = e.map;
+  return AF_OK;
 }
 
 int attention_tc_run(const AttnParams& p, int ns, cudaStream_t s) {
@@ -345,8 +430,16 @@ int attention_tc_run(const AttnParams& p, int ns, cudaStream_t s) {
     cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
     attr = true;
   }
+  CUtensorMap tk, tv;
+  memset(&tk, 0, sizeof(tk));
+  memset(&tv, 0, sizeof(tv));
+  if (p.kv_static) {
+    const int cols = p.n_kv_heads * 128;
+    if (int st = kv_tmap(&tk, p.pk, p.T, cols, p.kv_ld)) return st;
+    if (int st = kv_tmap(&tv, p.pv, p.T, cols, p.kv_ld)) return st;
+  }
   cudaError_t e = launch_ex(k_attention_tc, dim3((p.n_q_cap + kTQ - 1) / kTQ, p.n_heads, ns), dim3(kThreads, 1, 1),
-                            (size_t)kSmemTc, s, p.pdl != 0, dim3(1, 1, ns), p);
+                            (size_t)kSmemTc, s, p.pdl != 0, dim3(1, 1, ns), tk, tv, p);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("attention_tc: launch: ") + cudaGetErrorString(e));
   return check_launch("attention_tc");
 }

@@ -117,6 +117,9 @@ __device__ __forceinline__ uint4 ldg16(const void* p) {
   return r;
 }
 
+// Pull the 128-byte line holding `p` into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ void stg16(void* p, const uint4& v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");

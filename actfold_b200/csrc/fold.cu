@@ -976,6 +976,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.n_kv_heads = p->model.dims.n_kv_heads;
     ap.scale_log2 = (1.0f / sqrtf(128.f)) * 1.4426950408889634f;
     ap.pdl = pass_pdl() ? 1 : 0;
+    ap.kv_static = 1;  // the parent's K/V are fixed for the whole pass
     ap.status = w.status;
     AF_TIMED(FK_ATTN, if ((st = attention_run(ap, s))) return st);
 

@@ -78,60 +78,103 @@ __device__ __forceinline__ uint4 pack8(const float* y) {
   return o;
 }
 
-// Epilogue of 8 consecutive tile rows r0..r0+7 (r0 % 8 == 0) for token gm: `a`
-// holds their fp32 sums, `b` those of rows r0 ^ 64 (the RoPE rotation partner
-// and the SwiGLU up rows). Writes one 16-byte vector; returns the sum of the
-// bf16 outputs (EPI_STORE) for the logit row sums.
-__device__ __forceinline__ float epi_chunk(const GemmDev& p, int n0, int r0, int gm, const float* a, const float* b) {
-  const int64_t orow = p.out_rows ? p.out_rows[gm] : gm;
+// Epilogues of 8 consecutive tile rows r0..r0+7 (r0 % 8 == 0) of one token,
+// written as one 16-byte vector to output row `orow`. `a` holds the rows' fp32
+// sums; `b` those of rows r0 ^ 64 (the RoPE rotation partner, the SwiGLU up
+// rows). Every global operand (residual vector, RoPE cos/sin) is loaded by the
+// caller ahead of the split-K reduction, so its latency overlaps the reads of
+// the peer partial tiles.
+
+// Plain store; returns the sum of the bf16 outputs (logit row sums).
+__device__ __forceinline__ float epi_store(const GemmDev& p, int n0, int r0, int64_t orow, const float* a) {
   float y[8];
   float rs = 0.f;
-  if (p.epi == EPI_STORE) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      y[i] = bf(a[i]);
-      rs += y[i];
-    }
-    stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
-  } else if (p.epi == EPI_RESIDUAL) {
-    const int64_t rrow = p.res_rows ? p.res_rows[gm] : gm;
-    float rv[8];
-    unpack<AF_DTYPE_BF16>(ldg16(p.res + rrow * p.ldr + n0 + r0), rv);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(rv[i], bf(a[i]));
-    stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
-  } else if (p.epi == EPI_SWIGLU) {
-    if (r0 < 64) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float g = bf(a[i]), u = bf(b[i]);
-        const float silu = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
-        y[i] = __fmul_rn(silu, u);
-      }
-      stg16(p.out + orow * p.ldo + (n0 >> 1) + r0, pack8(y));
-    }
-  } else {  // EPI_ROPE
-    const int n = n0 + r0;
-    if (n < p.rope_cols) {
-      const int pos = p.positions[gm];
-      const int i0 = r0 & (p.half_dim - 1);
-      float cs[8], sn[8];
-      load8(p.rope_cos + (int64_t)pos * p.half_dim + i0, cs);
-      load8(p.rope_sin + (int64_t)pos * p.half_dim + i0, sn);
-      const bool second = (r0 & p.half_dim) != 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float x = bf(a[i]), other = bf(b[i]);
-        y[i] = second ? __fadd_rn(__fmul_rn(x, cs[i]), __fmul_rn(other, sn[i]))
-                      : __fsub_rn(__fmul_rn(x, cs[i]), __fmul_rn(other, sn[i]));
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = bf(a[i]);
-    }
-    stg16(p.out + orow * p.ldo + n, pack8(y));
+  for (int i = 0; i < 8; ++i) {
+    y[i] = bf(a[i]);
+    rs += y[i];
   }
+  stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
   return rs;
+}
+
+// out = bf16(bf16(acc) + residual), residual vector `rv` (8 bf16).
+__device__ __forceinline__ void epi_residual(const GemmDev& p, int n0, int r0, int64_t orow, const uint4& rv,
+                                             const float* a) {
+  float r[8], y[8];
+  unpack<AF_DTYPE_BF16>(rv, r);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(r[i], bf(a[i]));
+  stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
+}
+
+// out[:, (n0 >> 1) + r0 ..] = silu(bf16(gate)) * bf16(up) for gate rows r0 < 64.
+__device__ __forceinline__ void epi_swiglu(const GemmDev& p, int n0, int r0, int64_t orow, const float* a,
+                                           const float* b) {
+  float y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float g = bf(a[i]), u = bf(b[i]);
+    const float silu = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+    y[i] = __fmul_rn(silu, u);
+  }
+  stg16(p.out + orow * p.ldo + (n0 >> 1) + r0, pack8(y));
+}
+
+// Rotary embedding of the 8 rows (half-dimension 64, rotation partner r0 ^ 64);
+// `cs` / `sn` hold cos / sin of the token's position at i0 = r0 & 63.
+__device__ __forceinline__ void epi_rope(const GemmDev& p, int n0, int r0, int64_t orow, const float* a,
+                                         const float* b, const float* cs, const float* sn) {
+  float y[8];
+  const bool second = (r0 & p.half_dim) != 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float x = bf(a[i]), other = bf(b[i]);
+    y[i] = second ? __fadd_rn(__fmul_rn(x, cs[i]), __fmul_rn(other, sn[i]))
+                  : __fsub_rn(__fmul_rn(x, cs[i]), __fmul_rn(other, sn[i]));
+  }
+  stg16(p.out + orow * p.ldo + n0 + r0, pack8(y));
+}
+
+// Global operands of one (token, chunk pair) unit: rows r0 = 8c and 8c + 64.
+struct EpiOperands {
+  uint4 ra, rb;         // residual vectors (EPI_RESIDUAL)
+  float cs[8], sn[8];   // RoPE cos / sin (EPI_ROPE, rotated columns); shared by both rows
+};
+
+__device__ __forceinline__ void epi_operands(const GemmDev& p, int n0, int c, int rrow, int pos, EpiOperands& o) {
+  if (p.epi == EPI_RESIDUAL) {
+    const __nv_bfloat16* rp = p.res + (int64_t)rrow * p.ldr + n0 + 8 * c;
+    o.ra = ldg16(rp);
+    o.rb = ldg16(rp + 64);
+  } else if (p.epi == EPI_ROPE && n0 < p.rope_cols) {
+    const int i0 = (8 * c) & (p.half_dim - 1);
+    load8(p.rope_cos + (int64_t)pos * p.half_dim + i0, o.cs);
+    load8(p.rope_sin + (int64_t)pos * p.half_dim + i0, o.sn);
+  }
+}
+
+// Both rows of a unit: r0 = 8c with partner rows `b`, and r0 + 64 with partner `a`.
+__device__ __forceinline__ void epi_pair(const GemmDev& p, int n0, int c, int64_t orow, const EpiOperands& o,
+                                         const float* a, const float* b) {
+  const int r0 = 8 * c;
+  if (p.epi == EPI_RESIDUAL) {
+    epi_residual(p, n0, r0, orow, o.ra, a);
+    epi_residual(p, n0, r0 + 64, orow, o.rb, b);
+  } else if (p.epi == EPI_SWIGLU) {
+    epi_swiglu(p, n0, r0, orow, a, b);
+  } else if (p.epi == EPI_ROPE) {
+    if (n0 < p.rope_cols) {
+      epi_rope(p, n0, r0, orow, a, b, o.cs, o.sn);
+      epi_rope(p, n0, r0 + 64, orow, b, a, o.cs, o.sn);
+    } else {
+      epi_store(p, n0, r0, orow, a);
+      epi_store(p, n0, r0 + 64, orow, b);
+    }
+  } else {
+    epi_store(p, n0, r0, orow, a);
+    epi_store(p, n0, r0 + 64, orow, b);
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmW,
@@ -181,6 +224,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * stage_bytes + 16 * S + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 16);
   volatile int* issued_slot = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 24);
+  // Per-token epilogue metadata (output row, residual row, RoPE position).
+  int* s_orow = reinterpret_cast<int*>(gbase + S * stage_bytes + 16 * S + 64);
+  int* s_rrow = s_orow + p.ntok;
+  int* s_pos = s_rrow + p.ntok;
 
   uint32_t ncols = 32;
   while ((int)ncols < p.ntok) ncols <<= 1;
@@ -255,6 +302,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     // ---------------- TMEM -> shared memory (128 threads, one tile row each) ----------------
     const int q = warp & 3;
     const int r = 32 * q + lane;
+    // While the ring streams: per-token metadata into shared memory, and the
+    // epilogue's global operands (residual rows, RoPE cos/sin rows) into L2.
+    for (int m = threadIdx.x - 64; m < Mv; m += kThreads - 64) {
+      const int gm = m0 + m;
+      s_orow[m] = p.out_rows ? p.out_rows[gm] : gm;
+      if (p.epi == EPI_RESIDUAL) {
+        const int rrow = p.res_rows ? p.res_rows[gm] : gm;
+        s_rrow[m] = rrow;
+        const char* rp = reinterpret_cast<const char*>(p.res + (int64_t)rrow * p.ldr + n0);
+        prefetch_l2(rp);
+        prefetch_l2(rp + 128);
+        prefetch_l2(rp + 255);
+      } else if (p.epi == EPI_ROPE) {
+        const int pos = p.positions[gm];
+        s_pos[m] = pos;
+        if (n0 < p.rope_cols) {
+          const char* cp = reinterpret_cast<const char*>(p.rope_cos + (int64_t)pos * p.half_dim);
+          const char* sp = reinterpret_cast<const char*>(p.rope_sin + (int64_t)pos * p.half_dim);
+          for (int o = 0; o < p.half_dim * 4; o += 128) {
+            prefetch_l2(cp + o);
+            prefetch_l2(sp + o);
+          }
+        }
+      }
+    }
     if (!mbar_wait(accb, 0, abort_flag)) {
       atomicOr(p.status, AF_STATUS_TIMEOUT);
       *abort_flag = 1;
@@ -275,33 +347,45 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   __syncthreads();
   const bool ok = !*abort_flag;
 
-  const bool partner = p.epi == EPI_SWIGLU || p.epi == EPI_ROPE;
   if (p.splits == 1) {
-    // ---------------- epilogue: 16 chunks of 8 rows per token, all threads ----------------
-    // Warp-uniform loop: a warp's lanes 0-15 and 16-31 cover the 16 chunks of
-    // two tokens, so the logit row sums reduce over half-warps.
-    if (ok) {
-      const int total = Mv * (kTileN / 8);
-      for (int base_ch = warp * 32; base_ch < total; base_ch += kThreads) {
-        const int ch = base_ch + lane;
-        const bool valid = ch < total;
+    if (ok && p.epi == EPI_SWIGLU) {
+      // ---------------- SwiGLU: one unit per (token, gate chunk), all threads ----------------
+      const int total = Mv * 8;
+      for (int u = threadIdx.x; u < total; u += kThreads) {
+        const int m = u >> 3, r0 = 8 * (u & 7);
+        float a[8], b[8];
+        load8(tile + m * kLdt + r0, a);
+        load8(tile + m * kLdt + r0 + 64, b);
+        epi_swiglu(p, n0, r0, s_orow[m], a, b);
+      }
+    } else if (ok) {
+      // ---------------- units (token m, chunk pair c / c + 8), warp-uniform loop ----------------
+      // Lanes 8k..8k+7 of a warp cover the 8 units of one token, so the logit
+      // row sums reduce over groups of 8 lanes.
+      const int total = Mv * 8;
+      for (int base_u = warp * 32; base_u < total; base_u += kThreads) {
+        const int u = base_u + lane;
+        const bool valid = u < total;
+        const int m = u >> 3, c = u & 7;
         float rs = 0.f;
         if (valid) {
-          const int m = ch >> 4, r0 = 8 * (ch & 15);
+          EpiOperands o;
+          epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
           float a[8], b[8];
-          load8(tile + m * kLdt + r0, a);
-          if (partner) load8(tile + m * kLdt + (r0 ^ 64), b);
-          rs = epi_chunk(p, n0, r0, m0 + m, a, b);
+          load8(tile + m * kLdt + 8 * c, a);
+          load8(tile + m * kLdt + 8 * c + 64, b);
+          if (p.epi == EPI_STORE) {
+            rs = epi_store(p, n0, 8 * c, s_orow[m], a);
+            rs += epi_store(p, n0, 8 * c + 64, s_orow[m], b);
+          } else {
+            epi_pair(p, n0, c, s_orow[m], o, a, b);
+          }
         }
         if (p.row_sums) {
           rs += __shfl_xor_sync(0xffffffffu, rs, 1);
           rs += __shfl_xor_sync(0xffffffffu, rs, 2);
           rs += __shfl_xor_sync(0xffffffffu, rs, 4);
-          rs += __shfl_xor_sync(0xffffffffu, rs, 8);
-          if (valid && (lane & 15) == 0) {
-            const int gm = m0 + (ch >> 4);
-            atomicAdd(p.row_sums + (p.out_rows ? p.out_rows[gm] : gm), rs);
-          }
+          if (valid && (lane & 7) == 0) atomicAdd(p.row_sums + s_orow[m], rs);
         }
       }
     }
@@ -312,27 +396,42 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     // Units of work: (token m, chunk pair c / c + 8), i.e. rows 8c..8c+7 and
     // their partners 64+8c..64+8c+7; CTA j of the cluster takes a contiguous
     // share of the Mv * 8 units and sums them over all CTAs in a fixed order.
+    // Per unit the global operands are requested first, then every peer's
+    // partial sums (up to 4 peers in flight), so their latencies overlap.
     const int j = blockIdx.y, Sp = p.splits;
     const int units = Mv * 8;
     const int lo = (j * units) / Sp, hi = ((j + 1) * units) / Sp;
     if (ok) {
       for (int u = lo + threadIdx.x; u < hi; u += kThreads) {
         const int m = u >> 3, c = u & 7;
+        EpiOperands o;
+        epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
         const uint32_t oa = base + (uint32_t)((m * kLdt + 8 * c) * 4);
         const uint32_t ob = oa + 64 * 4;
         float sa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, sb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int src = 0; src < Sp; ++src) {
-          const float4 a0 = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
-          const float4 a1 = ld_cluster_f4(cluster_map(oa + 16, (uint32_t)src));
-          const float4 b0 = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
-          const float4 b1 = ld_cluster_f4(cluster_map(ob + 16, (uint32_t)src));
-          sa[0] += a0.x; sa[1] += a0.y; sa[2] += a0.z; sa[3] += a0.w;
-          sa[4] += a1.x; sa[5] += a1.y; sa[6] += a1.z; sa[7] += a1.w;
-          sb[0] += b0.x; sb[1] += b0.y; sb[2] += b0.z; sb[3] += b0.w;
-          sb[4] += b1.x; sb[5] += b1.y; sb[6] += b1.z; sb[7] += b1.w;
+        for (int s0 = 0; s0 < Sp; s0 += 4) {
+          float4 v[4][4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (s0 + q < Sp) {
+              const uint32_t src = (uint32_t)(s0 + q);
+              v[q][0] = ld_cluster_f4(cluster_map(oa, src));
+              v[q][1] = ld_cluster_f4(cluster_map(oa + 16, src));
+              v[q][2] = ld_cluster_f4(cluster_map(ob, src));
+              v[q][3] = ld_cluster_f4(cluster_map(ob + 16, src));
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (s0 + q < Sp) {
+              sa[0] += v[q][0].x; sa[1] += v[q][0].y; sa[2] += v[q][0].z; sa[3] += v[q][0].w;
+              sa[4] += v[q][1].x; sa[5] += v[q][1].y; sa[6] += v[q][1].z; sa[7] += v[q][1].w;
+              sb[0] += v[q][2].x; sb[1] += v[q][2].y; sb[2] += v[q][2].z; sb[3] += v[q][2].w;
+              sb[4] += v[q][3].x; sb[5] += v[q][3].y; sb[6] += v[q][3].z; sb[7] += v[q][3].w;
+            }
+          }
         }
-        epi_chunk(p, n0, 8 * c, m0 + m, sa, sb);
-        epi_chunk(p, n0, 8 * c + 64, m0 + m, sb, sa);
+        epi_pair(p, n0, c, s_orow[m], o, sa, sb);
       }
     }
     __syncwarp();
@@ -449,8 +548,11 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   st = std::max(2, std::min(16, st));
   const int tile_bytes = g.ntok * kLdt * 4;  // fp32 staging of the accumulator
   while (st * stage < tile_bytes) ++st;
+  // Ring + alignment slack + barriers/flags + per-token metadata (3 ints per token).
+  auto smem_of = [&](int stages) { return stages * stage + 1024 + 16 * stages + 64 + 12 * g.ntok; };
+  while (st > 2 && smem_of(st) > 227 * 1024 && (st - 1) * stage >= tile_bytes) --st;
   g.stages = st;
-  g.smem = st * stage + 1024 + 16 * st + 64;
+  g.smem = smem_of(st);
   return g;
 }
 
