@@ -182,32 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
-  if (threadIdx.x == 0) {
-    // Weights never depend on the preceding kernel: pull this CTA's first
-    // k-blocks into L2 while that kernel may still be finishing.
-    const int kb_first = blockIdx.y * p.kb_per_split;
-    const int nkb_cta = min(p.kb_per_split, p.nkb - kb_first);
-    const int rot = nkb_cta > 0 ? (int)(blockIdx.x % nkb_cta) : 0;
-    const int npf = min(nkb_cta, 2 * p.stages);
-    for (int i = 0; i < npf; ++i) {
-      int kb = i + rot;
-      if (kb >= nkb_cta) kb -= nkb_cta;
-      kb += kb_first;
-      if (p.w_tiled)
-        tma_prefetch_l2_3d(&tmW, 0, 0, blockIdx.x * p.nkb + kb);
-      else
-        tma_prefetch_l2_2d(&tmW, kb * kBlockK, blockIdx.x * kTileN);
-    }
-  }
-  pdl_wait();
-  int M = p.m_dev ? *p.m_dev : p.m_cap;
-  if (M > p.m_cap) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
-    M = p.m_cap;
-  }
   const int m0 = blockIdx.z * p.ntok;
-  if (m0 >= M) return;  // uniform over a cluster (all its CTAs share blockIdx.x / z)
-  const int Mv = min(p.ntok, M - m0);
   const int n0 = blockIdx.x * kTileN;
   const int kb0 = blockIdx.y * p.kb_per_split;
   const int nkb = min(p.kb_per_split, p.nkb - kb0);
@@ -229,8 +204,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   int* s_rrow = s_orow + p.ntok;
   int* s_pos = s_rrow + p.ntok;
 
-  uint32_t ncols = 32;
-  while ((int)ncols < p.ntok) ncols <<= 1;
+  // Tiles start at different k-blocks (rotation by tile index) so concurrent CTAs
+  // do not all read the same activation lines at the same time.
+  const int rot = blockIdx.x % nkb;
+  auto kb_of = [&](int i) {
+    int kb = i + rot;
+    if (kb >= nkb) kb -= nkb;
+    return kb + kb0;
+  };
+  auto load_w = [&](int i, uint32_t dst, uint32_t bar) {
+    if (p.w_tiled)
+      tma_load_3d(dst, &tmW, bar, 0, 0, blockIdx.x * p.nkb + kb_of(i));
+    else
+      tma_load_2d(dst, &tmW, bar, kb_of(i) * kBlockK, n0);
+  };
+  // Stages whose weight tile is loaded before the dependency wait.
+  const int npre = min(S, nkb);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -243,7 +232,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     fence_barrier_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
+    // Weights never depend on the preceding kernel: the first ring stages are
+    // filled with weight tiles, and the next k-blocks pulled into L2, while
+    // that kernel may still be running. Each of these stages expects its
+    // weight bytes now and is armed (arrive + activation bytes) after the wait,
+    // so it cannot complete before its activation tile has landed.
+    for (int i = 0; i < npre; ++i) {
+      mbar_expect_tx(full0 + 8 * i, w_bytes);
+      load_w(i, base + i * stage_bytes, full0 + 8 * i);
+    }
+    for (int i = npre; i < min(nkb, 2 * S); ++i) {
+      if (p.w_tiled)
+        tma_prefetch_l2_3d(&tmW, 0, 0, blockIdx.x * p.nkb + kb_of(i));
+      else
+        tma_prefetch_l2_2d(&tmW, kb_of(i) * kBlockK, n0);
+    }
   }
+  pdl_wait();
+  int M = p.m_dev ? *p.m_dev : p.m_cap;
+  if (M > p.m_cap) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
+    M = p.m_cap;
+  }
+  if (m0 >= M) {  // uniform over a cluster (all its CTAs share blockIdx.x / z)
+    // No tokens for this tile: the early weight loads land before the CTA exits.
+    if (threadIdx.x == 0) {
+      volatile int no_abort = 0;
+      for (int i = 0; i < npre; ++i) {
+        mbar_arrive(full0 + 8 * i);
+        mbar_wait(full0 + 8 * i, 0, &no_abort);
+      }
+    }
+    return;
+  }
+  const int Mv = min(p.ntok, M - m0);
+
+  uint32_t ncols = 32;
+  while ((int)ncols < p.ntok) ncols <<= 1;
+
   if (warp == 1) tmem_alloc(smem_u32(tmem_slot), ncols);
   tc_fence_before();
   __syncthreads();
@@ -254,28 +280,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
-    // Tiles start at different k-blocks (rotation by tile index) so concurrent CTAs
-    // do not all read the same activation lines at the same time.
-    const int rot = blockIdx.x % nkb;
     int i = 0;
     for (; i < nkb; ++i) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1;
-      if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) {
-        atomicOr(p.status, AF_STATUS_TIMEOUT);
-        *abort_flag = 1;
-        break;
-      }
       const uint32_t st = base + s * stage_bytes;
-      mbar_arrive_expect_tx(full0 + 8 * s, stage_bytes);
-      int kb = i + rot;
-      if (kb >= nkb) kb -= nkb;
-      kb += kb0;
-      if (p.w_tiled)
-        tma_load_3d(st, &tmW, full0 + 8 * s, 0, 0, blockIdx.x * p.nkb + kb);
-      else
-        tma_load_2d(st, &tmW, full0 + 8 * s, kb * kBlockK, n0);
-      tma_load_2d(st + w_bytes, &tmX, full0 + 8 * s, kb * kBlockK, m0);
+      if (i < npre) {
+        mbar_arrive_expect_tx(full0 + 8 * s, x_bytes);  // weight tile already requested
+      } else {
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) {
+          atomicOr(p.status, AF_STATUS_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(full0 + 8 * s, stage_bytes);
+        load_w(i, st, full0 + 8 * s);
+      }
+      tma_load_2d(st + w_bytes, &tmX, full0 + 8 * s, kb_of(i) * kBlockK, m0);
     }
     *issued_slot = i;
   } else if (warp == 1 && lane == 0) {
