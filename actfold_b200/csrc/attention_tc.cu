@@ -210,7 +210,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   uint32_t vm[kMaxBlk];  // valid keys among this thread's 32 columns of each block
   const float sc = p.scale_log2;
   if (!s_bad) {
-    for (int j = 0; j < nbl; ++j) {
+#pragma unroll
+    for (int j = 0; j < kMaxBlk; ++j) {
+      if (j >= nbl) break;
       const int b = b_lo + j;
       uint32_t v = 0;
       if (b < n_pb) {
@@ -226,22 +228,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
         }
       }
       vm[j] = v;
-      uint32_t sv[32];
-      tmem_ld32_nowait(lane_base + (uint32_t)(j * kTK + c0), sv);
-      tmem_wait_ld();
+    }
+    auto sweep1 = [&](int j, const uint32_t* sv) {
+      const uint32_t v = vm[j];
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if ((v >> i) & 1u) m = fmaxf(m, __uint_as_float(sv[i]) * sc);
+    };
+    uint32_t sa[32], sb[32];
+#pragma unroll
+    for (int jp = 0; jp < kMaxBlk; jp += 2) {
+      if (jp < nbl) {
+        tmem_ld32_nowait(lane_base + (uint32_t)(jp * kTK + c0), sa);
+        if (jp + 1 < nbl) tmem_ld32_nowait(lane_base + (uint32_t)((jp + 1) * kTK + c0), sb);
+        tmem_wait_ld();
+        sweep1(jp, sa);
+        if (jp + 1 < nbl) sweep1(jp + 1, sb);
+      }
     }
   }
   red[cg * kTQ + r] = m;
   __syncthreads();
   m = fmaxf(fmaxf(red[r], red[kTQ + r]), fmaxf(red[2 * kTQ + r], red[3 * kTQ + r]));
   if (!s_bad) {
-    for (int j = 0; j < nbl; ++j) {
-      uint32_t sv[32];
-      tmem_ld32_nowait(lane_base + (uint32_t)(j * kTK + c0), sv);
-      tmem_wait_ld();
+    auto sweep2 = [&](int j, const uint32_t* sv) {
       const uint32_t v = vm[j];
 #pragma unroll
       for (int g = 0; g < 4; ++g) {  // 8-key groups of the thread's 32 keys
@@ -249,7 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const bool ok = ((v >> (8 * g + i)) & 1u) && m != -INFINITY;
-          pv[i] = ok ? exp2f(__uint_as_float(sv[8 * g + i]) * sc - m) : 0.f;
+          // The special-function unit's exp2 (ex2.approx.ftz: relative error near
+          // 2^-22, far below the bf16 rounding of P right after); x <= 0 here.
+          float e;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__uint_as_float(sv[8 * g + i]) * sc - m));
+          pv[i] = ok ? e : 0.f;
           l += pv[i];
         }
         const int key8 = (c0 >> 3) + g;
@@ -257,6 +271,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(pack2(pv[0], pv[1])),
                      "r"(pack2(pv[2], pv[3])), "r"(pack2(pv[4], pv[5])), "r"(pack2(pv[6], pv[7]))
                      : "memory");
+      }
+    };
+    // Blocks in pairs: both TMEM loads in flight before one wait.
+    uint32_t sa[32], sb[32];
+#pragma unroll
+    for (int jp = 0; jp < kMaxBlk; jp += 2) {
+      if (jp < nbl) {
+        tmem_ld32_nowait(lane_base + (uint32_t)(jp * kTK + c0), sa);
+        if (jp + 1 < nbl) tmem_ld32_nowait(lane_base + (uint32_t)((jp + 1) * kTK + c0), sb);
+        tmem_wait_ld();
+        sweep2(jp, sa);
+        if (jp + 1 < nbl) sweep2(jp + 1, sb);
       }
     }
   }
