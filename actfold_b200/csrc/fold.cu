@@ -8,7 +8,8 @@
 //
 //   candidates  = fresh rows (+ any row the parent itself fails the gate on)
 //   k_fold_gate     gate(child row, parent row) + copy + attention RMSNorm   [CTA / candidate]
-//   k_fold_compact  divergent list, fresh-key bitmap, next layer's candidates  [1 CTA]
+//   (compaction)    divergent list, fresh-key bitmap, next layer's candidates: a side task of
+//                   the QKV GEMM's epilogue warps (compact.cuh)
 //   QKV GEMM (+RoPE) on candidates           (tcgen05)
 //   attention of divergent rows over parent K/V + fresh K/V
 //   O GEMM + residual, RMSNorm, gate/up GEMM + SwiGLU, down GEMM + residual
@@ -27,6 +28,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "compact.cuh"
 #include "gate_row.cuh"
 #include "gemm_tc.cuh"
 
@@ -264,77 +266,6 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
     if (j < nvec) stg16(xc + 16 * j, hv[i]);
   }
   rmsnorm_regs<NV>(hv, nvec, g.H, g.norm_w, g.eps, reinterpret_cast<char*>(g.a + (int64_t)r * g.H), tid, rows);
-}
-
-// ----------------------------------------------------------------------------
-// Divergent compaction + fresh-key bitmap + next layer's candidates (1 CTA).
-// ----------------------------------------------------------------------------
-struct CompactArgs {
-  int C, T, m_cap, bits_ld;
-  const int* n_cand;
-  const uint8_t* stable;
-  const int* cand_child;
-  const int* cand_pos;
-  int* div_cand;
-  int* div_child;
-  int* div_pos;
-  int* n_div;
-  int* div_count;       // [C] divergent rows per child
-  unsigned* bits;       // [C, bits_ld] candidates of this layer (fresh keys)
-  unsigned* final_bits; // nullable: divergent rows of this layer (last layer only)
-  float* zero_f;        // nullable: buffer zeroed here (logit row sums, last layer)
-  int zero_n;
-  int write_next;
-  int* next_child;
-  int* next_pos;
-  int* next_src;
-  int* next_n_cand;
-};
-
-__global__ void __launch_bounds__(1024) k_fold_compact(const CompactArgs a) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ int wbuf[32];
-  const int nb = a.C * a.bits_ld;
-  for (int i = threadIdx.x; i < nb; i += 1024) {
-    a.bits[i] = 0u;
-    if (a.final_bits) a.final_bits[i] = 0u;
-  }
-  for (int i = threadIdx.x; i < a.C; i += 1024) a.div_count[i] = 0;
-  if (a.zero_f)
-    for (int i = threadIdx.x; i < a.zero_n; i += 1024) a.zero_f[i] = 0.f;
-  __syncthreads();
-  const int n = min(*a.n_cand, a.m_cap);
-  int base = 0, total;
-  for (int r0 = 0; r0 < n || r0 == 0; r0 += 1024) {
-    const int r = r0 + threadIdx.x;
-    int c = 0, t = 0, d = 0;
-    if (r < n) {
-      c = a.cand_child[r];
-      t = a.cand_pos[r];
-      atomicOr(&a.bits[c * a.bits_ld + (t >> 5)], 1u << (t & 31));
-      d = a.stable[r] ? 0 : 1;
-    }
-    const int rank = base + block_scan_1024(d, wbuf, &total);
-    if (d) {
-      a.div_cand[rank] = r;
-      a.div_child[rank] = c;
-      a.div_pos[rank] = c * a.T + t;
-      atomicAdd(&a.div_count[c], 1);
-      if (a.final_bits) atomicOr(&a.final_bits[c * a.bits_ld + (t >> 5)], 1u << (t & 31));
-      if (a.write_next) {
-        a.next_child[rank] = c;
-        a.next_pos[rank] = t;
-        a.next_src[rank] = rank;
-      }
-    }
-    base += total;
-    if (r0 + 1024 >= n) break;
-  }
-  if (threadIdx.x == 0) {
-    *a.n_div = base;
-    if (a.write_next) *a.next_n_cand = base;
-  }
 }
 
 // ----------------------------------------------------------------------------
@@ -929,9 +860,12 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     a.next_pos = w.cand_pos + (int64_t)(l + 1) * M;
     a.next_src = w.cand_src + (int64_t)(l + 1) * M;
     a.next_n_cand = w.n_cand + l + 1;
-    AF_TIMED(FK_COMPACT, AF_LAUNCH(k_fold_compact, 1, 1024, 0, s, a));
 
+    // The QKV GEMM runs the compaction in the epilogue warps of one CTA while
+    // its weights stream (all consumers come after it).
     GemmCall c = base_call(w.status);
+    c.has_side = 1;
+    c.side = a;
     c.x = w.A;
     c.ldx = z.H;
     c.m_cap = M;

@@ -55,6 +55,8 @@ struct GemmDev {
   int rope_cols, half_dim;
   unsigned* status;
   float* row_sums;
+  int has_side;  // CTA (0, 0, 0) runs `side` (the layer compaction) in its epilogue warps
+  CompactArgs side;
 };
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -206,6 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   int* s_orow = reinterpret_cast<int*>(gbase + S * stage_bytes + 16 * S + 64);
   int* s_rrow = s_orow + p.ntok;
   int* s_pos = s_rrow + p.ntok;
+  int* s_scan = s_pos + p.ntok;  // 32 ints: the side task's scan buffer
+  const bool side_cta = p.has_side && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
 
   // Tiles start at different k-blocks (rotation by tile index) so concurrent CTAs
   // do not all read the same activation lines at the same time.
@@ -258,7 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     M = p.m_cap;
   }
   if (m0 >= M) {  // uniform over a cluster (all its CTAs share blockIdx.x / z)
-    // No tokens for this tile: the early weight loads land before the CTA exits.
+    // No tokens for this tile (none at all for CTA (0, 0, 0)): the side task
+    // still runs, with every thread of the CTA.
+    if (side_cta) compact_rows<kThreads>(p.side, s_scan, threadIdx.x, 1);
+    // The early weight loads land before the CTA exits.
     if (threadIdx.x == 0) {
       volatile int no_abort = 0;
       for (int i = 0; i < npre; ++i) {
@@ -326,8 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     // ---------------- TMEM -> shared memory (128 threads, one tile row each) ----------------
     const int q = warp & 3;
     const int r = 32 * q + lane;
-    // While the ring streams: per-token metadata into shared memory, and the
-    // epilogue's global operands (residual rows, RoPE cos/sin rows) into L2.
+    // While the ring streams: the side task, per-token metadata into shared
+    // memory, and the epilogue's global operands (residual rows, RoPE cos/sin
+    // rows) into L2.
+    if (side_cta) compact_rows<kThreads - 64>(p.side, s_scan, threadIdx.x - 64, 1);
     for (int m = threadIdx.x - 64; m < Mv; m += kThreads - 64) {
       const int gm = m0 + m;
       s_orow[m] = p.out_rows ? p.out_rows[gm] : gm;
@@ -572,8 +581,9 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   st = std::max(2, std::min(16, st));
   const int tile_bytes = g.ntok * kLdt * 4;  // fp32 staging of the accumulator
   while (st * stage < tile_bytes) ++st;
-  // Ring + alignment slack + barriers/flags + per-token metadata (3 ints per token).
-  auto smem_of = [&](int stages) { return stages * stage + 1024 + 16 * stages + 64 + 12 * g.ntok; };
+  // Ring + alignment slack + barriers/flags + per-token metadata (3 ints per
+  // token) + the side task's 32-int scan buffer.
+  auto smem_of = [&](int stages) { return stages * stage + 1024 + 16 * stages + 64 + 12 * g.ntok + 128; };
   while (st > 2 && smem_of(st) > 227 * 1024 && (st - 1) * stage >= tile_bytes) --st;
   g.stages = st;
   g.smem = smem_of(st);
@@ -635,6 +645,8 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.half_dim = c.head_dim / 2;
   d.status = c.status;
   d.row_sums = c.epi == EPI_STORE ? c.row_sums : nullptr;
+  d.has_side = c.has_side;
+  d.side = c.side;
 
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {

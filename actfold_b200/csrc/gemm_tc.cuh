@@ -1,6 +1,7 @@
 // Weight-streaming tcgen05 GEMM for packed token rows (sm_100a).
 #pragma once
 
+#include "compact.cuh"
 #include "tc_common.cuh"
 
 namespace af {
@@ -39,6 +40,10 @@ struct GemmCall {
   const CUtensorMap* tmap_x;
   int w_tiled;         // 1: w is stored tiled [n/128][k/64][128][64] (contiguous 16 KB tiles)
   int pdl;             // 1: programmatic dependent launch (the kernel waits for its predecessor)
+  // Optional side task: the layer compaction, run by CTA (0, 0, 0)'s epilogue
+  // warps while its weight ring streams (the folded pass's QKV GEMM).
+  int has_side;
+  CompactArgs side;
 };
 
 // Token-tile width the kernel uses for a given row capacity.
