@@ -91,33 +91,71 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
   const int N = a.C * a.T;
   int base = 0, total;
   if (a.layer == 0) {
-    for (int i0 = 0; i0 < N; i0 += 1024) {
-      const int i = i0 + threadIdx.x;
-      const int f = (i < N && a.ctok[i] != a.ptok[i % a.T]) ? 1 : 0;
-      const int rank = base + block_scan_1024(f, wbuf, &total);
-      if (i < N) {
-        int s = -1;
-        if (f) {
-          if (rank < a.m_cap) {
-            a.fresh0_pos[rank] = i;
-            s = rank;
+    // One pass, 8 consecutive positions per thread: the edited (fresh) tokens
+    // in order, then the candidates (fresh within capacity, or rows the parent
+    // fails its own gate on) in order.
+    constexpr int E = 8;
+    int base1 = 0;
+    for (int i0 = 0; i0 < N; i0 += 1024 * E) {
+      const int ib = i0 + threadIdx.x * E;
+      uint32_t fm = 0, sm = 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int i = ib + e;
+        if (i < N) {
+          const int t = i % a.T;
+          if (a.ctok[i] != a.ptok[t]) fm |= 1u << e;
+          if (a.self_stable && !a.self_stable[t]) sm |= 1u << e;
+        }
+      }
+      int total1, total2;
+      int r1 = base1 + block_scan_1024(__popc(fm), wbuf, &total1);
+      int src[E];
+      uint32_t cm = 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        src[e] = -1;
+        if ((fm >> e) & 1u) {
+          if (r1 < a.m_cap) {
+            a.fresh0_pos[r1] = ib + e;
+            src[e] = r1;
           } else {
             atomicOr(a.status, AF_STATUS_CAPACITY);
           }
+          ++r1;
         }
-        a.slot[i] = s;
+        if (src[e] >= 0 || ((sm >> e) & 1u)) cm |= 1u << e;
       }
-      base += total;
+      int r2 = base + block_scan_1024(__popc(cm), wbuf, &total2);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if ((cm >> e) & 1u) {
+          if (r2 < a.m_cap) {
+            a.cand_child[r2] = (ib + e) / a.T;
+            a.cand_pos[r2] = (ib + e) % a.T;
+            a.cand_src[r2] = src[e];
+          } else {
+            atomicOr(a.status, AF_STATUS_CAPACITY);
+          }
+          ++r2;
+        }
+      }
+      base1 += total1;
+      base += total2;
     }
-    if (threadIdx.x == 0) *a.n_fresh0 = min(base, a.m_cap);
-  } else {
-    for (int i = threadIdx.x; i < N; i += 1024) a.slot[i] = -1;
-    __syncthreads();
-    const int nd = *a.prev_n_div;
-    for (int j = threadIdx.x; j < nd; j += 1024) a.slot[a.prev_div_pos[j]] = j;
+    if (threadIdx.x == 0) {
+      *a.n_fresh0 = min(base1, a.m_cap);
+      *a.n_cand = min(base, a.m_cap);
+    }
+    return;
   }
+  // Later layers (the parent fails its own gate on some rows): fresh rows are
+  // the previous layer's divergent rows.
+  for (int i = threadIdx.x; i < N; i += 1024) a.slot[i] = -1;
   __syncthreads();
-  base = 0;
+  const int nd = *a.prev_n_div;
+  for (int j = threadIdx.x; j < nd; j += 1024) a.slot[a.prev_div_pos[j]] = j;
+  __syncthreads();
   for (int i0 = 0; i0 < N; i0 += 1024) {
     const int i = i0 + threadIdx.x;
     int s = -1, f = 0;
@@ -172,17 +210,23 @@ using RowGroup = CtaRows<kRowThreads>;
 
 template <int NV, class Rows = WarpRows>
 __device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int H, const __nv_bfloat16* w, float eps,
-                                             char* out, int tid, const Rows& rows = Rows()) {
+                                             char* out, int tid, const Rows& rows = Rows(), float ss_pre = -1.f) {
   constexpr int G = Rows::kThreads;
+  // ss_pre >= 0: the row's sum of squares, already reduced in exactly this
+  // order (the cosine gate's candidate norm), so the reduction is skipped.
   float ss = 0.f;
+  if (ss_pre >= 0.f) {
+    ss = ss_pre;
+  } else {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    float f[8];
-    unpack<AF_DTYPE_BF16>(v[i], f);
+    for (int i = 0; i < NV; ++i) {
+      float f[8];
+      unpack<AF_DTYPE_BF16>(v[i], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+      for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+    ss = rows.sum(ss);
   }
-  ss = rows.sum(ss);
   const float var = __fdiv_rn(ss, (float)H);
   const float rinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, eps)));
   const char* wb = reinterpret_cast<const char*>(w);
@@ -265,7 +309,7 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
     const int j = i * kRowThreads + tid;
     if (j < nvec) stg16(xc + 16 * j, hv[i]);
   }
-  rmsnorm_regs<NV>(hv, nvec, g.H, g.norm_w, g.eps, reinterpret_cast<char*>(g.a + (int64_t)r * g.H), tid, rows);
+  rmsnorm_regs<NV>(hv, nvec, g.H, g.norm_w, g.eps, reinterpret_cast<char*>(g.a + (int64_t)r * g.H), tid, rows, o.ss_c);
 }
 
 // ----------------------------------------------------------------------------

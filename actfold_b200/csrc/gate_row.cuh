@@ -16,6 +16,7 @@ struct GateConsts {
 struct GateOut {
   uint8_t stable;
   float sim;
+  float ss_c = -1.f;  // cosine metric: the candidate row's reduced fp32 sum of squares (else -1)
 };
 
 // Host-side rounding to a storage dtype (round to nearest even).
@@ -139,6 +140,7 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
   constexpr int E = Elt<DT>::kPerVec;
   constexpr int G = Rows::kThreads;
   float presum;
+  float ss_c = -1.f;
   if constexpr (METRIC == AF_METRIC_COSINE) {
     float sc = 0.f, sp = 0.f;
 #pragma unroll
@@ -153,6 +155,7 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
       }
     }
     rows.sum2(sc, sp);
+    ss_c = sc;
     float nc, np;
     finish_cos<DT, METRIC>(sc, sp, k, nc, np);
     const float rc = __frcp_rn(nc), rp = __frcp_rn(np);
@@ -232,6 +235,7 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
   GateOut o;
   o.sim = rnd<DT>(presum);
   o.stable = o.sim > k.tau_r ? 1 : 0;
+  o.ss_c = ss_c;
   return o;
 }
 
