@@ -133,8 +133,22 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Launch priority applied by launch_ex on this host thread (kNoPriority: the
+// stream's own). Set it for a stretch of launches with LaunchPriority.
+constexpr int kNoPriority = -1000000;
+inline int& launch_priority() {
+  static thread_local int prio = kNoPriority;
+  return prio;
+}
+struct LaunchPriority {
+  int saved;
+  explicit LaunchPriority(int prio) : saved(launch_priority()) { launch_priority() = prio; }
+  ~LaunchPriority() { launch_priority() = saved; }
+};
+
 // Launch `kernel` on `stream` as clusters of `cluster` CTAs (none when the
-// cluster has one CTA) and, when `pdl`, with programmatic dependent launch.
+// cluster has one CTA), when `pdl` with programmatic dependent launch, and at
+// the current launch_priority().
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                              bool pdl, dim3 cluster, Args&&... args) {
@@ -144,8 +158,13 @@ inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute at[2];
+  cudaLaunchAttribute at[3];
   int n = 0;
+  if (launch_priority() != kNoPriority) {
+    at[n].id = cudaLaunchAttributePriority;
+    at[n].val.priority = launch_priority();
+    ++n;
+  }
   if (cluster.x * cluster.y * cluster.z > 1) {
     at[n].id = cudaLaunchAttributeClusterDimension;
     at[n].val.clusterDim.x = cluster.x;

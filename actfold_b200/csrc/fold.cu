@@ -314,8 +314,12 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
 
 // ----------------------------------------------------------------------------
 // Logits of stable rows: copy the parent's row t to every child whose final
-// row t is not fresh (CTA per position; the parent row is read once).
+// row t is not fresh. CTA = one 16 KB chunk of one position (the parent chunk
+// is read once), so the fill's CTAs are short and free their SM slots quickly
+// when it runs beside the last layer at a lower launch priority.
 // ----------------------------------------------------------------------------
+constexpr int kFillChunk = 8192;  // logits per CTA
+
 __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logits, int64_t V, int C, int T,
                                                      const unsigned* final_bits, int bits_ld,
                                                      __nv_bfloat16* logits) {
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logi
   pdl_wait();
   extern __shared__ int kids[];  // children that take the parent row
   __shared__ int nk;
-  const int t = blockIdx.x;
+  const int t = blockIdx.y;
   if (threadIdx.x == 0) nk = 0;
   __syncthreads();
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
@@ -333,9 +337,9 @@ __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logi
   __syncthreads();
   const int n = nk;
   if (n == 0) return;
+  const int64_t v0 = (int64_t)blockIdx.x * (kFillChunk / 8), v1 = min(V / 8, v0 + kFillChunk / 8);
   const char* src = reinterpret_cast<const char*>(p_logits + (int64_t)t * V);
-  const int64_t nvec = V / 8;
-  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
     const uint4 x = ldg16(src + 16 * v);
     for (int k = 0; k < n; ++k)
       stg16(reinterpret_cast<char*>(logits + ((int64_t)kids[k] * T + t) * V) + 16 * v, x);
@@ -779,6 +783,16 @@ struct FoldPlan {
   CUtensorMap tm_lm, tx_A, tx_att, tx_bn, tx_f;
   KernelTimer tk;
   int64_t last_launches = 0;
+  // Side stream of the pass: the logits fill of stable rows runs there from the
+  // last layer's QKV GEMM (which writes the final divergent bitmap) on, beside
+  // the last layer and the LM head, and joins before the scores.
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  ~FoldPlan() {
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (ev_join) cudaEventDestroy(ev_join);
+    if (side) cudaStreamDestroy(side);
+  }
 };
 
 static int build_maps(FoldPlan* p) {
@@ -844,6 +858,24 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   AF_TIMED(FK_SETUP, AF_LAUNCH(k_fold_candidates, 1, 1024, 0, s, ca));
   AF_TIMED(FK_SETUP, AF_LAUNCH(k_embed_rows, mblocks, 256, 0, s, static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V,
                                                            ctok, w.fresh0_pos, w.n_fresh0, M, w.x_all, w.status));
+
+  // Logits fill on the side stream (not in the per-class timing mode, which
+  // times every launch class on the pass stream).
+  const int fill_smem = C * (int)sizeof(int);
+  const dim3 fill_grid((unsigned)((z.V + kFillChunk - 1) / kFillChunk), (unsigned)T);
+  const bool fork_fill = !p->tk.on;
+  // The pass's kernels launch at the device's greatest priority, the side
+  // stream's fill at the least: the block scheduler then prefers the pass's
+  // pending CTAs whenever a slot frees.
+  int prio_low = 0, prio_high = 0;
+  cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high);
+  LaunchPriority high(fork_fill ? prio_high : kNoPriority);
+  if (fork_fill && !p->side) {
+    if (cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p->ev_join, cudaEventDisableTiming) != cudaSuccess)
+      return check_launch("af_fold_run: side stream");
+  }
 
   for (int l = 0; l < L; ++l) {
     const af_layer_weights& lw = p->layers[l];
@@ -927,6 +959,23 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.tmap_w = &p->tm_qkv[l];
     c.tmap_x = &p->tx_A;
     AF_TIMED(FK_QKV, if ((st = gemm_run(c, s))) return st);
+    if (last && fork_fill) {
+      // The final divergent bitmap is complete once this GEMM (its compaction
+      // side task) is: copy the parent's logits into every stable row on the
+      // side stream while the last layer and the LM head run here.
+      if (cudaEventRecord(p->ev_fork, s) != cudaSuccess || cudaStreamWaitEvent(p->side, p->ev_fork, 0) != cudaSuccess)
+        return check_launch("af_fold_run: fork");
+      cudaError_t e;
+      {
+        LaunchPriority low(prio_low);
+        e = launch_ex(k_logits_fill, fill_grid, dim3(256), (size_t)fill_smem, p->side, false, dim3(1, 1, 1),
+                      static_cast<const __nv_bfloat16*>(p->parent.logits), (int64_t)z.V, C, T,
+                      (const unsigned*)w.final_bits, w.bits_ld, logits);
+      }
+      if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("af_fold_run: fill launch: ") + cudaGetErrorString(e));
+      ++p->tk.launches;
+      if (cudaEventRecord(p->ev_join, p->side) != cudaSuccess) return check_launch("af_fold_run: join");
+    }
 
     AttnParams ap;
     memset(&ap, 0, sizeof(ap));
@@ -1052,9 +1101,12 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   c.tmap_w = &p->tm_lm;
   c.tmap_x = &p->tx_A;
   AF_TIMED(FK_LM, if ((st = gemm_run(c, s))) return st);
-  const int smem = C * (int)sizeof(int);
-  AF_TIMED(FK_FILL, AF_LAUNCH(k_logits_fill, T, 256, smem, s, static_cast<const __nv_bfloat16*>(p->parent.logits),
-                               (int64_t)z.V, C, T, (const unsigned*)w.final_bits, w.bits_ld, logits));
+  if (fork_fill) {
+    if (cudaStreamWaitEvent(s, p->ev_join, 0) != cudaSuccess) return check_launch("af_fold_run: join");
+  } else {
+    AF_TIMED(FK_FILL, AF_LAUNCH(k_logits_fill, fill_grid, 256, fill_smem, s, static_cast<const __nv_bfloat16*>(p->parent.logits),
+                                 (int64_t)z.V, C, T, (const unsigned*)w.final_bits, w.bits_ld, logits));
+  }
   if (scores)
     AF_TIMED(FK_SCORES, AF_LAUNCH(k_scores, C, 256, 0, s, (const float*)p->parent.logit_row_sums,
                                   (const float*)w.row_sums, C, T, (int64_t)z.V, (const unsigned*)w.final_bits,
