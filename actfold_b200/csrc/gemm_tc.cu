@@ -55,6 +55,7 @@ struct GemmDev {
   int rope_cols, half_dim;
   unsigned* status;
   float* row_sums;
+  int push;      // split-K partials pushed into the owners' shared memory (else pulled over DSMEM)
   int has_side;  // CTA (0, 0, 0) runs `side` (the layer compaction) in its epilogue warps
   CompactArgs side;
 };
@@ -64,6 +65,16 @@ __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2b
 // Staged accumulator: tile[m * kLdt + r] (fp32, token-major) for tile row r
 // (feature n0 + r) and token m; the 4-float pad keeps rows 16-byte aligned.
 constexpr int kLdt = kTileN + 4;
+
+// Split-K by push: CTA j of an S-way cluster owns tokens [j*Mv/S, (j+1)*Mv/S);
+// after the staged tile, its shared memory holds S - 1 receive slots of
+// ceil(ntok/S) staged rows, slot k for source k < j and k - 1 for k > j.
+__host__ __device__ __forceinline__ int xch_slot_bytes(int ntok, int splits) {
+  return ((ntok + splits - 1) / splits) * kLdt * 4;
+}
+__host__ __device__ __forceinline__ int xch_recv_bytes(int ntok, int splits) {
+  return (splits - 1) * xch_slot_bytes(ntok, splits);
+}
 
 __device__ __forceinline__ void load8(const float* s, float* v) {
   const float4 x = *reinterpret_cast<const float4*>(s), y = *reinterpret_cast<const float4*>(s + 4);
@@ -204,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + S * stage_bytes + 16 * S + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 16);
   volatile int* issued_slot = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 24);
+  const uint32_t recv_bar = bars + 16 * S + 32;  // split-K push: this CTA's receive slots are full
   // Per-token epilogue metadata (output row, residual row, RoPE position).
   int* s_orow = reinterpret_cast<int*>(gbase + S * stage_bytes + 16 * S + 64);
   int* s_rrow = s_orow + p.ntok;
@@ -234,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(accb, 1);
+    if (p.push) mbar_init(recv_bar, 1);
     *abort_flag = 0;
     *issued_slot = 0;
     fence_barrier_init();
@@ -375,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 #pragma unroll
         for (int j = 0; j < 16; ++j) tile[(16 * c + j) * kLdt + r] = v[j];
       }
+      if (p.push) fence_proxy_async_smem();  // the staged rows are read by bulk copies (async proxy)
     }
   }
   __syncthreads();
@@ -423,18 +437,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       }
     }
   } else {
-    // ---------------- cluster split-K reduction through distributed shared memory ----------------
-    __syncwarp();
-    cluster_sync_all();  // every partial tile of the cluster is in shared memory
-    // Units of work: (token m, chunk pair c / c + 8), i.e. rows 8c..8c+7 and
-    // their partners 64+8c..64+8c+7; CTA j of the cluster takes a contiguous
-    // share of the Mv * 8 units and sums them over all CTAs in a fixed order.
-    // Per unit the global operands are requested first, then every peer's
-    // partial sums (up to 4 peers in flight), so their latencies overlap.
+    // ---------------- cluster split-K reduction ----------------
+    // CTA j owns tokens [tlo, thi) and sums their units (token m, chunk pair
+    // c / c + 8: rows 8c..8c+7 and their partners 64+8c..64+8c+7) over every
+    // CTA of the cluster in a fixed source order. The other CTAs' partial rows
+    // of those tokens are either pushed into this CTA's receive slots by bulk
+    // copies (push) or read from their shared memory (pull); the sums are the
+    // same. Per unit the global operands are requested first, then every
+    // source's partials (up to 4 in flight), so their latencies overlap.
     const int j = blockIdx.y, Sp = p.splits;
-    const int units = Mv * 8;
-    const int lo = (j * units) / Sp, hi = ((j + 1) * units) / Sp;
-    if (ok) {
+    const int tlo = (j * Mv) / Sp, thi = ((j + 1) * Mv) / Sp;
+    const int lo = tlo * 8, hi = thi * 8;
+    const uint32_t row_b = kLdt * 4;
+    const uint32_t recv_off = (uint32_t)(p.ntok * kLdt * 4);
+    const uint32_t slot_b = (uint32_t)xch_slot_bytes(p.ntok, Sp);
+    if (p.push && threadIdx.x == 0)
+      mbar_arrive_expect_tx(recv_bar, (uint32_t)((Sp - 1) * (thi - tlo)) * row_b);
+    __syncwarp();
+    cluster_sync_all();  // every partial tile is staged, every receive barrier armed, every ring idle
+    bool got = true;
+    if (p.push) {
+      if (threadIdx.x == 0)
+        for (int k = 0; k < Sp; ++k) {
+          const int klo = (k * Mv) / Sp, khi = ((k + 1) * Mv) / Sp;
+          if (k == j || khi <= klo) continue;
+          const uint32_t dst = cluster_map(base + recv_off + (uint32_t)(j < k ? j : j - 1) * slot_b, (uint32_t)k);
+          bulk_copy_s2c(dst, base + (uint32_t)klo * row_b, (uint32_t)(khi - klo) * row_b, cluster_map(recv_bar, (uint32_t)k));
+        }
+      volatile int no_abort = 0;
+      got = mbar_wait(recv_bar, 0, &no_abort);
+      if (!got && threadIdx.x == 0) atomicOr(p.status, AF_STATUS_TIMEOUT);
+    }
+    if (ok && got) {
       for (int u = lo + threadIdx.x; u < hi; u += kThreads) {
         const int m = u >> 3, c = u & 7;
         EpiOperands o;
@@ -447,11 +481,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             if (s0 + q < Sp) {
-              const uint32_t src = (uint32_t)(s0 + q);
-              v[q][0] = ld_cluster_f4(cluster_map(oa, src));
-              v[q][1] = ld_cluster_f4(cluster_map(oa + 16, src));
-              v[q][2] = ld_cluster_f4(cluster_map(ob, src));
-              v[q][3] = ld_cluster_f4(cluster_map(ob + 16, src));
+              const int src = s0 + q;
+              if (p.push) {
+                const float* t = src == j ? tile + m * kLdt + 8 * c
+                                          : reinterpret_cast<const float*>(gbase + recv_off + (src < j ? src : src - 1) * slot_b +
+                                                                           (m - tlo) * row_b) + 8 * c;
+                v[q][0] = *reinterpret_cast<const float4*>(t);
+                v[q][1] = *reinterpret_cast<const float4*>(t + 4);
+                v[q][2] = *reinterpret_cast<const float4*>(t + 64);
+                v[q][3] = *reinterpret_cast<const float4*>(t + 68);
+              } else {
+                v[q][0] = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
+                v[q][1] = ld_cluster_f4(cluster_map(oa + 16, (uint32_t)src));
+                v[q][2] = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
+                v[q][3] = ld_cluster_f4(cluster_map(ob + 16, (uint32_t)src));
+              }
             }
           }
 #pragma unroll
@@ -468,7 +512,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       }
     }
     __syncwarp();
-    cluster_sync_all();  // peers may still read this CTA's partial tile until here
+    // Pull: peers may still read this CTA's partial tile until here. Push:
+    // every CTA has received its slots, so this CTA's outgoing copies are done.
+    cluster_sync_all();
   }
 
   if (threadIdx.x == 0 && *abort_flag) {
@@ -544,6 +590,7 @@ int gemm_ntok(int m_cap) {
 
 struct GemmShape {
   int ntok, m_tiles, n_tiles, nkb, splits, kb_per, stages, smem;
+  int push;  // split-K partials pushed into the owners' shared memory (bulk copies)
 };
 
 static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_sums) {
@@ -585,6 +632,20 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   // token) + the side task's 32-int scan buffer.
   auto smem_of = [&](int stages) { return stages * stage + 1024 + 16 * stages + 64 + 12 * g.ntok + 128; };
   while (st > 2 && smem_of(st) > 227 * 1024 && (st - 1) * stage >= tile_bytes) --st;
+  // Split-K by push: the owners' receive slots follow the staged tile in the
+  // idle ring. Used when they fit, or when a deeper ring costs nothing (one
+  // CTA per SM); otherwise the owners pull the partials over DSMEM.
+  g.push = 0;
+  if (g.splits > 1) {
+    const int need = tile_bytes + xch_recv_bytes(g.ntok, g.splits);
+    int st2 = st;
+    if (tiles * g.splits <= sm_count())
+      while (st2 * stage < need && smem_of(st2 + 1) <= 227 * 1024) ++st2;
+    if (st2 * stage >= need) {
+      g.push = 1;
+      st = st2;
+    }
+  }
   g.stages = st;
   g.smem = smem_of(st);
   return g;
@@ -645,6 +706,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.half_dim = c.head_dim / 2;
   d.status = c.status;
   d.row_sums = c.epi == EPI_STORE ? c.row_sums : nullptr;
+  d.push = g.push;
   d.has_side = c.has_side;
   d.side = c.side;
 
