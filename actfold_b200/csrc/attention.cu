@@ -370,6 +370,11 @@ static int attention_splits(const AttnParams& p) {
   return ns;
 }
 
+bool attention_uses_tc(const AttnParams& p) {
+  const char* impl = std::getenv("ACTFOLD_ATTN_IMPL");
+  return !(impl && impl[0] == 'm') && attention_tc_splits(p) > 0;
+}
+
 int attention_run(const AttnParams& p, cudaStream_t s) {
   AF_REQUIRE(p.q && p.pk && p.pv && p.out, "attention: null pointer");
   AF_REQUIRE(p.n_heads > 0 && p.n_kv_heads > 0 && p.n_heads % p.n_kv_heads == 0, "attention: bad head counts");
@@ -384,6 +389,7 @@ int attention_run(const AttnParams& p, cudaStream_t s) {
     const int ns_tc = attention_tc_splits(p);
     if (ns_tc > 0) return attention_tc_run(p, ns_tc, s);
   }
+  AF_REQUIRE(!p.cand_tma && !p.out_rows, "attention: candidate-row mode and output row maps need the tcgen05 kernel");
   const int smem = kSmem;
   static bool attr = false;
   if (!attr) {

@@ -1,6 +1,8 @@
 // Packed-query attention over parent K/V with fresh-key overrides (see attention.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace af {
@@ -31,6 +33,15 @@ struct AttnParams {
   int pdl;           // 1: programmatic dependent launch (the kernel waits for its predecessor)
   int kv_static;     // 1: pk / pv are not written by the preceding kernels (a cached parent), so the
                      //    tcgen05 kernel loads them by TMA before it waits for its predecessor
+  // Output row of query row i (nullable: i); rows mapped to -1 are not written.
+  const int* out_rows;
+  // Candidate-row mode of the tcgen05 kernel: query rows are q + i * q_ld
+  // (qsrc null), and the query tile and the candidate key blocks (fk / fv,
+  // in the same buffer at columns fk_col / fv_col) are loaded by TMA through
+  // `tmap_c`, a map over that buffer ([n_q_cap rows, q_ld columns], box 64 x 128).
+  int cand_tma;
+  const CUtensorMap* tmap_c;
+  int fk_col, fv_col;
   unsigned* status;  // nullable: AF_STATUS_TIMEOUT is ORed in when a bounded wait runs out
 };
 
@@ -38,5 +49,7 @@ int attention_run(const AttnParams& p, cudaStream_t s);
 // tcgen05 kernel (attention_tc.cu): key splits for `p` (0: shape not supported) and launch.
 int attention_tc_splits(const AttnParams& p);
 int attention_tc_run(const AttnParams& p, int splits, cudaStream_t s);
+// Whether attention_run takes the tcgen05 kernel for `p`.
+bool attention_uses_tc(const AttnParams& p);
 
 }  // namespace af

@@ -75,6 +75,7 @@ __device__ __forceinline__ void load_op(uint32_t dst, RowPtr row_ptr, const void
 
 __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_constant__ CUtensorMap tmK,
                                                               const __grid_constant__ CUtensorMap tmV,
+                                                              const __grid_constant__ CUtensorMap tmC,
                                                               const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   pdl_trigger();
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   int* sF = reinterpret_cast<int*>(gb + kOffF);
   float* red = reinterpret_cast<float*>(gb + kOffQ);  // [2][4][128] row max / sum partials, after S is done
   const uint32_t barS = base + kOffBar, barO = barS + 8, barK = barS + 32, barV = barS + 40;
+  const uint32_t barC = barS + 48;  // candidate-row mode: query tile and candidate key blocks by TMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + kOffBar + 16);
   volatile int* fail = reinterpret_cast<volatile int*>(gb + kOffBar + 24);
 
@@ -111,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     mbar_init(barO, 1);
     mbar_init(barK, 1);
     mbar_init(barV, 1);
+    mbar_init(barC, 1);
     *fail = 0;
     fence_barrier_init();
     if (kv_tma) {
@@ -142,17 +145,43 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   }
   const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
   if (warp == 0) tmem_alloc(smem_u32(tmem_slot), 512);
+  const bool c_tma = p.cand_tma != 0;
+  if (c_tma && tid == 0) {
+    // Candidate-row mode: the query tile (rows q0..q0+127 of the buffer) and
+    // this CTA's candidate key blocks, as soon as their producer is done.
+    // Rows past the valid counts are masked below (queries are not written,
+    // keys get zero weight).
+    uint32_t bytes = kOpB;
+    for (int j = 0; j < nbl; ++j)
+      if (b_lo + j >= n_pb) bytes += 2 * kOpB;
+    mbar_arrive_expect_tx(barC, bytes);
+    for (int hf = 0; hf < 2; ++hf) tma_load_2d(sQ + hf * kTileB, &tmC, barC, h * 128 + 64 * hf, q0);
+    for (int j = 0; j < nbl; ++j) {
+      const int b = b_lo + j;
+      if (b < n_pb) continue;
+      const int y = (b - n_pb) * kTK;
+      for (int hf = 0; hf < 2; ++hf) {
+        tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmC, barC, p.fk_col + kvh * 128 + 64 * hf, y);
+        tma_load_2d(sV + j * kOpB + hf * kTileB, &tmC, barC, p.fv_col + kvh * 128 + 64 * hf, y);
+      }
+    }
+  }
 
-  // ---- operands (cp.async): Q rows, candidate blocks, and parent blocks without TMA ----
-  load_op(sQ, [&](int rr) -> const __nv_bfloat16* {
-    const int qi = q0 + rr;
-    if (qi >= n_q) return nullptr;
-    return p.q + (int64_t)(p.qsrc ? p.qsrc[qi] : qi) * p.q_ld + h * 128;
-  }, p.q, tid);
+  // ---- operands (cp.async): whatever is not loaded by TMA ----
+  if (!c_tma)
+    load_op(sQ, [&](int rr) -> const __nv_bfloat16* {
+      const int qi = q0 + rr;
+      if (qi >= n_q) return nullptr;
+      return p.q + (int64_t)(p.qsrc ? p.qsrc[qi] : qi) * p.q_ld + h * 128;
+    }, p.q, tid);
   for (int j = 0; j < nbl; ++j) {
     const int b = b_lo + j;
     const bool parent_blk = b < n_pb;
-    if (parent_blk && kv_tma) continue;
+    if (!parent_blk && tid < kTK) {
+      const int jj = (b - n_pb) * kTK + tid;
+      sF[j * kTK + tid] = jj >= n_f ? -2 : (p.fchild ? p.fchild[jj] : -1);
+    }
+    if ((parent_blk && kv_tma) || (!parent_blk && c_tma)) continue;
     const int r0 = (parent_blk ? b : b - n_pb) * kTK;
     const int lim = parent_blk ? p.T : n_f;
     const __nv_bfloat16* kb = parent_blk ? p.pk : p.fk;
@@ -164,10 +193,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     load_op(sV + j * kOpB, [&](int rr) -> const __nv_bfloat16* {
       return r0 + rr < lim ? vb + (int64_t)(r0 + rr) * ld + kvh * 128 : nullptr;
     }, p.q, tid);
-    if (!parent_blk && tid < kTK) {
-      const int jj = r0 + tid;
-      sF[j * kTK + tid] = jj >= n_f ? -2 : (p.fchild ? p.fchild[jj] : -1);
-    }
   }
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   fence_proxy_async();
@@ -180,12 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   // ---- S_j = Q K_j^T ----
   if (tid == 0 && nbl > 0) {
     bool k_ok = true;
-    if (kv_tma) {
-      volatile int no_abort = 0;
-      k_ok = mbar_wait(barK, 0, &no_abort);
-      if (!k_ok) *fail = 1;
-      tc_fence_after();
-    }
+    volatile int no_abort = 0;
+    if (kv_tma) k_ok = mbar_wait(barK, 0, &no_abort);
+    if (c_tma) k_ok = mbar_wait(barC, 0, &no_abort) && k_ok;
+    if (!k_ok) *fail = 1;
+    tc_fence_after();
     const uint32_t idesc = idesc_bf16(kTQ, kTK);
     for (int j = 0; j < nbl && k_ok; ++j)
 #pragma unroll
@@ -331,9 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     for (int i = 0; i < 32; ++i) o[i] = 0u;
   }
   if (ns == 1) {
-    if (row_ok && !bad) {
+    const int orow = row_ok ? (p.out_rows ? p.out_rows[q0 + r] : q0 + r) : -1;
+    if (orow >= 0 && !bad) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)(q0 + r) * p.out_ld + h * 128 + c0);
+      uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)orow * p.out_ld + h * 128 + c0);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint4 w;
@@ -388,12 +413,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
           acc.w += f * vk[k].w;
         }
       }
-      if (q0 + rr < n_q && !bad) {
+      const int orow = q0 + rr < n_q ? (p.out_rows ? p.out_rows[q0 + rr] : q0 + rr) : -1;
+      if (orow >= 0 && !bad) {
         const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
         uint2 w;
         w.x = pack2(acc.x * inv, acc.y * inv);
         w.y = pack2(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(p.out + (int64_t)(q0 + rr) * p.out_ld + h * 128 + 4 * c4) = w;
+        *reinterpret_cast<uint2*>(p.out + (int64_t)orow * p.out_ld + h * 128 + 4 * c4) = w;
       }
     }
     cluster_sync_all();  // peers may read this CTA's partials until here
@@ -456,16 +482,22 @@ int attention_tc_run(const AttnParams& p, int ns, cudaStream_t s) {
     cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
     attr = true;
   }
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv, tc;
   memset(&tk, 0, sizeof(tk));
   memset(&tv, 0, sizeof(tv));
+  memset(&tc, 0, sizeof(tc));
+  if (p.cand_tma) {
+    AF_REQUIRE(p.tmap_c && !p.qsrc && p.fk && p.fv && p.f_ld == p.q_ld && (p.fk_col | p.fv_col) % 8 == 0,
+               "attention_tc: candidate-row mode needs a buffer map, contiguous queries and key columns in that buffer");
+    tc = *p.tmap_c;
+  }
   if (p.kv_static) {
     const int cols = p.n_kv_heads * 128;
     if (int st = kv_tmap(&tk, p.pk, p.T, cols, p.kv_ld)) return st;
     if (int st = kv_tmap(&tv, p.pv, p.T, cols, p.kv_ld)) return st;
   }
   cudaError_t e = launch_ex(k_attention_tc, dim3((p.n_q_cap + kTQ - 1) / kTQ, p.n_heads, ns), dim3(kThreads, 1, 1),
-                            (size_t)kSmemTc, s, p.pdl != 0, dim3(1, 1, ns), tk, tv, p);
+                            (size_t)kSmemTc, s, p.pdl != 0, dim3(1, 1, ns), tk, tv, tc, p);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("attention_tc: launch: ") + cudaGetErrorString(e));
   return check_launch("attention_tc");
 }

@@ -64,6 +64,7 @@ struct CompactArgs {
   int* div_child;
   int* div_pos;
   int* n_div;
+  int* cand_div;        // nullable: [m_cap] divergent rank of each candidate, -1 if stable
   int* div_count;       // [C] divergent rows per child
   unsigned* bits;       // [C, bits_ld] candidates of this layer (fresh keys)
   unsigned* final_bits; // nullable: divergent rows of this layer (last layer only)
@@ -102,6 +103,7 @@ __device__ __forceinline__ void compact_rows(const CompactArgs& a, int* wbuf, in
       d = a.stable[r] ? 0 : 1;
     }
     const int rank = base + group_scan<NT>(d, wbuf, &total, tid, bar_id);
+    if (a.cand_div && r < n) a.cand_div[r] = d ? rank : -1;
     if (d) {
       a.div_cand[rank] = r;
       a.div_child[rank] = c;

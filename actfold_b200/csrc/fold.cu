@@ -669,6 +669,7 @@ struct FoldWs {
   __nv_bfloat16 *x_all, *xc, *A, *qkv, *att, *h1, *bn, *f;
   float* row_sums;  // [C*T] fresh logit row sums
   unsigned* status;
+  int* cand_div;  // [m_cap] divergent rank of each candidate of the current layer, -1 if stable
   int bits_ld;
 };
 
@@ -701,6 +702,7 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
   w.f = b.take<__nv_bfloat16>((int64_t)m_cap * z.FF);
   w.row_sums = b.take<float>((int64_t)C * T);
   w.status = b.take<unsigned>(1);
+  w.cand_div = b.take<int>(m_cap);
   return w;
 }
 
@@ -780,7 +782,7 @@ struct FoldPlan {
   FoldWs w;
   int ntok;
   std::vector<CUtensorMap> tm_qkv, tm_o, tm_gu, tm_down;
-  CUtensorMap tm_lm, tx_A, tx_att, tx_bn, tx_f;
+  CUtensorMap tm_lm, tx_A, tx_att, tx_bn, tx_f, tx_qkv;
   KernelTimer tk;
   int64_t last_launches = 0;
   // Side stream of the pass: the logits fill of stable rows runs there from the
@@ -815,6 +817,7 @@ static int build_maps(FoldPlan* p) {
   if ((st = make_tmap_bf16(&p->tx_A, p->w.A, p->m_cap, z.H, z.H, nt))) return st;
   if ((st = make_tmap_bf16(&p->tx_att, p->w.att, p->m_cap, z.q, z.q, nt))) return st;
   if ((st = make_tmap_bf16(&p->tx_bn, p->w.bn, p->m_cap, z.H, z.H, nt))) return st;
+  if ((st = make_tmap_bf16(&p->tx_qkv, p->w.qkv, p->m_cap, z.qkv, z.qkv, 128))) return st;
   if ((st = make_tmap_bf16(&p->tx_f, p->w.f, p->m_cap, z.FF, z.FF, nt))) return st;
   return AF_OK;
 }
@@ -926,6 +929,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     a.div_child = dchild;
     a.div_pos = dpos;
     a.n_div = nd;
+    a.cand_div = w.cand_div;
     a.div_count = w.div_count + (int64_t)l * C;
     a.bits = w.bits;
     a.final_bits = last ? w.final_bits : nullptr;
@@ -1005,6 +1009,20 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.pdl = pass_pdl() ? 1 : 0;
     ap.kv_static = 1;  // the parent's K/V are fixed for the whole pass
     ap.status = w.status;
+    if (attention_uses_tc(ap)) {
+      // Candidate-row mode: every candidate row is a query (the query tile is
+      // 128 rows whatever the divergent count), so the queries and the
+      // candidate keys are plain TMA boxes of the QKV output; only divergent
+      // rows are written, at their packed rank.
+      ap.qsrc = nullptr;
+      ap.qchild = cc;
+      ap.n_q_dev = nc;
+      ap.out_rows = w.cand_div;
+      ap.cand_tma = 1;
+      ap.tmap_c = &p->tx_qkv;
+      ap.fk_col = z.q;
+      ap.fv_col = z.q + z.kv;
+    }
     AF_TIMED(FK_ATTN, if ((st = attention_run(ap, s))) return st);
 
     c = base_call(w.status);
