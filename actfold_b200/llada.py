@@ -20,7 +20,6 @@ logits) with no host synchronisation until the caller reads a result.
 from __future__ import annotations
 
 import ctypes as C
-import math
 from dataclasses import dataclass
 from typing import Any, Sequence
 
@@ -470,27 +469,3 @@ def register_parent_in_cache(cache, branch_id: Any, pc: ParentCache) -> None:
     for li in range(L):
         put_views(branch_id, li, {"ffn_out": pc.layer_in[li + 1][None], "hidden_states": pc.layer_in[li][None]})
 
-
-def smoke_check() -> None:
-    """One tiny folded verification on cuda:0 checked against the oracle (used by smoke())."""
-    from actfold_b200 import workloads as W
-    from oracle import folding as OF
-    from oracle import llada as OL
-
-    dims = W.LLADA_TINY
-    w = W.llada_weights_numpy(dims, seed=7)
-    parent, children = W.llada_tokens(64, 16, 0.5, 4, 4, dims.mask_id, 42)
-    model = LLaDAModel.from_numpy(dims, w, device="cuda", max_pos=64)
-    pc = model.parent_pass(torch.from_numpy(parent).cuda(), tau=0.95)
-    logits, plan = model.verify(torch.from_numpy(children).cuda(), pc, 0.95)
-    plan.check_status()
-    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
-    ref_par = OF.llada_parent(parent, w, od)
-    ref = OF.llada_folded_children(children, ref_par, w, od, 0.95)
-    masks = plan.stable_masks().cpu().numpy()
-    assert (masks == ref["masks"]).mean() >= 0.999, "folded masks disagree with the oracle"
-    got = logits.float().cpu().numpy()
-    err = np.abs(got - ref["logits"]).max() / np.abs(ref["logits"]).max()
-    assert err <= 2e-2, f"folded logits rel err {err}"
-    cos = (got * ref["logits"]).sum() / math.sqrt((got * got).sum() * (ref["logits"] ** 2).sum())
-    assert cos >= 0.999, cos
