@@ -180,6 +180,7 @@ class ActivationCache:
         for layer in self._caches.values():
             for key in [k for k in layer if k[0] == branch_id]:
                 del layer[key]
+        drop_native_branches(self, branch_id)
 
     def clear_layer(self, layer_idx: int) -> None:
         if layer_idx in self._caches:
@@ -188,6 +189,7 @@ class ActivationCache:
     def clear_all(self) -> None:
         self._caches.clear()
         self._clock.clear()
+        drop_native_branches(self)
 
     def num_entries(self, layer_idx: int | None = None) -> int:
         """Number of cached token entries, optionally for one layer."""
@@ -213,3 +215,15 @@ class ActivationCache:
     def touch(self, branch_id: Any, layer_idx: int, selected: np.ndarray | None, T: int, step_idx: int = 0) -> None:
         """Apply the LRU touch of a ``get`` whose mask selects ``selected`` tokens (None = all)."""
         self._touch(branch_id, layer_idx, step_idx, selected, T)
+
+
+def drop_native_branches(cache: Any, branch_id: Any = None) -> None:
+    """Forget the native pass's dense parent caches and promotable children (all, or one branch)."""
+    for attr in ("native_parents", "native_children"):
+        d = getattr(cache, attr, None)
+        if d is None:
+            continue
+        if branch_id is None:
+            d.clear()
+        else:
+            d.pop(branch_id, None)

@@ -27,7 +27,7 @@ import numpy as np
 import torch
 
 from actfold_b200 import _lib
-from actfold_b200.core.activation_cache import _validate_activations
+from actfold_b200.core.activation_cache import _validate_activations, drop_native_branches
 from actfold_b200.core.fused_ops import masked_rows
 
 
@@ -177,6 +177,7 @@ class ChunkedActivationCache:
         for layer in self._caches.values():
             for key in [k for k in layer if k[0] == branch_id]:
                 del layer[key]
+        drop_native_branches(self, branch_id)
 
     def clear_layer(self, layer_idx: int) -> None:
         if layer_idx in self._caches:
@@ -185,6 +186,7 @@ class ChunkedActivationCache:
     def clear_all(self) -> None:
         self._caches.clear()
         self._clock.clear()
+        drop_native_branches(self)
 
     def num_entries(self, layer_idx: int | None = None) -> int:
         """Number of cached chunks, optionally for one layer."""

@@ -428,6 +428,91 @@ __global__ void __launch_bounds__(kRowThreads) k_self_gate(const __nv_bfloat16* 
 }
 
 // ----------------------------------------------------------------------------
+// Promotion of a verified child to a parent. The reference stores every
+// branch's per-layer activations, children included (_store_activations after
+// the merge, actfold/core/folded_transformer.py:190-199), so a child can be
+// the parent of the next verification. A child's layer-l input differs from
+// its parent's only on its fresh rows of layer l, so promoting it rewrites
+// just those rows of a parent cache: the layer input, the QKV row (kept by
+// k_keep_rows during the pass) and the self-gate flag.
+// ----------------------------------------------------------------------------
+
+// Candidate QKV rows of the current layer, copied to the caller's store
+// [L, m_cap, qkv] (one CTA per row) while promotion is enabled.
+__global__ void __launch_bounds__(256) k_keep_rows(const __nv_bfloat16* src, int cols, const int* n_dev, int n_cap,
+                                                   __nv_bfloat16* dst) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x;
+  if (i >= min(*n_dev, n_cap)) return;
+  const char* s = reinterpret_cast<const char*>(src + (int64_t)i * cols);
+  char* d = reinterpret_cast<char*>(dst + (int64_t)i * cols);
+  for (int v = threadIdx.x; v < cols / 8; v += blockDim.x) stg16(d + 16 * (int64_t)v, ldg16(s + 16 * (int64_t)v));
+}
+
+struct PromoteArgs {
+  int child, T, H, L, m_cap, qkv_cols;
+  const int *cand_child, *cand_pos, *cand_src, *n_cand;  // [(L+1) * m_cap], [L+1]
+  const __nv_bfloat16* x_all;                             // [L+1, m_cap, H] fresh rows of each layer
+  const __nv_bfloat16* kept_qkv;                          // [L, m_cap, qkv_cols] QKV row of each candidate
+  __nv_bfloat16* layer_in;                                // [L+1, T, H]
+  __nv_bfloat16* qkv;                                     // [L, T, qkv_cols]
+  uint8_t* self_stable;                                   // [L, T]
+  GateConsts k;
+};
+
+// One CTA per (candidate slot, layer): a fresh row of the promoted child is
+// written over the parent's, with its QKV row and its self-gate result (same
+// arithmetic as k_self_gate in the parent pass).
+template <int NV>
+__global__ void __launch_bounds__(kRowThreads) k_promote_rows(const PromoteArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[2 * kRowThreads / 32];
+  const int j = blockIdx.x, l = blockIdx.y;
+  if (j >= min(a.n_cand[l], a.m_cap)) return;
+  const int64_t cj = (int64_t)l * a.m_cap + j;
+  const int src = a.cand_src[cj];
+  if (a.cand_child[cj] != a.child || src < 0) return;
+  const int t = a.cand_pos[cj];
+  const int nvec = a.H / 8;
+  uint4 v[NV];
+  load_row<NV, kRowThreads>(reinterpret_cast<const char*>(a.x_all + ((int64_t)l * a.m_cap + src) * a.H), nvec,
+                            threadIdx.x, v);
+  char* drow = reinterpret_cast<char*>(a.layer_in + ((int64_t)l * a.T + t) * a.H);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int jj = i * kRowThreads + threadIdx.x;
+    if (jj < nvec) stg16(drow + 16 * (int64_t)jj, v[i]);
+  }
+  if (l >= a.L) return;  // the final hidden state has no QKV row or gate
+  const char* qs = reinterpret_cast<const char*>(a.kept_qkv + cj * a.qkv_cols);
+  char* qd = reinterpret_cast<char*>(a.qkv + ((int64_t)l * a.T + t) * a.qkv_cols);
+  for (int jj = threadIdx.x; jj < a.qkv_cols / 8; jj += kRowThreads) stg16(qd + 16 * (int64_t)jj, ldg16(qs + 16 * (int64_t)jj));
+  const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, a.H, a.k, threadIdx.x, RowGroup{red});
+  if (threadIdx.x == 0) a.self_stable[(int64_t)l * a.T + t] = o.stable;
+}
+
+// Logits rows and logit row sums of the promoted child's last-layer divergent
+// rows (its other rows hold the parent's logits already). One CTA per row.
+__global__ void __launch_bounds__(256) k_promote_final(int child, int T, int64_t V, const int* div_pos, const int* n_div,
+                                                       int m_cap, const __nv_bfloat16* child_logits,
+                                                       const float* fresh_row_sums, __nv_bfloat16* p_logits,
+                                                       float* p_row_sums) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x;
+  if (i >= min(*n_div, m_cap)) return;
+  const int pos = div_pos[i];
+  if (pos / T != child) return;
+  const int t = pos % T;
+  const char* s = reinterpret_cast<const char*>(child_logits + (int64_t)pos * V);
+  char* d = reinterpret_cast<char*>(p_logits + (int64_t)t * V);
+  for (int64_t v = threadIdx.x; v < V / 8; v += blockDim.x) stg16(d + 16 * v, ldg16(s + 16 * v));
+  if (threadIdx.x == 0) p_row_sums[t] = fresh_row_sums[pos];
+}
+
+// ----------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------
 struct Bump {
@@ -790,6 +875,9 @@ struct FoldPlan {
   // the last layer and the LM head, and joins before the scores.
   cudaStream_t side = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // Caller store [L, m_cap, qkv] for each layer's candidate QKV rows
+  // (af_fold_keep_kv); null when promotion is off.
+  __nv_bfloat16* kv_keep = nullptr;
   ~FoldPlan() {
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
@@ -1076,6 +1164,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.tmap_w = &p->tm_down[l];
     c.tmap_x = &p->tx_f;
     AF_TIMED(FK_DOWN, if ((st = gemm_run(c, s))) return st);
+    if (p->kv_keep)
+      AF_TIMED(FK_SETUP, AF_LAUNCH(k_keep_rows, (unsigned)M, 256, 0, s, (const __nv_bfloat16*)w.qkv, z.qkv,
+                                   (const int*)nc, M, p->kv_keep + (int64_t)l * M * z.qkv));
 
     if (next_su) {
       CandArgs cn;
@@ -1219,6 +1310,63 @@ extern "C" int af_fold_materialize(void* plan, int64_t layer, void* out, void* s
   k_state_scatter<<<(unsigned)((p->m_cap + 7) / 8), 256, 0, s>>>(p->w.x_all + layer * p->m_cap * z.H, z.H, pos, n,
                                                                   p->m_cap, o);
   return check_launch("af_fold_materialize");
+}
+
+extern "C" int af_fold_keep_kv(void* plan, void* store, int64_t store_bytes) {
+  AF_REQUIRE(plan, "af_fold_keep_kv: null plan");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  if (!store) {
+    p->kv_keep = nullptr;
+    return AF_OK;
+  }
+  const Sizes z = sizes_of(p->model.dims);
+  AF_REQUIRE(store_bytes >= (int64_t)z.L * p->m_cap * z.qkv * (int64_t)sizeof(__nv_bfloat16),
+             "af_fold_keep_kv: store smaller than n_layers * m_cap * (q_dim + 2 kv_dim) bf16");
+  AF_REQUIRE((reinterpret_cast<uintptr_t>(store) & 15) == 0, "af_fold_keep_kv: store must be 16-byte aligned");
+  p->kv_keep = static_cast<__nv_bfloat16*>(store);
+  return AF_OK;
+}
+
+extern "C" int af_fold_promote(void* plan, int64_t child, const int64_t* child_tokens, const void* child_logits,
+                               const af_parent_cache* dst, void* stream) {
+  AF_REQUIRE(plan && child_tokens && child_logits && dst, "af_fold_promote: null pointer");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  AF_REQUIRE(p->kv_keep, "af_fold_promote: the pass did not keep its QKV rows (call af_fold_keep_kv before af_fold_run)");
+  AF_REQUIRE(child >= 0 && child < p->C, "af_fold_promote: child out of range");
+  AF_REQUIRE(dst->seq == p->T, "af_fold_promote: destination length differs from the pass's");
+  AF_REQUIRE(dst->tokens && dst->layer_in && dst->qkv && dst->logits && dst->self_stable && dst->logit_row_sums,
+             "af_fold_promote: incomplete destination cache");
+  const Sizes z = sizes_of(p->model.dims);
+  const int T = p->T, M = p->m_cap;
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemcpyAsync(const_cast<int64_t*>(dst->tokens), child_tokens + child * T, (size_t)T * sizeof(int64_t),
+                                  cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("af_fold_promote: tokens: ") + cudaGetErrorString(e));
+  PromoteArgs a;
+  a.child = (int)child;
+  a.T = T;
+  a.H = z.H;
+  a.L = z.L;
+  a.m_cap = M;
+  a.qkv_cols = z.qkv;
+  a.cand_child = p->w.cand_child;
+  a.cand_pos = p->w.cand_pos;
+  a.cand_src = p->w.cand_src;
+  a.n_cand = p->w.n_cand;
+  a.x_all = p->w.x_all;
+  a.kept_qkv = p->kv_keep;
+  a.layer_in = static_cast<__nv_bfloat16*>(const_cast<void*>(dst->layer_in));
+  a.qkv = static_cast<__nv_bfloat16*>(const_cast<void*>(dst->qkv));
+  a.self_stable = const_cast<uint8_t*>(dst->self_stable);
+  a.k = make_gate_consts(AF_DTYPE_BF16, p->tau, 1e-8f, 0.f);
+  const dim3 grid((unsigned)M, (unsigned)(z.L + 1));
+  if (z.H / 8 <= kRowThreads) k_promote_rows<1><<<grid, kRowThreads, 0, s>>>(a);
+  else k_promote_rows<2><<<grid, kRowThreads, 0, s>>>(a);
+  k_promote_final<<<(unsigned)M, 256, 0, s>>>((int)child, T, (int64_t)z.V, p->w.div_pos + (int64_t)(z.L - 1) * M,
+                                              p->w.n_div + (z.L - 1), M, static_cast<const __nv_bfloat16*>(child_logits),
+                                              p->w.row_sums, static_cast<__nv_bfloat16*>(const_cast<void*>(dst->logits)),
+                                              const_cast<float*>(dst->logit_row_sums));
+  return check_launch("af_fold_promote");
 }
 
 extern "C" int af_fold_set_timing(void* plan, int enabled) {

@@ -80,6 +80,8 @@ _lib.SIGNATURES.update(
         "af_fold_run": (_i32, [_vp, _vp, _vp, _vp, _vp]),
         "af_fold_get_outputs": (_i32, [_vp, C.POINTER(_FoldOutputs)]),
         "af_fold_materialize": (_i32, [_vp, _i64, _vp, _vp]),
+        "af_fold_keep_kv": (_i32, [_vp, _vp, _i64]),
+        "af_fold_promote": (_i32, [_vp, _i64, _vp, _vp, C.POINTER(_Parent), _vp]),
         "af_fold_plan_destroy": (_i32, [_vp]),
         "af_fold_set_timing": (_i32, [_vp, _i32]),
         "af_fold_get_timing": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32, C.POINTER(_i64)]),
@@ -94,6 +96,7 @@ def _bind_late() -> C.CDLL:
     lib = _lib.load()
     for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
                  "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy",
+                 "af_fold_keep_kv", "af_fold_promote",
                  "af_fold_set_timing", "af_fold_get_timing"):
         fn = getattr(lib, name)
         fn.restype, fn.argtypes = _lib.SIGNATURES[name]
@@ -163,6 +166,10 @@ class ParentCache:
     def tensors(self) -> list[torch.Tensor]:
         return [self.tokens, self.layer_in, self.qkv, self.logits, self.self_stable, self.row_sums]
 
+    def clone(self) -> "ParentCache":
+        """Device copy of every array (the destination of a promotion that keeps this cache intact)."""
+        return ParentCache(*(t.clone() for t in self.tensors()), self.tau)
+
 
 class FoldPlan:
     """A prepared folded pass for C children of length T with m_cap candidate rows."""
@@ -215,6 +222,58 @@ class FoldPlan:
         st = self.lib.af_fold_run(self._plan, child_tokens.data_ptr(), logits.data_ptr(), _lib.ptr(scores),
                                   _lib.stream_ptr(child_tokens.device))
         _lib.check(st, "af_fold_run")
+        self.serial += 1
+        self.last_run = (child_tokens, logits)
+
+    serial = 0          # runs so far (a promotion refers to the last one)
+    last_run = None     # (child_tokens, logits) of the last run
+    _kv_store = None
+
+    def keep_kv(self, enabled: bool = True) -> None:
+        """Keep each layer's candidate QKV rows during the next runs, so any child can be promoted.
+
+        Costs one row-copy launch per layer and an [L, m_cap, q+2kv] bf16
+        store. Enable it before ``capture``.
+        """
+        d = self.model.dims
+        if enabled and self._kv_store is None:
+            self._kv_store = torch.empty((d.n_layers, self.m_cap, d.q_dim + 2 * d.kv_dim), dtype=torch.bfloat16,
+                                         device=self.model.device)
+        store = self._kv_store if enabled else None
+        _lib.check(self.lib.af_fold_keep_kv(self._plan, _lib.ptr(store), 0 if store is None else store.numel() * 2),
+                   "af_fold_keep_kv")
+        self.keeps_kv = enabled
+
+    keeps_kv = False
+
+    def promote(self, child: int, into: ParentCache | None = None) -> ParentCache:
+        """Parent cache of child ``child`` of the last run (the reference's cached child entries).
+
+        ``into=None`` writes a copy of the plan's parent; ``into=plan.parent``
+        promotes in place (the plan then verifies the promoted branch's
+        children, as long as ``LLaDAModel.plan`` finds its self-gate flags
+        unchanged). Stream-ordered; no host synchronisation.
+        """
+        if self.last_run is None:
+            raise RuntimeError("promote: the plan has not run")
+        if not self.keeps_kv:
+            raise RuntimeError("promote: enable keep_kv() before the run whose child is promoted")
+        if into is None:
+            into = self.parent.clone()
+        elif into is not self.parent and into.seq != self.T:
+            raise ValueError(f"promote: destination length {into.seq} differs from {self.T}")
+        toks, logits = self.last_run
+        dst = into.struct()
+        _lib.check(self.lib.af_fold_promote(self._plan, int(child), toks.data_ptr(), logits.data_ptr(), C.byref(dst),
+                                            _lib.stream_ptr(toks.device)), "af_fold_promote")
+        if self.tau != into.tau:
+            # Rows the promotion did not touch carry self-gate flags of another tau.
+            from actfold_b200.core.similarity_gate import SimilarityGate
+
+            x = into.layer_in[:-1]
+            into.self_stable.copy_(SimilarityGate(tau=self.tau)(x, x).to(torch.uint8))
+            into.tau = float(self.tau)
+        return into
 
     def capture(self, child_tokens: torch.Tensor, logits: torch.Tensor, scores: torch.Tensor | None = None
                 ) -> torch.cuda.CUDAGraph:
@@ -392,6 +451,8 @@ class LLaDAModel(nn.Module):
     def plan(self, parent: ParentCache, n_children: int, m_cap: int, tau: float, metric: str = "cosine") -> FoldPlan:
         key = (id(parent), n_children, m_cap, float(tau), metric)
         p = self._plans.get(key)
+        if p is not None and p.parent is parent and p.tau == parent.tau and not np.array_equal(p._su, parent.su_layers()):
+            p = None  # an in-place promotion changed the parent's self-gate flags
         if p is None or p.parent is not parent:
             p = FoldPlan(self, parent, n_children, m_cap, tau, metric)
             self._plans = {k: v for k, v in self._plans.items() if v.parent is parent}
@@ -409,7 +470,8 @@ class LLaDAModel(nn.Module):
         return min(cap, ((C * T + 15) // 16) * 16)
 
     def verify(self, child_tokens: torch.Tensor, parent: ParentCache, tau: float, metric: str = "cosine",
-               logits: torch.Tensor | None = None, scores: torch.Tensor | None = None, m_cap: int | None = None) -> tuple[torch.Tensor, FoldPlan]:
+               logits: torch.Tensor | None = None, scores: torch.Tensor | None = None, m_cap: int | None = None,
+               keep_kv: bool = False) -> tuple[torch.Tensor, FoldPlan]:
         """Folded verification of child_tokens [C, T] against ``parent``; returns (logits [C, T, V], plan)."""
         child_tokens = child_tokens.to(device=self.device, dtype=torch.int64).contiguous()
         if child_tokens.dim() != 2 or child_tokens.shape[1] != parent.seq:
@@ -418,6 +480,8 @@ class LLaDAModel(nn.Module):
         if m_cap is None:
             m_cap = self.capacity(child_tokens, parent, parent.su_layers())
         plan = self.plan(parent, Cn, m_cap, tau, metric)
+        if keep_kv and not plan.keeps_kv:
+            plan.keep_kv(True)
         if logits is None:
             logits = torch.empty((Cn, parent.seq, self.dims.vocab), dtype=torch.bfloat16, device=self.device)
         plan.run(child_tokens, logits, scores)
@@ -444,13 +508,28 @@ class LLaDAModel(nn.Module):
             parents[branch_id] = pc
             register_parent_in_cache(cache, branch_id, pc)
             return pc.logits[None]
+        children = getattr(cache, "native_children", None)
+        if children is None:
+            children = {}
+            cache.native_children = children
         pc = parents.get(parent_branch_id)
+        if pc is None:
+            pc = _promote_recorded_child(cache, parents, children, parent_branch_id)
         if pc is None or pc.seq != tokens.shape[1]:
             # No usable parent activations: recompute (folded_transformer.py:135-141).
             return self.forward(tokens)
-        logits, plan = self.verify(tokens, pc, gate.tau, gate.metric)
+        logits, plan = self.verify(tokens, pc, gate.tau, gate.metric, keep_kv=True)
         plan.check_status()
         ids = list(branch_id) if isinstance(branch_id, (list, tuple)) else [branch_id] * tokens.shape[0]
+        if len(set(ids)) == len(ids):
+            # Every verified child can be named as a later parent_branch_id (the
+            # reference caches each child's activations): it is promoted on
+            # first use, while its plan still holds this run.
+            for k in [k for k, (pl, _, se) in children.items() if pl.serial != se]:
+                del children[k]  # records of runs that are gone
+            for c, bid in enumerate(ids):
+                parents.pop(bid, None)
+                children[bid] = (plan, c, plan.serial)
         if len(set(ids)) == len(ids):
             GLOBAL_STABILITY_PROFILER.record_batch(ids, parent_branch_id, step_idx, plan.stable_masks(), gate.tau, gate.metric)
         else:
@@ -458,6 +537,20 @@ class LLaDAModel(nn.Module):
             for li in range(masks.shape[0]):
                 GLOBAL_STABILITY_PROFILER.record(ids[0], parent_branch_id, li, step_idx, masks[li], gate.tau, gate.metric)
         return logits
+
+
+def _promote_recorded_child(cache, parents: dict, children: dict, branch_id: Any) -> ParentCache | None:
+    """Parent cache of a child verified earlier, promoted from its plan's last run; None when that run is gone."""
+    rec = children.get(branch_id)
+    if rec is None:
+        return None
+    plan, c, serial = rec
+    if plan.serial != serial:
+        return None  # the plan has verified another batch since; that child's rows are overwritten
+    pc = plan.promote(c)
+    parents[branch_id] = pc
+    register_parent_in_cache(cache, branch_id, pc)
+    return pc
 
 
 def register_parent_in_cache(cache, branch_id: Any, pc: ParentCache) -> None:

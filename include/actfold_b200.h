@@ -288,6 +288,31 @@ int af_fold_materialize(void* plan, int64_t layer, void* out, void* stream);
 int af_fold_plan_destroy(void* plan);
 
 /*
+ * Promotion of a verified child to a parent. Replaces the child branch's own
+ * ActivationCache entries, which the reference writes after every merge
+ * (_store_activations, actfold/core/folded_transformer.py:190-199 and
+ * :260-274) so that a later call may name the child as parent_branch_id.
+ *
+ * af_fold_keep_kv: while `store` is set, every af_fold_run also copies each
+ * layer's candidate QKV rows into it (one extra launch per layer). `store`
+ * holds n_layers * m_cap * (q_dim + 2 kv_dim) bf16, 16-byte aligned; NULL
+ * turns the copy off. Set it before capturing a pass into a graph.
+ *
+ * af_fold_promote: writes child `child` of the last run into `dst`, whose
+ * arrays must hold a copy of the plan's parent cache or be the plan's parent
+ * cache itself (in place). Only the child's fresh rows are written: tokens,
+ * layer inputs, QKV rows, self-gate flags (at the plan's tau), and the logits
+ * rows and logit row sums of its last-layer divergent rows, taken from the
+ * run's `child_tokens` [C, T] and `child_logits` [C, T, vocab]. Stream-ordered
+ * after the run; valid until the plan runs again. After an in-place promotion
+ * the caller re-derives su_layers from self_stable and makes a new plan if it
+ * changed.
+ */
+int af_fold_keep_kv(void* plan, void* store, int64_t store_bytes);
+int af_fold_promote(void* plan, int64_t child, const int64_t* child_tokens, const void* child_logits,
+                    const af_parent_cache* dst, void* stream);
+
+/*
  * Per-kernel-class CUDA-event timing of af_fold_run, recorded on the pass's
  * stream when enabled. Classes: 0 candidates/embedding, 1 gate, 2 compaction,
  * 3 QKV GEMM, 4 attention, 5 O GEMM, 6 RMSNorm, 7 gate/up GEMM, 8 down GEMM,

@@ -83,3 +83,14 @@ def llada_folded_children(
             states[li + 1, c] = h[0]
         logits[c] = L.lm_head(h[0], weights, dims)
     return {"masks": masks, "states": states, "logits": logits}
+
+
+def llada_promote(folded: dict, c: int) -> dict:
+    """Child ``c`` of a folded result as a parent (TEST INFRASTRUCTURE).
+
+    The reference stores a verified child's merged per-layer states under its
+    own branch id (actfold/core/folded_transformer.py:190-199, :260-274), so a
+    later child that names it as parent_branch_id is gated against those
+    states and takes their outputs on stable rows.
+    """
+    return {"layer_in": np.ascontiguousarray(folded["states"][:, c]), "logits": np.ascontiguousarray(folded["logits"][c])}

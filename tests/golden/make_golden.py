@@ -18,6 +18,7 @@ Outputs (all small, compressed):
   demo.npz       reference folded pass of demo.py's synthetic model (config 1)
   llada_tiny.npz reference FoldedModel over the restated tiny LLaDA block (bf16)
   dream_tiny.npz same, GQA (Dream-shaped) tiny model
+  llada_chain.npz grandchildren folded against a verified child (chained folding)
 """
 
 from __future__ import annotations
@@ -38,7 +39,7 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 from actfold_b200 import workloads as W  # noqa: E402
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, digest, gate_inputs  # noqa: E402
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, digest, gate_inputs  # noqa: E402
 from oracle import llada as OL  # noqa: E402
 from oracle.llada_torch import TorchLLaDA  # noqa: E402
 
@@ -272,6 +273,53 @@ def make_llada(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     np.savez_compressed(os.path.join(HERE, fname), **out)
 
 
+def make_llada_chain(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
+    """Chained folding: grandchildren verified with parent_branch_id = a verified child's id.
+
+    The reference stores every child's activations (folded_transformer.py:190-199),
+    so the grandchildren fold against the child's merged per-layer states.
+    """
+    from actfold.core.model_wrapper import FoldedModel
+
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    T = spec["T"]
+    parent, children = W.llada_tokens(T, spec["n_prompt"], spec["mask_frac"], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"])
+    k = spec["chain_child"]
+    grand = W.llada_children(children[k], spec["chain_n"], spec["chain_d"], dims.mask_id, spec["chain_seed"])
+    model = TorchLLaDA(w, od, T)
+    cache = core.ActivationCache(max_entries_per_layer=(children.shape[0] + grand.shape[0] + 2) * T, device="cpu")
+    gate = core.SimilarityGate(tau=spec["tau"], metric="cosine")
+    folded = FoldedModel(model, cache, gate)
+    recorded: list = []
+    orig_forward = gate.forward
+
+    def rec_forward(hc, hp):
+        m = orig_forward(hc, hp)
+        recorded.append(m.clone())
+        return m
+
+    gate.forward = rec_forward
+    out = {}
+    with torch.no_grad():
+        folded(torch.from_numpy(parent)[None], branch_id="parent")
+        for c in range(children.shape[0]):
+            folded(torch.from_numpy(children[c])[None], branch_id=f"child{c}", parent_branch_id="parent")
+        masks, logits = [], []
+        for g in range(grand.shape[0]):
+            recorded.clear()
+            lg = folded(torch.from_numpy(grand[g])[None], branch_id=f"grand{g}", parent_branch_id=f"child{k}")
+            masks.append(torch.stack([m[0] for m in recorded]).numpy())
+            logits.append(lg[0].view(torch.int16).numpy().view(np.uint16))
+    out["masks"] = np.stack(masks, axis=1)  # [L, G, T]
+    out["logits_bits"] = np.stack(logits)  # [G, T, V]
+    out["parent"] = parent
+    out["children"] = children
+    out["chain_child"] = np.array(k)
+    out["grandchildren"] = grand
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
 def main() -> None:
     torch.manual_seed(42)
     core = _import_reference()
@@ -281,6 +329,7 @@ def main() -> None:
     make_demo(core)
     make_llada(core, W.LLADA_TINY, TINY_LLADA, "llada_tiny.npz")
     make_llada(core, W.DREAM_TINY, TINY_DREAM, "dream_tiny.npz")
+    make_llada_chain(core, W.LLADA_TINY, TINY_LLADA_CHAIN, "llada_chain.npz")
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from actfold_b200 import workloads as W
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, digest, gate_inputs
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, digest, gate_inputs
 from oracle import demo as OD
 from oracle import folding as OF
 from oracle import llada as OL
@@ -140,3 +140,21 @@ def test_llada_oracle_matches_reference(golden, which):
     # Divergent rows are exactly the unmasked (edited) positions in this workload.
     edited = g["children"] != g["parent"][None]
     assert ((~g["masks"][0]) == edited).all()
+
+
+def test_llada_chain_oracle_matches_reference(golden):
+    """Grandchildren folded against a verified child: the oracle's promotion follows the reference."""
+    g = golden("llada_chain")
+    dims, spec = W.LLADA_TINY, TINY_LLADA_CHAIN
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    parent, children = W.llada_tokens(spec["T"], spec["n_prompt"], spec["mask_frac"], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"])
+    k = int(g["chain_child"])
+    grand = W.llada_children(children[k], spec["chain_n"], spec["chain_d"], dims.mask_id, spec["chain_seed"])
+    np.testing.assert_array_equal(grand, g["grandchildren"])
+    res = OF.llada_folded_children(children, OF.llada_parent(parent, w, od), w, od, spec["tau"])
+    res2 = OF.llada_folded_children(grand, OF.llada_promote(res, k), w, od, spec["tau"])
+    np.testing.assert_array_equal(res2["masks"], g["masks"])
+    assert _bf16_close(res2["logits"], from_bf16_bits(g["logits_bits"])) <= 2e-2
+    # Only the grandchildren's own edits diverge at layer 0: the child's edits are in its promoted states.
+    assert ((~g["masks"][0]) == (grand != children[k][None])).all()
