@@ -42,6 +42,11 @@ struct AttnParams {
   int cand_tma;
   const CUtensorMap* tmap_c;
   int fk_col, fv_col;
+  // Candidate-row mode only: > 0 limits each query tile i to cand_win
+  // candidate key blocks centred on block i. Exact when no child has more
+  // than 128 * (cand_win - 1) / 2 + 1 candidates; a tile whose children have
+  // candidates outside its window ORs AF_STATUS_CAPACITY into status.
+  int cand_win;
   unsigned* status;  // nullable: AF_STATUS_TIMEOUT is ORed in when a bounded wait runs out
 };
 

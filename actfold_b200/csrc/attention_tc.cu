@@ -73,6 +73,12 @@ __device__ __forceinline__ void load_op(uint32_t dst, RowPtr row_ptr, const void
 
 }  // namespace
 
+// Candidate key blocks each query tile scans (see AttnParams::cand_win).
+__host__ __device__ __forceinline__ int cand_blocks(const AttnParams& p) {
+  const int all = p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0;
+  return (p.cand_tma && p.cand_win > 0 && p.cand_win < all) ? p.cand_win : all;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_constant__ CUtensorMap tmK,
                                                               const __grid_constant__ CUtensorMap tmV,
                                                               const __grid_constant__ CUtensorMap tmC,
@@ -91,7 +97,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   // cluster counts candidate blocks by capacity, so every CTA knows its parent
   // blocks (the first n_par of its blocks) before its predecessor finishes.
   const int n_pb = (p.T + kTK - 1) / kTK;
-  const int n_fb = p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0, nb = n_pb + n_fb;
+  // Candidate key blocks of this query tile: all of them, or in candidate-row
+  // mode with a window, the n_fb blocks from fb0 on (candidates are ordered by
+  // child, so the candidates of this tile's children lie around the tile's own
+  // block; checked after the dependency wait).
+  const int n_fb_all = p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0;
+  const int n_fb = cand_blocks(p), nb = n_pb + n_fb;
+  const int fb0 = n_fb < n_fb_all ? min(max((int)blockIdx.x - (p.cand_win - 1) / 2, 0), n_fb_all - n_fb) : 0;
   const int b_lo = split * nb / ns, b_hi = (split + 1) * nb / ns;  // balanced, at most kMaxBlk
   const int nbl = b_hi - b_lo;
   const int n_par = max(0, min(b_hi, n_pb) - b_lo);
@@ -144,6 +156,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     return;
   }
   const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
+  if (n_fb < n_fb_all && tid == 0 && p.fchild) {
+    // The window holds every candidate of this tile's children iff the
+    // candidates just outside it belong to other children (the list is
+    // ordered by child); otherwise keys would be missed: flag it.
+    const int qa = q0, qb = min(q0 + kTQ, n_q) - 1;
+    const int before = fb0 * kTK - 1, after = (fb0 + n_fb) * kTK;
+    const bool miss = (before >= 0 && before < n_f && p.fchild[before] == p.fchild[qa]) ||
+                      (after < n_f && p.fchild[after] == p.fchild[qb]);
+    if (miss && p.status) atomicOr(p.status, AF_STATUS_CAPACITY);
+  }
   if (warp == 0) tmem_alloc(smem_u32(tmem_slot), 512);
   const bool c_tma = p.cand_tma != 0;
   if (c_tma && tid == 0) {
@@ -159,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     for (int j = 0; j < nbl; ++j) {
       const int b = b_lo + j;
       if (b < n_pb) continue;
-      const int y = (b - n_pb) * kTK;
+      const int y = (fb0 + b - n_pb) * kTK;
       for (int hf = 0; hf < 2; ++hf) {
         tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmC, barC, p.fk_col + kvh * 128 + 64 * hf, y);
         tma_load_2d(sV + j * kOpB + hf * kTileB, &tmC, barC, p.fv_col + kvh * 128 + 64 * hf, y);
@@ -178,11 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     const int b = b_lo + j;
     const bool parent_blk = b < n_pb;
     if (!parent_blk && tid < kTK) {
-      const int jj = (b - n_pb) * kTK + tid;
+      const int jj = (fb0 + b - n_pb) * kTK + tid;
       sF[j * kTK + tid] = jj >= n_f ? -2 : (p.fchild ? p.fchild[jj] : -1);
     }
     if ((parent_blk && kv_tma) || (!parent_blk && c_tma)) continue;
-    const int r0 = (parent_blk ? b : b - n_pb) * kTK;
+    const int r0 = (parent_blk ? b : fb0 + b - n_pb) * kTK;
     const int lim = parent_blk ? p.T : n_f;
     const __nv_bfloat16* kb = parent_blk ? p.pk : p.fk;
     const __nv_bfloat16* vb = parent_blk ? p.pv : p.fv;
@@ -435,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
 // Key splits for the tcgen05 kernel, or 0 when the shape needs more than
 // kMaxBlk blocks per split in an 8-CTA cluster.
 int attention_tc_splits(const AttnParams& p) {
-  const int nb = (p.T + kTK - 1) / kTK + (p.fk ? (p.n_f_cap + kTK - 1) / kTK : 0);
+  const int nb = (p.T + kTK - 1) / kTK + cand_blocks(p);
   const int need = (nb + kMaxBlk - 1) / kMaxBlk;
   if (need > 8) return 0;
   // The slowest CTA (most key blocks) sets the time; among the split counts

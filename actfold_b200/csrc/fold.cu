@@ -878,6 +878,8 @@ struct FoldPlan {
   // Caller store [L, m_cap, qkv] for each layer's candidate QKV rows
   // (af_fold_keep_kv); null when promotion is off.
   __nv_bfloat16* kv_keep = nullptr;
+  // Bound on any child's candidate rows per layer (af_fold_set_child_cap); 0: none.
+  int child_cap = 0;
   ~FoldPlan() {
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
@@ -1097,7 +1099,12 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.pdl = pass_pdl() ? 1 : 0;
     ap.kv_static = 1;  // the parent's K/V are fixed for the whole pass
     ap.status = w.status;
-    if (attention_uses_tc(ap)) {
+    // Candidate keys of a query tile's children lie within cand_win candidate
+    // blocks of the tile when no child has more than child_cap candidates.
+    ap.cand_win = p->child_cap > 0 ? 2 * ((p->child_cap - 1 + 127) / 128) + 1 : 0;
+    AttnParams probe = ap;
+    probe.cand_tma = 1;
+    if (attention_uses_tc(probe)) {
       // Candidate-row mode: every candidate row is a query (the query tile is
       // 128 rows whatever the divergent count), so the queries and the
       // candidate keys are plain TMA boxes of the QKV output; only divergent
@@ -1310,6 +1317,14 @@ extern "C" int af_fold_materialize(void* plan, int64_t layer, void* out, void* s
   k_state_scatter<<<(unsigned)((p->m_cap + 7) / 8), 256, 0, s>>>(p->w.x_all + layer * p->m_cap * z.H, z.H, pos, n,
                                                                   p->m_cap, o);
   return check_launch("af_fold_materialize");
+}
+
+extern "C" int af_fold_set_child_cap(void* plan, int64_t max_candidates_per_child) {
+  AF_REQUIRE(plan, "af_fold_set_child_cap: null plan");
+  AF_REQUIRE(max_candidates_per_child >= 0 && max_candidates_per_child <= (1 << 24),
+             "af_fold_set_child_cap: bound out of range");
+  static_cast<FoldPlan*>(plan)->child_cap = (int)max_candidates_per_child;
+  return AF_OK;
 }
 
 extern "C" int af_fold_keep_kv(void* plan, void* store, int64_t store_bytes) {

@@ -81,6 +81,7 @@ _lib.SIGNATURES.update(
         "af_fold_get_outputs": (_i32, [_vp, C.POINTER(_FoldOutputs)]),
         "af_fold_materialize": (_i32, [_vp, _i64, _vp, _vp]),
         "af_fold_keep_kv": (_i32, [_vp, _vp, _i64]),
+        "af_fold_set_child_cap": (_i32, [_vp, _i64]),
         "af_fold_promote": (_i32, [_vp, _i64, _vp, _vp, C.POINTER(_Parent), _vp]),
         "af_fold_plan_destroy": (_i32, [_vp]),
         "af_fold_set_timing": (_i32, [_vp, _i32]),
@@ -96,7 +97,7 @@ def _bind_late() -> C.CDLL:
     lib = _lib.load()
     for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
                  "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy",
-                 "af_fold_keep_kv", "af_fold_promote",
+                 "af_fold_keep_kv", "af_fold_promote", "af_fold_set_child_cap",
                  "af_fold_set_timing", "af_fold_get_timing"):
         fn = getattr(lib, name)
         fn.restype, fn.argtypes = _lib.SIGNATURES[name]
@@ -245,6 +246,19 @@ class FoldPlan:
         self.keeps_kv = enabled
 
     keeps_kv = False
+    child_cap = 0
+
+    def set_child_cap(self, bound: int) -> None:
+        """Bound on any child's candidate rows per layer for the next runs (0: none).
+
+        Lets attention scan only the candidate keys near each tile of packed
+        queries (linear instead of quadratic in the child count); a run that
+        exceeds it reports a capacity error. Set it before ``capture``.
+        """
+        bound = int(bound)
+        if bound != self.child_cap:
+            _lib.check(self.lib.af_fold_set_child_cap(self._plan, bound), "af_fold_set_child_cap")
+            self.child_cap = bound
 
     def promote(self, child: int, into: ParentCache | None = None) -> ParentCache:
         """Parent cache of child ``child`` of the last run (the reference's cached child entries).
@@ -324,7 +338,8 @@ class FoldPlan:
             if s & 1:
                 raise TimeoutError(f"folded pass: a device wait timed out (status {s:#x})")
             if s & 2:
-                raise ValueError(f"folded pass: candidate rows exceeded m_cap={self.m_cap} (status {s:#x})")
+                raise ValueError(f"folded pass: candidate rows exceeded m_cap={self.m_cap} or the per-child bound "
+                                 f"{self.child_cap} (status {s:#x})")
             raise RuntimeError(f"folded pass: device check failed (status {s:#x})")
 
     def __del__(self) -> None:
@@ -462,12 +477,16 @@ class LLaDAModel(nn.Module):
     @staticmethod
     def capacity(child_tokens: torch.Tensor, parent: ParentCache, su: np.ndarray) -> int:
         """Rows a pass can need: edited rows + every child x every row the parent fails its own gate on."""
+        return LLaDAModel.capacity_and_bound(child_tokens, parent, su)[0]
+
+    @staticmethod
+    def capacity_and_bound(child_tokens: torch.Tensor, parent: ParentCache, su: np.ndarray) -> tuple[int, int]:
+        """(m_cap, bound on one child's candidate rows per layer), from one small device read."""
         C, T = child_tokens.shape
-        edited = int((child_tokens != parent.tokens[None]).sum().item())
+        per_child = (child_tokens != parent.tokens[None]).sum(dim=1)
+        edited, most = (int(v) for v in torch.stack([per_child.sum(), per_child.max()]).cpu())
         su_rows = int((parent.self_stable == 0).any(dim=0).sum().item()) if su.any() else 0
-        cap = edited + C * su_rows
-        cap = max(16, ((cap + 15) // 16) * 16)
-        return min(cap, ((C * T + 15) // 16) * 16)
+        return round_capacity(edited + C * su_rows, C, T), most + su_rows
 
     def verify(self, child_tokens: torch.Tensor, parent: ParentCache, tau: float, metric: str = "cosine",
                logits: torch.Tensor | None = None, scores: torch.Tensor | None = None, m_cap: int | None = None,
@@ -477,9 +496,12 @@ class LLaDAModel(nn.Module):
         if child_tokens.dim() != 2 or child_tokens.shape[1] != parent.seq:
             raise ValueError(f"children must be [C, {parent.seq}], got {tuple(child_tokens.shape)}")
         Cn = child_tokens.shape[0]
+        child_cap = None
         if m_cap is None:
-            m_cap = self.capacity(child_tokens, parent, parent.su_layers())
+            m_cap, child_cap = self.capacity_and_bound(child_tokens, parent, parent.su_layers())
         plan = self.plan(parent, Cn, m_cap, tau, metric)
+        if child_cap is not None:
+            plan.set_child_cap(child_cap)
         if keep_kv and not plan.keeps_kv:
             plan.keep_kv(True)
         if logits is None:
@@ -537,6 +559,12 @@ class LLaDAModel(nn.Module):
             for li in range(masks.shape[0]):
                 GLOBAL_STABILITY_PROFILER.record(ids[0], parent_branch_id, li, step_idx, masks[li], gate.tau, gate.metric)
         return logits
+
+
+def round_capacity(rows: int, C: int, T: int) -> int:
+    """Candidate capacity of a pass: ``rows`` rounded up to 16, at least 16, at most C x T (rounded)."""
+    cap = max(16, ((rows + 15) // 16) * 16)
+    return min(cap, ((C * T + 15) // 16) * 16)
 
 
 def _promote_recorded_child(cache, parents: dict, children: dict, branch_id: Any) -> ParentCache | None:

@@ -24,7 +24,7 @@ import numpy as np
 import torch
 
 from actfold_b200.core.similarity_gate import SimilarityGate
-from actfold_b200.llada import LLaDAModel, ParentCache
+from actfold_b200.llada import LLaDAModel, ParentCache, round_capacity
 from actfold_b200.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER, StabilityProfile
 
 
@@ -125,17 +125,21 @@ class ActFoldVerificationEngine:
             }
             self._host = {key: bufs}
         bufs["tok"].copy_(child_tokens_host, non_blocking=True)
-        m_cap = self._m_cap(child_tokens_host, pc, Cn, T)
+        m_cap, child_cap = self._m_cap(child_tokens_host, pc, Cn, T)
         if self.use_graphs:
             plan = self.model.plan(pc, Cn, m_cap, self.gate.tau, self.gate.metric)
-            entry = self._graphs.get(id(plan))
+            plan.set_child_cap(child_cap)
+            gkey = (id(plan), child_cap)
+            entry = self._graphs.get(gkey)
             if entry is None or entry[1] is not plan or entry[2] is not bufs:
                 if len(self._graphs) >= 8:
                     self._graphs = {}
                 entry = (plan.capture(bufs["tok"], bufs["logits"], bufs["scores"]), plan, bufs)
-                self._graphs[id(plan)] = entry
+                self._graphs[gkey] = entry
             entry[0].replay()
         else:
+            plan = self.model.plan(pc, Cn, m_cap, self.gate.tau, self.gate.metric)
+            plan.set_child_cap(child_cap)
             _, plan = self.model.verify(bufs["tok"], pc, self.gate.tau, self.gate.metric, logits=bufs["logits"],
                                         scores=bufs["scores"], m_cap=m_cap)
         bufs["h_scores"].copy_(bufs["scores"], non_blocking=True)
@@ -153,17 +157,15 @@ class ActFoldVerificationEngine:
             "plan": plan,
         }
 
-    def _m_cap(self, child_tokens_host: torch.Tensor, pc: ParentCache, Cn: int, T: int) -> int:
-        # Capacity from the host copy of the tokens (no device round trip).
+    def _m_cap(self, child_tokens_host: torch.Tensor, pc: ParentCache, Cn: int, T: int) -> tuple[int, int]:
+        # (capacity, per-child candidate bound) from the host copy of the tokens (no device round trip).
         ptok = self._parent_host_tokens(pc)
-        edited = int((child_tokens_host.numpy() != ptok[None]).sum())
+        per_child = (child_tokens_host.numpy() != ptok[None]).sum(axis=1)
         su_rows = getattr(pc, "_su_rows", None)
         if su_rows is None:  # rows the parent fails its own gate on (one device read per parent)
             su_rows = int((pc.self_stable == 0).any(dim=0).sum().item())
             pc._su_rows = su_rows
-        cap = edited + Cn * su_rows
-        cap = max(16, ((cap + 15) // 16) * 16)
-        return min(cap, ((Cn * T + 15) // 16) * 16)
+        return round_capacity(int(per_child.sum()) + Cn * su_rows, Cn, T), int(per_child.max()) + su_rows
 
     def _parent_host_tokens(self, pc: ParentCache) -> np.ndarray:
         cached = getattr(pc, "_host_tokens", None)

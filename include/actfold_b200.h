@@ -286,6 +286,20 @@ int af_fold_get_outputs(void* plan, af_fold_outputs* out);
 /* Dense input of layer `layer` (0..n_layers) for every child: out [C, T, hidden] bf16. */
 int af_fold_materialize(void* plan, int64_t layer, void* out, void* stream);
 int af_fold_plan_destroy(void* plan);
+/*
+ * Bound on the candidate rows of any one child per layer, for the next runs
+ * (0, the default: no bound). A child's candidates at layer l are its edited
+ * tokens that are still divergent plus the rows its parent fails its own gate
+ * on, so max edited tokens per child + such parent rows is a bound. With it,
+ * attention lets each tile of 128 packed query rows scan only the candidate
+ * keys near its own rows (the candidate list is ordered by child) instead of
+ * every candidate of every child, which makes attention linear rather than
+ * quadratic in the number of children. A run in which some child exceeds the
+ * bound sets AF_STATUS_CAPACITY in the status word. Host-side setting: make it
+ * before capturing a run into a graph. Has no counterpart in the reference
+ * (the reference recomputes each child separately).
+ */
+int af_fold_set_child_cap(void* plan, int64_t max_candidates_per_child);
 
 /*
  * Promotion of a verified child to a parent. Replaces the child branch's own
