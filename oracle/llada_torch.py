@@ -1,8 +1,9 @@
 """torch (CPU, bf16) module with the arithmetic of ``oracle.llada`` (TEST INFRASTRUCTURE).
 
-Used only by ``tests/golden/make_golden.py``: the reference's FoldedModel
-wraps this module so the golden vectors record the reference's folding
-decisions over the restated LLaDA block. Rounding points are those listed in
+Used by ``tests/golden/make_golden.py`` (the reference's FoldedModel wraps
+this module so the golden vectors record the reference's folding decisions
+over the restated LLaDA block) and, on the GPU at full LLaDA-8B size, by
+``tests/test_full_size_gpu.py`` as the fp32 restatement of one block. Rounding points are those listed in
 ``oracle.llada``.
 """
 
@@ -40,6 +41,18 @@ class TorchLLaDABlock(nn.Module):
             self.register_buffer(k, _t(v))
         self.register_buffer("cos", torch.from_numpy(cos))
         self.register_buffer("sin", torch.from_numpy(sin))
+
+    @classmethod
+    def from_tensors(cls, lw: dict, dims: L.LLaDADims, cos: torch.Tensor, sin: torch.Tensor) -> "TorchLLaDABlock":
+        """Block over bf16 tensors already on a device (wq, wk, wv, wo, w_gate, w_up, w_down, norms)."""
+        blk = cls.__new__(cls)
+        nn.Module.__init__(blk)
+        blk.dims = dims
+        for k, v in lw.items():
+            blk.register_buffer(k, v.to(BF))
+        blk.register_buffer("cos", cos.float())
+        blk.register_buffer("sin", sin.float())
+        return blk
 
     def _rope(self, x: torch.Tensor) -> torch.Tensor:
         T = x.shape[1]
