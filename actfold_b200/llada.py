@@ -167,6 +167,34 @@ class ParentCache:
     def tensors(self) -> list[torch.Tensor]:
         return [self.tokens, self.layer_in, self.qkv, self.logits, self.self_stable, self.row_sums]
 
+    def resized(self, T: int) -> "ParentCache":
+        """The cache as seen by children of length ``T`` (a new cache; the last one is kept for reuse).
+
+        The reference gathers the parent's entry of every child position and
+        zero-fills the positions the parent has none for
+        (actfold/core/fused_ops.py:54-87, 256-324). Rows past this parent's
+        length are therefore zero, with token id -1 so that every child counts
+        them as edited (they gate as divergent against the zero rows); a
+        shorter child sees the first ``T`` rows.
+        """
+        T = int(T)
+        last = getattr(self, "_resized", None)
+        if last is not None and last[0] == T:
+            return last[1]
+        n = min(T, self.seq)
+
+        def fit(a: torch.Tensor, axis: int, fill: float) -> torch.Tensor:
+            shape = list(a.shape)
+            shape[axis] = T
+            b = torch.full(shape, fill, dtype=a.dtype, device=a.device)
+            b.narrow(axis, 0, n).copy_(a.narrow(axis, 0, n))
+            return b
+
+        out = ParentCache(fit(self.tokens, 0, -1), fit(self.layer_in, 1, 0), fit(self.qkv, 1, 0), fit(self.logits, 0, 0),
+                          fit(self.self_stable, 1, 1), fit(self.row_sums, 0, 0), self.tau)
+        self._resized = (T, out)
+        return out
+
     def clone(self) -> "ParentCache":
         """Device copy of every array (the destination of a promotion that keeps this cache intact)."""
         return ParentCache(*(t.clone() for t in self.tensors()), self.tau)
@@ -537,9 +565,11 @@ class LLaDAModel(nn.Module):
         pc = parents.get(parent_branch_id)
         if pc is None:
             pc = _promote_recorded_child(cache, parents, children, parent_branch_id)
-        if pc is None or pc.seq != tokens.shape[1]:
+        if pc is None:
             # No usable parent activations: recompute (folded_transformer.py:135-141).
             return self.forward(tokens)
+        if pc.seq != tokens.shape[1]:
+            pc = pc.resized(tokens.shape[1])  # zero-filled / truncated parent rows, as the reference gathers them
         logits, plan = self.verify(tokens, pc, gate.tau, gate.metric, keep_kv=True)
         plan.check_status()
         ids = list(branch_id) if isinstance(branch_id, (list, tuple)) else [branch_id] * tokens.shape[0]

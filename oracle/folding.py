@@ -94,3 +94,26 @@ def llada_promote(folded: dict, c: int) -> dict:
     states and takes their outputs on stable rows.
     """
     return {"layer_in": np.ascontiguousarray(folded["states"][:, c]), "logits": np.ascontiguousarray(folded["logits"][c])}
+
+
+def llada_resize_parent(parent: dict, T: int) -> dict:
+    """The parent's cached rows for a child of length ``T`` (TEST INFRASTRUCTURE).
+
+    The reference gathers the parent's entry of every child position and
+    zero-fills positions the parent has no entry for
+    (actfold/core/fused_ops.py:54-87, 256-324): rows past the parent's length
+    are zeros; a shorter child sees the parent's first ``T`` rows.
+    """
+    out = {}
+    for k in ("layer_in", "logits"):
+        a = parent[k]
+        ax = a.ndim - 2  # the position axis
+        n = min(T, a.shape[ax])
+        shape = list(a.shape)
+        shape[ax] = T
+        b = np.zeros(shape, a.dtype)
+        idx = [slice(None)] * a.ndim
+        idx[ax] = slice(0, n)
+        b[tuple(idx)] = a[tuple(idx)]
+        out[k] = b
+    return out

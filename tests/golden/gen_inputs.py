@@ -62,5 +62,8 @@ def digest(*arrays: np.ndarray) -> str:
 TINY_LLADA = dict(T=64, n_prompt=16, mask_frac=0.5, n_children=4, d=4, tau=0.95, weight_seed=7, token_seed=42)
 # Chained folding: grandchildren of child `chain_child` of the TINY_LLADA workload.
 TINY_LLADA_CHAIN = dict(TINY_LLADA, chain_child=1, chain_n=3, chain_d=3, chain_seed=44)
+# Children of another length than their parent: a 48-id parent, children of 64 ids
+# (16 appended) and of 40 ids (a prefix with d edits).
+TINY_LLADA_RESIZE = dict(TINY_LLADA, parent_len=48, short_len=40, n_children=3, d=2)
 TINY_DREAM = dict(T=64, n_prompt=16, mask_frac=0.75, n_children=3, d=3, tau=0.95, weight_seed=11, token_seed=43)
 DEMO = dict(T=16, n_children=2, tau=0.95, weight_seed=42, token_seed=42)

@@ -19,6 +19,7 @@ Outputs (all small, compressed):
   llada_tiny.npz reference FoldedModel over the restated tiny LLaDA block (bf16)
   dream_tiny.npz same, GQA (Dream-shaped) tiny model
   llada_chain.npz grandchildren folded against a verified child (chained folding)
+  llada_resize.npz children longer / shorter than their parent (zero-filled parent rows)
 """
 
 from __future__ import annotations
@@ -39,7 +40,7 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 from actfold_b200 import workloads as W  # noqa: E402
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, digest, gate_inputs  # noqa: E402
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, digest, gate_inputs  # noqa: E402
 from oracle import llada as OL  # noqa: E402
 from oracle.llada_torch import TorchLLaDA  # noqa: E402
 
@@ -320,6 +321,52 @@ def make_llada_chain(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     np.savez_compressed(os.path.join(HERE, fname), **out)
 
 
+def make_llada_resize(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
+    """Children longer and shorter than their parent.
+
+    The reference gathers the parent's entries for the child's positions and
+    zero-fills the ones the parent lacks (fused_ops.py:54-87), so appended
+    positions gate as divergent against zero rows while the shared prefix folds.
+    """
+    from actfold.core.model_wrapper import FoldedModel
+
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    T, Tp, Ts = spec["T"], spec["parent_len"], spec["short_len"]
+    full, _ = W.llada_tokens(T, spec["n_prompt"], spec["mask_frac"], 1, 1, dims.mask_id, spec["token_seed"])
+    parent = full[:Tp].copy()
+    rng = np.random.default_rng(spec["token_seed"] + 1)
+    longer = np.repeat(full[None], spec["n_children"], axis=0)
+    longer[:, Tp:] = rng.integers(0, dims.mask_id, size=(spec["n_children"], T - Tp))
+    shorter = W.llada_children(parent[:Ts], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"] + 2)
+    model = TorchLLaDA(w, od, T)
+    cache = core.ActivationCache(max_entries_per_layer=(2 * spec["n_children"] + 2) * T, device="cpu")
+    gate = core.SimilarityGate(tau=spec["tau"], metric="cosine")
+    folded = FoldedModel(model, cache, gate)
+    recorded: list = []
+    orig_forward = gate.forward
+
+    def rec_forward(hc, hp):
+        m = orig_forward(hc, hp)
+        recorded.append(m.clone())
+        return m
+
+    gate.forward = rec_forward
+    out = {"parent": parent, "longer": longer, "shorter": shorter}
+    with torch.no_grad():
+        folded(torch.from_numpy(parent)[None], branch_id="parent")
+        for name, kids in (("longer", longer), ("shorter", shorter)):
+            masks, logits = [], []
+            for c in range(kids.shape[0]):
+                recorded.clear()
+                lg = folded(torch.from_numpy(kids[c])[None], branch_id=f"{name}{c}", parent_branch_id="parent")
+                masks.append(torch.stack([m[0] for m in recorded]).numpy())
+                logits.append(lg[0].view(torch.int16).numpy().view(np.uint16))
+            out[f"{name}_masks"] = np.stack(masks, axis=1)
+            out[f"{name}_logits_bits"] = np.stack(logits)
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
 def main() -> None:
     torch.manual_seed(42)
     core = _import_reference()
@@ -330,6 +377,7 @@ def main() -> None:
     make_llada(core, W.LLADA_TINY, TINY_LLADA, "llada_tiny.npz")
     make_llada(core, W.DREAM_TINY, TINY_DREAM, "dream_tiny.npz")
     make_llada_chain(core, W.LLADA_TINY, TINY_LLADA_CHAIN, "llada_chain.npz")
+    make_llada_resize(core, W.LLADA_TINY, TINY_LLADA_RESIZE, "llada_resize.npz")
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from actfold_b200 import workloads as W
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, digest, gate_inputs
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, digest, gate_inputs
 from oracle import demo as OD
 from oracle import folding as OF
 from oracle import llada as OL
@@ -158,3 +158,17 @@ def test_llada_chain_oracle_matches_reference(golden):
     assert _bf16_close(res2["logits"], from_bf16_bits(g["logits_bits"])) <= 2e-2
     # Only the grandchildren's own edits diverge at layer 0: the child's edits are in its promoted states.
     assert ((~g["masks"][0]) == (grand != children[k][None])).all()
+
+
+def test_llada_resize_oracle_matches_reference(golden):
+    """Children longer / shorter than the parent fold against zero-filled / truncated parent rows."""
+    g = golden("llada_resize")
+    dims, spec = W.LLADA_TINY, TINY_LLADA_RESIZE
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    par = OF.llada_parent(g["parent"], w, od)
+    for name in ("longer", "shorter"):
+        kids = g[name]
+        res = OF.llada_folded_children(kids, OF.llada_resize_parent(par, kids.shape[1]), w, od, spec["tau"])
+        np.testing.assert_array_equal(res["masks"], g[f"{name}_masks"])
+        assert _bf16_close(res["logits"], from_bf16_bits(g[f"{name}_logits_bits"])) <= 2e-2

@@ -142,3 +142,64 @@ def test_folded_model_chains_through_a_verified_child(chain, golden):
     assert set(cache.get(f"child{k}", 0, ones)) == {"ffn_out", "hidden_states"}
     cache.clear_branch(f"child{k}")
     assert f"child{k}" not in cache.native_parents and f"child{k}" not in cache.native_children
+
+
+@pytest.mark.parametrize("name", ["longer", "shorter"])
+def test_children_of_another_length_fold_like_the_reference(golden, name):
+    """A child longer than its parent folds against zero-filled parent rows; a shorter one against a prefix."""
+    from actfold_b200.core import ActivationCache, FoldedModel, SimilarityGate
+    from actfold_b200.llada import LLaDAModel
+    from gen_inputs import TINY_LLADA_RESIZE
+
+    g = golden("llada_resize")
+    spec = TINY_LLADA_RESIZE
+    w = W.llada_weights_numpy(DIMS, seed=spec["weight_seed"])
+    model = LLaDAModel.from_numpy(DIMS, w, device="cuda", max_pos=64)
+    fm = FoldedModel(model, ActivationCache(max_entries_per_layer=1 << 16, device="cuda"), SimilarityGate(tau=spec["tau"]))
+    fm(torch.from_numpy(g["parent"])[None].cuda(), branch_id="parent")
+    kids = g[name]
+    lg = fm(torch.from_numpy(kids).cuda(), branch_id=[f"{name}{i}" for i in range(kids.shape[0])], parent_branch_id="parent")
+    torch.cuda.synchronize()
+    od = _odims(DIMS)
+    ref = OF.llada_folded_children(kids, OF.llada_resize_parent(OF.llada_parent(g["parent"], w, od), kids.shape[1]), w, od,
+                                   spec["tau"])
+    np.testing.assert_array_equal(ref["masks"], g[f"{name}_masks"])
+    got = lg.float().cpu().numpy()
+    for want in (ref["logits"], from_bf16_bits(g[f"{name}_logits_bits"])):
+        assert _rel(got, want) <= 2e-2 and _cos(got, want) >= 0.999 and _argmax_agreement(got, want) >= 0.999
+    from actfold_b200.profiler import GLOBAL_STABILITY_PROFILER
+
+    for i in range(kids.shape[0]):
+        prof = GLOBAL_STABILITY_PROFILER.get_profile(f"{name}{i}")
+        np.testing.assert_allclose([s.stable_ratio for s in prof.layer_stats], g[f"{name}_masks"][:, i].mean(-1), atol=1e-6)
+
+
+def test_autoregressive_chain_folds_natively(chain):
+    """Greedy next-token generation as folded_generate runs it (speculative/folded_generation.py:44-138):
+    each step's child is the previous branch plus one token, verified with the previous branch as its parent.
+
+    Every step folds on the native pass (a one-row-longer child against the zero-filled, promoted parent)
+    and matches the oracle chain (resize + fold + promote) on the same tokens.
+    """
+    from actfold_b200.core import ActivationCache, FoldedModel, SimilarityGate
+
+    m, w = chain["model"], chain["w"]
+    od = _odims(DIMS)
+    cache = ActivationCache(max_entries_per_layer=1 << 16, device="cuda")
+    fm = FoldedModel(m, cache, SimilarityGate(tau=SPEC["tau"]))
+    tokens = chain["parent"][:56].copy()
+    logits = fm(torch.from_numpy(tokens)[None].cuda(), branch_id="root")
+    ref_parent = OF.llada_parent(tokens, w, od)
+    pid = "root"
+    for step in range(4):
+        nxt = int(logits[0, -1].float().argmax())
+        tokens = np.concatenate([tokens, [nxt]])
+        cid = f"{pid}/t{step}/d0"
+        logits = fm(torch.from_numpy(tokens)[None].cuda(), branch_id=cid, parent_branch_id=pid)
+        assert cid in cache.native_children  # verified on the folded pass, promotable
+        ref = OF.llada_folded_children(tokens[None], OF.llada_resize_parent(ref_parent, tokens.size), w, od, SPEC["tau"])
+        assert (~ref["masks"][0, 0]).sum() == 1 and not ref["masks"][0, 0, -1]  # only the new token diverges at layer 0
+        got = logits[0].float().cpu().numpy()
+        assert _rel(got, ref["logits"][0]) <= 2e-2 and _cos(got, ref["logits"][0]) >= 0.999
+        ref_parent = OF.llada_promote(ref, 0)
+        pid = cid
