@@ -1,10 +1,12 @@
 // Similarity gate with fused stream compaction (sm_100a).
 //
-// One warp per token row. The row is loaded once with 128-bit non-coherent
-// loads into registers (up to 16 vectors per lane: H <= 4096 bf16 or 2048 f32),
-// then reduced twice from registers (norms, then normalized products) with
-// warp-shuffle sums in fp32. Larger or unaligned rows use a scalar path that
-// re-reads the row.
+// One warp per token row of up to 64 16-byte vectors, one 256-thread CTA per
+// longer row (up to 512 vectors: H <= 4096 bf16 or 2048 f32), and for a bf16
+// cosine gate against one parent row shared by every child, one CTA per
+// position and 8 children. The row is loaded once with 128-bit non-coherent
+// loads into registers, then reduced twice from registers (norms, then
+// normalized products) with shuffle / block sums in fp32. Larger or unaligned
+// rows use a scalar path that re-reads the row.
 //
 // Numerics follow the reference gate (actfold/core/similarity_gate.py:76-103
 // -> ATen cosine_similarity): for reduced-precision inputs every elementwise
@@ -41,6 +43,115 @@ __global__ void __launch_bounds__(256) k_gate_vec(const GateParams p) {
   if (lane == 0) {
     p.mask[b * p.m_bs + t] = r.stable;
     if (p.sim) p.sim[row] = r.sim;
+  }
+}
+
+// Rows of more than 64 16-byte vectors (bf16 H > 512): one CTA of
+// kGateRowThreads threads per row, at most two vectors per thread per tensor,
+// and block reductions. With a warp per row such rows keep up to 128 values
+// per lane in registers and add them in one dependent chain, which caps the
+// kernel far below HBM speed (one CTA per SM, latency bound).
+constexpr int kGateRowThreads = 256;
+
+template <int DT, int METRIC, int NV>
+__global__ void __launch_bounds__(kGateRowThreads) k_gate_row(const GateParams p) {
+  __shared__ float red[2 * kGateRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  if (row >= p.rows) return;
+  const int64_t b = row / p.T, t = row - b * p.T;
+  uint4 cv[NV], pv[NV];
+  load_row<NV, kGateRowThreads>(p.child + b * p.c_bs + t * p.c_ts, p.nvec, threadIdx.x, cv);
+  load_row<NV, kGateRowThreads>(p.parent + b * p.p_bs + t * p.p_ts, p.nvec, threadIdx.x, pv);
+  GateOut r;
+  if constexpr (DT == AF_DTYPE_BF16 && METRIC == AF_METRIC_COSINE)
+    r = gate_regs_bf16_cos<NV>(cv, pv, p.nvec, p.k, threadIdx.x, CtaRows<kGateRowThreads>{red});
+  else
+    r = gate_regs<DT, METRIC, NV>(cv, pv, p.nvec, p.H, p.k, threadIdx.x, CtaRows<kGateRowThreads>{red});
+  if (threadIdx.x == 0) {
+    p.mask[b * p.m_bs + t] = r.stable;
+    if (p.sim) p.sim[row] = r.sim;
+  }
+}
+
+// bf16 cosine gate of children against ONE parent row per position (parent
+// batch stride 0, the cached parent broadcast over the children): CTA
+// (t, chunk) takes position t for kBcastChildren children. The parent row is
+// loaded and normalised once; each child's row is loaded while the previous
+// child's row is reduced, so the CTA streams rows instead of waiting on one.
+// Same per-thread summation order as gate_regs_bf16_cos: the same bits.
+constexpr int kBcastChildren = 8;
+
+template <int NV>
+__global__ void __launch_bounds__(kGateRowThreads) k_gate_bcast(const GateParams p) {
+  constexpr int G = kGateRowThreads;
+  __shared__ float red[2 * G / 32];
+  const CtaRows<G> rows{red};
+  const int tid = threadIdx.x;
+  const int64_t t = blockIdx.x;
+  const int64_t B = p.rows / p.T;
+  const int64_t b0 = (int64_t)blockIdx.y * kBcastChildren;
+  const int64_t b1 = min(B, b0 + kBcastChildren);
+  if (t >= p.T || b0 >= B) return;
+  uint4 pv[NV], cv[NV], nv[NV];
+  load_row<NV, G>(p.parent + t * p.p_ts, p.nvec, tid, pv);
+  load_row<NV, G>(p.child + b0 * p.c_bs + t * p.c_ts, p.nvec, tid, cv);
+  // Parent: norm and normalised values, once.
+  float yp[NV][8];
+  float sp = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    unpack<AF_DTYPE_BF16>(pv[i], yp[i]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sp = fmaf(yp[i][e], yp[i][e], sp);
+  }
+  sp = rows.sum(sp);
+  float np = rnd<AF_DTYPE_BF16>(__fsqrt_rn(sp));
+  np = np < p.k.eps_r ? p.k.eps_r : np;  // clamp_min keeps NaN
+  const float rp = __frcp_rn(np);
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float2 y = __bfloat1622float2(
+          __floats2bfloat162_rn(quot_bf16(yp[i][e], np, rp), quot_bf16(yp[i][e + 1], np, rp)));
+      yp[i][e] = y.x;
+      yp[i][e + 1] = y.y;
+    }
+  for (int64_t b = b0; b < b1; ++b) {
+    if (b + 1 < b1) load_row<NV, G>(p.child + (b + 1) * p.c_bs + t * p.c_ts, p.nvec, tid, nv);
+    float fc[NV][8];
+    float sc = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      unpack<AF_DTYPE_BF16>(cv[i], fc[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sc = fmaf(fc[i][e], fc[i][e], sc);
+    }
+    sc = rows.sum(sc);
+    float nc = rnd<AF_DTYPE_BF16>(__fsqrt_rn(sc));
+    nc = nc < p.k.eps_r ? p.k.eps_r : nc;  // clamp_min keeps NaN
+    const float rc = __frcp_rn(nc);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i * G + tid >= p.nvec) continue;
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float2 yc = __bfloat1622float2(
+            __floats2bfloat162_rn(quot_bf16(fc[i][e], nc, rc), quot_bf16(fc[i][e + 1], nc, rc)));
+        const float2 pr =
+            __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(yc.x, yp[i][e]), __fmul_rn(yc.y, yp[i][e + 1])));
+        s = __fadd_rn(s, pr.x);
+        s = __fadd_rn(s, pr.y);
+      }
+    }
+    const float sim = rnd<AF_DTYPE_BF16>(rows.sum(s));
+    if (tid == 0) {
+      p.mask[b * p.m_bs + t] = sim > p.k.tau_r ? 1 : 0;
+      if (p.sim) p.sim[b * p.T + t] = sim;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cv[i] = nv[i];
   }
 }
 
@@ -119,6 +230,23 @@ static int launch_gate(const GateParams& p, bool vec, cudaStream_t s) {
   if (!vec) {
     k_gate_scalar<DT, METRIC><<<(unsigned)blocks, threads, 0, s>>>(p);
     return check_launch("af_gate(scalar)");
+  }
+  if constexpr (DT == AF_DTYPE_BF16 && METRIC == AF_METRIC_COSINE) {
+    if (p.p_bs == 0 && p.nvec > 64 && p.nvec <= 2 * kGateRowThreads) {
+      const int64_t B = p.rows / p.T;
+      if (p.T > 0x7fffffff) return fail(AF_ERR_ARG, "af_gate: seq too large");
+      const dim3 grid((unsigned)p.T, (unsigned)ceil_div(B, (int64_t)kBcastChildren));
+      if (grid.y > 65535) return fail(AF_ERR_ARG, "af_gate: batch too large");
+      if (p.nvec <= kGateRowThreads) k_gate_bcast<1><<<grid, kGateRowThreads, 0, s>>>(p);
+      else k_gate_bcast<2><<<grid, kGateRowThreads, 0, s>>>(p);
+      return check_launch("af_gate(broadcast)");
+    }
+  }
+  if (p.nvec > 64 && p.nvec <= 2 * kGateRowThreads) {
+    if (p.rows > 0x7fffffff) return fail(AF_ERR_ARG, "af_gate: too many rows");
+    if (p.nvec <= kGateRowThreads) k_gate_row<DT, METRIC, 1><<<(unsigned)p.rows, kGateRowThreads, 0, s>>>(p);
+    else k_gate_row<DT, METRIC, 2><<<(unsigned)p.rows, kGateRowThreads, 0, s>>>(p);
+    return check_launch("af_gate(row)");
   }
   const int nv = (p.nvec + 31) / 32;
   if (nv <= 1) k_gate_vec<DT, METRIC, 1><<<(unsigned)blocks, threads, 0, s>>>(p);

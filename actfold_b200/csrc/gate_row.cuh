@@ -239,6 +239,68 @@ __device__ __forceinline__ GateOut gate_regs(const uint4 (&cv)[NV], const uint4 
   return o;
 }
 
+// bf16 x / n for bf16 x and n > 0: x * (1/n) in fp32 rounds to the same bf16
+// value as the fp32 quotient. The exact quotient of two bf16 values is never a
+// bf16 rounding midpoint (a midpoint has an odd 9-bit significand M, and
+// x = M * n / 2^s would need 2^s to divide n's 8-bit significand, leaving
+// x's significand >= M > 255), and when it is not one it lies at least 2^-17
+// (relative) away from every midpoint, while the product and the quotient are
+// within 2^-23 of it. Only results in the subnormal range, where those bounds
+// do not hold, take the IEEE division.
+__device__ __forceinline__ float quot_bf16(float x, float n, float r) {
+  float y = __fmul_rn(x, r);
+  if (fabsf(y) < 0x1p-125f) y = __fdiv_rn(x, n);
+  return y;  // rounded to bf16 by the caller
+}
+
+// gate_regs<bf16, cosine> with the same per-thread order of every fp32 sum, so
+// the same similarity bit for bit, in fewer instructions: the row's floats are
+// kept from the norm pass, the normalised values and their products are
+// rounded two at a time (cvt.rn.bf16x2.f32), and the quotient needs no check
+// (quot_bf16). The product of two bf16 values is exact in fp32, so rounding it
+// once equals rnd(fmul).
+template <int NV, class Rows>
+__device__ __forceinline__ GateOut gate_regs_bf16_cos(const uint4 (&cv)[NV], const uint4 (&pv)[NV], int nvec,
+                                                      const GateConsts& k, int tid, const Rows& rows) {
+  constexpr int G = Rows::kThreads;
+  float fc[NV][8], fp[NV][8];
+  float sc = 0.f, sp = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    unpack<AF_DTYPE_BF16>(cv[i], fc[i]);
+    unpack<AF_DTYPE_BF16>(pv[i], fp[i]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sc = fmaf(fc[i][e], fc[i][e], sc);
+      sp = fmaf(fp[i][e], fp[i][e], sp);
+    }
+  }
+  rows.sum2(sc, sp);
+  float nc, np;
+  finish_cos<AF_DTYPE_BF16, AF_METRIC_COSINE>(sc, sp, k, nc, np);
+  const float rc = __frcp_rn(nc), rp = __frcp_rn(np);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i * G + tid >= nvec) continue;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float2 yc = __bfloat1622float2(
+          __floats2bfloat162_rn(quot_bf16(fc[i][e], nc, rc), quot_bf16(fc[i][e + 1], nc, rc)));
+      const float2 yp = __bfloat1622float2(
+          __floats2bfloat162_rn(quot_bf16(fp[i][e], np, rp), quot_bf16(fp[i][e + 1], np, rp)));
+      const float2 pr = __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(yc.x, yp.x), __fmul_rn(yc.y, yp.y)));
+      s = __fadd_rn(s, pr.x);
+      s = __fadd_rn(s, pr.y);
+    }
+  }
+  GateOut o;
+  o.sim = rnd<AF_DTYPE_BF16>(rows.sum(s));
+  o.stable = o.sim > k.tau_r ? 1 : 0;
+  o.ss_c = sc;
+  return o;
+}
+
 // Scalar fallback: any H and alignment; re-reads the row for each pass.
 template <int DT, int METRIC>
 __device__ __forceinline__ GateOut gate_row_scalar(const char* c, const char* q, int H, const GateConsts& k,

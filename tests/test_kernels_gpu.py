@@ -71,6 +71,25 @@ def test_gate_bf16_edges_on_device():
     assert SimilarityGate(0.95)(c, p.expand(4, 5, 256)).all()
 
 
+@pytest.mark.parametrize("B,H", [(20, 4096), (3, 3584), (9, 1024)])
+def test_gate_broadcast_parent_kernel(B, H):
+    """A parent row shared by every child (batch stride 0) takes the broadcast kernel: the same similarity
+    bits as the per-row kernel on a materialised parent, and the oracle's decisions."""
+    from actfold_b200.core import SimilarityGate
+
+    c, p = gate_inputs(40 + B, B, 64, H, "bf16")
+    p1 = p[:1]
+    sg = SimilarityGate(tau=0.95)
+    tp = _dev(p1, "bf16")
+    sim_b = sg.similarity(_dev(c, "bf16"), tp.expand(B, 64, H)).cpu().numpy()
+    sim_r = sg.similarity(_dev(c, "bf16"), tp.expand(B, 64, H).contiguous()).cpu().numpy()
+    np.testing.assert_array_equal(sim_b.view(np.uint32), sim_r.view(np.uint32))
+    mask = sg(_dev(c, "bf16"), tp.expand(B, 64, H)).cpu().numpy()
+    ora = gate(c, np.broadcast_to(p1, c.shape), 0.95, "cosine", 1e-8, "bf16")
+    assert not ((mask != ora.mask) & ~exempt_rows(ora)).any()
+    assert ((sim_b == ora.sim) | (np.isnan(sim_b) & np.isnan(ora.sim))).mean() >= 0.999
+
+
 @pytest.mark.parametrize("H", [4096, 3584, 100])
 def test_gate_large_and_odd_hidden(H):
     from actfold_b200.core import SimilarityGate
