@@ -5,8 +5,11 @@
 // The array lives in this translation unit alone, so under lazy module
 // loading its device memory is taken only by processes that call this entry
 // point. Its device address is looked up once per device with
-// cudaGetSymbolAddress (the device that owns the stream must be current) and
-// cached; the call then runs af_dense_forward unchanged on that scratch.
+// cudaGetSymbolAddress (the device that owns the stream must be current; a
+// stream of another device is refused) and cached for the life of the
+// process: after cudaDeviceReset the cached address is stale, so a process
+// that resets a device must not call this entry point again. The call then
+// runs af_dense_forward unchanged on that scratch.
 // Every scratch buffer of the dense pass is written in full before it is read
 // (normalised rows, attention output, residual rows, SwiGLU rows, positions),
 // so no part of the array has to start at zero; the outputs that must start
@@ -60,6 +63,18 @@ extern "C" int af_dense_forward_static(const af_model* model, const int64_t* tok
     return af::fail(AF_ERR_CAPACITY, "af_dense_forward_static: T=" + std::to_string(T) + " needs " + std::to_string(need) +
                                          " scratch bytes, above the static limit of " +
                                          std::to_string((long long)AF_DENSE_STATIC_WORKSPACE_BYTES));
+  if (stream) {
+    // The cached address belongs to the current device; a stream of another
+    // device would hand the kernels a scratch pointer of the wrong GPU.
+    int cur = -1, sdev = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e == cudaSuccess) e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+    if (e != cudaSuccess)
+      return af::fail(AF_ERR_CUDA, std::string("af_dense_forward_static: stream device: ") + cudaGetErrorString(e));
+    if (sdev != cur)
+      return af::fail(AF_ERR_ARG, "af_dense_forward_static: the stream belongs to device " + std::to_string(sdev) +
+                                      " but device " + std::to_string(cur) + " is current");
+  }
   void* scratch = nullptr;
   if ((st = scratch_of_current_device(&scratch))) return st;
   return af_dense_forward(model, tokens, T, tau, layer_in, qkv, logits, self_stable, logit_row_sums, scratch,

@@ -199,6 +199,16 @@ class ParentCache:
         """Device copy of every array (the destination of a promotion that keeps this cache intact)."""
         return ParentCache(*(t.clone() for t in self.tensors()), self.tau)
 
+    # Values derived from the device arrays and kept on the host for reuse:
+    # the host copy of the token ids, the count of rows the parent fails its
+    # own gate on, and the last resized view.
+    _DERIVED = ("_host_tokens", "_su_rows", "_resized")
+
+    def contents_changed(self) -> None:
+        """Drop the host-side values derived from this cache (after its arrays are rewritten in place)."""
+        for name in self._DERIVED:
+            self.__dict__.pop(name, None)
+
 
 class FoldPlan:
     """A prepared folded pass for C children of length T with m_cap candidate rows."""
@@ -308,6 +318,7 @@ class FoldPlan:
         dst = into.struct()
         _lib.check(self.lib.af_fold_promote(self._plan, int(child), toks.data_ptr(), logits.data_ptr(), C.byref(dst),
                                             _lib.stream_ptr(toks.device)), "af_fold_promote")
+        into.contents_changed()  # its token ids and self-gate rows are the child's now
         if self.tau != into.tau:
             # Rows the promotion did not touch carry self-gate flags of another tau.
             from actfold_b200.core.similarity_gate import SimilarityGate

@@ -75,19 +75,48 @@ def broadcast_parent_cache(pc: ParentCache, src: int = 0, group: dist.ProcessGro
     for t in pc.tensors():
         # Every tensor moves as its bytes (uint8 is supported by every backend).
         dist.broadcast(t.view(torch.uint8), src=src, group=group)
+    pc.contents_changed()
     return pc
 
 
 def gather_child_results(scores: torch.Tensor, div_count: torch.Tensor, group: dist.ProcessGroup | None = None
                          ) -> tuple[torch.Tensor, torch.Tensor]:
-    """All-gather every rank's per-child scores [c] and divergent counts [L, c] (equal c on all ranks).
+    """All-gather every rank's per-child scores [c_r] and divergent counts [L, c_r].
 
-    Returns (scores [world * c], div_count [L, world * c]) in rank order, i.e. in
-    global child order for the contiguous shards of `shard_children`.
+    Ranks may hold different child counts c_r (``shard_children`` gives the last
+    ranks fewer children when C is not a multiple of the world size). The
+    counts are gathered first; every rank then sends its rows padded to the
+    largest count, so all ranks take part in equal-sized collectives, and the
+    padding is dropped. A rank whose layer count differs raises ValueError on
+    every rank. Returns (scores [sum c_r], div_count [L, sum c_r]) in rank
+    order, i.e. in global child order for the contiguous shards of
+    ``shard_children``.
     """
     world = dist.get_world_size(group)
-    s_all = [torch.empty_like(scores) for _ in range(world)]
-    d_all = [torch.empty_like(div_count) for _ in range(world)]
-    dist.all_gather(s_all, scores.contiguous(), group=group)
-    dist.all_gather(d_all, div_count.contiguous(), group=group)
-    return torch.cat(s_all), torch.cat(d_all, dim=-1)
+    dev = scores.device
+    # A malformed call is reported on every rank, after the first collective,
+    # so no rank is left waiting in the next one.
+    ok = int(scores.dim() == 1 and div_count.dim() == 2 and div_count.shape[1] == scores.shape[0])
+    meta = torch.tensor([scores.shape[0], div_count.shape[0] if div_count.dim() == 2 else -1, ok],
+                        dtype=torch.int64, device=dev)
+    metas = [torch.empty_like(meta) for _ in range(world)]
+    dist.all_gather(metas, meta, group=group)
+    if not all(int(m[2]) for m in metas):
+        raise ValueError(f"gather_child_results: scores [c] and div_count [L, c] disagree on some rank "
+                         f"(this rank: scores {tuple(scores.shape)}, div_count {tuple(div_count.shape)})")
+    counts = [int(m[0]) for m in metas]
+    layers = {int(m[1]) for m in metas}
+    if len(layers) != 1:
+        raise ValueError(f"gather_child_results: ranks disagree on the layer count ({sorted(layers)})")
+    cmax = max(counts)
+    L = div_count.shape[0]
+    s_pad = torch.zeros(cmax, dtype=scores.dtype, device=dev)
+    s_pad[: scores.shape[0]] = scores
+    d_pad = torch.zeros((L, cmax), dtype=div_count.dtype, device=dev)
+    d_pad[:, : div_count.shape[1]] = div_count
+    s_all = [torch.empty_like(s_pad) for _ in range(world)]
+    d_all = [torch.empty_like(d_pad) for _ in range(world)]
+    dist.all_gather(s_all, s_pad, group=group)
+    dist.all_gather(d_all, d_pad, group=group)
+    return (torch.cat([s[:c] for s, c in zip(s_all, counts)]),
+            torch.cat([d[:, :c] for d, c in zip(d_all, counts)], dim=-1))

@@ -141,6 +141,26 @@ def llada_children(parent: np.ndarray, n_children: int, d: int, mask_id: int, se
     return _unmask_children(parent, masked, n_children, d, mask_id, rng)
 
 
+def uniform_edit_children(parent: np.ndarray, n_children: int, d: int, id_hi: int, seed: int) -> np.ndarray:
+    """Children [C, T] that each differ from the parent at ``d`` uniformly chosen positions.
+
+    The new ids are uniform over [0, id_hi) and never equal the parent's id at
+    that position (the Dream-7B workload: 16 children, 8 positions each).
+    """
+    rng = np.random.default_rng(seed)
+    T = parent.shape[0]
+    if d > T:
+        raise ValueError(f"d={d} exceeds the sequence length {T}")
+    children = np.repeat(parent[None], n_children, axis=0)
+    for c in range(n_children):
+        for p in rng.choice(T, size=d, replace=False):
+            new = parent[p]
+            while new == parent[p]:
+                new = int(rng.integers(0, id_hi))
+            children[c, p] = new
+    return children
+
+
 def demo_weights(seed: int = 42, vocab: int = 1000, hidden: int = 128, n_layers: int = 4, std: float = 0.02) -> dict:
     """Weights of demo.py's SyntheticTransformer re-drawn N(0, std); zero biases, unit LayerNorms."""
     rng = np.random.default_rng(seed)

@@ -13,9 +13,11 @@ verifies its own 8 children (weak scaling, no collective inside a step).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Prints one JSON line (rank 0). ``--impl reference`` times the reference
-algorithm (full-layer recompute per child, gate, merge, LM head) restated in
-numpy on the host cores, on a bounded sample extrapolated to one pass.
+Prints one JSON line (rank 0). ``--impl reference`` times the reference's own
+path on the host cores (``oracle.reference_cpu``: its FoldedModel layer flow
+with the per-token activation cache, the full-layer recompute of every row and
+the full-vocabulary LM head, in bf16 on torch CPU kernels), one whole child
+verification per step.
 """
 
 from __future__ import annotations
@@ -63,6 +65,7 @@ def parse_args():
     ap.add_argument("--model", choices=sorted(MODEL_DEFAULTS), default="llada8b")
     ap.add_argument("--children", type=int, default=None, help="children per GPU (model default)")
     ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--prompt", type=int, default=None, help="prompt ids (default: a quarter of --seq)")
     ap.add_argument("--d", type=int, default=None, help="unmasked positions per child (model default)")
     ap.add_argument("--tau", type=float, default=0.95)
     ap.add_argument("--layers", type=int, default=None, help="override layer count (small profiling captures only)")
@@ -75,7 +78,26 @@ def parse_args():
     for k, v in MODEL_DEFAULTS[a.model].items():
         if getattr(a, k, None) is None:
             setattr(a, k, v)
+    if a.prompt is None:
+        a.prompt = a.seq // 4
     return a
+
+
+def workload_tokens(a, dims, rank: int):
+    """Parent ids [T] and this rank's children [C, T] (seeded; shared by both arms).
+
+    LLaDA-8B: a prompt of uniform ids, then generation positions of which
+    ``mask_fraction`` hold the mask id; each child unmasks ``d`` of them.
+    Dream-7B: each child differs from the parent at ``d`` uniformly chosen positions.
+    """
+    from actfold_b200 import workloads as W
+
+    parent, _ = W.llada_tokens(a.seq, a.prompt, MODEL_DEFAULTS[a.model]["mask_fraction"], 1, 1, dims.mask_id, seed=42)
+    if a.model == "dream7b":
+        children = W.uniform_edit_children(parent, a.children, a.d, dims.mask_id, seed=1000 + rank)
+    else:
+        children = W.llada_children(parent, a.children, a.d, dims.mask_id, seed=1000 + rank)
+    return parent, children
 
 
 def workload_name(a) -> str:
@@ -99,7 +121,7 @@ def config_dict(a, n):
         "children_per_gpu": a.children,
         "global_children": a.children * n,
         "seq_len": a.seq,
-        "prompt": 256,
+        "prompt": a.prompt,
         "mask_fraction": MODEL_DEFAULTS[a.model]["mask_fraction"],
         "d_unmasked_per_child": a.d,
         "tau": a.tau,
@@ -195,27 +217,40 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- reference arm
+def reference_dims(a):
+    base = base_dims(a)
+    if a.layers is None:
+        return base
+    import dataclasses
+
+    return dataclasses.replace(base, n_layers=a.layers)
+
+
+def reference_sample(path, C: int, L: int, V: int, T: int, timed: int, warm: int) -> str:
+    from oracle.reference_cpu import host_description
+
+    return (f"{timed} children verified one at a time through the reference's per-layer folded path "
+            f"(per-token activation-cache get/put, cosine gate, full-layer recompute of all {T} rows, merge) "
+            f"over {L} bf16 layers and the full {V}-id LM head, after {warm} warm-up children; "
+            f"the reference verifies children sequentially, so {C} of them make one {C}-child pass; "
+            f"torch CPU kernels on {host_description(path.threads)}")
+
+
 def run_reference(a, rank: int) -> None:
+    """The reference's CPU path, one child verification per step (rank 0; other ranks exit)."""
     if rank != 0:
         return
-    from oracle.cpu_baseline import CpuSample
-    from oracle.llada import LLaDADims
+    from oracle.reference_cpu import ReferenceCpuPath
 
-    from actfold_b200 import workloads as W
-
-    d = base_dims(a)
-    dims = LLaDADims(a.layers or d.n_layers, d.hidden, d.n_heads, d.n_kv_heads, d.head_dim, d.ffn, d.vocab, d.rms_eps, d.rope_theta)
-    s = CpuSample(dims, a.seq, a.children, a.tau)
-    for _ in range(min(max(1, a.warmup), 2)):
-        s.time_pass()
-    n_samples = min(max(1, a.steps), 10)
-    ts = [s.time_pass()[0] for _ in range(n_samples)]
-    t = statistics.median(ts)
-    value = a.children * a.seq / t
-    arch = "LLaDA-8B" if a.model == "llada8b" else "Dream-7B"
-    sample = (f"median of {n_samples} samples of one {arch} block (T={a.seq}, numpy f32 BLAS, all host threads) + gate "
-              f"+ merge + LM head on a {s.vs}-column vocabulary slice, extrapolated to {a.children} children x "
-              f"{dims.n_layers} layers per pass")
+    dims = reference_dims(a)
+    parent, children = workload_tokens(a, dims, 0)
+    path = ReferenceCpuPath(dims, a.seq, a.tau)
+    path.parent_pass(parent)
+    for i in range(a.warmup):
+        path.time_child(children[i % a.children])
+    times = [path.time_child(children[i % a.children]) for i in range(a.steps)]
+    sec = sum(times) / len(times)
+    value = a.seq / sec
     line = {
         "impl": "reference",
         "metric": metric_of(a),
@@ -224,17 +259,38 @@ def run_reference(a, rank: int) -> None:
         "n_gpus": a.gpus,
         "steps": a.steps,
         "warmup": a.warmup,
-        "ms_per_step": t * 1e3,
+        "ms_per_step": sec * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic (seeded)",
+        "dtype": "bf16",
+        "data": "synthetic (seeded weights and token ids, the same token ids as the GPU arm)",
         "config": config_dict(a, 1),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": s.threads, "kind": "port", "sample": sample},
+        "step": "one child verified completely (all layers + full logits) through the reference's path",
+        "children_verified": a.steps,
+        "pass_equivalents": a.steps / a.children,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": path.threads, "kind": "port",
+                         "sample": reference_sample(path, a.children, dims.n_layers, dims.vocab, a.seq, a.steps, a.warmup)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_leg(a, dims, parent, children) -> dict:
+    """One child of the workload through the reference's CPU path (about 10-30 s of host work)."""
+    from oracle.reference_cpu import ReferenceCpuPath
+
+    path = ReferenceCpuPath(dims, a.seq, a.tau)
+    path.parent_pass(parent)
+    path.time_child(children[0])
+    t = path.time_child(children[1 % len(children)])
+    return {
+        "value": a.seq / t,
+        "unit": UNIT,
+        "cores": path.threads,
+        "kind": "port",
+        "sample": reference_sample(path, a.children, dims.n_layers, dims.vocab, a.seq, 1, 1),
+    }
 
 
 # --------------------------------------------------------------------------- our arm
@@ -366,8 +422,7 @@ def main() -> None:
     base = base_dims(a)
     dims = base if a.layers is None else W.ModelDims(a.layers, base.hidden, base.n_heads, base.n_kv_heads, base.head_dim, base.ffn, base.vocab, base.rms_eps, base.rope_theta, base.mask_id)
     model = LLaDAModel.random(dims, seed=1234, device=dev, max_pos=max(a.seq, 1024))
-    parent_np, _ = W.llada_tokens(a.seq, 256, MODEL_DEFAULTS[a.model]["mask_fraction"], 1, 1, dims.mask_id, seed=42)
-    children_np = W.llada_children(parent_np, a.children, a.d, dims.mask_id, seed=1000 + rank)
+    parent_np, children_np = workload_tokens(a, dims, rank)
 
     # ---- parent pass (rank 0) + broadcast of the parent cache
     torch.cuda.synchronize()
@@ -520,21 +575,7 @@ def main() -> None:
     # ---- CPU baseline (rank 0, single GPU runs only)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        from oracle.cpu_baseline import CpuSample
-        from oracle.llada import LLaDADims
-
-        od = LLaDADims(L, H, dims.n_heads, dims.n_kv_heads, dims.head_dim, FF, V, dims.rms_eps, dims.rope_theta)
-        cs = CpuSample(od, a.seq, a.children, a.tau)
-        cs.time_pass()
-        t_cpu = min(cs.time_pass()[0] for _ in range(2))
-        cpu = {
-            "value": a.children * a.seq / t_cpu,
-            "unit": UNIT,
-            "cores": cs.threads,
-            "kind": "port",
-            "sample": f"one {'LLaDA-8B' if a.model == 'llada8b' else 'Dream-7B'} block on {a.seq} rows + gate + merge + LM head on a {cs.vs}-column vocab slice "
-                      f"(numpy f32 BLAS, all host threads), extrapolated to {a.children} children x {L} layers",
-        }
+        cpu = cpu_baseline_leg(a, reference_dims(a), parent_np, children_np)
 
     if rank == 0:
         line = {

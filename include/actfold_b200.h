@@ -246,7 +246,9 @@ int af_dense_forward(const af_model* model, const int64_t* tokens, int64_t T, fl
  *   - The first call on a device looks up the array's address with
  *     cudaGetSymbolAddress, with that device current, and caches it; make that
  *     first call before any stream capture. The device owning `stream` must be
- *     current on every call.
+ *     current on every call (a stream of another device: AF_ERR_ARG). The
+ *     cached address does not survive cudaDeviceReset; do not call this entry
+ *     point again in a process after resetting the device.
  *   - No part of the scratch has to start at zero.
  *   - There is one array per device: calls that overlap on the same device
  *     (another stream or host thread before the previous call's kernels have

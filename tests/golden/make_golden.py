@@ -1,9 +1,9 @@
 """Generate the golden vectors under tests/golden/ by running the REFERENCE itself.
 
-Run from the repository root in a container where the reference checkout is
-mounted at /root/reference (read-only):
+Run from the repository root, naming the reference checkout (read-only) with
+``--reference`` or the ACTFOLD_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <path to the ActFold checkout>
 
 The reference is pure Python/PyTorch. Importing ``actfold.core`` pulls
 ``actfold/profiler/visualization.py``, which imports matplotlib (absent here),
@@ -33,7 +33,6 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = "/root/reference"
 sys.path.insert(0, ROOT)
 sys.path.insert(0, HERE)
 
@@ -45,7 +44,7 @@ from oracle import llada as OL  # noqa: E402
 from oracle.llada_torch import TorchLLaDA  # noqa: E402
 
 
-def _import_reference():
+def _import_reference(ref: str):
     shim = tempfile.mkdtemp(prefix="af_mpl_shim_")
     os.makedirs(os.path.join(shim, "matplotlib"))
     with open(os.path.join(shim, "matplotlib", "__init__.py"), "w") as f:
@@ -55,7 +54,7 @@ def _import_reference():
     os.makedirs(os.path.join(shim, "seaborn"))
     with open(os.path.join(shim, "seaborn", "__init__.py"), "w") as f:
         f.write("")
-    sys.path.insert(0, REF)
+    sys.path.insert(0, ref)
     sys.path.insert(0, shim)
     import actfold.core as core  # noqa: F401
 
@@ -368,8 +367,16 @@ def make_llada_resize(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
 
 
 def main() -> None:
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("ACTFOLD_REFERENCE"),
+                    help="path of the ActFold checkout (default: $ACTFOLD_REFERENCE)")
+    a = ap.parse_args()
+    if not a.reference or not os.path.isdir(os.path.join(a.reference, "actfold")):
+        raise SystemExit("make_golden: pass --reference <ActFold checkout> (or set ACTFOLD_REFERENCE)")
     torch.manual_seed(42)
-    core = _import_reference()
+    core = _import_reference(a.reference)
     make_gate(core)
     make_merge(core)
     make_cache(core)

@@ -69,6 +69,15 @@ def _worker(rank, world, port, scenario, q):
             assert torch.equal(s_all, torch.arange(C, dtype=torch.float32))
             assert torch.equal(d_all, torch.stack([torch.arange(C, dtype=torch.int32) + 100 * l for l in range(L)]))
             q.put((rank, "ok"))
+        elif scenario == "gather_bad":
+            L = dims.n_layers
+            scores = torch.zeros(4)
+            div = torch.zeros((L, 4 if rank == 0 else 3), dtype=torch.int32)
+            try:
+                gather_child_results(scores, div)
+                q.put((rank, "no error"))
+            except ValueError as e:
+                q.put((rank, "raised" if "disagree" in str(e) else f"wrong message {e}"))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:  # reported to the parent, which fails the test
@@ -119,3 +128,14 @@ def test_parent_cache_shape_mismatch_raises_on_every_rank():
 def test_gather_child_results_in_global_order():
     out = _run("gather")
     assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_gather_child_results_unequal_shards():
+    # 8 children on 3 ranks: shards of 3, 3 and 2 children.
+    out = _run("gather", world=3)
+    assert out == {0: "ok", 1: "ok", 2: "ok"}, out
+
+
+def test_gather_child_results_bad_shapes_raise_on_every_rank():
+    out = _run("gather_bad")
+    assert out == {0: "raised", 1: "raised"}, out
