@@ -30,14 +30,23 @@ from actfold_b200.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER, 
 
 @dataclass
 class Branch:
+    """A candidate branch: the fields, order and checks of actfold/speculative/branch.py:10-40."""
+
     branch_id: Any
     parent_id: Any | None
-    tokens: torch.Tensor  # [1, T] or [T]
+    tokens: torch.Tensor  # [batch, seq_len]
+    scores: torch.Tensor | None = None
+    accepted: bool = False
     metadata: dict = field(default_factory=dict)
-    accepted: bool | None = None
+
+    def __post_init__(self) -> None:
+        if self.tokens.dim() != 2:
+            raise ValueError(f"tokens must be 2D [batch, seq_len], got {self.tokens.shape}")
+        if self.scores is not None and self.scores.shape != self.tokens.shape:
+            raise ValueError(f"scores shape {self.scores.shape} must match tokens shape {self.tokens.shape}")
 
 
-@dataclass
+@dataclass(frozen=True)
 class VerificationResult:
     accepted: bool
     child_branch: Branch

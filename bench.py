@@ -456,7 +456,7 @@ def main() -> None:
 
     gate = SimilarityGate(a.tau)
     engine = ActFoldVerificationEngine(model, gate=gate, use_graphs=not a.eager)
-    pbranch = Branch("parent", None, pc.tokens)
+    pbranch = Branch("parent", None, pc.tokens[None])
     engine.set_parent_cache(pbranch, pc)
     host_children = torch.from_numpy(children_np).pin_memory()
     ct = host_children.to(dev)

@@ -67,3 +67,16 @@ TINY_LLADA_CHAIN = dict(TINY_LLADA, chain_child=1, chain_n=3, chain_d=3, chain_s
 TINY_LLADA_RESIZE = dict(TINY_LLADA, parent_len=48, short_len=40, n_children=3, d=2)
 TINY_DREAM = dict(T=64, n_prompt=16, mask_frac=0.75, n_children=3, d=3, tau=0.95, weight_seed=11, token_seed=43)
 DEMO = dict(T=16, n_children=2, tau=0.95, weight_seed=42, token_seed=42)
+# Verification-engine contract: the TINY_LLADA workload (4 children) verified at
+# two acceptance thresholds (0 and one between the children's stable ratios),
+# then grandchildren of an accepted child verified against it.
+# Child c unmasks child_d[c] positions, so the children's stable ratios differ.
+TINY_ENGINE = dict(TINY_LLADA, child_d=(2, 4, 6, 8), chain_n=2, chain_d=2, chain_seed=45)
+
+
+def engine_children(parent, mask_id: int, spec: dict):
+    """Children [C, T] of the engine workload: child c unmasks spec["child_d"][c] positions."""
+    from actfold_b200 import workloads as W
+
+    return np.concatenate([W.llada_children(parent, 1, d, mask_id, spec["token_seed"] + 100 + c)
+                           for c, d in enumerate(spec["child_d"])])

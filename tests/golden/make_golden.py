@@ -20,6 +20,9 @@ Outputs (all small, compressed):
   dream_tiny.npz same, GQA (Dream-shaped) tiny model
   llada_chain.npz grandchildren folded against a verified child (chained folding)
   llada_resize.npz children longer / shorter than their parent (zero-filled parent rows)
+  engine.npz     reference ActFoldVerificationEngine.verify_branch over the tiny
+                 LLaDA block: acceptance, stable ratio, score, per-layer profile
+                 and cache clearing at two thresholds, and a chained step
 """
 
 from __future__ import annotations
@@ -39,7 +42,7 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 from actfold_b200 import workloads as W  # noqa: E402
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, digest, gate_inputs  # noqa: E402
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_ENGINE, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, digest, engine_children, gate_inputs  # noqa: E402
 from oracle import llada as OL  # noqa: E402
 from oracle.llada_torch import TorchLLaDA  # noqa: E402
 
@@ -366,25 +369,125 @@ def make_llada_resize(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     np.savez_compressed(os.path.join(HERE, fname), **out)
 
 
+def make_engine(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
+    """The reference verification engine over FoldedModel(restated tiny LLaDA).
+
+    verify_branch (actfold/speculative/verification_engine.py:75-144) re-runs
+    the parent pass, folds the child, takes the profile's mean stable ratio,
+    sets metadata["actfold_score"] = mean of the child's logits and
+    metadata["stable_ratio"], accepts when stable_ratio >= threshold and
+    clears a rejected child's cache entries. Recorded per threshold and child:
+    accepted, stable ratio, score, per-layer stable ratios and whether the
+    child still has cache entries; then grandchildren of the first accepted
+    child (threshold 0) verified with ``verify_branch(child, grandchild)``.
+    """
+    import torch.nn as nn
+    from actfold.core.model_wrapper import FoldedModel
+    from actfold.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER
+    from actfold.speculative.branch import Branch
+    from actfold.speculative.fast_dllm_adapter import FastDLLMAdapter
+    from actfold.speculative.verification_engine import ActFoldVerificationEngine
+
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    T = spec["T"]
+    parent, _ = W.llada_tokens(T, spec["n_prompt"], spec["mask_frac"], 1, 1, dims.mask_id, spec["token_seed"])
+    children = engine_children(parent, dims.mask_id, spec)
+    C = children.shape[0]
+
+    class Emb(nn.Module):
+        def __init__(self, table):
+            super().__init__()
+            self.table = table
+
+        def forward(self, tokens):
+            return self.table[tokens]
+
+    def run(threshold: float, chain: np.ndarray | None = None):
+        model = TorchLLaDA(w, od, T)
+        model.embedding = Emb(model.embed)  # the adapter looks the input embeddings up here
+        cache = core.ActivationCache(max_entries_per_layer=(C + 4) * T, device="cpu")
+        gate = core.SimilarityGate(tau=spec["tau"], metric="cosine")
+        folded = FoldedModel(model, cache, gate)
+        adapter = FastDLLMAdapter(folded.wrapped_model, num_layers=dims.n_layers, hidden_dim=dims.hidden,
+                                  num_heads=dims.n_heads, vocab_size=dims.vocab, folded_model=folded)
+        engine = ActFoldVerificationEngine(adapter, cache, gate, acceptance_threshold=threshold)
+        pb = Branch("parent", None, torch.from_numpy(parent)[None])
+        rec = {"accepted": [], "ratio": [], "score": [], "layer_ratio": [], "cached": []}
+        with torch.no_grad():
+            for c in range(C):
+                cb = Branch(f"child{c}", "parent", torch.from_numpy(children[c])[None])
+                r = engine.verify_branch(pb, cb)
+                assert r.accepted == cb.accepted and cb.metadata["stable_ratio"] == r.stable_ratio
+                rec["accepted"].append(bool(r.accepted))
+                rec["ratio"].append(float(r.stable_ratio))
+                rec["score"].append(float(cb.metadata["actfold_score"]))
+                prof = GLOBAL_STABILITY_PROFILER.get_profile(f"child{c}")
+                rec["layer_ratio"].append([s.stable_ratio for s in prof.layer_stats])
+                rec["cached"].append(any(k[0] == f"child{c}" for lc in cache._caches.values() for k in lc))
+            grand = {"ratio": [], "score": [], "layer_ratio": []}
+            if chain is not None:
+                k = rec["accepted"].index(True)
+                kb = Branch(f"child{k}", "parent", torch.from_numpy(children[k])[None])
+                for g in range(chain.shape[0]):
+                    # verify_branch re-runs the dense pass of its parent branch (here the
+                    # accepted child, whose cached entries it replaces) before folding.
+                    gb = Branch(f"grand{g}", f"child{k}", torch.from_numpy(chain[g])[None])
+                    r = engine.verify_branch(kb, gb)
+                    prof = GLOBAL_STABILITY_PROFILER.get_profile(gb.branch_id)
+                    grand["ratio"].append(float(r.stable_ratio))
+                    grand["score"].append(float(gb.metadata["actfold_score"]))
+                    grand["layer_ratio"].append([s.stable_ratio for s in prof.layer_stats])
+                grand["child"] = k
+        return rec, grand
+
+    out = {"parent": parent, "children": children}
+    first, _ = run(0.0)
+    ratios = sorted(set(first["ratio"]))
+    thr = (ratios[0] + ratios[1]) / 2 if len(ratios) > 1 else ratios[0]
+    grand_tokens = None
+    for name, t in (("t0", 0.0), ("t1", thr)):
+        if name == "t0":
+            k = 0
+            grand_tokens = W.llada_children(children[k], spec["chain_n"], spec["chain_d"], dims.mask_id, spec["chain_seed"])
+        rec, grand = run(t, grand_tokens if name == "t0" else None)
+        out[f"{name}/threshold"] = np.array(t)
+        for key, v in rec.items():
+            out[f"{name}/{key}"] = np.array(v)
+        if name == "t0":
+            out["grand/child"] = np.array(grand["child"])
+            out["grand/tokens"] = grand_tokens
+            for key in ("ratio", "score", "layer_ratio"):
+                out[f"grand/{key}"] = np.array(grand[key])
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
 def main() -> None:
     import argparse
 
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ACTFOLD_REFERENCE"),
                     help="path of the ActFold checkout (default: $ACTFOLD_REFERENCE)")
+    ap.add_argument("--only", default=None, help="write only this fixture (e.g. engine)")
     a = ap.parse_args()
     if not a.reference or not os.path.isdir(os.path.join(a.reference, "actfold")):
         raise SystemExit("make_golden: pass --reference <ActFold checkout> (or set ACTFOLD_REFERENCE)")
     torch.manual_seed(42)
     core = _import_reference(a.reference)
-    make_gate(core)
-    make_merge(core)
-    make_cache(core)
-    make_demo(core)
-    make_llada(core, W.LLADA_TINY, TINY_LLADA, "llada_tiny.npz")
-    make_llada(core, W.DREAM_TINY, TINY_DREAM, "dream_tiny.npz")
-    make_llada_chain(core, W.LLADA_TINY, TINY_LLADA_CHAIN, "llada_chain.npz")
-    make_llada_resize(core, W.LLADA_TINY, TINY_LLADA_RESIZE, "llada_resize.npz")
+    jobs = {
+        "gate": lambda: make_gate(core),
+        "merge": lambda: make_merge(core),
+        "cache": lambda: make_cache(core),
+        "demo": lambda: make_demo(core),
+        "llada_tiny": lambda: make_llada(core, W.LLADA_TINY, TINY_LLADA, "llada_tiny.npz"),
+        "dream_tiny": lambda: make_llada(core, W.DREAM_TINY, TINY_DREAM, "dream_tiny.npz"),
+        "llada_chain": lambda: make_llada_chain(core, W.LLADA_TINY, TINY_LLADA_CHAIN, "llada_chain.npz"),
+        "llada_resize": lambda: make_llada_resize(core, W.LLADA_TINY, TINY_LLADA_RESIZE, "llada_resize.npz"),
+        "engine": lambda: make_engine(core, W.LLADA_TINY, TINY_ENGINE, "engine.npz"),
+    }
+    for name, job in jobs.items():
+        if a.only in (None, name):
+            job()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

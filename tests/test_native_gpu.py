@@ -218,7 +218,7 @@ def test_engine_graph_replay_matches_eager_launches(tiny):
     others = W.llada_children(tiny["parent"], kids.shape[0], spec["d"] + 1, dims.mask_id, seed=77)
     eng_g = ActFoldVerificationEngine(model, gate=SimilarityGate(spec["tau"]), use_graphs=True)
     eng_e = ActFoldVerificationEngine(model, gate=SimilarityGate(spec["tau"]), use_graphs=False)
-    pb = Branch("parent", None, parent)
+    pb = Branch("parent", None, parent.reshape(1, -1))
     for batch in (kids, others, kids):
         host = torch.from_numpy(np.ascontiguousarray(batch)).pin_memory()
         rg = eng_g.verify_tokens(pb, host)

@@ -172,3 +172,34 @@ def test_llada_resize_oracle_matches_reference(golden):
         res = OF.llada_folded_children(kids, OF.llada_resize_parent(par, kids.shape[1]), w, od, spec["tau"])
         np.testing.assert_array_equal(res["masks"], g[f"{name}_masks"])
         assert _bf16_close(res["logits"], from_bf16_bits(g[f"{name}_logits_bits"])) <= 2e-2
+
+
+def test_engine_oracle_matches_reference(golden):
+    """The engine contract restated on the oracle: stable ratio = mean over layers of the stable fraction,
+    score = mean of the child's logits, acceptance = ratio >= threshold; the chained step re-runs the
+    dense pass of the accepted child as the new parent (verify_branch re-runs its parent every call)."""
+    from gen_inputs import TINY_ENGINE, engine_children
+
+    g = golden("engine")
+    dims, spec = W.LLADA_TINY, TINY_ENGINE
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    parent, _ = W.llada_tokens(spec["T"], spec["n_prompt"], spec["mask_frac"], 1, 1, dims.mask_id, spec["token_seed"])
+    children = engine_children(parent, dims.mask_id, spec)
+    np.testing.assert_array_equal(children, g["children"])
+    res = OF.llada_folded_children(children, OF.llada_parent(parent, w, od), w, od, spec["tau"])
+    layer_ratio = res["masks"].mean(axis=2).T  # [C, L]
+    for name in ("t0", "t1"):
+        np.testing.assert_allclose(layer_ratio, g[f"{name}/layer_ratio"], atol=1e-6)
+        ratio = layer_ratio.mean(axis=1)
+        np.testing.assert_allclose(ratio, g[f"{name}/ratio"], atol=1e-6)
+        np.testing.assert_array_equal(ratio >= float(g[f"{name}/threshold"]), g[f"{name}/accepted"])
+        np.testing.assert_array_equal(g[f"{name}/accepted"], g[f"{name}/cached"])  # rejected children are cleared
+        scale = np.abs(res["logits"]).max(axis=(1, 2))
+        assert (np.abs(res["logits"].mean(axis=(1, 2)) - g[f"{name}/score"]) <= 2e-2 * scale).all()
+    k = int(g["grand/child"])
+    grand = g["grand/tokens"]
+    res2 = OF.llada_folded_children(grand, OF.llada_parent(children[k], w, od), w, od, spec["tau"])
+    np.testing.assert_allclose(res2["masks"].mean(axis=2).T, g["grand/layer_ratio"], atol=1e-6)
+    scale = np.abs(res2["logits"]).max(axis=(1, 2))
+    assert (np.abs(res2["logits"].mean(axis=(1, 2)) - g["grand/score"]) <= 2e-2 * scale).all()
