@@ -1,9 +1,14 @@
 """FoldedTransformerLayer: the per-layer fold decision for an arbitrary layer module.
 
-Drop-in for actfold/core/folded_transformer.py:23-274 (same constructor,
-``forward`` signature, branch-context resolution, scheduler handling,
-KeyError/RuntimeError -> recompute fallbacks, tuple outputs and kwargs
-filtering). This is the GENERIC path: the wrapped layer is user code and runs
+Drop-in for actfold/core/folded_transformer.py:23-274: the same constructor
+and ``forward`` signature, and the same observable decisions -- the branch
+context (explicit arguments, else FOLDING_CONTEXT), the scheduler's
+should_fold / get_tau, a full recompute when there is no parent, the parent's
+rows are missing (KeyError / RuntimeError) or no row is stable, the parent's
+output when every row is stable, a merge otherwise (a missing parent output is
+a RuntimeError there), the first element of tuple outputs, keyword arguments
+filtered to what the wrapped layer accepts, and the child's input and output
+stored afterwards. This is the GENERIC path: the wrapped layer is user code and runs
 on all rows, exactly as in the reference; around it the gate, merge and cache
 traffic run on the CUDA kernels:
 
@@ -24,7 +29,6 @@ from __future__ import annotations
 import inspect
 from typing import Any
 
-import numpy as np
 import torch
 import torch.nn as nn
 
@@ -34,7 +38,7 @@ from actfold_b200.core.fused_ops import merge_stable_divergent
 from actfold_b200.core.similarity_gate import SimilarityGate
 from actfold_b200.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER
 
-_ACTFOLD_KWARGS = {"branch_id", "parent_branch_id", "step_idx"}
+_BRANCH_KEYS = frozenset({"branch_id", "parent_branch_id", "step_idx"})
 
 
 def _dense_get(cache, branch_id, layer_idx, token_mask):
@@ -42,6 +46,22 @@ def _dense_get(cache, branch_id, layer_idx, token_mask):
     if hasattr(cache, "get_dense"):
         return cache.get_dense(branch_id, layer_idx, token_mask)
     return cache.get(branch_id, layer_idx, token_mask)
+
+
+class _LayerCall:
+    """How to call a wrapped layer: which keyword arguments it takes (its signature, read once)."""
+
+    def __init__(self, layer: nn.Module) -> None:
+        params = inspect.signature(layer.forward).parameters
+        self.names = frozenset(params)
+        self.any_kw = any(p.kind == inspect.Parameter.VAR_KEYWORD for p in params.values())
+
+    def __call__(self, layer: nn.Module, x: torch.Tensor, attention_mask, kwargs: dict) -> torch.Tensor:
+        kw = {k: v for k, v in kwargs.items() if k not in _BRANCH_KEYS and (self.any_kw or k in self.names)}
+        if attention_mask is not None and "attention_mask" in self.names:
+            kw["attention_mask"] = attention_mask
+        out = layer(x, **kw)
+        return out[0] if isinstance(out, tuple) else out  # (hidden_states, ...) layers: the first element
 
 
 class FoldedTransformerLayer(nn.Module):
@@ -59,6 +79,7 @@ class FoldedTransformerLayer(nn.Module):
         self.gate = gate
         self.layer_idx = layer_idx
         self.scheduler = scheduler
+        self._call: _LayerCall | None = None
 
     def forward(
         self,
@@ -69,111 +90,79 @@ class FoldedTransformerLayer(nn.Module):
         step_idx: int = 0,
         **kwargs: Any,
     ) -> torch.Tensor:
-        if branch_id is None:
-            ctx = FOLDING_CONTEXT.get()
-            if ctx is not None:
-                branch_id = ctx["branch_id"]
+        if branch_id is None:  # explicit arguments win over the folding context
+            ctx = FOLDING_CONTEXT.get() or {}
+            branch_id = ctx.get("branch_id")
+            if branch_id is not None:
                 parent_branch_id = ctx.get("parent_branch_id", parent_branch_id)
                 step_idx = ctx.get("step_idx", step_idx)
         if branch_id is None:
             raise ValueError(
                 "FoldedTransformerLayer requires a branch_id either as an argument or via the ActFold folding context."
             )
-        if parent_branch_id is None:
-            output = self._recompute_all(hidden_states, attention_mask, **kwargs)
-            self._store_activations(branch_id, output, hidden_states)
-            return output
-        if self.scheduler is not None and not self.scheduler.should_fold(self.layer_idx, step_idx):
-            output = self._recompute_all(hidden_states, attention_mask, **kwargs)
-            self._store_activations(branch_id, output, hidden_states)
-            return output
-        if self.scheduler is not None:
-            self.gate.set_tau(self.scheduler.get_tau(layer_idx=self.layer_idx, step_idx=step_idx, task_type="general"))
+        out = None
+        if parent_branch_id is not None and self._folds_at(step_idx):
+            out = self._fold(hidden_states, branch_id, parent_branch_id, step_idx, attention_mask, kwargs)
+        if out is None:  # no parent, an unfolded layer, parent rows missing, or nothing stable
+            out = self._run_layer(hidden_states, attention_mask, kwargs)
+        self.cache.put(branch_id=branch_id, layer_idx=self.layer_idx,
+                       activations={"ffn_out": out, "hidden_states": hidden_states})
+        return out
 
-        B, T = hidden_states.shape[:2]
-        # Parent layer input (cache.get with an all-ones mask, folded_transformer.py:124-141).
-        h_parent = None
-        try:
-            h_parent = self.cache.dense_rows(parent_branch_id, self.layer_idx, "hidden_states", T)
-            if h_parent is not None:
-                self.cache.touch(parent_branch_id, self.layer_idx, None, T)
-                if h_parent.shape[0] == 1 and B > 1:
-                    h_parent = h_parent.expand(B, *h_parent.shape[1:])
-            else:
-                ones = torch.ones((B, T), dtype=torch.bool, device=hidden_states.device)
-                h_parent = _dense_get(self.cache, parent_branch_id, self.layer_idx, ones).get("hidden_states")
-        except (KeyError, RuntimeError):
-            h_parent = None
-        if h_parent is None:
-            output = self._recompute_all(hidden_states, attention_mask, **kwargs)
-            self._store_activations(branch_id, output, hidden_states)
-            return output
-        h_parent = h_parent.to(dtype=hidden_states.dtype, device=hidden_states.device)
+    def _folds_at(self, step_idx: int) -> bool:
+        """Scheduler decision for this layer; sets the shared gate's tau when the layer folds."""
+        if self.scheduler is None:
+            return True
+        if not self.scheduler.should_fold(self.layer_idx, step_idx):
+            return False
+        self.gate.set_tau(self.scheduler.get_tau(layer_idx=self.layer_idx, step_idx=step_idx, task_type="general"))
+        return True
 
-        g = self.gate.forward_compact(hidden_states, h_parent)
-        stable_mask = g.stable_mask
-        GLOBAL_STABILITY_PROFILER.record(
-            branch_id=branch_id,
-            parent_branch_id=parent_branch_id,
-            layer_idx=self.layer_idx,
-            step_idx=step_idx,
-            stable_mask=stable_mask,
-            tau=self.gate.tau,
-            metric=self.gate.metric,
-        )
-        # The single host synchronisation of this layer: divergent total + per-token "any stable".
-        host = torch.cat([g.div_count.sum().view(1), stable_mask.any(dim=0).to(torch.int32)]).cpu().numpy()
-        n_div, any_stable = int(host[0]), host[1:].astype(bool)
-
-        if n_div == 0:  # all stable -> parent output (folded_transformer.py:162-179)
-            ffn_out = None
-            try:
-                ffn_out = _dense_get(self.cache, parent_branch_id, self.layer_idx, stable_mask).get("ffn_out")
-            except (KeyError, RuntimeError):
-                ffn_out = None
-            if ffn_out is not None:
-                self._store_activations(branch_id, ffn_out, hidden_states)
-                return ffn_out
-            output = self._recompute_all(hidden_states, attention_mask, **kwargs)
-            self._store_activations(branch_id, output, hidden_states)
-            return output
-        if n_div == B * T:  # nothing stable -> recompute (folded_transformer.py:183-186)
-            output = self._recompute_all(hidden_states, attention_mask, **kwargs)
-            self._store_activations(branch_id, output, hidden_states)
-            return output
-
-        parent_ffn = self._get_parent_ffn_output(parent_branch_id, stable_mask, any_stable, T)
-        child_out = self._recompute_all(hidden_states, attention_mask, **kwargs)
-        if parent_ffn.shape[0] == 1 and B > 1:
-            parent_ffn = parent_ffn.expand(B, *parent_ffn.shape[1:])
-        h_out = merge_stable_divergent(parent_ffn, child_out, stable_mask)
-        self._store_activations(branch_id, h_out, hidden_states)
-        return h_out
-
-    def _get_parent_ffn_output(self, parent_branch_id, stable_mask: torch.Tensor, any_stable: np.ndarray, T: int) -> torch.Tensor:
-        """Parent ``ffn_out`` rows for the merge; RuntimeError when the parent has none."""
-        rows = self.cache.dense_rows(parent_branch_id, self.layer_idx, "ffn_out", T)
+    def _parent_rows(self, parent_branch_id, name: str, B: int, T: int, device, any_stable=None):
+        """The parent's cached ``name`` rows for this layer; None when the cache has none."""
+        rows = self.cache.dense_rows(parent_branch_id, self.layer_idx, name, T)
         if rows is not None:
             self.cache.touch(parent_branch_id, self.layer_idx, any_stable, T)
-            return rows
-        acts = _dense_get(self.cache, parent_branch_id, self.layer_idx, stable_mask)
-        ffn_out = acts.get("ffn_out")
-        if ffn_out is None:
-            raise RuntimeError(f"Parent FFN output missing for branch={parent_branch_id}, layer={self.layer_idx}")
-        return ffn_out
+            return rows.expand(B, *rows.shape[1:]) if rows.shape[0] == 1 and B > 1 else rows
+        mask = torch.ones((B, T), dtype=torch.bool, device=device) if any_stable is None else any_stable
+        return _dense_get(self.cache, parent_branch_id, self.layer_idx, mask).get(name)
 
-    def _recompute_all(self, hidden_states: torch.Tensor, attention_mask: torch.Tensor | None, **kwargs: Any) -> torch.Tensor:
-        """Run the wrapped layer on every row; the first element of a tuple output is the result."""
-        sig = inspect.signature(self.original_layer.forward)
-        accepted = set(sig.parameters)
-        has_varkw = any(p.kind == inspect.Parameter.VAR_KEYWORD for p in sig.parameters.values())
-        layer_kwargs = {k: v for k, v in kwargs.items() if k not in _ACTFOLD_KWARGS}
-        if not has_varkw:
-            layer_kwargs = {k: v for k, v in layer_kwargs.items() if k in accepted}
-        if attention_mask is not None and "attention_mask" in accepted:
-            layer_kwargs["attention_mask"] = attention_mask
-        raw = self.original_layer(hidden_states, **layer_kwargs)
-        return raw[0] if isinstance(raw, tuple) else raw
+    def _fold(self, hidden_states, branch_id, parent_branch_id, step_idx, attention_mask, kwargs):
+        """The folded output, or None when the layer has to be recomputed on every row."""
+        B, T = hidden_states.shape[:2]
+        try:
+            h_parent = self._parent_rows(parent_branch_id, "hidden_states", B, T, hidden_states.device)
+        except (KeyError, RuntimeError):
+            return None
+        if h_parent is None:
+            return None
+        g = self.gate.forward_compact(hidden_states, h_parent.to(dtype=hidden_states.dtype, device=hidden_states.device))
+        stable = g.stable_mask
+        GLOBAL_STABILITY_PROFILER.record(branch_id=branch_id, parent_branch_id=parent_branch_id, layer_idx=self.layer_idx,
+                                         step_idx=step_idx, stable_mask=stable, tau=self.gate.tau, metric=self.gate.metric)
+        # One host read per layer: the divergent total and, per position, whether any row keeps the parent's.
+        host = torch.cat([g.div_count.sum().view(1), stable.any(dim=0).to(torch.int32)]).cpu().numpy()
+        n_div, any_stable = int(host[0]), host[1:].astype(bool)
+        if n_div == B * T:
+            return None
+        if n_div == 0:
+            try:
+                return _dense_get(self.cache, parent_branch_id, self.layer_idx, stable).get("ffn_out")
+            except (KeyError, RuntimeError):
+                return None
+        parent_out = self.cache.dense_rows(parent_branch_id, self.layer_idx, "ffn_out", T)
+        if parent_out is not None:
+            self.cache.touch(parent_branch_id, self.layer_idx, any_stable, T)
+        else:  # a missing parent output here is an error, as in the reference's merge path
+            parent_out = _dense_get(self.cache, parent_branch_id, self.layer_idx, stable).get("ffn_out")
+            if parent_out is None:
+                raise RuntimeError(f"Parent FFN output missing for branch={parent_branch_id}, layer={self.layer_idx}")
+        fresh = self._run_layer(hidden_states, attention_mask, kwargs)
+        if parent_out.shape[0] == 1 and B > 1:
+            parent_out = parent_out.expand(B, *parent_out.shape[1:])
+        return merge_stable_divergent(parent_out, fresh, stable)
 
-    def _store_activations(self, branch_id: str, ffn_out: torch.Tensor, hidden_states: torch.Tensor) -> None:
-        self.cache.put(branch_id=branch_id, layer_idx=self.layer_idx, activations={"ffn_out": ffn_out, "hidden_states": hidden_states})
+    def _run_layer(self, hidden_states: torch.Tensor, attention_mask, kwargs: dict) -> torch.Tensor:
+        if self._call is None:
+            self._call = _LayerCall(self.original_layer)
+        return self._call(self.original_layer, hidden_states, attention_mask, kwargs)

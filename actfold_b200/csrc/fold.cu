@@ -72,6 +72,7 @@ struct CandArgs {
   const int64_t* ctok;           // [C*T]  (layer 0)
   const int64_t* ptok;           // [T]    (layer 0)
   const uint8_t* self_stable;    // [T] of this layer, nullable
+  int all_rows;                  // 1: every row is a candidate (a layer that does not fold)
   const int* prev_div_pos;       // layer >= 1: fresh rows = previous layer's divergent rows
   const int* prev_n_div;
   int* slot;                     // [C*T] scratch
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
         if (i < N) {
           const int t = i % a.T;
           if (a.ctok[i] != a.ptok[t]) fm |= 1u << e;
-          if (a.self_stable && !a.self_stable[t]) sm |= 1u << e;
+          if (a.all_rows || (a.self_stable && !a.self_stable[t])) sm |= 1u << e;
         }
       }
       int total1, total2;
@@ -149,8 +150,8 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
     }
     return;
   }
-  // Later layers (the parent fails its own gate on some rows): fresh rows are
-  // the previous layer's divergent rows.
+  // Later layers (the parent fails its own gate on some rows, or the layer
+  // does not fold): fresh rows are the previous layer's divergent rows.
   for (int i = threadIdx.x; i < N; i += 1024) a.slot[i] = -1;
   __syncthreads();
   const int nd = *a.prev_n_div;
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
     int s = -1, f = 0;
     if (i < N) {
       s = a.slot[i];
-      f = (s >= 0 || (a.self_stable && !a.self_stable[i % a.T])) ? 1 : 0;
+      f = (a.all_rows || s >= 0 || (a.self_stable && !a.self_stable[i % a.T])) ? 1 : 0;
     }
     const int rank = base + block_scan_1024(f, wbuf, &total);
     if (f) {
@@ -279,6 +280,7 @@ struct FoldGateArgs {
   const __nv_bfloat16* norm_w;
   float eps;
   GateConsts k;
+  int force_div;                  // 1: the layer does not fold, every candidate is divergent
   uint8_t* stable;
   __nv_bfloat16* xc;              // packed candidate hidden [m_cap, H]
   __nv_bfloat16* a;               // packed normalized rows [m_cap, H]
@@ -302,7 +304,7 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
   load_row<NV, kRowThreads>(hrow, nvec, tid, hv);
   load_row<NV, kRowThreads>(prow, nvec, tid, pv);
   const GateOut o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, tid, rows);
-  if (tid == 0) g.stable[r] = o.stable;
+  if (tid == 0) g.stable[r] = g.force_div ? 0 : o.stable;
   char* xc = reinterpret_cast<char*>(g.xc + (int64_t)r * g.H);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
@@ -864,6 +866,9 @@ struct FoldPlan {
   float tau;
   int metric;
   std::vector<uint8_t> su;
+  std::vector<float> taus;       // gate threshold per layer
+  std::vector<uint8_t> folds;    // 0: the layer recomputes every row
+  const uint8_t* self_stable;    // [L, T] parent self-gate results at the plan's thresholds
   FoldWs w;
   int ntok;
   std::vector<CUtensorMap> tm_qkv, tm_o, tm_gu, tm_down;
@@ -924,7 +929,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   const int C = p->C, T = p->T, M = p->m_cap, L = z.L;
   const float eps = p->model.dims.rms_eps;
   const unsigned mblocks = (unsigned)((M + 7) / 8);
-  const GateConsts gk = make_gate_consts(AF_DTYPE_BF16, p->tau, 1e-8f, (float)(std::sqrt((double)z.H) + 1e-8));
+  const float hn = (float)(std::sqrt((double)z.H) + 1e-8);
   const __nv_bfloat16* p_in = static_cast<const __nv_bfloat16*>(p->parent.layer_in);
   const __nv_bfloat16* p_qkv = static_cast<const __nv_bfloat16*>(p->parent.qkv);
   int st;
@@ -939,7 +944,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   ca.m_cap = M;
   ca.ctok = ctok;
   ca.ptok = p->parent.tokens;
-  ca.self_stable = p->su[0] ? p->parent.self_stable : nullptr;
+  ca.self_stable = p->su[0] ? p->self_stable : nullptr;
+  ca.all_rows = p->folds[0] ? 0 : 1;
   ca.slot = w.slot;
   ca.cand_child = w.cand_child;
   ca.cand_pos = w.cand_pos;
@@ -985,7 +991,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     __nv_bfloat16* x_l = w.x_all + (int64_t)l * M * z.H;
     __nv_bfloat16* x_next = w.x_all + (int64_t)(l + 1) * M * z.H;
     const bool last = l == L - 1;
-    const bool next_su = !last && p->su[l + 1];
+    const bool next_su = !last && (p->su[l + 1] || !p->folds[l + 1]);
 
     FoldGateArgs g;
     g.n_cand = nc;
@@ -997,7 +1003,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     g.p_in = pin_l;
     g.norm_w = static_cast<const __nv_bfloat16*>(lw.attn_norm);
     g.eps = eps;
-    g.k = gk;
+    g.k = make_gate_consts(AF_DTYPE_BF16, p->taus[l], 1e-8f, hn);
+    g.force_div = p->folds[l] ? 0 : 1;
     g.stable = w.stable;
     g.xc = w.xc;
     g.a = w.A;
@@ -1182,7 +1189,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
       cn.C = C;
       cn.T = T;
       cn.m_cap = M;
-      cn.self_stable = p->parent.self_stable + (int64_t)(l + 1) * T;
+      cn.self_stable = p->su[l + 1] ? p->self_stable + (int64_t)(l + 1) * T : nullptr;
+      cn.all_rows = p->folds[l + 1] ? 0 : 1;
       cn.prev_div_pos = dpos;
       cn.prev_n_div = nd;
       cn.slot = w.slot;
@@ -1268,6 +1276,16 @@ extern "C" int af_fold_plan_create(const af_model* m, const af_parent_cache* par
   p->tau = cfg->tau;
   p->metric = cfg->metric;
   p->su.assign(cfg->su_layers, cfg->su_layers + m->dims.n_layers);
+  p->taus.assign(m->dims.n_layers, cfg->tau);
+  if (cfg->tau_layers) p->taus.assign(cfg->tau_layers, cfg->tau_layers + m->dims.n_layers);
+  p->folds.assign(m->dims.n_layers, 1);
+  if (cfg->fold_layers) p->folds.assign(cfg->fold_layers, cfg->fold_layers + m->dims.n_layers);
+  p->self_stable = cfg->self_stable ? cfg->self_stable : parent->self_stable;
+  for (uint8_t f : p->folds)
+    if (!f && p->m_cap < p->C * p->T) {
+      delete p;
+      return fail(AF_ERR_ARG, "af_fold_plan_create: a layer that does not fold needs m_cap >= n_children * seq");
+    }
   Bump b(workspace, workspace_bytes);
   p->w = carve_fold(b, sizes_of(m->dims), p->C, p->T, p->m_cap);
   if (b.off > workspace_bytes) {

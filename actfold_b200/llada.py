@@ -20,7 +20,7 @@ logits) with no host synchronisation until the caller reads a result.
 from __future__ import annotations
 
 import ctypes as C
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any, Sequence
 
 import numpy as np
@@ -60,7 +60,8 @@ class _Parent(C.Structure):
 
 
 class _FoldConfig(C.Structure):
-    _fields_ = [("n_children", _i64), ("seq", _i64), ("m_cap", _i64), ("tau", _f32), ("metric", _i32), ("su_layers", _vp)]
+    _fields_ = [("n_children", _i64), ("seq", _i64), ("m_cap", _i64), ("tau", _f32), ("metric", _i32), ("su_layers", _vp),
+                ("tau_layers", _vp), ("fold_layers", _vp), ("self_stable", _vp)]
 
 
 class _FoldOutputs(C.Structure):
@@ -151,6 +152,8 @@ class ParentCache:
     self_stable: torch.Tensor   # [L, T] uint8
     row_sums: torch.Tensor      # [T] fp32
     tau: float
+    # Bumped by contents_changed() whenever the arrays are rewritten in place.
+    version: int = field(default=0, compare=False)
 
     @property
     def seq(self) -> int:
@@ -199,28 +202,83 @@ class ParentCache:
         """Device copy of every array (the destination of a promotion that keeps this cache intact)."""
         return ParentCache(*(t.clone() for t in self.tensors()), self.tau)
 
-    # Values derived from the device arrays and kept on the host for reuse:
-    # the host copy of the token ids, the count of rows the parent fails its
-    # own gate on, and the last resized view.
-    _DERIVED = ("_host_tokens", "_su_rows", "_resized")
+    # Values derived from the arrays and kept for reuse: the host copy of the
+    # token ids, the self-gate results at other thresholds and the count of
+    # rows the parent fails its own gate on, and the last resized view.
+    _DERIVED = ("_host_tokens", "_self_stable_at", "_su_rows_at", "_resized")
 
     def contents_changed(self) -> None:
-        """Drop the host-side values derived from this cache (after its arrays are rewritten in place)."""
+        """Record an in-place rewrite of the arrays: drop every value derived from them."""
+        self.version += 1
         for name in self._DERIVED:
             self.__dict__.pop(name, None)
 
+    def self_stable_at(self, taus: Sequence[float]) -> torch.Tensor:
+        """[L, T] uint8: the parent's own gate result of each row, layer l at threshold ``taus[l]``.
+
+        The parent pass stored these at the cache's own ``tau``; layers with
+        another threshold are gated again (one SimilarityGate call per
+        distinct threshold), and the result is kept until the contents change.
+        """
+        taus = tuple(float(t) for t in taus)
+        if all(t == self.tau for t in taus):
+            return self.self_stable
+        memo = self.__dict__.setdefault("_self_stable_at", {})
+        out = memo.get(taus)
+        if out is None:
+            from actfold_b200.core.similarity_gate import SimilarityGate
+
+            x = self.layer_in[:-1]
+            out = self.self_stable.clone()
+            for t in sorted(set(taus) - {self.tau}):
+                ls = [i for i, lt in enumerate(taus) if lt == t]
+                out[ls] = SimilarityGate(tau=t)(x[ls], x[ls]).to(torch.uint8)
+            memo[taus] = out
+        return out
+
+    def su_rows_at(self, taus: Sequence[float]) -> int:
+        """Rows the parent fails its own gate on at some layer, at thresholds ``taus`` (one device read, kept)."""
+        taus = tuple(float(t) for t in taus)
+        memo = self.__dict__.setdefault("_su_rows_at", {})
+        n = memo.get(taus)
+        if n is None:
+            n = int((self.self_stable_at(taus) == 0).any(dim=0).sum().item())
+            memo[taus] = n
+        return n
+
 
 class FoldPlan:
-    """A prepared folded pass for C children of length T with m_cap candidate rows."""
+    """A prepared folded pass for C children of length T with m_cap candidate rows.
 
-    def __init__(self, model: "LLaDAModel", parent: ParentCache, n_children: int, m_cap: int, tau: float, metric: str = "cosine") -> None:
+    ``layer_taus`` / ``layer_folds`` (optional, one entry per layer) give each
+    layer its own gate threshold and say which layers fold at all: the
+    per-layer decisions a FoldingScheduler makes inside the reference's folded
+    layers (actfold/core/folded_transformer.py:107-119). A layer that does not
+    fold recomputes every row of every child, so a plan with one needs
+    ``m_cap = C * T``.
+    """
+
+    def __init__(self, model: "LLaDAModel", parent: ParentCache, n_children: int, m_cap: int, tau: float,
+                 metric: str = "cosine", layer_taus=None, layer_folds=None) -> None:
         self.lib = _bind_late()
         self.model = model
         self.parent = parent
+        L = model.dims.n_layers
         self.C, self.T, self.m_cap, self.tau = n_children, parent.seq, m_cap, tau
-        su = parent.su_layers() if tau == parent.tau else self._su_for_tau(tau)
+        self.layer_taus = tuple(float(t) for t in layer_taus) if layer_taus is not None else (float(tau),) * L
+        self.layer_folds = tuple(bool(f) for f in layer_folds) if layer_folds is not None else (True,) * L
+        if len(self.layer_taus) != L or len(self.layer_folds) != L:
+            raise ValueError(f"layer_taus / layer_folds must have {L} entries")
+        if not all(self.layer_folds) and m_cap < n_children * parent.seq:
+            raise ValueError("a layer that does not fold recomputes every row: m_cap must be C * T")
+        self.self_stable = parent.self_stable_at(self.layer_taus)
+        self._parent_version = parent.version
+        su = (self.self_stable == 0).any(dim=1).cpu().numpy() | ~np.array(self.layer_folds)
         self._su = np.ascontiguousarray(su.astype(np.uint8))
-        self._cfg = _FoldConfig(n_children, self.T, m_cap, float(tau), _lib.METRIC[metric], self._su.ctypes.data)
+        self._taus = np.ascontiguousarray(np.array(self.layer_taus, np.float32))
+        self._folds = np.ascontiguousarray(np.array(self.layer_folds, np.uint8))
+        self._cfg = _FoldConfig(n_children, self.T, m_cap, float(tau), _lib.METRIC[metric], self._su.ctypes.data,
+                                self._taus.ctypes.data, self._folds.ctypes.data, self.self_stable.data_ptr())
         nbytes = _i64()
         _lib.check(self.lib.af_fold_workspace_bytes(C.byref(model._cmodel.dims), C.byref(self._cfg), C.byref(nbytes)))
         self.workspace = torch.zeros(int(nbytes.value), dtype=torch.uint8, device=model.device)
@@ -231,7 +289,6 @@ class FoldPlan:
         self._plan = plan
         out = _FoldOutputs()
         _lib.check(self.lib.af_fold_get_outputs(plan, C.byref(out)))
-        L = model.dims.n_layers
         ws = self.workspace
         base = ws.data_ptr()
 
@@ -247,13 +304,19 @@ class FoldPlan:
         self.status = view(out.status, 1, torch.int32)
         self.n_fresh0 = view(out.n_fresh0, 1, torch.int32)
 
-    def _su_for_tau(self, tau: float) -> np.ndarray:
-        # Self-gate results depend on tau; recompute the flags for a different tau.
-        from actfold_b200.core.similarity_gate import SimilarityGate
+    def parent_rewritten(self) -> bool:
+        """After an in-place rewrite of the parent (a promotion): refresh the plan's self-gate rows.
 
-        x = self.parent.layer_in[:-1]
-        m = SimilarityGate(tau=tau)(x, x)
-        return (~m).any(dim=1).to(torch.uint8).cpu().numpy()
+        Returns True when the plan can no longer run this parent (the layers
+        where the parent fails its own gate changed, so the launch sequence
+        does); otherwise the plan, and any graph captured from it, stays valid.
+        """
+        fresh = self.parent.self_stable_at(self.layer_taus)
+        if fresh is not self.self_stable:
+            self.self_stable.copy_(fresh)
+        su = ((self.self_stable == 0).any(dim=1).cpu().numpy() | ~np.array(self.layer_folds)).astype(np.uint8)
+        self._parent_version = self.parent.version
+        return not np.array_equal(su, self._su)
 
     def run(self, child_tokens: torch.Tensor, logits: torch.Tensor, scores: torch.Tensor | None = None) -> None:
         if child_tokens.shape != (self.C, self.T) or child_tokens.dtype != torch.int64 or not child_tokens.is_contiguous():
@@ -318,7 +381,6 @@ class FoldPlan:
         dst = into.struct()
         _lib.check(self.lib.af_fold_promote(self._plan, int(child), toks.data_ptr(), logits.data_ptr(), C.byref(dst),
                                             _lib.stream_ptr(toks.device)), "af_fold_promote")
-        into.contents_changed()  # its token ids and self-gate rows are the child's now
         if self.tau != into.tau:
             # Rows the promotion did not touch carry self-gate flags of another tau.
             from actfold_b200.core.similarity_gate import SimilarityGate
@@ -326,6 +388,7 @@ class FoldPlan:
             x = into.layer_in[:-1]
             into.self_stable.copy_(SimilarityGate(tau=self.tau)(x, x).to(torch.uint8))
             into.tau = float(self.tau)
+        into.contents_changed()  # its token ids and self-gate rows are the child's now
         return into
 
     def capture(self, child_tokens: torch.Tensor, logits: torch.Tensor, scores: torch.Tensor | None = None
@@ -502,43 +565,65 @@ class LLaDAModel(nn.Module):
         return torch.stack([self.parent_pass(tokens[b]).logits for b in range(tokens.shape[0])])
 
     # ------------------------------------------------------------ folded pass
-    def plan(self, parent: ParentCache, n_children: int, m_cap: int, tau: float, metric: str = "cosine") -> FoldPlan:
-        key = (id(parent), n_children, m_cap, float(tau), metric)
+    def schedule(self, tau: float, layer_taus=None, layer_folds=None) -> tuple[tuple, tuple]:
+        """(per-layer thresholds, per-layer fold flags), ``tau`` and True everywhere by default."""
+        L = self.dims.n_layers
+        taus = tuple(float(t) for t in layer_taus) if layer_taus is not None else (float(tau),) * L
+        folds = tuple(bool(f) for f in layer_folds) if layer_folds is not None else (True,) * L
+        if len(taus) != L or len(folds) != L:
+            raise ValueError(f"a schedule needs {L} entries per layer")
+        return taus, folds
+
+    def plan(self, parent: ParentCache, n_children: int, m_cap: int, tau: float, metric: str = "cosine",
+             layer_taus=None, layer_folds=None) -> FoldPlan:
+        taus, folds = self.schedule(tau, layer_taus, layer_folds)
+        key = (id(parent), n_children, m_cap, float(tau), metric, taus, folds)
         p = self._plans.get(key)
-        if p is not None and p.parent is parent and p.tau == parent.tau and not np.array_equal(p._su, parent.su_layers()):
-            p = None  # an in-place promotion changed the parent's self-gate flags
+        if p is not None and p.parent is parent and p._parent_version != parent.version and p.parent_rewritten():
+            p = None  # an in-place promotion changed where the parent fails its own gate
         if p is None or p.parent is not parent:
-            p = FoldPlan(self, parent, n_children, m_cap, tau, metric)
+            p = FoldPlan(self, parent, n_children, m_cap, tau, metric, taus, folds)
             self._plans = {k: v for k, v in self._plans.items() if v.parent is parent}
             self._plans[key] = p
         return p
 
     @staticmethod
-    def capacity(child_tokens: torch.Tensor, parent: ParentCache, su: np.ndarray) -> int:
+    def capacity(child_tokens: torch.Tensor, parent: ParentCache, taus: Sequence[float] | None = None) -> int:
         """Rows a pass can need: edited rows + every child x every row the parent fails its own gate on."""
-        return LLaDAModel.capacity_and_bound(child_tokens, parent, su)[0]
+        return LLaDAModel.capacity_and_bound(child_tokens, parent, taus)[0]
 
     @staticmethod
-    def capacity_and_bound(child_tokens: torch.Tensor, parent: ParentCache, su: np.ndarray) -> tuple[int, int]:
-        """(m_cap, bound on one child's candidate rows per layer), from one small device read."""
+    def capacity_and_bound(child_tokens: torch.Tensor, parent: ParentCache, taus: Sequence[float] | None = None,
+                           folds: Sequence[bool] | None = None) -> tuple[int, int]:
+        """(m_cap, bound on one child's candidate rows per layer), from one small device read.
+
+        With a layer that does not fold every row is a candidate there: m_cap = C * T, bound T.
+        """
         C, T = child_tokens.shape
+        if folds is not None and not all(folds):
+            return round_capacity(C * T, C, T), T
+        taus = tuple(taus) if taus is not None else (parent.tau,) * parent.self_stable.shape[0]
         per_child = (child_tokens != parent.tokens[None]).sum(dim=1)
         edited, most = (int(v) for v in torch.stack([per_child.sum(), per_child.max()]).cpu())
-        su_rows = int((parent.self_stable == 0).any(dim=0).sum().item()) if su.any() else 0
+        su_rows = parent.su_rows_at(taus)
         return round_capacity(edited + C * su_rows, C, T), most + su_rows
 
     def verify(self, child_tokens: torch.Tensor, parent: ParentCache, tau: float, metric: str = "cosine",
                logits: torch.Tensor | None = None, scores: torch.Tensor | None = None, m_cap: int | None = None,
-               keep_kv: bool = False) -> tuple[torch.Tensor, FoldPlan]:
-        """Folded verification of child_tokens [C, T] against ``parent``; returns (logits [C, T, V], plan)."""
+               keep_kv: bool = False, layer_taus=None, layer_folds=None) -> tuple[torch.Tensor, FoldPlan]:
+        """Folded verification of child_tokens [C, T] against ``parent``; returns (logits [C, T, V], plan).
+
+        ``layer_taus`` / ``layer_folds``: an optional per-layer schedule (see FoldPlan).
+        """
         child_tokens = child_tokens.to(device=self.device, dtype=torch.int64).contiguous()
         if child_tokens.dim() != 2 or child_tokens.shape[1] != parent.seq:
             raise ValueError(f"children must be [C, {parent.seq}], got {tuple(child_tokens.shape)}")
         Cn = child_tokens.shape[0]
+        taus, folds = self.schedule(tau, layer_taus, layer_folds)
         child_cap = None
         if m_cap is None:
-            m_cap, child_cap = self.capacity_and_bound(child_tokens, parent, parent.su_layers())
-        plan = self.plan(parent, Cn, m_cap, tau, metric)
+            m_cap, child_cap = self.capacity_and_bound(child_tokens, parent, taus, folds)
+        plan = self.plan(parent, Cn, m_cap, tau, metric, taus, folds)
         if child_cap is not None:
             plan.set_child_cap(child_cap)
         if keep_kv and not plan.keeps_kv:
@@ -550,11 +635,17 @@ class LLaDAModel(nn.Module):
 
     def native_folded_forward(self, tokens: torch.Tensor, cache, gate, branch_id: Any, parent_branch_id: Any = None,
                               step_idx: int = 0, scheduler=None, **kwargs: Any) -> torch.Tensor:
-        """FoldedModel.forward for this architecture (see actfold_b200.core.model_wrapper)."""
+        """FoldedModel.forward for this architecture (see actfold_b200.core.model_wrapper).
+
+        With a ``scheduler`` every layer takes the reference's per-layer
+        decisions (actfold/core/folded_transformer.py:107-119): a layer where
+        ``should_fold(layer, step_idx)`` is False recomputes every row and is
+        not recorded by the profiler; a folding layer gates at
+        ``get_tau(layer, step_idx, "general")``, which the gate keeps as its
+        ``tau`` afterwards (the reference sets it on the shared gate).
+        """
         from actfold_b200.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER
 
-        if scheduler is not None:
-            raise NotImplementedError("the native LLaDA pass folds with one tau for every layer; use scheduler=None")
         tokens = tokens.to(self.device)
         if tokens.dim() == 1:
             tokens = tokens[None]
@@ -569,6 +660,12 @@ class LLaDAModel(nn.Module):
             parents[branch_id] = pc
             register_parent_in_cache(cache, branch_id, pc)
             return pc.logits[None]
+        L = self.dims.n_layers
+        taus, folds = None, None
+        if scheduler is not None:
+            folds = [bool(scheduler.should_fold(li, step_idx)) for li in range(L)]
+            taus = [float(scheduler.get_tau(layer_idx=li, step_idx=step_idx, task_type="general")) if folds[li]
+                    else float(gate.tau) for li in range(L)]
         children = getattr(cache, "native_children", None)
         if children is None:
             children = {}
@@ -581,7 +678,7 @@ class LLaDAModel(nn.Module):
             return self.forward(tokens)
         if pc.seq != tokens.shape[1]:
             pc = pc.resized(tokens.shape[1])  # zero-filled / truncated parent rows, as the reference gathers them
-        logits, plan = self.verify(tokens, pc, gate.tau, gate.metric, keep_kv=True)
+        logits, plan = self.verify(tokens, pc, gate.tau, gate.metric, keep_kv=True, layer_taus=taus, layer_folds=folds)
         plan.check_status()
         ids = list(branch_id) if isinstance(branch_id, (list, tuple)) else [branch_id] * tokens.shape[0]
         if len(set(ids)) == len(ids):
@@ -593,12 +690,19 @@ class LLaDAModel(nn.Module):
             for c, bid in enumerate(ids):
                 parents.pop(bid, None)
                 children[bid] = (plan, c, plan.serial)
-        if len(set(ids)) == len(ids):
-            GLOBAL_STABILITY_PROFILER.record_batch(ids, parent_branch_id, step_idx, plan.stable_masks(), gate.tau, gate.metric)
-        else:
-            masks = plan.stable_masks()
-            for li in range(masks.shape[0]):
-                GLOBAL_STABILITY_PROFILER.record(ids[0], parent_branch_id, li, step_idx, masks[li], gate.tau, gate.metric)
+        folded = [li for li in range(L) if plan.layer_folds[li]]
+        if folded:
+            masks = plan.stable_masks()[folded]
+            layer_tau = [plan.layer_taus[li] for li in folded]
+            if len(set(ids)) == len(ids):
+                GLOBAL_STABILITY_PROFILER.record_batch(ids, parent_branch_id, step_idx, masks, layer_tau, gate.metric,
+                                                       layer_ids=folded)
+            else:
+                for i, li in enumerate(folded):
+                    GLOBAL_STABILITY_PROFILER.record(ids[0], parent_branch_id, li, step_idx, masks[i], layer_tau[i],
+                                                     gate.metric)
+            if scheduler is not None:
+                gate.set_tau(layer_tau[-1])
         return logits
 
 

@@ -14,7 +14,7 @@ from __future__ import annotations
 
 from collections import defaultdict
 from dataclasses import dataclass, field
-from typing import Any, Optional
+from typing import Any, Optional, Sequence
 
 import torch
 
@@ -101,14 +101,23 @@ class StabilityProfiler:
         parent_branch_id: Optional[Any],
         step_idx: int,
         masks: torch.Tensor,
-        tau: float,
+        tau: float | Sequence[float],
         metric: str = "cosine",
         layer_offset: int = 0,
+        layer_ids: Optional[Sequence[int]] = None,
     ) -> None:
-        """Queue a whole pass: ``masks`` [L, C, T] (True = stable) for children ``branch_ids``."""
+        """Queue a whole pass: ``masks`` [n, C, T] (True = stable) for children ``branch_ids``.
+
+        Row i of ``masks`` is layer ``layer_ids[i]`` (default ``layer_offset + i``);
+        ``tau`` is one threshold for every row or one per row.
+        """
         if not self.enabled:
             return
-        self._pending.append(("batch", list(branch_ids), parent_branch_id, layer_offset, step_idx, masks.detach(), tau, metric))
+        layers = list(layer_ids) if layer_ids is not None else [layer_offset + i for i in range(masks.shape[0])]
+        taus = list(tau) if isinstance(tau, (list, tuple)) else [tau] * len(layers)
+        if len(layers) != masks.shape[0] or len(taus) != masks.shape[0]:
+            raise ValueError("record_batch: one layer index and one tau per mask row")
+        self._pending.append(("batch", list(branch_ids), parent_branch_id, layers, step_idx, masks.detach(), taus, metric))
 
     def flush(self) -> None:
         """Resolve queued records with one device-to-host copy."""
@@ -117,13 +126,13 @@ class StabilityProfiler:
         pending, self._pending = self._pending, []
         host = [p[5].to("cpu", non_blocking=False) for p in pending] if pending else []
         for p, m in zip(pending, host):
-            kind, bid, pid, layer_or_off, step, _, tau, metric = p
+            kind, bid, pid, layer, step, _, tau, metric = p
             if kind == "mask":
-                self._add(bid, pid, layer_or_off, step, m.bool(), tau, metric)
+                self._add(bid, pid, layer, step, m.bool(), tau, metric)
             else:
                 for li in range(m.shape[0]):
                     for ci, b in enumerate(bid):
-                        self._add(b, pid, layer_or_off + li, step, m[li, ci][None].bool(), tau, metric)
+                        self._add(b, pid, layer[li], step, m[li, ci][None].bool(), tau[li], metric)
 
     def _add(self, branch_id, parent_branch_id, layer_idx, step_idx, mask: torch.Tensor, tau, metric) -> None:
         num = int(mask.numel())

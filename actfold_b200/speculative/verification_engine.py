@@ -170,10 +170,7 @@ class ActFoldVerificationEngine:
         # (capacity, per-child candidate bound) from the host copy of the tokens (no device round trip).
         ptok = self._parent_host_tokens(pc)
         per_child = (child_tokens_host.numpy() != ptok[None]).sum(axis=1)
-        su_rows = getattr(pc, "_su_rows", None)
-        if su_rows is None:  # rows the parent fails its own gate on (one device read per parent)
-            su_rows = int((pc.self_stable == 0).any(dim=0).sum().item())
-            pc._su_rows = su_rows
+        su_rows = pc.su_rows_at((self.gate.tau,) * self.model.dims.n_layers)  # one device read per parent
         return round_capacity(int(per_child.sum()) + Cn * su_rows, Cn, T), int(per_child.max()) + su_rows
 
     def _parent_host_tokens(self, pc: ParentCache) -> np.ndarray:

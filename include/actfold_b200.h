@@ -264,7 +264,20 @@ typedef struct {
   int64_t m_cap;               /* capacity for candidate / divergent rows per layer (all children) */
   float tau;                   /* SimilarityGate tau (compared in bf16) */
   int32_t metric;              /* af_metric */
-  const uint8_t* su_layers;    /* host [n_layers]: 1 where some parent row fails its own gate */
+  const uint8_t* su_layers;    /* host [n_layers]: 1 where some parent row fails its own gate
+                                  (at this layer's threshold) or where the layer does not fold */
+  /* Per-layer schedule, all nullable (null: the plain pass above). It replaces
+   * FoldingScheduler.get_tau / should_fold inside FoldedTransformerLayer.forward
+   * (actfold/core/folded_transformer.py:107-119, folding_scheduler.py:48-115):
+   *   tau_layers  host [n_layers]: the gate threshold of each layer;
+   *   fold_layers host [n_layers]: 0 where the layer does not fold -- every row
+   *               of every child is recomputed, as _recompute_all does there
+   *               (needs m_cap = n_children * seq and a per-child bound of seq);
+   *   self_stable device [n_layers, seq]: the parent's own gate results at these
+   *               thresholds (null: the parent cache's, taken at its own tau). */
+  const float* tau_layers;
+  const uint8_t* fold_layers;
+  const uint8_t* self_stable;
 } af_fold_config;
 
 typedef struct {

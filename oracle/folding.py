@@ -14,6 +14,10 @@ activations are cached:
 The cache is assumed large enough to hold every parent entry (the plain
 ActivationCache with max_entries_per_layer >= 2 T), so the KeyError fallbacks
 of :135-141 never fire.
+
+With a FoldingScheduler (:107-119) each layer has its own threshold
+(``get_tau``), and a layer where ``should_fold`` is False recomputes the
+whole child sequence without gating (no stable mask is recorded for it).
 """
 
 from __future__ import annotations
@@ -62,13 +66,19 @@ def llada_folded_children(
     weights: dict,
     dims: L.LLaDADims,
     tau: float,
+    layer_taus=None,
+    layer_folds=None,
 ) -> dict:
     """Verify each child [C, T] against the cached parent, sequentially (as the reference does).
 
-    Returns masks [L, C, T] (True = stable), per-layer child states
-    [L+1, C, T, H] and logits [C, T, V].
+    Returns masks [L, C, T] (True = stable; all False on a layer that does not
+    fold), per-layer child states [L+1, C, T, H] and logits [C, T, V].
+    ``layer_taus`` / ``layer_folds``: the per-layer schedule (default: ``tau``
+    and folding on every layer).
     """
     C, T = children.shape
+    taus = list(layer_taus) if layer_taus is not None else [tau] * dims.n_layers
+    folds = list(layer_folds) if layer_folds is not None else [True] * dims.n_layers
     cos, sin = L.rope_tables(T, dims.head_dim, dims.rope_theta)
     masks = np.zeros((dims.n_layers, C, T), bool)
     states = np.zeros((dims.n_layers + 1, C, T, dims.hidden), np.float32)
@@ -78,8 +88,11 @@ def llada_folded_children(
         states[0, c] = h[0]
         for li, lw in enumerate(weights["layers"]):
             layer = lambda x, lw=lw: L.block(x, lw, dims, cos, sin)  # noqa: E731
-            h, m = folded_layer(layer, h, parent["layer_in"][li][None], parent["layer_in"][li + 1][None], tau, "bf16")
-            masks[li, c] = m[0]
+            if folds[li]:
+                h, m = folded_layer(layer, h, parent["layer_in"][li][None], parent["layer_in"][li + 1][None], taus[li], "bf16")
+                masks[li, c] = m[0]
+            else:
+                h = layer(h[0])[None]
             states[li + 1, c] = h[0]
         logits[c] = L.lm_head(h[0], weights, dims)
     return {"masks": masks, "states": states, "logits": logits}

@@ -80,3 +80,6 @@ def engine_children(parent, mask_id: int, spec: dict):
 
     return np.concatenate([W.llada_children(parent, 1, d, mask_id, spec["token_seed"] + 100 + c)
                            for c, d in enumerate(spec["child_d"])])
+# FoldingScheduler over a 4-layer tiny LLaDA: base tau 0.95, 4 diffusion steps,
+# layer 1 disabled; children verified at steps 0, 2 and 3 (the final step folds nothing).
+TINY_SCHED = dict(TINY_LLADA, n_layers=4, num_steps=4, disabled_layers=(1,), steps=(0, 2, 3))

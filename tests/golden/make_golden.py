@@ -20,6 +20,8 @@ Outputs (all small, compressed):
   dream_tiny.npz same, GQA (Dream-shaped) tiny model
   llada_chain.npz grandchildren folded against a verified child (chained folding)
   llada_resize.npz children longer / shorter than their parent (zero-filled parent rows)
+  sched.npz      reference FoldedModel with a FoldingScheduler (per-layer tau,
+                 a disabled layer, the final layer and step unfolded)
   engine.npz     reference ActFoldVerificationEngine.verify_branch over the tiny
                  LLaDA block: acceptance, stable ratio, score, per-layer profile
                  and cache clearing at two thresholds, and a chained step
@@ -42,7 +44,7 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 from actfold_b200 import workloads as W  # noqa: E402
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_ENGINE, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, digest, engine_children, gate_inputs  # noqa: E402
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_ENGINE, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, TINY_SCHED, digest, engine_children, gate_inputs  # noqa: E402
 from oracle import llada as OL  # noqa: E402
 from oracle.llada_torch import TorchLLaDA  # noqa: E402
 
@@ -369,6 +371,66 @@ def make_llada_resize(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     np.savez_compressed(os.path.join(HERE, fname), **out)
 
 
+def make_sched(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
+    """FoldedModel(..., scheduler=FoldingScheduler) over the restated tiny LLaDA block.
+
+    Per folded layer the reference sets the shared gate's tau to
+    get_tau(layer, step) and records the mask; a layer where should_fold is
+    False (a disabled layer, the final layer, every layer of the final step)
+    recomputes without gating (actfold/core/folded_transformer.py:107-119).
+    Recorded per step: the folded layers, their tau, masks, logits and the
+    gate's tau after the step.
+    """
+    import dataclasses
+
+    from actfold.core.folding_scheduler import FoldingScheduler
+    from actfold.core.model_wrapper import FoldedModel
+    from actfold.profiler.stability_profiler import GLOBAL_STABILITY_PROFILER
+
+    dims = dataclasses.replace(dims, n_layers=spec["n_layers"])
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    T = spec["T"]
+    parent, children = W.llada_tokens(T, spec["n_prompt"], spec["mask_frac"], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"])
+    C = children.shape[0]
+    model = TorchLLaDA(w, od, T)
+    cache = core.ActivationCache(max_entries_per_layer=(C * len(spec["steps"]) + 2) * T, device="cpu")
+    gate = core.SimilarityGate(tau=spec["tau"], metric="cosine")
+    sched = FoldingScheduler(base_tau=spec["tau"], num_layers=dims.n_layers, num_steps=spec["num_steps"],
+                             disabled_layers=set(spec["disabled_layers"]))
+    folded = FoldedModel(model, cache, gate, scheduler=sched)
+    out = {"parent": parent, "children": children}
+    with torch.no_grad():
+        folded(torch.from_numpy(parent)[None], branch_id="parent")
+        for step in spec["steps"]:
+            masks, taus, layers, logits = [], [], None, []
+            for c in range(C):
+                bid = f"s{step}c{c}"
+                GLOBAL_STABILITY_PROFILER.reset_branch(bid)
+                lg = folded(torch.from_numpy(children[c])[None], branch_id=bid, parent_branch_id="parent", step_idx=step)
+                prof = GLOBAL_STABILITY_PROFILER.get_profile(bid)
+                stats = prof.layer_stats if prof is not None else []
+                ls = [st.layer_idx for st in stats]
+                assert layers is None or layers == ls
+                layers = ls
+                taus = [st.tau_used for st in stats]
+                m = np.zeros((len(ls), T), bool)
+                for i, st in enumerate(stats):
+                    if st.divergence_positions is not None:
+                        m[i] = True
+                        m[i, st.divergence_positions[:, 1].numpy()] = False
+                    else:
+                        m[i] = True
+                masks.append(m)
+                logits.append(lg[0].view(torch.int16).numpy().view(np.uint16))
+            out[f"step{step}/layers"] = np.array(layers, np.int64)
+            out[f"step{step}/taus"] = np.array(taus, np.float64)
+            out[f"step{step}/masks"] = np.stack(masks, axis=1) if layers else np.zeros((0, C, T), bool)
+            out[f"step{step}/logits_bits"] = np.stack(logits)
+            out[f"step{step}/gate_tau_after"] = np.array(gate.tau)
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
 def make_engine(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     """The reference verification engine over FoldedModel(restated tiny LLaDA).
 
@@ -484,6 +546,7 @@ def main() -> None:
         "llada_chain": lambda: make_llada_chain(core, W.LLADA_TINY, TINY_LLADA_CHAIN, "llada_chain.npz"),
         "llada_resize": lambda: make_llada_resize(core, W.LLADA_TINY, TINY_LLADA_RESIZE, "llada_resize.npz"),
         "engine": lambda: make_engine(core, W.LLADA_TINY, TINY_ENGINE, "engine.npz"),
+        "sched": lambda: make_sched(core, W.LLADA_TINY, TINY_SCHED, "sched.npz"),
     }
     for name, job in jobs.items():
         if a.only in (None, name):

@@ -203,3 +203,60 @@ def test_engine_oracle_matches_reference(golden):
     np.testing.assert_allclose(res2["masks"].mean(axis=2).T, g["grand/layer_ratio"], atol=1e-6)
     scale = np.abs(res2["logits"]).max(axis=(1, 2))
     assert (np.abs(res2["logits"].mean(axis=(1, 2)) - g["grand/score"]) <= 2e-2 * scale).all()
+
+
+def _sched_case():
+    import dataclasses
+
+    from actfold_b200.core import FoldingScheduler
+    from gen_inputs import TINY_SCHED
+
+    spec = TINY_SCHED
+    dims = dataclasses.replace(W.LLADA_TINY, n_layers=spec["n_layers"])
+    sched = FoldingScheduler(base_tau=spec["tau"], num_layers=dims.n_layers, num_steps=spec["num_steps"],
+                             disabled_layers=set(spec["disabled_layers"]))
+    return spec, dims, sched
+
+
+# After a layer that does not fold, every row is recomputed, so the next folded
+# layer gates rows that differ from the parent's by more than rounding. Two
+# correct recomputations that round differently (numpy against torch here, the
+# CUDA kernels against the reference on the GPU) can then disagree on rows whose
+# similarity lies near the bf16 decision boundary: measured up to 4.5e-3 apart
+# in f32 similarity on this workload. Rows within SCHED_WINDOW of the boundary
+# are exempt from the mask comparison; every other row must agree.
+SCHED_WINDOW = 1e-2
+
+
+def sched_exempt(states: np.ndarray, parent_in: np.ndarray, tau: float) -> np.ndarray:
+    """[C, T] rows of a folded layer whose f32 similarity (oracle rows) lies within SCHED_WINDOW of the boundary."""
+    r = gate(states, np.broadcast_to(parent_in[None], states.shape), tau, "cosine", 1e-8, "bf16")
+    return exempt_rows(r, SCHED_WINDOW)
+
+
+def test_scheduler_oracle_matches_reference(golden):
+    """FoldingScheduler decisions: per-layer tau, disabled / final layer and final step recompute unfolded."""
+    g = golden("sched")
+    spec, dims, sched = _sched_case()
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    parent, children = W.llada_tokens(spec["T"], spec["n_prompt"], spec["mask_frac"], spec["n_children"], spec["d"], dims.mask_id, spec["token_seed"])
+    np.testing.assert_array_equal(children, g["children"])
+    par = OF.llada_parent(parent, w, od)
+    for step in spec["steps"]:
+        folds = [sched.should_fold(li, step) for li in range(dims.n_layers)]
+        taus = [sched.get_tau(li, step) if folds[li] else spec["tau"] for li in range(dims.n_layers)]
+        layers = [li for li in range(dims.n_layers) if folds[li]]
+        np.testing.assert_array_equal(layers, g[f"step{step}/layers"])
+        np.testing.assert_allclose([taus[li] for li in layers], g[f"step{step}/taus"], rtol=0, atol=1e-12)
+        res = OF.llada_folded_children(children, par, w, od, spec["tau"], taus, folds)
+        ok_rows = np.ones(children.shape, bool)
+        for i, li in enumerate(layers):
+            mism = res["masks"][li] != g[f"step{step}/masks"][i]
+            exempt = sched_exempt(res["states"][li], par["layer_in"][li], taus[li]) if li > 0 else exempt_rows(
+                gate(res["states"][li], np.broadcast_to(par["layer_in"][li][None], res["states"][li].shape), taus[li],
+                     "cosine", 1e-8, "bf16"))
+            assert not (mism & ~exempt).any(), (step, li, np.argwhere(mism & ~exempt))
+            ok_rows &= ~mism
+        ref = from_bf16_bits(g[f"step{step}/logits_bits"])
+        assert _bf16_close(res["logits"][ok_rows], ref[ok_rows]) <= 2e-2
