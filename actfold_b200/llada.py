@@ -673,14 +673,24 @@ class LLaDAModel(nn.Module):
         pc = parents.get(parent_branch_id)
         if pc is None:
             pc = _promote_recorded_child(cache, parents, children, parent_branch_id)
+        ids = list(branch_id) if isinstance(branch_id, (list, tuple)) else [branch_id] * tokens.shape[0]
         if pc is None:
-            # No usable parent activations: recompute (folded_transformer.py:135-141).
-            return self.forward(tokens)
+            # No usable parent activations: every layer recomputes (folded_transformer.py:135-141), and
+            # the reference then holds each child's activations under its id, so each row's dense pass
+            # becomes a parent cache that later children can fold against.
+            rows = []
+            for i, bid in enumerate(ids):
+                cpc = self.parent_pass(tokens[i], tau=gate.tau)
+                if len(set(ids)) == len(ids):
+                    children.pop(bid, None)
+                    parents[bid] = cpc
+                    register_parent_in_cache(cache, bid, cpc)
+                rows.append(cpc.logits)
+            return torch.stack(rows)
         if pc.seq != tokens.shape[1]:
             pc = pc.resized(tokens.shape[1])  # zero-filled / truncated parent rows, as the reference gathers them
         logits, plan = self.verify(tokens, pc, gate.tau, gate.metric, keep_kv=True, layer_taus=taus, layer_folds=folds)
         plan.check_status()
-        ids = list(branch_id) if isinstance(branch_id, (list, tuple)) else [branch_id] * tokens.shape[0]
         if len(set(ids)) == len(ids):
             # Every verified child can be named as a later parent_branch_id (the
             # reference caches each child's activations): it is promoted on

@@ -83,3 +83,32 @@ def engine_children(parent, mask_id: int, spec: dict):
 # FoldingScheduler over a 4-layer tiny LLaDA: base tau 0.95, 4 diffusion steps,
 # layer 1 disabled; children verified at steps 0, 2 and 3 (the final step folds nothing).
 TINY_SCHED = dict(TINY_LLADA, n_layers=4, num_steps=4, disabled_layers=(1,), steps=(0, 2, 3))
+# folded_generate over the tiny LLaDA block: a 24-id prompt, 4 new tokens,
+# greedy single-candidate steps, then 3 drafted candidates per step chosen by
+# the greedy policy. The prompt seed is the first from prompt_seed on whose
+# every greedy choice has a top-2 logit margin of at least min_margin.
+TINY_FGEN = dict(T=24, max_new_tokens=4, n_branches=3, weight_seed=7, prompt_seed=50, min_margin=0.03, tau=0.95)
+
+
+class AppendDraft:
+    """Deterministic drafts for folded_generate: each candidate appends one id drawn from a seeded PCG64 stream.
+
+    ``generate(parent, num_branches, seed, max_new_tokens)`` follows the
+    reference DraftGenerator's call; only ``.tokens`` of the returned objects
+    is read.
+    """
+
+    def __init__(self, id_hi: int, base_seed: int = 777) -> None:
+        self.id_hi, self.base_seed = id_hi, base_seed
+
+    def generate(self, parent, num_branches: int = 2, seed=None, max_new_tokens: int = 0):
+        import types
+
+        import torch
+
+        rng = np.random.default_rng(self.base_seed + (seed or 0))
+        out = []
+        for _ in range(num_branches):
+            new = torch.from_numpy(rng.integers(0, self.id_hi, size=(parent.tokens.shape[0], max_new_tokens)))
+            out.append(types.SimpleNamespace(tokens=torch.cat([parent.tokens, new.to(parent.tokens.dtype)], dim=1)))
+        return out

@@ -22,6 +22,8 @@ Outputs (all small, compressed):
   llada_resize.npz children longer / shorter than their parent (zero-filled parent rows)
   sched.npz      reference FoldedModel with a FoldingScheduler (per-layer tau,
                  a disabled layer, the final layer and step unfolded)
+  fgen.npz       reference folded_generate (greedy steps, and drafted candidates
+                 with the greedy policy) over the tiny LLaDA block
   engine.npz     reference ActFoldVerificationEngine.verify_branch over the tiny
                  LLaDA block: acceptance, stable ratio, score, per-layer profile
                  and cache clearing at two thresholds, and a chained step
@@ -44,7 +46,7 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 from actfold_b200 import workloads as W  # noqa: E402
-from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_ENGINE, TINY_LLADA, TINY_LLADA_CHAIN, TINY_LLADA_RESIZE, TINY_SCHED, digest, engine_children, gate_inputs  # noqa: E402
+from gen_inputs import DEMO, GATE_CASES, TINY_DREAM, TINY_ENGINE, TINY_LLADA, TINY_LLADA_CHAIN, TINY_FGEN, TINY_LLADA_RESIZE, TINY_SCHED, AppendDraft, digest, engine_children, gate_inputs  # noqa: E402
 from oracle import llada as OL  # noqa: E402
 from oracle.llada_torch import TorchLLaDA  # noqa: E402
 
@@ -431,6 +433,103 @@ def make_sched(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     np.savez_compressed(os.path.join(HERE, fname), **out)
 
 
+def make_fgen(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
+    """The reference folded_generate (actfold/speculative/folded_generation.py:44-238) over FoldedModel.
+
+    Greedy mode: each step appends the argmax of the accepted sequence's last
+    logits and folds the child against it. Draft mode: AppendDraft proposes
+    n_branches one-id extensions per step, each folded against the accepted
+    sequence, GreedyAcceptancePolicy keeps the one with the largest
+    last-position logit. Recorded: the accepted tokens after every step, the
+    accepted node's stable ratio, the greedy top-2 margins (greedy mode) and
+    every candidate's score (draft mode), and the final result fields.
+    """
+    import torch.nn as nn
+    from actfold.core.model_wrapper import FoldedModel
+    from actfold.speculative.acceptance_policy import GreedyAcceptancePolicy
+    from actfold.speculative.fast_dllm_adapter import FastDLLMAdapter
+    from actfold.speculative.folded_generation import folded_generate
+
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    Tmax = spec["T"] + spec["max_new_tokens"]
+
+    class Emb(nn.Module):
+        def __init__(self, table):
+            super().__init__()
+            self.table = table
+
+        def forward(self, tokens):
+            return self.table[tokens]
+
+    class Recording(GreedyAcceptancePolicy):
+        def __init__(self):
+            self.scores = []
+
+        def select(self, candidates, logits=None):
+            self.scores.append([float(n.logits[:, -1, :].max(dim=-1).values.mean()) for n in candidates])
+            return super().select(candidates, logits)
+
+    def run(prompt, draft):
+        model = TorchLLaDA(w, od, Tmax)
+        model.embedding = Emb(model.embed)
+        cache = core.ActivationCache(max_entries_per_layer=64 * Tmax, device="cpu")
+        gate = core.SimilarityGate(tau=spec["tau"], metric="cosine")
+        folded = FoldedModel(model, cache, gate)
+        adapter = FastDLLMAdapter(folded.wrapped_model, num_layers=dims.n_layers, hidden_dim=dims.hidden,
+                                  num_heads=dims.n_heads, vocab_size=dims.vocab, folded_model=folded)
+        pol = Recording()
+        steps = []
+        orig = pol.select
+
+        def select(cands, logits=None):
+            chosen = orig(cands, logits)
+            steps.append((chosen.tokens[0].clone(), float(chosen.metadata.get("stable_ratio", -1.0)),
+                          [n.tokens[0].clone() for n in cands]))
+            return chosen
+
+        pol.select = select
+        with torch.no_grad():
+            res = folded_generate(adapter, prompt, spec["max_new_tokens"], folded_model=folded,
+                                  draft_generator=draft, acceptance_policy=pol,
+                                  num_branches_per_step=spec["n_branches"] if draft is not None else 1)
+        return res, steps, pol.scores
+
+    def greedy_margins(prompt, steps):
+        # top-2 margin of the last logits of each accepted sequence that a greedy step extended
+        model = TorchLLaDA(w, od, Tmax)
+        seqs = [prompt[0]] + [st[0] for st in steps[:-1]]
+        out = []
+        with torch.no_grad():
+            for sq in seqs:
+                lg = model(sq[None])[0, -1].float()
+                top = lg.topk(2).values
+                out.append(float(top[0] - top[1]))
+        return out
+
+    seed = spec["prompt_seed"]
+    while True:
+        prompt = torch.from_numpy(np.random.default_rng(seed).integers(0, dims.mask_id, size=(1, spec["T"])))
+        res_g, steps_g, _ = run(prompt, None)
+        margins = greedy_margins(prompt, steps_g)
+        if min(margins) >= spec["min_margin"]:
+            break
+        seed += 1
+    res_d, steps_d, scores_d = run(prompt, AppendDraft(dims.mask_id))
+    out = {"prompt": prompt.numpy(), "prompt_seed": np.array(seed), "greedy/margins": np.array(margins)}
+    for name, res, steps in (("greedy", res_g, steps_g), ("draft", res_d, steps_d)):
+        out[f"{name}/tokens"] = res.tokens.numpy()
+        out[f"{name}/stable_ratio"] = np.array(res.stable_ratio)
+        out[f"{name}/num_folded_steps"] = np.array(res.num_folded_steps)
+        out[f"{name}/final_branch_id"] = np.array(str(res.final_branch_id))
+        out[f"{name}/step_ratio"] = np.array([st[1] for st in steps])
+        for i, st in enumerate(steps):
+            out[f"{name}/step{i}/tokens"] = st[0].numpy()
+            out[f"{name}/step{i}/candidates"] = np.stack([c.numpy() for c in st[2]])
+    out["draft/scores"] = np.array(scores_d)
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
 def make_engine(core, dims: W.ModelDims, spec: dict, fname: str) -> None:
     """The reference verification engine over FoldedModel(restated tiny LLaDA).
 
@@ -547,6 +646,7 @@ def main() -> None:
         "llada_resize": lambda: make_llada_resize(core, W.LLADA_TINY, TINY_LLADA_RESIZE, "llada_resize.npz"),
         "engine": lambda: make_engine(core, W.LLADA_TINY, TINY_ENGINE, "engine.npz"),
         "sched": lambda: make_sched(core, W.LLADA_TINY, TINY_SCHED, "sched.npz"),
+        "fgen": lambda: make_fgen(core, W.LLADA_TINY, TINY_FGEN, "fgen.npz"),
     }
     for name, job in jobs.items():
         if a.only in (None, name):

@@ -260,3 +260,25 @@ def test_scheduler_oracle_matches_reference(golden):
             ok_rows &= ~mism
         ref = from_bf16_bits(g[f"step{step}/logits_bits"])
         assert _bf16_close(res["logits"][ok_rows], ref[ok_rows]) <= 2e-2
+
+
+def test_folded_generate_oracle_matches_reference(golden):
+    """The greedy folded_generate trajectory on the oracle: each step's child (the accepted sequence plus the
+    argmax of its last logits) folds against the accepted sequence's activations, zero-filled at the new position."""
+    from gen_inputs import TINY_FGEN
+
+    g = golden("fgen")
+    dims, spec = W.LLADA_TINY, TINY_FGEN
+    od = OL.LLaDADims(dims.n_layers, dims.hidden, dims.n_heads, dims.n_kv_heads, dims.head_dim, dims.ffn, dims.vocab, dims.rms_eps, dims.rope_theta)
+    w = W.llada_weights_numpy(dims, seed=spec["weight_seed"])
+    seq = g["prompt"][0]
+    parent = OF.llada_parent(seq, w, od)  # the root's parent pass (its logits pick the first token)
+    for i in range(spec["max_new_tokens"]):
+        nxt = int(np.argmax(parent["logits"][-1]))
+        child = np.concatenate([seq, [nxt]])
+        np.testing.assert_array_equal(child, g[f"greedy/step{i}/tokens"])
+        res = OF.llada_folded_children(child[None], OF.llada_resize_parent(parent, child.size), w, od, spec["tau"])
+        ratio = float(res["masks"].mean(axis=(1, 2)).mean())
+        assert abs(ratio - float(g["greedy/step_ratio"][i])) <= 1e-6
+        parent, seq = OF.llada_promote(res, 0), child
+    np.testing.assert_array_equal(seq, g["greedy/tokens"][0])
