@@ -250,11 +250,69 @@ __device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int
   }
 }
 
+// Rows whose split-K GEMM left fp32 partials (GemmCall::partial_out): the
+// row's value is the residual GEMM epilogue applied here, bit for bit:
+// bf16(res + bf16(p_0 + p_1 + ... + p_{S-1})), the splits summed from 0 up.
+struct PartialRows {
+  const float* part;               // [S][m_cap][H] fp32, null: rows are read from `in`
+  int64_t split_stride;            // m_cap * H
+  int nsplit;                      // S (<= 4)
+  const __nv_bfloat16* res;        // residual rows [.., H]
+  const int* res_rows;             // nullable: residual row of row i
+  __nv_bfloat16* store;            // the finished rows are written here (row i)
+};
+
+template <int NV>
+__device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row, int nvec, int tid, uint4 (&v)[NV]) {
+  const int64_t rrow = pr.res_rows ? pr.res_rows[row] : row;
+  const char* rp = reinterpret_cast<const char*>(pr.res + rrow * (int64_t)(nvec * 8));
+  const float* pp = pr.part + (int64_t)row * (nvec * 8);
+  float4 a[NV][2][4];
+  uint4 rv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * kRowThreads + tid;
+    if (j >= nvec) continue;
+    rv[i] = ldg16(rp + 16 * (int64_t)j);
+#pragma unroll
+    for (int sp = 0; sp < 4; ++sp)
+      if (sp < pr.nsplit) {
+        const float4* q = reinterpret_cast<const float4*>(pp + sp * pr.split_stride + 8 * (int64_t)j);
+        a[i][0][sp] = q[0];
+        a[i][1][sp] = q[1];
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * kRowThreads + tid;
+    if (j >= nvec) {
+      v[i] = make_uint4(0u, 0u, 0u, 0u);
+      continue;
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int sp = 0; sp < 4; ++sp)
+      if (sp < pr.nsplit) {
+        acc[0] += a[i][0][sp].x; acc[1] += a[i][0][sp].y; acc[2] += a[i][0][sp].z; acc[3] += a[i][0][sp].w;
+        acc[4] += a[i][1][sp].x; acc[5] += a[i][1][sp].y; acc[6] += a[i][1][sp].z; acc[7] += a[i][1][sp].w;
+      }
+    float r[8];
+    unpack<AF_DTYPE_BF16>(rv[i], r);
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&v[i]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      ow[e] = pack_bf16x2(__fadd_rn(r[2 * e], rnd<AF_DTYPE_BF16>(acc[2 * e])),
+                          __fadd_rn(r[2 * e + 1], rnd<AF_DTYPE_BF16>(acc[2 * e + 1])));
+    stg16(reinterpret_cast<char*>(pr.store + (int64_t)row * (nvec * 8)) + 16 * (int64_t)j, v[i]);
+  }
+}
+
 // out[i] = rmsnorm(in[i]) * w for i < n (rows strided by H); one CTA per row.
+// With pr.part, row i is first finished from its split-K partials (and stored).
 template <int NV>
 __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat16* in, const __nv_bfloat16* w, int H,
                                                               float eps, const int* n_dev, int n_cap,
-                                                              __nv_bfloat16* out) {
+                                                              __nv_bfloat16* out, const PartialRows pr) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
@@ -263,7 +321,10 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat1
   if (i >= n) return;
   const int nvec = H / 8;
   uint4 v[NV];
-  load_row<NV, kRowThreads>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, threadIdx.x, v);
+  if (pr.part)
+    load_row_partials<NV>(pr, i, nvec, threadIdx.x, v);
+  else
+    load_row<NV, kRowThreads>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, threadIdx.x, v);
   rmsnorm_regs<NV>(v, nvec, H, w, eps, reinterpret_cast<char*>(out + (int64_t)i * H), threadIdx.x, RowGroup{red});
 }
 
@@ -281,6 +342,7 @@ struct FoldGateArgs {
   float eps;
   GateConsts k;
   int force_div;                  // 1: the layer does not fold, every candidate is divergent
+  PartialRows fresh_part;         // part non-null: fresh rows are finished here from the previous down GEMM's partials
   uint8_t* stable;
   __nv_bfloat16* xc;              // packed candidate hidden [m_cap, H]
   __nv_bfloat16* a;               // packed normalized rows [m_cap, H]
@@ -301,8 +363,11 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
   const char* prow = reinterpret_cast<const char*>(g.p_in + (int64_t)t * g.H);
   const char* hrow = src >= 0 ? reinterpret_cast<const char*>(g.x_fresh + (int64_t)src * g.H) : prow;
   uint4 hv[NV], pv[NV];
-  load_row<NV, kRowThreads>(hrow, nvec, tid, hv);
   load_row<NV, kRowThreads>(prow, nvec, tid, pv);
+  if (src >= 0 && g.fresh_part.part)
+    load_row_partials<NV>(g.fresh_part, src, nvec, tid, hv);  // also stores the finished row into x_fresh
+  else
+    load_row<NV, kRowThreads>(hrow, nvec, tid, hv);
   const GateOut o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, tid, rows);
   if (tid == 0) g.stable[r] = g.force_div ? 0 : o.stable;
   char* xc = reinterpret_cast<char*>(g.xc + (int64_t)r * g.H);
@@ -534,6 +599,17 @@ struct Bump {
 // dependent launch (each waits for its predecessor inside the kernel, see
 // pdl_wait), so a kernel's launch and prologue overlap the previous kernel's
 // tail. ACTFOLD_PDL=0 turns it off.
+// ACTFOLD_SPLITK_PARTIALS=0: the O / down GEMMs reduce their k-splits inside
+// the launch (thread-block cluster) instead of leaving fp32 partials to the
+// next row kernel (comparison runs).
+static bool partials_off() {
+  static const bool off = [] {
+    const char* e = getenv("ACTFOLD_SPLITK_PARTIALS");
+    return e && e[0] == '0';
+  }();
+  return off;
+}
+
 static bool pass_pdl() {
   static const bool on = [] {
     const char* e = getenv("ACTFOLD_PDL");
@@ -649,7 +725,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     __nv_bfloat16* xnext = xin + (int64_t)(l + 1) * Ti * z.H;
     __nv_bfloat16* qkv_l = qkvb + (int64_t)l * Ti * z.qkv;
     AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, x, static_cast<const __nv_bfloat16*>(lw.attn_norm), z.H, eps, nullptr,
-                     Ti, w.A);
+                     Ti, w.A, PartialRows{});
     AF_DISPATCH_ROWS(z.H, k_self_gate, Ti, s, x, z.H, Ti, gk, self_stable + (int64_t)l * Ti);
     GemmCall c = base_call(stw);
     c.x = w.A;
@@ -697,7 +773,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
     c.ldr = z.H;
     if ((st = gemm_run(c, s))) return st;
     AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm), z.H, eps,
-                     nullptr, Ti, w.bn);
+                     nullptr, Ti, w.bn, PartialRows{});
     c = base_call(stw);
     c.x = w.bn;
     c.ldx = z.H;
@@ -725,7 +801,7 @@ extern "C" int af_dense_forward(const af_model* m, const int64_t* tokens, int64_
   }
   const __nv_bfloat16* xl = xin + (int64_t)z.L * Ti * z.H;
   AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, Ti, s, xl, static_cast<const __nv_bfloat16*>(m->final_norm), z.H, eps,
-                   nullptr, Ti, w.A);
+                   nullptr, Ti, w.A, PartialRows{});
   AF_LAUNCH(k_zero_f32, (Ti + 255) / 256, 256, 0, s, logit_row_sums, (int64_t)Ti);
   GemmCall c = base_call(stw);
   c.x = w.A;
@@ -758,6 +834,10 @@ struct FoldWs {
   unsigned* status;
   int* cand_div;  // [m_cap] divergent rank of each candidate of the current layer, -1 if stable
   int bits_ld;
+  // Split-K partials of the O and down GEMMs ([S][m_cap][H] fp32, S = their
+  // k-splits), finished by the next row kernel; null when neither splits.
+  float* part;
+  int split_o, split_down;
 };
 
 static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
@@ -790,6 +870,11 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
   w.row_sums = b.take<float>((int64_t)C * T);
   w.status = b.take<unsigned>(1);
   w.cand_div = b.take<int>(m_cap);
+  w.split_o = gemm_splits(z.H, z.q, m_cap);
+  w.split_down = gemm_splits(z.H, z.FF, m_cap);
+  const int S = std::max(w.split_o, w.split_down);
+  w.part = (S > 1 && S <= 4 && !partials_off()) ? b.take<float>((int64_t)S * m_cap * z.H) : nullptr;
+  if (!w.part) w.split_o = w.split_down = 1;
   return w;
 }
 
@@ -1005,6 +1090,16 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     g.eps = eps;
     g.k = make_gate_consts(AF_DTYPE_BF16, p->taus[l], 1e-8f, hn);
     g.force_div = p->folds[l] ? 0 : 1;
+    memset(&g.fresh_part, 0, sizeof(g.fresh_part));
+    if (l > 0 && w.split_down > 1) {
+      // Layer l's fresh rows are the previous down GEMM's outputs, left as
+      // split-K partials: finish them here (residual = that layer's h1).
+      g.fresh_part.part = w.part;
+      g.fresh_part.split_stride = (int64_t)M * z.H;
+      g.fresh_part.nsplit = w.split_down;
+      g.fresh_part.res = w.h1;
+      g.fresh_part.store = x_l;
+    }
     g.stable = w.stable;
     g.xc = w.xc;
     g.a = w.A;
@@ -1143,10 +1238,21 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.res_rows = dcand;
     c.tmap_w = &p->tm_o[l];
     c.tmap_x = &p->tx_att;
+    c.partial_out = w.split_o > 1 ? w.part : nullptr;
     AF_TIMED(FK_O, if ((st = gemm_run(c, s))) return st);
 
+    PartialRows pr_o;
+    memset(&pr_o, 0, sizeof(pr_o));
+    if (w.split_o > 1) {  // h1 = xc + O, finished from the O GEMM's partials
+      pr_o.part = w.part;
+      pr_o.split_stride = (int64_t)M * z.H;
+      pr_o.nsplit = w.split_o;
+      pr_o.res = w.xc;
+      pr_o.res_rows = dcand;
+      pr_o.store = w.h1;
+    }
     AF_TIMED(FK_NORM, AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, M, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm),
-                                       z.H, eps, nd, M, w.bn));
+                                       z.H, eps, nd, M, w.bn, pr_o));
     c = base_call(w.status);
     c.x = w.bn;
     c.ldx = z.H;
@@ -1177,6 +1283,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.ldr = z.H;
     c.tmap_w = &p->tm_down[l];
     c.tmap_x = &p->tx_f;
+    c.partial_out = w.split_down > 1 ? w.part : nullptr;  // finished by the next gate (or the final norm)
     AF_TIMED(FK_DOWN, if ((st = gemm_run(c, s))) return st);
     if (p->kv_keep)
       AF_TIMED(FK_SETUP, AF_LAUNCH(k_keep_rows, (unsigned)M, 256, 0, s, (const __nv_bfloat16*)w.qkv, z.qkv,
@@ -1207,8 +1314,18 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   int* nd_last = w.n_div + (L - 1);
   int* pos_last = w.div_pos + (int64_t)(L - 1) * M;
   const __nv_bfloat16* x_final = w.x_all + (int64_t)L * M * z.H;
+  PartialRows pr_f;
+  memset(&pr_f, 0, sizeof(pr_f));
+  if (w.split_down > 1) {  // the last layer's outputs, finished from its down GEMM's partials
+    pr_f.part = w.part;
+    pr_f.split_stride = (int64_t)M * z.H;
+    pr_f.nsplit = w.split_down;
+    pr_f.res = w.h1;
+    pr_f.store = const_cast<__nv_bfloat16*>(x_final);
+  }
   AF_TIMED(FK_NORM, AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, M, s, x_final,
-                                     static_cast<const __nv_bfloat16*>(p->model.final_norm), z.H, eps, nd_last, M, w.A));
+                                     static_cast<const __nv_bfloat16*>(p->model.final_norm), z.H, eps, nd_last, M, w.A,
+                                     pr_f));
   GemmCall c = base_call(w.status);
   c.x = w.A;
   c.ldx = z.H;

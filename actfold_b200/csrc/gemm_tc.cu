@@ -39,7 +39,7 @@ constexpr int kThreads = 192;
 constexpr int kMaxSplits = 8; // portable cluster size
 
 struct GemmDev {
-  int n, k, m_cap, ntok, n_tiles, nkb, kb_per_split, splits, stages;
+  int n, k, m_cap, ntok, n_tiles, m_tiles, nkb, kb_per_split, splits, stages;
   int w_tiled;  // 1: weights stored as contiguous 128 x 64 tiles (3-D descriptor)
   const int* m_dev;
   int epi;
@@ -58,6 +58,7 @@ struct GemmDev {
   int push;      // split-K partials pushed into the owners' shared memory (else pulled over DSMEM)
   int has_side;  // CTA (0, 0, 0) runs `side` (the layer compaction) in its epilogue warps
   CompactArgs side;
+  float* partial;  // split-K partials to global memory, reduced by the consumer (no cluster)
 };
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -198,8 +199,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
-  const int m0 = blockIdx.z * p.ntok;
-  const int n0 = blockIdx.x * kTileN;
+  // Grid x enumerates (weight tile, token tile) with the token tile fastest:
+  // the CTAs that stream the same weight tile for different token tiles are
+  // launched next to each other, so they run together and the second reads the
+  // tile from L2 instead of HBM.
+  const int mtile = blockIdx.x % p.m_tiles, wtile = blockIdx.x / p.m_tiles;
+  const int m0 = mtile * p.ntok;
+  const int n0 = wtile * kTileN;
   const int kb0 = blockIdx.y * p.kb_per_split;
   const int nkb = min(p.kb_per_split, p.nkb - kb0);
   const int S = p.stages;
@@ -221,11 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   int* s_rrow = s_orow + p.ntok;
   int* s_pos = s_rrow + p.ntok;
   int* s_scan = s_pos + p.ntok;  // 32 ints: the side task's scan buffer
-  const bool side_cta = p.has_side && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  const bool side_cta = p.has_side && blockIdx.x == 0 && blockIdx.y == 0;
 
   // Tiles start at different k-blocks (rotation by tile index) so concurrent CTAs
   // do not all read the same activation lines at the same time.
-  const int rot = blockIdx.x % nkb;
+  const int rot = wtile % nkb;
   auto kb_of = [&](int i) {
     int kb = i + rot;
     if (kb >= nkb) kb -= nkb;
@@ -233,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   };
   auto load_w = [&](int i, uint32_t dst, uint32_t bar) {
     if (p.w_tiled)
-      tma_load_3d(dst, &tmW, bar, 0, 0, blockIdx.x * p.nkb + kb_of(i));
+      tma_load_3d(dst, &tmW, bar, 0, 0, wtile * p.nkb + kb_of(i));
     else
       tma_load_2d(dst, &tmW, bar, kb_of(i) * kBlockK, n0);
   };
@@ -263,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
     for (int i = npre; i < min(nkb, 2 * S); ++i) {
       if (p.w_tiled)
-        tma_prefetch_l2_3d(&tmW, 0, 0, blockIdx.x * p.nkb + kb_of(i));
+        tma_prefetch_l2_3d(&tmW, 0, 0, wtile * p.nkb + kb_of(i));
       else
         tma_prefetch_l2_2d(&tmW, kb_of(i) * kBlockK, n0);
     }
@@ -271,10 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   pdl_wait();
   int M = p.m_dev ? *p.m_dev : p.m_cap;
   if (M > p.m_cap) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
     M = p.m_cap;
   }
-  if (m0 >= M) {  // uniform over a cluster (all its CTAs share blockIdx.x / z)
+  if (m0 >= M) {  // uniform over a cluster (all its CTAs share blockIdx.x)
     // No tokens for this tile (none at all for CTA (0, 0, 0)): the side task
     // still runs, with every thread of the CTA.
     if (side_cta) compact_rows<kThreads>(p.side, s_scan, threadIdx.x, 1);
@@ -394,7 +400,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   __syncthreads();
   const bool ok = !*abort_flag;
 
-  if (p.splits == 1) {
+  if (p.partial) {
+    // ---------------- split j's fp32 partial rows to global memory ----------------
+    // Row m of this tile: 128 features = 512 contiguous bytes, one warp-wide
+    // 16-byte store per lane; the consumer sums the splits.
+    if (ok) {
+      float* dst = p.partial + ((int64_t)blockIdx.y * p.m_cap + m0) * p.n + n0;
+      for (int idx = threadIdx.x; idx < Mv * 32; idx += kThreads) {
+        const int m = idx >> 5, c4 = idx & 31;
+        *reinterpret_cast<float4*>(dst + (int64_t)m * p.n + 4 * c4) =
+            *reinterpret_cast<const float4*>(tile + m * kLdt + 4 * c4);
+      }
+    }
+  } else if (p.splits == 1) {
     if (ok && p.epi == EPI_SWIGLU) {
       // ---------------- SwiGLU: one unit per (token, gate chunk), all threads ----------------
       const int total = Mv * 8;
@@ -651,6 +669,8 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   return g;
 }
 
+int gemm_splits(int n, int k, int m_cap) { return plan_shape(n, k, m_cap, 0, false).splits; }
+
 int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.x && c.w && c.out && c.status, "gemm: null pointer");
   AF_REQUIRE(c.n > 0 && c.n % kTileN == 0, "gemm: n must be a positive multiple of 128");
@@ -664,7 +684,10 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.epi != EPI_RESIDUAL || c.res, "gemm: residual epilogue needs res");
   AF_REQUIRE(c.epi != EPI_ROPE || (c.rope_cos && c.rope_sin && c.positions && c.head_dim == 128 && c.rope_cols % 128 == 0),
              "gemm: rope epilogue needs cos/sin/positions and head_dim 128");
-  const GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr);
+  GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr);
+  const bool partial = c.partial_out && g.splits > 1;
+  AF_REQUIRE(!partial || (reinterpret_cast<uintptr_t>(c.partial_out) & 15u) == 0, "gemm: partial_out must be 16-byte aligned");
+  if (partial) g.push = 0;  // no exchange between the splits: no receive slots in shared memory
   AF_REQUIRE(g.smem <= 227 * 1024, "gemm: shared memory budget exceeded");
 
   CUtensorMap tw, tx;
@@ -686,6 +709,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.m_cap = c.m_cap;
   d.ntok = g.ntok;
   d.n_tiles = g.n_tiles;
+  d.m_tiles = g.m_tiles;
   d.nkb = g.nkb;
   d.kb_per_split = g.kb_per;
   d.splits = g.splits;
@@ -709,13 +733,14 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.push = g.push;
   d.has_side = c.has_side;
   d.side = c.side;
+  d.partial = partial ? c.partial_out : nullptr;
 
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  cudaError_t e = launch_ex(k_gemm_tc, dim3(g.n_tiles, g.splits, g.m_tiles), dim3(kThreads, 1, 1), (size_t)g.smem, stream,
-                            c.pdl != 0, dim3(1, g.splits, 1), *pw, *px, d);
+  cudaError_t e = launch_ex(k_gemm_tc, dim3(g.n_tiles * g.m_tiles, g.splits, 1), dim3(kThreads, 1, 1), (size_t)g.smem, stream,
+                            c.pdl != 0, dim3(1, partial ? 1 : g.splits, 1), *pw, *px, d);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_tc launch: ") + cudaGetErrorString(e));
   return check_launch("gemm_tc");
 }

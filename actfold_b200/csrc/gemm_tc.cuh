@@ -44,7 +44,15 @@ struct GemmCall {
   // warps while its weight ring streams (the folded pass's QKV GEMM).
   int has_side;
   CompactArgs side;
+  // Split-K without a reduction in the GEMM (nullable): when the launch splits
+  // k, split j writes its fp32 partial rows to partial_out[j][m][0..n) (m <
+  // m_cap) and no epilogue runs; the next row kernel sums the splits in order
+  // 0, 1, ... and applies the epilogue (gemm_splits tells it how many).
+  float* partial_out;
 };
+
+// k-splits a launch of this shape uses (1: no split).
+int gemm_splits(int n, int k, int m_cap);
 
 // Token-tile width the kernel uses for a given row capacity.
 int gemm_ntok(int m_cap);

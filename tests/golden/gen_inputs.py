@@ -110,5 +110,5 @@ class AppendDraft:
         out = []
         for _ in range(num_branches):
             new = torch.from_numpy(rng.integers(0, self.id_hi, size=(parent.tokens.shape[0], max_new_tokens)))
-            out.append(types.SimpleNamespace(tokens=torch.cat([parent.tokens, new.to(parent.tokens.dtype)], dim=1)))
+            out.append(types.SimpleNamespace(tokens=torch.cat([parent.tokens, new.to(parent.tokens.device, parent.tokens.dtype)], dim=1)))
         return out
