@@ -79,6 +79,28 @@ def broadcast_parent_cache(pc: ParentCache, src: int = 0, group: dist.ProcessGro
     return pc
 
 
+def parent_cache_checksum(pc: ParentCache) -> torch.Tensor:
+    """Two int64 checksums per array of the cache (sum of its 32-bit words, and of every other word)."""
+    out = []
+    for t in pc.tensors():
+        b = t.contiguous().view(torch.uint8).reshape(-1)
+        pad = (-b.numel()) % 4
+        if pad:
+            b = torch.cat([b, b.new_zeros(pad)])
+        w = b.view(torch.int32)
+        out += [w.sum(dtype=torch.int64), w[::2].sum(dtype=torch.int64)]
+    return torch.stack(out)
+
+
+def check_parent_cache_agrees(pc: ParentCache, group: dist.ProcessGroup | None = None) -> None:
+    """Raise ValueError on every rank unless all ranks hold bit-identical parent caches (by checksum)."""
+    mine = parent_cache_checksum(pc)
+    allc = [torch.empty_like(mine) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(allc, mine, group=group)
+    if any(not torch.equal(c, allc[0]) for c in allc):
+        raise ValueError("parent cache differs between ranks after the broadcast")
+
+
 def gather_child_results(scores: torch.Tensor, div_count: torch.Tensor, group: dist.ProcessGroup | None = None
                          ) -> tuple[torch.Tensor, torch.Tensor]:
     """All-gather every rank's per-child scores [c_r] and divergent counts [L, c_r].

@@ -64,6 +64,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", choices=sorted(MODEL_DEFAULTS), default="llada8b")
     ap.add_argument("--children", type=int, default=None, help="children per GPU (model default)")
+    ap.add_argument("--global-children", type=int, default=None,
+                    help="strong scaling: this many children of one parent in total, split into contiguous shards "
+                         "over the ranks (default: --children per GPU, weak scaling)")
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--prompt", type=int, default=None, help="prompt ids (default: a quarter of --seq)")
     ap.add_argument("--d", type=int, default=None, help="unmasked positions per child (model default)")
@@ -83,25 +86,36 @@ def parse_args():
     return a
 
 
-def workload_tokens(a, dims, rank: int):
-    """Parent ids [T] and this rank's children [C, T] (seeded; shared by both arms).
+def workload_tokens(a, dims, rank: int, world: int = 1):
+    """Parent ids [T], this rank's children [c, T] and the global index of its first child (seeded; both arms).
 
     LLaDA-8B: a prompt of uniform ids, then generation positions of which
     ``mask_fraction`` hold the mask id; each child unmasks ``d`` of them.
     Dream-7B: each child differs from the parent at ``d`` uniformly chosen positions.
+    Weak scaling (default): every rank draws its own ``--children`` children.
+    Strong scaling (``--global-children C``): the C children are drawn once and
+    rank r verifies its contiguous shard of them.
     """
     from actfold_b200 import workloads as W
+    from actfold_b200.sharding import shard_children
 
     parent, _ = W.llada_tokens(a.seq, a.prompt, MODEL_DEFAULTS[a.model]["mask_fraction"], 1, 1, dims.mask_id, seed=42)
+    n, seed = (a.global_children, 1000) if a.global_children else (a.children, 1000 + rank)
     if a.model == "dream7b":
-        children = W.uniform_edit_children(parent, a.children, a.d, dims.mask_id, seed=1000 + rank)
+        children = W.uniform_edit_children(parent, n, a.d, dims.mask_id, seed=seed)
     else:
-        children = W.llada_children(parent, a.children, a.d, dims.mask_id, seed=1000 + rank)
-    return parent, children
+        children = W.llada_children(parent, n, a.d, dims.mask_id, seed=seed)
+    if not a.global_children:
+        return parent, children, rank * a.children
+    start, count = shard_children(a.global_children, rank, world)
+    return parent, children[start:start + count], start
 
 
 def workload_name(a) -> str:
     arch = "LLaDA-8B" if a.model == "llada8b" else "Dream-7B"
+    if a.global_children:
+        return (f"{arch} arch folded verification, {a.global_children} children x {a.seq} tokens in total, split over "
+                f"the GPUs, d={a.d}, tau={a.tau}")
     return f"{arch} arch folded verification, {a.children} children x {a.seq} tokens per GPU, d={a.d}, tau={a.tau}"
 
 
@@ -118,14 +132,15 @@ def config_dict(a, n):
     return {
         "workload": workload_name(a),
         "model": model_desc(a),
-        "children_per_gpu": a.children,
-        "global_children": a.children * n,
+        "children_per_gpu": -(-a.global_children // n) if a.global_children else a.children,
+        "global_children": a.global_children or a.children * n,
         "seq_len": a.seq,
         "prompt": a.prompt,
         "mask_fraction": MODEL_DEFAULTS[a.model]["mask_fraction"],
         "d_unmasked_per_child": a.d,
         "tau": a.tau,
         "parallelism": "children sharded across ranks, parent cache NCCL-broadcast once" if n > 1 else "single GPU",
+        "scaling": "strong" if a.global_children else "weak",
         "launch": "eager kernel launches" if a.eager else "CUDA graph replay of the pass",
         "l2": f"inputs larger than L2: {weight_gb(a):.1f} GB of weights streamed every step",
     }
@@ -243,12 +258,12 @@ def run_reference(a, rank: int) -> None:
     from oracle.reference_cpu import ReferenceCpuPath
 
     dims = reference_dims(a)
-    parent, children = workload_tokens(a, dims, 0)
+    parent, children, _ = workload_tokens(a, dims, 0)
     path = ReferenceCpuPath(dims, a.seq, a.tau)
     path.parent_pass(parent)
     for i in range(a.warmup):
-        path.time_child(children[i % a.children])
-    times = [path.time_child(children[i % a.children]) for i in range(a.steps)]
+        path.time_child(children[i % len(children)])
+    times = [path.time_child(children[i % len(children)]) for i in range(a.steps)]
     sec = sum(times) / len(times)
     value = a.seq / sec
     line = {
@@ -268,9 +283,10 @@ def run_reference(a, rank: int) -> None:
         "config": config_dict(a, 1),
         "step": "one child verified completely (all layers + full logits) through the reference's path",
         "children_verified": a.steps,
-        "pass_equivalents": a.steps / a.children,
+        "pass_equivalents": a.steps / (a.global_children or a.children),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": path.threads, "kind": "port",
-                         "sample": reference_sample(path, a.children, dims.n_layers, dims.vocab, a.seq, a.steps, a.warmup)},
+                         "sample": reference_sample(path, a.global_children or a.children, dims.n_layers, dims.vocab,
+                                                    a.seq, a.steps, a.warmup)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -289,7 +305,7 @@ def cpu_baseline_leg(a, dims, parent, children) -> dict:
         "unit": UNIT,
         "cores": path.threads,
         "kind": "port",
-        "sample": reference_sample(path, a.children, dims.n_layers, dims.vocab, a.seq, 1, 1),
+        "sample": reference_sample(path, a.global_children or a.children, dims.n_layers, dims.vocab, a.seq, 1, 1),
     }
 
 
@@ -422,7 +438,11 @@ def main() -> None:
     base = base_dims(a)
     dims = base if a.layers is None else W.ModelDims(a.layers, base.hidden, base.n_heads, base.n_kv_heads, base.head_dim, base.ffn, base.vocab, base.rms_eps, base.rope_theta, base.mask_id)
     model = LLaDAModel.random(dims, seed=1234, device=dev, max_pos=max(a.seq, 1024))
-    parent_np, children_np = workload_tokens(a, dims, rank)
+    parent_np, children_np, first_child = workload_tokens(a, dims, rank, world)
+    n_local = children_np.shape[0]
+    n_total = a.global_children or a.children * world
+    if n_local == 0:
+        raise SystemExit(f"--global-children {a.global_children} leaves rank {rank} of {world} without children")
 
     # ---- parent pass (rank 0) + broadcast of the parent cache
     torch.cuda.synchronize()
@@ -453,6 +473,10 @@ def main() -> None:
         e1.record()
         torch.cuda.synchronize()
         bcast_ms = e0.elapsed_time(e1)
+        # Every rank must hold the same parent cache: compare per-array checksums (raises on every rank).
+        from actfold_b200.sharding import check_parent_cache_agrees
+
+        check_parent_cache_agrees(pc)
 
     gate = SimilarityGate(a.tau)
     engine = ActFoldVerificationEngine(model, gate=gate, use_graphs=not a.eager)
@@ -460,10 +484,10 @@ def main() -> None:
     engine.set_parent_cache(pbranch, pc)
     host_children = torch.from_numpy(children_np).pin_memory()
     ct = host_children.to(dev)
-    m_cap, child_cap = engine._m_cap(host_children, pc, a.children, a.seq)
-    logits = torch.empty((a.children, a.seq, dims.vocab), dtype=torch.bfloat16, device=dev)
-    scores = torch.empty((a.children,), dtype=torch.float32, device=dev)
-    plan = model.plan(pc, a.children, m_cap, a.tau)
+    m_cap, child_cap = engine._m_cap(host_children, pc, n_local, a.seq)
+    logits = torch.empty((n_local, a.seq, dims.vocab), dtype=torch.bfloat16, device=dev)
+    scores = torch.empty((n_local,), dtype=torch.float32, device=dev)
+    plan = model.plan(pc, n_local, m_cap, a.tau)
     plan.set_child_cap(child_cap)
     _, plan = model.verify(ct, pc, a.tau, logits=logits, scores=scores, m_cap=m_cap)
     torch.cuda.synchronize()
@@ -503,7 +527,7 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     step_ms_max = float(t_max.item())
-    value = a.children * world * a.seq / (step_ms_max / 1e3)
+    value = n_total * a.seq / (step_ms_max / 1e3)
 
     # ---- per-kernel-class device times (same stream, same workload)
     plan.set_timing(True)  # events around every launch class: always the eager launch sequence
@@ -568,9 +592,17 @@ def main() -> None:
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = a.children * world * a.seq / (float(e2e_ms.item()) / 1e3)
+    e2e_value = n_total * a.seq / (float(e2e_ms.item()) / 1e3)
     h2d = host_children.numel() * host_children.element_size()
-    d2h = a.children * 4 + L * a.children * 4 + 4
+    d2h = n_local * 4 + L * n_local * 4 + 4
+    # Per-child results in global child order on every rank (NCCL all-gather of the shards' scores and counts).
+    if world > 1:
+        from actfold_b200.sharding import gather_child_results
+
+        s_all, d_all = gather_child_results(torch.from_numpy(res["scores"]).to(dev),
+                                            torch.from_numpy(res["div_count"]).to(dev))
+        if s_all.shape[0] != n_total or d_all.shape != (L, n_total):
+            raise RuntimeError(f"gathered {tuple(d_all.shape)} results for {n_total} children")
 
     # ---- CPU baseline (rank 0, single GPU runs only)
     cpu = None
@@ -587,7 +619,7 @@ def main() -> None:
             "warmup": a.warmup,
             "ms_per_step": step_ms_max,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if a.global_children else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,0.02) weights drawn on the GPU, seeded token ids",
@@ -603,6 +635,8 @@ def main() -> None:
             "parent_pass_first_ms": parent_first_ms,
             "parent_broadcast_ms": bcast_ms,
             "parent_broadcast_bytes": sum(t.numel() * t.element_size() for t in pc.tensors()),
+            # The same throughput with one parent pass and one broadcast charged to every step.
+            "value_with_parent_pass": n_total * a.seq / ((step_ms_max + parent_ms + bcast_ms) / 1e3),
             "stable_ratio_mean": float(np.mean(res["stable_ratio"])),
         }
         print(json.dumps(line), flush=True)

@@ -19,7 +19,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from actfold_b200 import workloads as W
-from actfold_b200.sharding import broadcast_parent_cache, empty_parent_cache, gather_child_results, shard_children
+from actfold_b200.sharding import (broadcast_parent_cache, check_parent_cache_agrees, empty_parent_cache,
+                                   gather_child_results, shard_children)
 
 
 def _free_port() -> int:
@@ -47,6 +48,7 @@ def _worker(rank, world, port, scenario, q):
         if scenario == "broadcast":
             pc = _filled_cache(dims, T, tau, 7) if rank == 0 else empty_parent_cache(dims, T, tau, "cpu")
             broadcast_parent_cache(pc, src=0)
+            check_parent_cache_agrees(pc)
             ref = _filled_cache(dims, T, tau, 7)
             for a, b in zip(pc.tensors(), ref.tensors()):
                 assert a.dtype == b.dtype and a.shape == b.shape
@@ -69,6 +71,13 @@ def _worker(rank, world, port, scenario, q):
             assert torch.equal(s_all, torch.arange(C, dtype=torch.float32))
             assert torch.equal(d_all, torch.stack([torch.arange(C, dtype=torch.int32) + 100 * l for l in range(L)]))
             q.put((rank, "ok"))
+        elif scenario == "diverged":
+            pc = _filled_cache(dims, T, tau, 7 + rank)  # different caches on the two ranks
+            try:
+                check_parent_cache_agrees(pc)
+                q.put((rank, "no error"))
+            except ValueError:
+                q.put((rank, "raised"))
         elif scenario == "gather_bad":
             L = dims.n_layers
             scores = torch.zeros(4)
@@ -134,6 +143,11 @@ def test_gather_child_results_unequal_shards():
     # 8 children on 3 ranks: shards of 3, 3 and 2 children.
     out = _run("gather", world=3)
     assert out == {0: "ok", 1: "ok", 2: "ok"}, out
+
+
+def test_diverged_parent_caches_are_detected_on_every_rank():
+    out = _run("diverged")
+    assert out == {0: "raised", 1: "raised"}, out
 
 
 def test_gather_child_results_bad_shapes_raise_on_every_rank():
