@@ -16,7 +16,7 @@ import torch
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libactfold_b200.so")
 
-AF_OK, AF_ERR_ARG, AF_ERR_CAPACITY, AF_ERR_DEVICE, AF_ERR_TIMEOUT, AF_ERR_CUDA = range(6)
+AF_OK, AF_ERR_ARG, AF_ERR_CAPACITY, AF_ERR_DEVICE, AF_ERR_TIMEOUT, AF_ERR_CUDA, AF_ERR_COMM = range(7)
 DTYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 METRIC = {"cosine": 0, "l2": 1, "pearson": 2}
 

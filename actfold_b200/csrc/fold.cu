@@ -838,9 +838,10 @@ struct FoldWs {
   // k-splits), finished by the next row kernel; null when neither splits.
   float* part;
   int split_o, split_down;
+  int part_o, part_down;  // 1: that GEMM leaves its partials in `part`
 };
 
-static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
+static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool partial_always) {
   FoldWs w;
   const int L = z.L;
   w.bits_ld = (T + 31) / 32;
@@ -873,8 +874,10 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap) {
   w.split_o = gemm_splits(z.H, z.q, m_cap);
   w.split_down = gemm_splits(z.H, z.FF, m_cap);
   const int S = std::max(w.split_o, w.split_down);
-  w.part = (S > 1 && S <= 4 && !partials_off()) ? b.take<float>((int64_t)S * m_cap * z.H) : nullptr;
-  if (!w.part) w.split_o = w.split_down = 1;
+  const bool use = S <= 4 && (partial_always || (S > 1 && !partials_off()));
+  w.part = use ? b.take<float>((int64_t)S * m_cap * z.H) : nullptr;
+  w.part_o = use && (partial_always || w.split_o > 1);
+  w.part_down = use && (partial_always || w.split_down > 1);
   return w;
 }
 
@@ -970,6 +973,12 @@ struct FoldPlan {
   __nv_bfloat16* kv_keep = nullptr;
   // Bound on any child's candidate rows per layer (af_fold_set_child_cap); 0: none.
   int child_cap = 0;
+  // Tensor-parallel shard (af_fold_set_tensor_parallel): cross-rank sums, the
+  // full embedding's rows, the whole vocabulary.
+  bool partial_always = false;
+  af_collective_fn coll = nullptr;
+  void* coll_user = nullptr;
+  int64_t embed_rows = 0, vocab_total = 0;
   ~FoldPlan() {
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
@@ -1008,6 +1017,15 @@ static void launch_fold_gate(const FoldGateArgs& g, int H, int rows, cudaStream_
   else AF_LAUNCH((k_fold_gate<METRIC, 2>), (unsigned)rows, kRowThreads, 0, s, g);
 }
 
+// A cross-rank sum of a tensor-parallel pass, handed to the caller's hook on the pass stream.
+static int collective(FoldPlan* p, int kind, int layer, void* data, int64_t count, cudaStream_t s) {
+  ++p->tk.launches;
+  const int rc = p->coll(p->coll_user, kind, layer, data, count, static_cast<void*>(s));
+  if (rc) return fail(AF_ERR_COMM, "af_fold_run: the collective hook failed (kind " + std::to_string(kind) + ", layer " +
+                                       std::to_string(layer) + ", code " + std::to_string(rc) + ")");
+  return AF_OK;
+}
+
 static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, float* scores, cudaStream_t s) {
   const Sizes z = sizes_of(p->model.dims);
   const FoldWs& w = p->w;
@@ -1040,7 +1058,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   ca.n_fresh0 = w.n_fresh0;
   ca.status = w.status;
   AF_TIMED(FK_SETUP, AF_LAUNCH(k_fold_candidates, 1, 1024, 0, s, ca));
-  AF_TIMED(FK_SETUP, AF_LAUNCH(k_embed_rows, mblocks, 256, 0, s, static_cast<const __nv_bfloat16*>(p->model.embed), z.H, z.V,
+  AF_TIMED(FK_SETUP, AF_LAUNCH(k_embed_rows, mblocks, 256, 0, s, static_cast<const __nv_bfloat16*>(p->model.embed), z.H,
+                               p->embed_rows ? p->embed_rows : (int64_t)z.V,
                                                            ctok, w.fresh0_pos, w.n_fresh0, M, w.x_all, w.status));
 
   // Logits fill on the side stream (not in the per-class timing mode, which
@@ -1091,7 +1110,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     g.k = make_gate_consts(AF_DTYPE_BF16, p->taus[l], 1e-8f, hn);
     g.force_div = p->folds[l] ? 0 : 1;
     memset(&g.fresh_part, 0, sizeof(g.fresh_part));
-    if (l > 0 && w.split_down > 1) {
+    if (l > 0 && w.part_down) {
       // Layer l's fresh rows are the previous down GEMM's outputs, left as
       // split-K partials: finish them here (residual = that layer's h1).
       g.fresh_part.part = w.part;
@@ -1238,12 +1257,13 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.res_rows = dcand;
     c.tmap_w = &p->tm_o[l];
     c.tmap_x = &p->tx_att;
-    c.partial_out = w.split_o > 1 ? w.part : nullptr;
+    c.partial_out = w.part_o ? w.part : nullptr;
     AF_TIMED(FK_O, if ((st = gemm_run(c, s))) return st);
+    if (p->coll && (st = collective(p, AF_COLL_O, l, w.part, (int64_t)w.split_o * M * z.H, s))) return st;
 
     PartialRows pr_o;
     memset(&pr_o, 0, sizeof(pr_o));
-    if (w.split_o > 1) {  // h1 = xc + O, finished from the O GEMM's partials
+    if (w.part_o) {  // h1 = xc + O, finished from the O GEMM's partials
       pr_o.part = w.part;
       pr_o.split_stride = (int64_t)M * z.H;
       pr_o.nsplit = w.split_o;
@@ -1283,8 +1303,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.ldr = z.H;
     c.tmap_w = &p->tm_down[l];
     c.tmap_x = &p->tx_f;
-    c.partial_out = w.split_down > 1 ? w.part : nullptr;  // finished by the next gate (or the final norm)
+    c.partial_out = w.part_down ? w.part : nullptr;  // finished by the next gate (or the final norm)
     AF_TIMED(FK_DOWN, if ((st = gemm_run(c, s))) return st);
+    if (p->coll && (st = collective(p, AF_COLL_DOWN, l, w.part, (int64_t)w.split_down * M * z.H, s))) return st;
     if (p->kv_keep)
       AF_TIMED(FK_SETUP, AF_LAUNCH(k_keep_rows, (unsigned)M, 256, 0, s, (const __nv_bfloat16*)w.qkv, z.qkv,
                                    (const int*)nc, M, p->kv_keep + (int64_t)l * M * z.qkv));
@@ -1316,7 +1337,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   const __nv_bfloat16* x_final = w.x_all + (int64_t)L * M * z.H;
   PartialRows pr_f;
   memset(&pr_f, 0, sizeof(pr_f));
-  if (w.split_down > 1) {  // the last layer's outputs, finished from its down GEMM's partials
+  if (w.part_down) {  // the last layer's outputs, finished from its down GEMM's partials
     pr_f.part = w.part;
     pr_f.split_stride = (int64_t)M * z.H;
     pr_f.nsplit = w.split_down;
@@ -1342,6 +1363,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   c.tmap_w = &p->tm_lm;
   c.tmap_x = &p->tx_A;
   AF_TIMED(FK_LM, if ((st = gemm_run(c, s))) return st);
+  if (p->coll && (st = collective(p, AF_COLL_ROWSUM, L - 1, w.row_sums, (int64_t)C * T, s))) return st;
   if (fork_fill) {
     if (cudaStreamWaitEvent(s, p->ev_join, 0) != cudaSuccess) return check_launch("af_fold_run: join");
   } else {
@@ -1350,7 +1372,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   }
   if (scores)
     AF_TIMED(FK_SCORES, AF_LAUNCH(k_scores, C, 256, 0, s, (const float*)p->parent.logit_row_sums,
-                                  (const float*)w.row_sums, C, T, (int64_t)z.V, (const unsigned*)w.final_bits,
+                                  (const float*)w.row_sums, C, T, p->vocab_total ? p->vocab_total : (int64_t)z.V,
+                                  (const unsigned*)w.final_bits,
                                   w.bits_ld, scores));
   p->last_launches = p->tk.launches;
   return check_launch("af_fold_run");
@@ -1362,7 +1385,7 @@ extern "C" int af_fold_workspace_bytes(const af_model_dims* d, const af_fold_con
   AF_REQUIRE(d && cfg && bytes, "af_fold_workspace_bytes: null pointer");
   AF_REQUIRE(cfg->n_children > 0 && cfg->seq > 0 && cfg->m_cap > 0, "af_fold_workspace_bytes: bad sizes");
   Bump b(nullptr, 0);
-  carve_fold(b, sizes_of(*d), (int)cfg->n_children, (int)cfg->seq, (int)cfg->m_cap);
+  carve_fold(b, sizes_of(*d), (int)cfg->n_children, (int)cfg->seq, (int)cfg->m_cap, cfg->partial_always != 0);
   *bytes = b.off + 256;
   return AF_OK;
 }
@@ -1404,7 +1427,12 @@ extern "C" int af_fold_plan_create(const af_model* m, const af_parent_cache* par
       return fail(AF_ERR_ARG, "af_fold_plan_create: a layer that does not fold needs m_cap >= n_children * seq");
     }
   Bump b(workspace, workspace_bytes);
-  p->w = carve_fold(b, sizes_of(m->dims), p->C, p->T, p->m_cap);
+  p->w = carve_fold(b, sizes_of(m->dims), p->C, p->T, p->m_cap, cfg->partial_always != 0);
+  if (cfg->partial_always && !p->w.part) {
+    delete p;
+    return fail(AF_ERR_ARG, "af_fold_plan_create: partial_always needs at most 4 k-splits in the O / down projections");
+  }
+  p->partial_always = cfg->partial_always != 0;
   if (b.off > workspace_bytes) {
     delete p;
     return fail(AF_ERR_ARG, "af_fold_plan_create: workspace too small");
@@ -1459,6 +1487,19 @@ extern "C" int af_fold_set_child_cap(void* plan, int64_t max_candidates_per_chil
   AF_REQUIRE(max_candidates_per_child >= 0 && max_candidates_per_child <= (1 << 24),
              "af_fold_set_child_cap: bound out of range");
   static_cast<FoldPlan*>(plan)->child_cap = (int)max_candidates_per_child;
+  return AF_OK;
+}
+
+extern "C" int af_fold_set_tensor_parallel(void* plan, int64_t embed_rows, int64_t vocab_total,
+                                           af_collective_fn collective, void* user) {
+  AF_REQUIRE(plan && collective, "af_fold_set_tensor_parallel: null pointer");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  AF_REQUIRE(p->partial_always, "af_fold_set_tensor_parallel: the plan must be created with partial_always = 1");
+  AF_REQUIRE(embed_rows > 0 && vocab_total >= p->model.dims.vocab, "af_fold_set_tensor_parallel: bad vocabulary sizes");
+  p->coll = collective;
+  p->coll_user = user;
+  p->embed_rows = embed_rows;
+  p->vocab_total = vocab_total;
   return AF_OK;
 }
 

@@ -685,7 +685,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.epi != EPI_ROPE || (c.rope_cos && c.rope_sin && c.positions && c.head_dim == 128 && c.rope_cols % 128 == 0),
              "gemm: rope epilogue needs cos/sin/positions and head_dim 128");
   GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr);
-  const bool partial = c.partial_out && g.splits > 1;
+  const bool partial = c.partial_out != nullptr;  // the caller asks for partials (also with one split)
   AF_REQUIRE(!partial || (reinterpret_cast<uintptr_t>(c.partial_out) & 15u) == 0, "gemm: partial_out must be 16-byte aligned");
   if (partial) g.push = 0;  // no exchange between the splits: no receive slots in shared memory
   AF_REQUIRE(g.smem <= 227 * 1024, "gemm: shared memory budget exceeded");

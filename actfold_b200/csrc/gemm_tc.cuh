@@ -44,10 +44,10 @@ struct GemmCall {
   // warps while its weight ring streams (the folded pass's QKV GEMM).
   int has_side;
   CompactArgs side;
-  // Split-K without a reduction in the GEMM (nullable): when the launch splits
-  // k, split j writes its fp32 partial rows to partial_out[j][m][0..n) (m <
-  // m_cap) and no epilogue runs; the next row kernel sums the splits in order
-  // 0, 1, ... and applies the epilogue (gemm_splits tells it how many).
+  // GEMM without a reduction or epilogue (nullable): split j of the k-range
+  // writes its fp32 partial rows to partial_out[j][m][0..n) (m < m_cap); the
+  // next row kernel sums the splits in order 0, 1, ... and applies the
+  // epilogue (gemm_splits tells it how many; one split is allowed).
   float* partial_out;
 };
 

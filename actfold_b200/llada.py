@@ -61,7 +61,11 @@ class _Parent(C.Structure):
 
 class _FoldConfig(C.Structure):
     _fields_ = [("n_children", _i64), ("seq", _i64), ("m_cap", _i64), ("tau", _f32), ("metric", _i32), ("su_layers", _vp),
-                ("tau_layers", _vp), ("fold_layers", _vp), ("self_stable", _vp)]
+                ("tau_layers", _vp), ("fold_layers", _vp), ("self_stable", _vp), ("partial_always", _i32)]
+
+
+# int (*)(void* user, int32 kind, int32 layer, void* data, int64 count, void* stream): a cross-rank sum
+COLLECTIVE_FN = C.CFUNCTYPE(_i32, _vp, _i32, _i32, _vp, _i64, _vp)
 
 
 class _FoldOutputs(C.Structure):
@@ -87,6 +91,7 @@ _lib.SIGNATURES.update(
         "af_fold_plan_destroy": (_i32, [_vp]),
         "af_fold_set_timing": (_i32, [_vp, _i32]),
         "af_fold_get_timing": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32, C.POINTER(_i64)]),
+        "af_fold_set_tensor_parallel": (_i32, [_vp, _i64, _i64, COLLECTIVE_FN, _vp]),
     }
 )
 
@@ -99,7 +104,7 @@ def _bind_late() -> C.CDLL:
     for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
                  "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy",
                  "af_fold_keep_kv", "af_fold_promote", "af_fold_set_child_cap",
-                 "af_fold_set_timing", "af_fold_get_timing"):
+                 "af_fold_set_timing", "af_fold_get_timing", "af_fold_set_tensor_parallel"):
         fn = getattr(lib, name)
         fn.restype, fn.argtypes = _lib.SIGNATURES[name]
     return lib
@@ -128,14 +133,18 @@ class LLaDABlock(nn.Module):
     the logical [n, k] of each.
     """
 
-    def __init__(self, attn_norm, w_qkv, w_o, ffn_norm, w_gateup, w_down) -> None:
+    def __init__(self, attn_norm, w_qkv, w_o, ffn_norm, w_gateup, w_down, tiled: bool = False) -> None:
         super().__init__()
         self.register_buffer("attn_norm", attn_norm.contiguous())
         self.register_buffer("ffn_norm", ffn_norm.contiguous())
         self.shapes = {}
         for k, v in dict(w_qkv=w_qkv, w_o=w_o, w_gateup=w_gateup, w_down=w_down).items():
-            self.shapes[k] = tuple(v.shape)
-            self.register_buffer(k, tile_weight(v))
+            if tiled:  # already [n/128, k/64, 128, 64]
+                self.shapes[k] = (v.shape[0] * 128, v.shape[1] * 64)
+                self.register_buffer(k, v.contiguous())
+            else:
+                self.shapes[k] = tuple(v.shape)
+                self.register_buffer(k, tile_weight(v))
 
     def forward(self, hidden_states: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
         raise RuntimeError("LLaDABlock runs inside the native folded pass; call LLaDAModel or FoldedModel instead")
@@ -259,7 +268,7 @@ class FoldPlan:
     """
 
     def __init__(self, model: "LLaDAModel", parent: ParentCache, n_children: int, m_cap: int, tau: float,
-                 metric: str = "cosine", layer_taus=None, layer_folds=None) -> None:
+                 metric: str = "cosine", layer_taus=None, layer_folds=None, partial_always: bool = False) -> None:
         self.lib = _bind_late()
         self.model = model
         self.parent = parent
@@ -278,7 +287,8 @@ class FoldPlan:
         self._taus = np.ascontiguousarray(np.array(self.layer_taus, np.float32))
         self._folds = np.ascontiguousarray(np.array(self.layer_folds, np.uint8))
         self._cfg = _FoldConfig(n_children, self.T, m_cap, float(tau), _lib.METRIC[metric], self._su.ctypes.data,
-                                self._taus.ctypes.data, self._folds.ctypes.data, self.self_stable.data_ptr())
+                                self._taus.ctypes.data, self._folds.ctypes.data, self.self_stable.data_ptr(),
+                                1 if partial_always else 0)
         nbytes = _i64()
         _lib.check(self.lib.af_fold_workspace_bytes(C.byref(model._cmodel.dims), C.byref(self._cfg), C.byref(nbytes)))
         self.workspace = torch.zeros(int(nbytes.value), dtype=torch.uint8, device=model.device)
@@ -304,6 +314,34 @@ class FoldPlan:
         self.status = view(out.status, 1, torch.int32)
         self.n_fresh0 = view(out.n_fresh0, 1, torch.int32)
 
+    def set_tensor_parallel(self, embed_rows: int, vocab_total: int, collective) -> None:
+        """Make this plan one rank's shard of a tensor-parallel pass (see actfold_b200.tensor_parallel).
+
+        ``collective(kind, layer, tensor)`` must sum the fp32 ``tensor`` (a view
+        of this plan's workspace) over the ranks in place, on the current stream.
+        """
+        def hook(user, kind, layer, data, count, stream):
+            try:
+                collective(int(kind), int(layer), self.workspace_view(data, int(count), torch.float32))
+                return 0
+            except Exception as exc:  # reported through the C status; the message is kept for the caller
+                self.collective_error = exc
+                return 1
+
+        self._hook = COLLECTIVE_FN(hook)  # kept alive as long as the plan
+        _lib.check(self.lib.af_fold_set_tensor_parallel(self._plan, int(embed_rows), int(vocab_total), self._hook, None),
+                   "af_fold_set_tensor_parallel")
+
+    collective_error = None
+
+    def workspace_view(self, ptr: int, n: int, dtype: torch.dtype) -> torch.Tensor:
+        """``n`` elements of ``dtype`` at device address ``ptr`` inside this plan's workspace."""
+        off = int(ptr) - self.workspace.data_ptr()
+        size = n * torch.empty((), dtype=dtype).element_size()
+        if off < 0 or off + size > self.workspace.numel():
+            raise ValueError("workspace_view: address outside the plan's workspace")
+        return self.workspace[off: off + size].view(dtype)
+
     def parent_rewritten(self) -> bool:
         """After an in-place rewrite of the parent (a promotion): refresh the plan's self-gate rows.
 
@@ -323,6 +361,9 @@ class FoldPlan:
             raise ValueError(f"child_tokens must be contiguous int64 [{self.C}, {self.T}]")
         st = self.lib.af_fold_run(self._plan, child_tokens.data_ptr(), logits.data_ptr(), _lib.ptr(scores),
                                   _lib.stream_ptr(child_tokens.device))
+        if st == _lib.AF_ERR_COMM and self.collective_error is not None:
+            err, self.collective_error = self.collective_error, None
+            raise err
         _lib.check(st, "af_fold_run")
         self.serial += 1
         self.last_run = (child_tokens, logits)
@@ -457,13 +498,14 @@ class FoldPlan:
 class LLaDAModel(nn.Module):
     """LLaDA/Dream-architecture weights + native dense and folded passes (CUDA only)."""
 
-    def __init__(self, dims: ModelDims, embed, layers: Sequence[LLaDABlock], final_norm, lm_head, max_pos: int = 4096) -> None:
+    def __init__(self, dims: ModelDims, embed, layers: Sequence[LLaDABlock], final_norm, lm_head, max_pos: int = 4096,
+                 lm_head_tiled: bool = False) -> None:
         super().__init__()
         self.dims = dims
         self.register_buffer("embed", embed.contiguous())
         self.layers = nn.ModuleList(layers)
         self.register_buffer("final_norm", final_norm.contiguous())
-        self.register_buffer("lm_head", tile_weight(lm_head))
+        self.register_buffer("lm_head", lm_head.contiguous() if lm_head_tiled else tile_weight(lm_head))
         cos, sin = rope_tables(max_pos, dims.head_dim, dims.rope_theta, embed.device)
         self.register_buffer("rope_cos", cos)
         self.register_buffer("rope_sin", sin)

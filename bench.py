@@ -72,6 +72,9 @@ def parse_args():
     ap.add_argument("--d", type=int, default=None, help="unmasked positions per child (model default)")
     ap.add_argument("--tau", type=float, default=0.95)
     ap.add_argument("--layers", type=int, default=None, help="override layer count (small profiling captures only)")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor parallel: every rank verifies the same children (--global-children, default "
+                         "--children) with its slice of the weights; cross-rank sums over NCCL inside the pass")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch the pass kernel by kernel instead of replaying its CUDA graph")
     ap.add_argument("--block-decoding", action="store_true",
@@ -404,6 +407,101 @@ def run_block_decoding(a) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_tensor_parallel(a, rank: int, world: int, local_rank: int) -> None:
+    """One child batch verified by all ranks together, each with its slice of the weights (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from actfold_b200 import workloads as W
+    from actfold_b200.llada import LLaDAModel
+    from actfold_b200.tensor_parallel import TensorParallelVerifier
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    else:  # one rank: the cross-rank sums are the identity; the group only serves the barriers
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    base = base_dims(a)
+    dims = base if a.layers is None else W.ModelDims(a.layers, base.hidden, base.n_heads, base.n_kv_heads, base.head_dim,
+                                                     base.ffn, base.vocab, base.rms_eps, base.rope_theta, base.mask_id)
+    C = a.global_children or a.children
+    a.global_children = C
+    model = LLaDAModel.random(dims, seed=1234, device=dev, max_pos=max(a.seq, 1024))
+    parent_np, children_np, _ = workload_tokens(a, dims, 0, 1)  # every rank verifies all C children
+    t0 = time.perf_counter()
+    pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)  # whole weights on every rank: no broadcast
+    torch.cuda.synchronize()
+    parent_ms = (time.perf_counter() - t0) * 1e3
+    tp = TensorParallelVerifier(model)
+    pcl = tp.shard_parent(pc)
+    ct = torch.from_numpy(children_np).to(dev)
+    scores = torch.empty((C,), dtype=torch.float32, device=dev)
+    logits, plan = tp.verify(ct, pcl, a.tau, scores=scores)
+    torch.cuda.synchronize()
+    plan.check_status()
+    graph = plan.capture(ct, logits, scores) if not a.eager else None
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            plan.run(ct, logits, scores)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = sampler.stop()
+    plan.check_status()
+    t_max = torch.tensor([ev0.elapsed_time(ev1) / a.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    if rank == 0:
+        per_run = plan.get_timing()[2]
+        line = {
+            "metric": metric_of(a),
+            "value": C * a.seq / (ms / 1e3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": a.steps,
+            "warmup": a.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: seeded N(0,0.02) weights drawn on the GPU, seeded token ids",
+            "config": dict(config_dict(a, world), parallelism=f"tensor parallel over {world} GPUs (heads, FFN and "
+                                                             f"vocabulary split; NCCL all-reduce after O and down)"),
+            "gpu_launches": int(per_run * a.steps),
+            "clocks": clocks,
+            "parent_pass_ms": parent_ms,
+            "stable_ratio_mean": float(1.0 - plan.div_count.float().mean().item() / a.seq),
+            "scores_head": [float(x) for x in scores[:4].cpu()],
+        }
+        print(json.dumps(line), flush=True)
+    graph = None  # a graph holding NCCL calls is released before the process group
+    del plan, tp
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -414,6 +512,9 @@ def main() -> None:
         return
     if a.block_decoding:
         run_block_decoding(a)
+        return
+    if a.tp:
+        run_tensor_parallel(a, rank, world, local_rank)
         return
 
     import numpy as np

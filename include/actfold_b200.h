@@ -31,7 +31,8 @@ typedef enum {
   AF_ERR_CAPACITY = 2, /* a size exceeds a buffer capacity                    */
   AF_ERR_DEVICE = 3,   /* a device-side check failed (status word set)       */
   AF_ERR_TIMEOUT = 4,  /* a bounded device wait ran out                       */
-  AF_ERR_CUDA = 5      /* a CUDA runtime call failed                          */
+  AF_ERR_CUDA = 5,     /* a CUDA runtime call failed                          */
+  AF_ERR_COMM = 6      /* a cross-rank collective (caller hook) failed        */
 } af_status;
 
 typedef enum { AF_DTYPE_F32 = 0, AF_DTYPE_F16 = 1, AF_DTYPE_BF16 = 2 } af_dtype;
@@ -278,6 +279,10 @@ typedef struct {
   const float* tau_layers;
   const uint8_t* fold_layers;
   const uint8_t* self_stable;
+  /* 1: the O and down projections always leave fp32 partials [S][m_cap][hidden]
+   * for the next row kernel (needed by tensor-parallel shards, whose partials
+   * are summed across ranks in between); 0: only when they split k. */
+  int32_t partial_always;
 } af_fold_config;
 
 typedef struct {
@@ -315,6 +320,29 @@ int af_fold_plan_destroy(void* plan);
  * (the reference recomputes each child separately).
  */
 int af_fold_set_child_cap(void* plan, int64_t max_candidates_per_child);
+
+/*
+ * Tensor-parallel folded pass (no counterpart in the reference, which runs a
+ * child on one device). Every rank holds a shard of each layer -- a slice of
+ * the attention heads (Wq / Wk / Wv rows, Wo columns), a slice of the FFN
+ * (gate / up rows, down columns) and a slice of the LM-head vocabulary -- plus
+ * the full embedding table and its own slice of the parent cache, and runs the
+ * same pass. Three sums cross the ranks, through `collective`, which must
+ * add the `count` fp32 values at `data` over every rank, in place and
+ * stream-ordered on `stream` (e.g. an NCCL all-reduce), and return 0:
+ *   AF_COLL_O     after layer `layer`'s O projection: its split-K partials;
+ *   AF_COLL_DOWN  after its down projection: its split-K partials;
+ *   AF_COLL_ROWSUM after the LM head: the fresh logits' row sums [C * T].
+ * Needs a plan created with partial_always = 1. embed_rows: rows of the
+ * (full) embedding table; vocab_total: the whole vocabulary (the scores are
+ * means over it). Host-side setting: make it before capturing a run.
+ */
+#define AF_COLL_O 0
+#define AF_COLL_DOWN 1
+#define AF_COLL_ROWSUM 2
+typedef int (*af_collective_fn)(void* user, int32_t kind, int32_t layer, void* data, int64_t count, void* stream);
+int af_fold_set_tensor_parallel(void* plan, int64_t embed_rows, int64_t vocab_total, af_collective_fn collective,
+                                void* user);
 
 /*
  * Promotion of a verified child to a parent. Replaces the child branch's own
