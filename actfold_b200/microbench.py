@@ -16,6 +16,13 @@ reference's per-token tensor work:
              (fused_ops.py:256-324) with half the rows selected: selected rows
              read, every row written (zeros elsewhere).
 
+Beside ``merge``, the same merge done the reference's ways, on the same
+tensors and with the same byte count: ``merge_torch_where`` (its torch
+fallback, fused_ops.py:38-51) and ``merge_reference_triton`` (its own
+``merge_stable_divergent``, which runs its Triton ``_merge_kernel`` on CUDA,
+fused_ops.py:95-135, imported from the reference package installed under
+``baseline/_ref`` when it is there; skipped otherwise).
+
 Inputs are bf16 [C, T, H] (268 MB at the defaults, above the 126 MB L2). Each
 kernel's calls are captured in a CUDA graph of ``reps`` launches, replayed
 after warm-up and timed with CUDA events on the capturing stream; one JSON
@@ -65,13 +72,39 @@ def _time(fn, reps: int, rounds: int = 5) -> float:
     return best
 
 
+def _reference_merge():
+    """The reference's merge_stable_divergent from baseline/_ref, or (None, reason)."""
+    import sys
+    import tempfile
+
+    ref = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "actfold")):
+        return None, "reference package not installed under baseline/_ref"
+    # The reference package imports matplotlib / seaborn (for its plots) on import; neither is
+    # installed here, so empty stand-ins go on the path first. Nothing of them is used.
+    shim = tempfile.mkdtemp(prefix="af_ref_shim_")
+    for name, body in (("matplotlib", "def use(*a, **k):\n    pass\n"), ("seaborn", "")):
+        os.makedirs(os.path.join(shim, name))
+        with open(os.path.join(shim, name, "__init__.py"), "w") as f:
+            f.write(body)
+    with open(os.path.join(shim, "matplotlib", "pyplot.py"), "w") as f:
+        f.write("def __getattr__(name):\n    raise AttributeError(name)\n")
+    sys.path[:0] = [shim, ref]
+    try:
+        from actfold.core.fused_ops import merge_stable_divergent as ref_merge
+    except Exception as exc:  # reported in the output line, not raised
+        return None, f"reference import failed: {exc}"
+    return ref_merge, "baseline/_ref"
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--children", type=int, default=32)
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--hidden", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=20)
-    ap.add_argument("--only", choices=["gate", "merge", "gather"], default=None, help="time one kernel")
+    ap.add_argument("--only", choices=["gate", "merge", "merge_torch_where", "merge_reference_triton", "gather"],
+                    default=None, help="time one kernel")
     a = ap.parse_args()
 
     from actfold_b200.core import SimilarityGate, merge_stable_divergent
@@ -92,8 +125,15 @@ def main() -> None:
     cases = {
         "gate": (lambda: gate.forward_compact(child, pexp), C * T * row + T * row + C * T * (1 + 4) + C * 4),
         "merge": (lambda: merge_stable_divergent(other, child, half), 2 * C * T * row),
+        "merge_torch_where": (lambda: torch.where(half[..., None], other, child), 2 * C * T * row),
         "gather": (lambda: masked_rows(child, half), int(half.sum()) * row + C * T * row),
     }
+    if a.only in (None, "merge_reference_triton"):
+        ref_merge, why = _reference_merge()
+        if ref_merge is None:
+            print(json.dumps({"kernel": "merge_reference_triton", "skipped": why}), flush=True)
+        else:
+            cases["merge_reference_triton"] = (lambda: ref_merge(other, child, half), 2 * C * T * row)
     for name, (fn, nbytes) in cases.items():
         if a.only and name != a.only:
             continue
