@@ -73,6 +73,9 @@ struct CandArgs {
   const int64_t* ptok;           // [T]    (layer 0)
   const uint8_t* self_stable;    // [T] of this layer, nullable
   int all_rows;                  // 1: every row is a candidate (a layer that does not fold)
+  const uint8_t* ss_all;         // layer 0, nullable: [L, T] parent self-gate results of the pass
+  int n_layers;
+  uint8_t* later;                // layer 0, nullable: later[t] = 1 if some layer >= 1 fails the parent's gate at t
   const int* prev_div_pos;       // layer >= 1: fresh rows = previous layer's divergent rows
   const int* prev_n_div;
   int* slot;                     // [C*T] scratch
@@ -148,6 +151,12 @@ __global__ void __launch_bounds__(1024) k_fold_candidates(const CandArgs a) {
       *a.n_fresh0 = min(base1, a.m_cap);
       *a.n_cand = min(base, a.m_cap);
     }
+    if (a.later)
+      for (int t = threadIdx.x; t < a.T; t += 1024) {
+        uint8_t v = 0;
+        for (int l = 1; l < a.n_layers && !v; ++l) v = a.ss_all[(int64_t)l * a.T + t] == 0;
+        a.later[t] = v;
+      }
     return;
   }
   // Later layers (the parent fails its own gate on some rows, or the layer
@@ -307,6 +316,28 @@ __device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row
   }
 }
 
+// part[0][i] = part[0][i] + part[1][i] + ... (splits in order), i < n: the
+// tensor-parallel pass adds its k-splits locally before the cross-rank sum,
+// which then moves one slice instead of one per split.
+__global__ void __launch_bounds__(256) k_sum_splits(float* part, int64_t stride, int nsplit, int64_t n4,
+                                                    const int* rows_dev, int64_t row_len4) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t lim = rows_dev ? min(n4, (int64_t)(*rows_dev) * row_len4) : n4;
+  float4* p0 = reinterpret_cast<float4*>(part);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < lim; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float4 v = reinterpret_cast<const float4*>(part + sp * stride)[i];
+      a.x += v.x;
+      a.y += v.y;
+      a.z += v.z;
+      a.w += v.w;
+    }
+    p0[i] = a;
+  }
+}
+
 // out[i] = rmsnorm(in[i]) * w for i < n (rows strided by H); one CTA per row.
 // With pr.part, row i is first finished from its split-K partials (and stored).
 template <int NV>
@@ -387,8 +418,22 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
 // ----------------------------------------------------------------------------
 constexpr int kFillChunk = 8192;  // logits per CTA
 
+// Which children take the parent's logits row t:
+//   FILL_ALL   every child whose final row t is not fresh (final_bits);
+//   FILL_EARLY, right after layer 0, every child whose row t was stable at layer 0 (bits0) at a
+//              position that no later layer can make a candidate again (later[t] == 0): such a row
+//              keeps the parent's input at every layer, so it is stable at the end;
+//   FILL_LATE  after the last layer, the remaining final-stable rows (fresh at layer 0, or at a
+//              position a later layer re-examines).
+enum FillMode : int { FILL_ALL = 0, FILL_EARLY = 1, FILL_LATE = 2 };
+
+__device__ __forceinline__ bool bit_of(const unsigned* b, int bits_ld, int c, int t) {
+  return (b[c * bits_ld + (t >> 5)] >> (t & 31)) & 1u;
+}
+
 __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logits, int64_t V, int C, int T,
-                                                     const unsigned* final_bits, int bits_ld,
+                                                     const unsigned* final_bits, const unsigned* bits0,
+                                                     const uint8_t* later, int mode, int bits_ld,
                                                      __nv_bfloat16* logits) {
   pdl_trigger();
   pdl_wait();
@@ -397,9 +442,13 @@ __global__ void __launch_bounds__(256) k_logits_fill(const __nv_bfloat16* p_logi
   const int t = blockIdx.y;
   if (threadIdx.x == 0) nk = 0;
   __syncthreads();
+  const bool later_t = mode != FILL_ALL && later[t] != 0;
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    const bool fresh = (final_bits[c * bits_ld + (t >> 5)] >> (t & 31)) & 1u;
-    if (!fresh) kids[atomicAdd(&nk, 1)] = c;
+    bool take;
+    if (mode == FILL_EARLY) take = !later_t && !bit_of(bits0, bits_ld, c, t);
+    else if (mode == FILL_LATE) take = !bit_of(final_bits, bits_ld, c, t) && (later_t || bit_of(bits0, bits_ld, c, t));
+    else take = !bit_of(final_bits, bits_ld, c, t);
+    if (take) kids[atomicAdd(&nk, 1)] = c;
   }
   __syncthreads();
   const int n = nk;
@@ -605,6 +654,16 @@ struct Bump {
 static bool partials_off() {
   static const bool off = [] {
     const char* e = getenv("ACTFOLD_SPLITK_PARTIALS");
+    return e && e[0] == '0';
+  }();
+  return off;
+}
+
+// ACTFOLD_EARLY_FILL=0: every parent logits row is copied after the last
+// layer instead of from layer 0 on (comparison runs).
+static bool early_fill_off() {
+  static const bool off = [] {
+    const char* e = getenv("ACTFOLD_EARLY_FILL");
     return e && e[0] == '0';
   }();
   return off;
@@ -839,6 +898,8 @@ struct FoldWs {
   float* part;
   int split_o, split_down;
   int part_o, part_down;  // 1: that GEMM leaves its partials in `part`
+  unsigned* bits0;        // [C, bits_ld] divergent rows of layer 0 (the early logits fill)
+  uint8_t* later;         // [T] positions a layer >= 1 re-examines (the parent fails its own gate there)
 };
 
 static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool partial_always) {
@@ -871,6 +932,8 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool 
   w.row_sums = b.take<float>((int64_t)C * T);
   w.status = b.take<unsigned>(1);
   w.cand_div = b.take<int>(m_cap);
+  w.bits0 = b.take<unsigned>((int64_t)C * w.bits_ld);
+  w.later = b.take<uint8_t>(T);
   w.split_o = gemm_splits(z.H, z.q, m_cap);
   w.split_down = gemm_splits(z.H, z.FF, m_cap);
   const int S = std::max(w.split_o, w.split_down);
@@ -1026,6 +1089,17 @@ static int collective(FoldPlan* p, int kind, int layer, void* data, int64_t coun
   return AF_OK;
 }
 
+// Tensor parallel: this rank's k-splits of an O / down projection added into
+// the first slice, then that slice summed over the ranks by the hook.
+static int cross_rank_sum(FoldPlan* p, int kind, int layer, int nsplit, const int* rows_dev, cudaStream_t s) {
+  const Sizes z = sizes_of(p->model.dims);
+  const int64_t n = (int64_t)p->m_cap * z.H;
+  if (nsplit > 1)
+    AF_TIMED(FK_NORM, AF_LAUNCH(k_sum_splits, (unsigned)(2 * sm_count()), 256, 0, s, p->w.part, n, nsplit, n / 4,
+                                rows_dev, (int64_t)z.H / 4));
+  return collective(p, kind, layer, p->w.part, n, s);
+}
+
 static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, float* scores, cudaStream_t s) {
   const Sizes z = sizes_of(p->model.dims);
   const FoldWs& w = p->w;
@@ -1049,6 +1123,16 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   ca.ptok = p->parent.tokens;
   ca.self_stable = p->su[0] ? p->self_stable : nullptr;
   ca.all_rows = p->folds[0] ? 0 : 1;
+  // Logits rows that are the parent's can be filled from layer 0 on when no
+  // later layer recomputes every row (a row stable at layer 0 then keeps the
+  // parent's input, and stays stable, unless the parent fails its own gate at
+  // that position in a later layer: `later`).
+  const bool fork_fill = !p->tk.on;
+  bool early = fork_fill && L > 1 && !early_fill_off();
+  for (int l = 1; l < L; ++l) early = early && p->folds[l];
+  ca.ss_all = p->self_stable;
+  ca.n_layers = L;
+  ca.later = early ? w.later : nullptr;
   ca.slot = w.slot;
   ca.cand_child = w.cand_child;
   ca.cand_pos = w.cand_pos;
@@ -1066,7 +1150,6 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   // times every launch class on the pass stream).
   const int fill_smem = C * (int)sizeof(int);
   const dim3 fill_grid((unsigned)((z.V + kFillChunk - 1) / kFillChunk), (unsigned)T);
-  const bool fork_fill = !p->tk.on;
   // The pass's kernels launch at the device's greatest priority, the side
   // stream's fill at the least: the block scheduler then prefers the pass's
   // pending CTAs whenever a slot frees.
@@ -1115,7 +1198,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
       // split-K partials: finish them here (residual = that layer's h1).
       g.fresh_part.part = w.part;
       g.fresh_part.split_stride = (int64_t)M * z.H;
-      g.fresh_part.nsplit = w.split_down;
+      g.fresh_part.nsplit = p->coll ? 1 : w.split_down;  // tensor parallel: already added up
       g.fresh_part.res = w.h1;
       g.fresh_part.store = x_l;
     }
@@ -1143,7 +1226,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     a.cand_div = w.cand_div;
     a.div_count = w.div_count + (int64_t)l * C;
     a.bits = w.bits;
-    a.final_bits = last ? w.final_bits : nullptr;
+    a.final_bits = last ? w.final_bits : (l == 0 && early ? w.bits0 : nullptr);
     a.zero_f = last ? w.row_sums : nullptr;
     a.zero_n = C * T;
     a.write_next = !next_su;
@@ -1174,22 +1257,26 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.tmap_w = &p->tm_qkv[l];
     c.tmap_x = &p->tx_A;
     AF_TIMED(FK_QKV, if ((st = gemm_run(c, s))) return st);
-    if (last && fork_fill) {
-      // The final divergent bitmap is complete once this GEMM (its compaction
-      // side task) is: copy the parent's logits into every stable row on the
-      // side stream while the last layer and the LM head run here.
+    if (fork_fill && ((l == 0 && early) || last)) {
+      // After layer 0's compaction (a side task of this GEMM) the rows stable
+      // for good are known; after the last layer's, every final-stable row is.
+      // Their logits are the parent's: copy them on the side stream, at the
+      // least priority, while the pass goes on here (the LM head writes only
+      // final-divergent rows, so the copies never meet its stores).
       if (cudaEventRecord(p->ev_fork, s) != cudaSuccess || cudaStreamWaitEvent(p->side, p->ev_fork, 0) != cudaSuccess)
         return check_launch("af_fold_run: fork");
+      const int mode = !last ? FILL_EARLY : (early ? FILL_LATE : FILL_ALL);
       cudaError_t e;
       {
         LaunchPriority low(prio_low);
         e = launch_ex(k_logits_fill, fill_grid, dim3(256), (size_t)fill_smem, p->side, false, dim3(1, 1, 1),
                       static_cast<const __nv_bfloat16*>(p->parent.logits), (int64_t)z.V, C, T,
-                      (const unsigned*)w.final_bits, w.bits_ld, logits);
+                      (const unsigned*)w.final_bits, (const unsigned*)w.bits0, (const uint8_t*)w.later, mode,
+                      w.bits_ld, logits);
       }
       if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("af_fold_run: fill launch: ") + cudaGetErrorString(e));
       ++p->tk.launches;
-      if (cudaEventRecord(p->ev_join, p->side) != cudaSuccess) return check_launch("af_fold_run: join");
+      if (last && cudaEventRecord(p->ev_join, p->side) != cudaSuccess) return check_launch("af_fold_run: join");
     }
 
     AttnParams ap;
@@ -1259,14 +1346,14 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.tmap_x = &p->tx_att;
     c.partial_out = w.part_o ? w.part : nullptr;
     AF_TIMED(FK_O, if ((st = gemm_run(c, s))) return st);
-    if (p->coll && (st = collective(p, AF_COLL_O, l, w.part, (int64_t)w.split_o * M * z.H, s))) return st;
+    if (p->coll && (st = cross_rank_sum(p, AF_COLL_O, l, w.split_o, nd, s))) return st;
 
     PartialRows pr_o;
     memset(&pr_o, 0, sizeof(pr_o));
     if (w.part_o) {  // h1 = xc + O, finished from the O GEMM's partials
       pr_o.part = w.part;
       pr_o.split_stride = (int64_t)M * z.H;
-      pr_o.nsplit = w.split_o;
+      pr_o.nsplit = p->coll ? 1 : w.split_o;
       pr_o.res = w.xc;
       pr_o.res_rows = dcand;
       pr_o.store = w.h1;
@@ -1305,7 +1392,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.tmap_x = &p->tx_f;
     c.partial_out = w.part_down ? w.part : nullptr;  // finished by the next gate (or the final norm)
     AF_TIMED(FK_DOWN, if ((st = gemm_run(c, s))) return st);
-    if (p->coll && (st = collective(p, AF_COLL_DOWN, l, w.part, (int64_t)w.split_down * M * z.H, s))) return st;
+    if (p->coll && (st = cross_rank_sum(p, AF_COLL_DOWN, l, w.split_down, nd, s))) return st;
     if (p->kv_keep)
       AF_TIMED(FK_SETUP, AF_LAUNCH(k_keep_rows, (unsigned)M, 256, 0, s, (const __nv_bfloat16*)w.qkv, z.qkv,
                                    (const int*)nc, M, p->kv_keep + (int64_t)l * M * z.qkv));
@@ -1340,7 +1427,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   if (w.part_down) {  // the last layer's outputs, finished from its down GEMM's partials
     pr_f.part = w.part;
     pr_f.split_stride = (int64_t)M * z.H;
-    pr_f.nsplit = w.split_down;
+    pr_f.nsplit = p->coll ? 1 : w.split_down;
     pr_f.res = w.h1;
     pr_f.store = const_cast<__nv_bfloat16*>(x_final);
   }
@@ -1368,7 +1455,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     if (cudaStreamWaitEvent(s, p->ev_join, 0) != cudaSuccess) return check_launch("af_fold_run: join");
   } else {
     AF_TIMED(FK_FILL, AF_LAUNCH(k_logits_fill, fill_grid, 256, fill_smem, s, static_cast<const __nv_bfloat16*>(p->parent.logits),
-                                 (int64_t)z.V, C, T, (const unsigned*)w.final_bits, w.bits_ld, logits));
+                                 (int64_t)z.V, C, T, (const unsigned*)w.final_bits, (const unsigned*)nullptr,
+                                 (const uint8_t*)nullptr, (int)FILL_ALL, w.bits_ld, logits));
   }
   if (scores)
     AF_TIMED(FK_SCORES, AF_LAUNCH(k_scores, C, 256, 0, s, (const float*)p->parent.logit_row_sums,

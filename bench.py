@@ -556,11 +556,14 @@ def main() -> None:
     parent_first_ms = (time.perf_counter() - t0) * 1e3
     parent_ms = parent_first_ms
     if rank == 0:
-        # A second dense pass: the first includes one-time module loading and kernel set-up.
-        t0 = time.perf_counter()
-        pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)
-        torch.cuda.synchronize()
-        parent_ms = (time.perf_counter() - t0) * 1e3
+        # More dense passes (the first includes one-time module loading and kernel set-up): the fastest.
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)
+            torch.cuda.synchronize()
+            times.append((time.perf_counter() - t0) * 1e3)
+        parent_ms = min(times)
     bcast_ms = 0.0
     if world > 1:
         dist.barrier()
