@@ -265,7 +265,7 @@ __device__ __forceinline__ void rmsnorm_regs(const uint4 (&v)[NV], int nvec, int
 struct PartialRows {
   const float* part;               // [S][m_cap][H] fp32, null: rows are read from `in`
   int64_t split_stride;            // m_cap * H
-  int nsplit;                      // S (<= 4)
+  int nsplit;                      // S (<= 16)
   const __nv_bfloat16* res;        // residual rows [.., H]
   const int* res_rows;             // nullable: residual row of row i
   __nv_bfloat16* store;            // the finished rows are written here (row i)
@@ -276,20 +276,37 @@ __device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row
   const int64_t rrow = pr.res_rows ? pr.res_rows[row] : row;
   const char* rp = reinterpret_cast<const char*>(pr.res + rrow * (int64_t)(nvec * 8));
   const float* pp = pr.part + (int64_t)row * (nvec * 8);
-  float4 a[NV][2][4];
+  float acc[NV][8];
   uint4 rv[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int j = i * kRowThreads + tid;
-    if (j >= nvec) continue;
-    rv[i] = ldg16(rp + 16 * (int64_t)j);
 #pragma unroll
-    for (int sp = 0; sp < 4; ++sp)
-      if (sp < pr.nsplit) {
-        const float4* q = reinterpret_cast<const float4*>(pp + sp * pr.split_stride + 8 * (int64_t)j);
-        a[i][0][sp] = q[0];
-        a[i][1][sp] = q[1];
-      }
+    for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+    if (j < nvec) rv[i] = ldg16(rp + 16 * (int64_t)j);
+  }
+  // Splits in order, four at a time in flight (the sum order is split 0, 1, 2, ...).
+  for (int s0 = 0; s0 < pr.nsplit; s0 += 4) {
+    float4 a[NV][4][2];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * kRowThreads + tid;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (j < nvec && s0 + q < pr.nsplit) {
+          const float4* src = reinterpret_cast<const float4*>(pp + (s0 + q) * pr.split_stride + 8 * (int64_t)j);
+          a[i][q][0] = src[0];
+          a[i][q][1] = src[1];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (s0 + q < pr.nsplit) {
+          acc[i][0] += a[i][q][0].x; acc[i][1] += a[i][q][0].y; acc[i][2] += a[i][q][0].z; acc[i][3] += a[i][q][0].w;
+          acc[i][4] += a[i][q][1].x; acc[i][5] += a[i][q][1].y; acc[i][6] += a[i][q][1].z; acc[i][7] += a[i][q][1].w;
+        }
   }
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
@@ -298,20 +315,13 @@ __device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row
       v[i] = make_uint4(0u, 0u, 0u, 0u);
       continue;
     }
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int sp = 0; sp < 4; ++sp)
-      if (sp < pr.nsplit) {
-        acc[0] += a[i][0][sp].x; acc[1] += a[i][0][sp].y; acc[2] += a[i][0][sp].z; acc[3] += a[i][0][sp].w;
-        acc[4] += a[i][1][sp].x; acc[5] += a[i][1][sp].y; acc[6] += a[i][1][sp].z; acc[7] += a[i][1][sp].w;
-      }
     float r[8];
     unpack<AF_DTYPE_BF16>(rv[i], r);
     uint32_t* ow = reinterpret_cast<uint32_t*>(&v[i]);
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      ow[e] = pack_bf16x2(__fadd_rn(r[2 * e], rnd<AF_DTYPE_BF16>(acc[2 * e])),
-                          __fadd_rn(r[2 * e + 1], rnd<AF_DTYPE_BF16>(acc[2 * e + 1])));
+      ow[e] = pack_bf16x2(__fadd_rn(r[2 * e], rnd<AF_DTYPE_BF16>(acc[i][2 * e])),
+                          __fadd_rn(r[2 * e + 1], rnd<AF_DTYPE_BF16>(acc[i][2 * e + 1])));
     stg16(reinterpret_cast<char*>(pr.store + (int64_t)row * (nvec * 8)) + 16 * (int64_t)j, v[i]);
   }
 }
@@ -934,13 +944,16 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool 
   w.cand_div = b.take<int>(m_cap);
   w.bits0 = b.take<unsigned>((int64_t)C * w.bits_ld);
   w.later = b.take<uint8_t>(T);
-  w.split_o = gemm_splits(z.H, z.q, m_cap);
-  w.split_down = gemm_splits(z.H, z.FF, m_cap);
+  // The O / down projections leave partials where they split k (always for
+  // a tensor-parallel shard); their split counts are then those of launches
+  // without a cluster.
+  const bool split_o = gemm_splits(z.H, z.q, m_cap) > 1, split_d = gemm_splits(z.H, z.FF, m_cap) > 1;
+  w.part_o = partial_always || (split_o && !partials_off());
+  w.part_down = partial_always || (split_d && !partials_off());
+  w.split_o = w.part_o ? gemm_splits(z.H, z.q, m_cap, true) : 1;
+  w.split_down = w.part_down ? gemm_splits(z.H, z.FF, m_cap, true) : 1;
   const int S = std::max(w.split_o, w.split_down);
-  const bool use = S <= 4 && (partial_always || (S > 1 && !partials_off()));
-  w.part = use ? b.take<float>((int64_t)S * m_cap * z.H) : nullptr;
-  w.part_o = use && (partial_always || w.split_o > 1);
-  w.part_down = use && (partial_always || w.split_down > 1);
+  w.part = (w.part_o || w.part_down) ? b.take<float>((int64_t)S * m_cap * z.H) : nullptr;
   return w;
 }
 
@@ -1516,10 +1529,6 @@ extern "C" int af_fold_plan_create(const af_model* m, const af_parent_cache* par
     }
   Bump b(workspace, workspace_bytes);
   p->w = carve_fold(b, sizes_of(m->dims), p->C, p->T, p->m_cap, cfg->partial_always != 0);
-  if (cfg->partial_always && !p->w.part) {
-    delete p;
-    return fail(AF_ERR_ARG, "af_fold_plan_create: partial_always needs at most 4 k-splits in the O / down projections");
-  }
   p->partial_always = cfg->partial_always != 0;
   if (b.off > workspace_bytes) {
     delete p;

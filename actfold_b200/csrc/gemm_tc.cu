@@ -37,6 +37,7 @@ constexpr int kBlockK = 64;   // bf16 elements per k-block (one 128-byte swizzle
 constexpr int kTileN = 128;   // weight rows per CTA (MMA M)
 constexpr int kThreads = 192;
 constexpr int kMaxSplits = 8; // portable cluster size
+constexpr int kMaxPartialSplits = 16;  // launches that leave partials need no cluster
 
 struct GemmDev {
   int n, k, m_cap, ntok, n_tiles, m_tiles, nkb, kb_per_split, splits, stages;
@@ -611,7 +612,16 @@ struct GemmShape {
   int push;  // split-K partials pushed into the owners' shared memory (bulk copies)
 };
 
-static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_sums) {
+// Tuning override of the k-splits of launches that leave partials (0: the heuristic).
+static int env_partial_splits() {
+  static const int v = [] {
+    const char* e = getenv("ACTFOLD_PARTIAL_SPLITS");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
+static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_sums, bool partial = false) {
   GemmShape g;
   g.ntok = gemm_ntok(m_cap);
   g.m_tiles = (m_cap + g.ntok - 1) / g.ntok;
@@ -624,6 +634,7 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   }();
   const int tiles = g.n_tiles * g.m_tiles;
   int splits = want_splits;
+  if (splits <= 0 && partial && env_partial_splits() > 0) splits = env_partial_splits();
   if (splits <= 0) {
     // About 4/3 CTAs per SM, at most 4 splits: measured on B200 for the
     // LLaDA/Dream projections, more and shorter split CTAs lose more to their
@@ -632,8 +643,9 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
     splits = std::max(1, std::min(splits, 4));
     splits = std::min(splits, std::max(1, g.nkb / 4));
   }
+  if (partial) splits = std::min(splits, kMaxPartialSplits);
   if (row_sums) splits = 1;
-  splits = std::min(splits, kMaxSplits);
+  if (!partial) splits = std::min(splits, kMaxSplits);
   g.kb_per = (g.nkb + splits - 1) / splits;
   g.splits = (g.nkb + g.kb_per - 1) / g.kb_per;
   // A CTA streams at most (bytes its ring keeps in flight) / (load latency):
@@ -669,7 +681,7 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   return g;
 }
 
-int gemm_splits(int n, int k, int m_cap) { return plan_shape(n, k, m_cap, 0, false).splits; }
+int gemm_splits(int n, int k, int m_cap, bool partial) { return plan_shape(n, k, m_cap, 0, false, partial).splits; }
 
 int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.x && c.w && c.out && c.status, "gemm: null pointer");
@@ -684,8 +696,8 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(c.epi != EPI_RESIDUAL || c.res, "gemm: residual epilogue needs res");
   AF_REQUIRE(c.epi != EPI_ROPE || (c.rope_cos && c.rope_sin && c.positions && c.head_dim == 128 && c.rope_cols % 128 == 0),
              "gemm: rope epilogue needs cos/sin/positions and head_dim 128");
-  GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr);
   const bool partial = c.partial_out != nullptr;  // the caller asks for partials (also with one split)
+  GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr, partial);
   AF_REQUIRE(!partial || (reinterpret_cast<uintptr_t>(c.partial_out) & 15u) == 0, "gemm: partial_out must be 16-byte aligned");
   if (partial) g.push = 0;  // no exchange between the splits: no receive slots in shared memory
   AF_REQUIRE(g.smem <= 227 * 1024, "gemm: shared memory budget exceeded");

@@ -51,8 +51,8 @@ struct GemmCall {
   float* partial_out;
 };
 
-// k-splits a launch of this shape uses (1: no split).
-int gemm_splits(int n, int k, int m_cap);
+// k-splits a launch of this shape uses (1: no split); `partial`: one that leaves partials.
+int gemm_splits(int n, int k, int m_cap, bool partial = false);
 
 // Token-tile width the kernel uses for a given row capacity.
 int gemm_ntok(int m_cap);
