@@ -116,7 +116,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   int* sF = reinterpret_cast<int*>(gb + kOffF);
   float* red = reinterpret_cast<float*>(gb + kOffQ);  // [2][4][128] row max / sum partials, after S is done
   const uint32_t barS = base + kOffBar, barO = barS + 8, barK = barS + 32, barV = barS + 40;
-  const uint32_t barC = barS + 48;  // candidate-row mode: query tile and candidate key blocks by TMA
+  const uint32_t barC = barS + 48;   // candidate-row mode: query tile and candidate key blocks by TMA
+  const uint32_t barCV = barS + 56;  // candidate-row mode: candidate value blocks by TMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + kOffBar + 16);
   volatile int* fail = reinterpret_cast<volatile int*>(gb + kOffBar + 24);
 
@@ -126,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     mbar_init(barK, 1);
     mbar_init(barV, 1);
     mbar_init(barC, 1);
+    mbar_init(barCV, 1);
     *fail = 0;
     fence_barrier_init();
     if (kv_tma) {
@@ -134,13 +136,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
       const uint32_t bytes = (uint32_t)n_par * kOpB;
       mbar_arrive_expect_tx(barK, bytes);
       mbar_arrive_expect_tx(barV, bytes);
-      for (int j = 0; j < n_par; ++j) {
-        const int y = (b_lo + j) * kTK;
-        for (int hf = 0; hf < 2; ++hf) {
-          tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmK, barK, kvh * 128 + 64 * hf, y);
-          tma_load_2d(sV + j * kOpB + hf * kTileB, &tmV, barV, kvh * 128 + 64 * hf, y);
-        }
-      }
+      // Every K block first: S needs only K, V is not read before P.V.
+      for (int j = 0; j < n_par; ++j)
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmK, barK, kvh * 128 + 64 * hf, (b_lo + j) * kTK);
+      for (int j = 0; j < n_par; ++j)
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_2d(sV + j * kOpB + hf * kTileB, &tmV, barV, kvh * 128 + 64 * hf, (b_lo + j) * kTK);
     }
   }
   pdl_wait();
@@ -173,19 +175,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     // this CTA's candidate key blocks, as soon as their producer is done.
     // Rows past the valid counts are masked below (queries are not written,
     // keys get zero weight).
-    uint32_t bytes = kOpB;
+    uint32_t kbytes = kOpB, vbytes = 0;
     for (int j = 0; j < nbl; ++j)
-      if (b_lo + j >= n_pb) bytes += 2 * kOpB;
-    mbar_arrive_expect_tx(barC, bytes);
+      if (b_lo + j >= n_pb) {
+        kbytes += kOpB;
+        vbytes += kOpB;
+      }
+    mbar_arrive_expect_tx(barC, kbytes);
+    mbar_arrive_expect_tx(barCV, vbytes);  // zero bytes: the barrier completes on the arrival alone
     for (int hf = 0; hf < 2; ++hf) tma_load_2d(sQ + hf * kTileB, &tmC, barC, h * 128 + 64 * hf, q0);
     for (int j = 0; j < nbl; ++j) {
       const int b = b_lo + j;
       if (b < n_pb) continue;
       const int y = (fb0 + b - n_pb) * kTK;
-      for (int hf = 0; hf < 2; ++hf) {
+      for (int hf = 0; hf < 2; ++hf)
         tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmC, barC, p.fk_col + kvh * 128 + 64 * hf, y);
-        tma_load_2d(sV + j * kOpB + hf * kTileB, &tmC, barC, p.fv_col + kvh * 128 + 64 * hf, y);
-      }
+    }
+    for (int j = 0; j < nbl; ++j) {
+      const int b = b_lo + j;
+      if (b < n_pb) continue;
+      const int y = (fb0 + b - n_pb) * kTK;
+      for (int hf = 0; hf < 2; ++hf)
+        tma_load_2d(sV + j * kOpB + hf * kTileB, &tmC, barCV, p.fv_col + kvh * 128 + 64 * hf, y);
     }
   }
 
@@ -342,9 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   // ---- O = sum_j P_j V_j ----
   const bool have_o = nbl > 0 && !s_bad;
   bool v_ok = true;
-  if (tid == 0 && kv_tma) {  // also on the failure paths: the V loads land before the CTA moves on
+  if (tid == 0 && (kv_tma || c_tma)) {  // also on the failure paths: the V loads land before the CTA moves on
     volatile int no_abort = 0;
-    v_ok = mbar_wait(barV, 0, &no_abort);
+    if (kv_tma) v_ok = mbar_wait(barV, 0, &no_abort);
+    if (c_tma) v_ok = mbar_wait(barCV, 0, &no_abort) && v_ok;
     if (!v_ok) *fail = 1;
     tc_fence_after();
   }
@@ -392,47 +404,55 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
       }
     }
   } else {
-    // Partials into the (now idle) V region: O rows [128][kPoLd] f32, then (m, l) [128].
-    constexpr int kPoLd = 132;  // padded row: conflict-free 16-byte stores
-    float* po = reinterpret_cast<float*>(gb + kOffV);
-    float2* pml = reinterpret_cast<float2*>(gb + kOffV + 128 * kPoLd * 4);
-#pragma unroll
-    for (int i = 0; i < 32; i += 4)
-      *reinterpret_cast<float4*>(po + r * kPoLd + c0 + i) = make_float4(
-          __uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]), __uint_as_float(o[i + 3]));
-    if (cg == 0) pml[r] = make_float2(bad ? -INFINITY : m, bad ? 0.f : l);
-    cluster_sync_all();
+    // Push: the V region of CTA k (idle once every CTA's P.V is done) receives, from every split s,
+    // the partial rows k owns: O rows [s][rows_per][kPoLd] f32, then (m, l)
+    // [s][rows_per]. Each thread stores its own row's 32 columns straight into
+    // the owner's shared memory (posted DSMEM stores, no round trips); after
+    // one cluster barrier every owner combines from its own shared memory.
+    constexpr int kPoLd = 132;  // padded row: conflict-free 16-byte accesses
     const int rows_per = (kTQ + ns - 1) / ns;
-    const int rlo = split * rows_per, rhi = min(kTQ, rlo + rows_per);
+    float* po = reinterpret_cast<float*>(gb + kOffV);
+    float2* pml = reinterpret_cast<float2*>(gb + kOffV + ns * rows_per * kPoLd * 4);
     const uint32_t po_s = smem_u32(po), pml_s = smem_u32(pml);
+    cluster_sync_all();  // every CTA's P.V is done: the V regions are free to receive
+    {
+      const int owner = r / rows_per, lr = r - owner * rows_per;
+      const uint32_t dst = cluster_map(po_s + 4u * (uint32_t)((split * rows_per + lr) * kPoLd + c0), (uint32_t)owner);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        st_cluster_f4(dst + 4u * i, make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]),
+                                                __uint_as_float(o[i + 2]), __uint_as_float(o[i + 3])));
+      if (cg == 0)
+        st_cluster_f2(cluster_map(pml_s + 8u * (uint32_t)(split * rows_per + lr), (uint32_t)owner),
+                      make_float2(bad ? -INFINITY : m, bad ? 0.f : l));
+    }
+    cluster_sync_all();  // every partial has landed in its owner's shared memory
+    const int rlo = split * rows_per, rhi = min(kTQ, rlo + rows_per);
     for (int idx = tid; idx < (rhi - rlo) * 32; idx += kThreads) {
-      const int rr = rlo + idx / 32, c4 = idx % 32;
+      const int lr = idx / 32, c4 = idx % 32, rr = rlo + lr;
       float mk[8], lk[8];
       float mx = -INFINITY;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (k < ns) {
-          const float2 v = ld_cluster_f2(cluster_map(pml_s + 8u * rr, (uint32_t)k));
+          const float2 v = pml[k * rows_per + lr];
           mk[k] = v.x;
           lk[k] = v.y;
           mx = fmaxf(mx, v.x);
         }
       }
-      float4 vk[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (k < ns) vk[k] = ld_cluster_f4(cluster_map(po_s + 4u * (rr * kPoLd + 4 * c4), (uint32_t)k));
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       float lsum = 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (k < ns && mk[k] != -INFINITY) {
+          const float4 v = *reinterpret_cast<const float4*>(po + (k * rows_per + lr) * kPoLd + 4 * c4);
           const float f = exp2f(mk[k] - mx);
           lsum += f * lk[k];
-          acc.x += f * vk[k].x;
-          acc.y += f * vk[k].y;
-          acc.z += f * vk[k].z;
-          acc.w += f * vk[k].w;
+          acc.x += f * v.x;
+          acc.y += f * v.y;
+          acc.z += f * v.z;
+          acc.w += f * v.w;
         }
       }
       const int orow = q0 + rr < n_q ? (p.out_rows ? p.out_rows[q0 + rr] : q0 + rr) : -1;
@@ -444,7 +464,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
         *reinterpret_cast<uint2*>(p.out + (int64_t)orow * p.out_ld + h * 128 + 4 * c4) = w;
       }
     }
-    cluster_sync_all();  // peers may read this CTA's partials until here
   }
   tc_fence_before();
   __syncthreads();
