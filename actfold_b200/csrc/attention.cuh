@@ -31,6 +31,7 @@ struct AttnParams {
   int n_heads, n_kv_heads;
   float scale_log2;  // softmax scale * log2(e)
   int pdl;           // 1: programmatic dependent launch (the kernel waits for its predecessor)
+  const __nv_bfloat16* kv_hm;  // nullable: parent K / V head-major [2][n_kv_heads][T][128] (this layer), used with kv_static
   int kv_static;     // 1: pk / pv are not written by the preceding kernels (a cached parent), so the
                      //    tcgen05 kernel loads them by TMA before it waits for its predecessor
   // Output row of query row i (nullable: i); rows mapped to -1 are not written.

@@ -137,12 +137,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
       mbar_arrive_expect_tx(barK, bytes);
       mbar_arrive_expect_tx(barV, bytes);
       // Every K block first: S needs only K, V is not read before P.V.
+      // Head-major parent K / V: a block of one head's keys is 32 KB of
+      // contiguous memory (row-major [T, q + 2 kv] rows would cost one DRAM
+      // page per 128-byte key row).
       for (int j = 0; j < n_par; ++j)
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmK, barK, kvh * 128 + 64 * hf, (b_lo + j) * kTK);
+        for (int hf = 0; hf < 2; ++hf) {
+          if (p.kv_hm) tma_load_3d(sKP + j * kOpB + hf * kTileB, &tmK, barK, 64 * hf, (b_lo + j) * kTK, kvh);
+          else tma_load_2d(sKP + j * kOpB + hf * kTileB, &tmK, barK, kvh * 128 + 64 * hf, (b_lo + j) * kTK);
+        }
       for (int j = 0; j < n_par; ++j)
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_2d(sV + j * kOpB + hf * kTileB, &tmV, barV, kvh * 128 + 64 * hf, (b_lo + j) * kTK);
+        for (int hf = 0; hf < 2; ++hf) {
+          if (p.kv_hm) tma_load_3d(sV + j * kOpB + hf * kTileB, &tmV, barV, 64 * hf, (b_lo + j) * kTK, kvh);
+          else tma_load_2d(sV + j * kOpB + hf * kTileB, &tmV, barV, kvh * 128 + 64 * hf, (b_lo + j) * kTK);
+        }
     }
   }
   pdl_wait();
@@ -492,8 +499,9 @@ int attention_tc_splits(const AttnParams& p) {
 }
 
 // Tensor maps of a cached parent's K or V ([T keys, n_kv_heads * 128] columns
-// of a row-major buffer with row stride ld), reused across passes: the parent
-// cache keeps its buffers for its lifetime.
+// of a row-major buffer with row stride ld, or head-major [heads][T][128]
+// when cols < 0), reused across passes: the parent cache keeps its buffers
+// for its lifetime.
 static int kv_tmap(CUtensorMap* map, const __nv_bfloat16* base, int T, int cols, int64_t ld) {
   struct Entry {
     const void* base;
@@ -510,7 +518,10 @@ static int kv_tmap(CUtensorMap* map, const __nv_bfloat16* base, int T, int cols,
       return AF_OK;
     }
   Entry e{base, T, cols, ld, {}};
-  if (int st = make_tmap_bf16(&e.map, base, (uint64_t)T, (uint64_t)cols, (uint64_t)ld, 128)) return st;
+  // cols < 0: head-major layout of -cols heads ([heads][T][128]).
+  if (int st = cols < 0 ? make_tmap_bf16_heads(&e.map, base, (uint64_t)T, (uint64_t)(-cols))
+                        : make_tmap_bf16(&e.map, base, (uint64_t)T, (uint64_t)cols, (uint64_t)ld, 128))
+    return st;
   if (cache.size() >= 512) cache.erase(cache.begin());
   cache.push_back(e);
   *map = e.map;
@@ -532,7 +543,11 @@ int attention_tc_run(const AttnParams& p, int ns, cudaStream_t s) {
                "attention_tc: candidate-row mode needs a buffer map, contiguous queries and key columns in that buffer");
     tc = *p.tmap_c;
   }
-  if (p.kv_static) {
+  if (p.kv_static && p.kv_hm) {
+    const __nv_bfloat16* vbase = p.kv_hm + (int64_t)p.n_kv_heads * p.T * 128;
+    if (int st = kv_tmap(&tk, p.kv_hm, p.T, -p.n_kv_heads, 0)) return st;
+    if (int st = kv_tmap(&tv, vbase, p.T, -p.n_kv_heads, 0)) return st;
+  } else if (p.kv_static) {
     const int cols = p.n_kv_heads * 128;
     if (int st = kv_tmap(&tk, p.pk, p.T, cols, p.kv_ld)) return st;
     if (int st = kv_tmap(&tv, p.pv, p.T, cols, p.kv_ld)) return st;

@@ -577,13 +577,14 @@ __global__ void __launch_bounds__(256) k_keep_rows(const __nv_bfloat16* src, int
 }
 
 struct PromoteArgs {
-  int child, T, H, L, m_cap, qkv_cols;
+  int child, T, H, L, m_cap, qkv_cols, q_cols, n_kv_heads;
   const int *cand_child, *cand_pos, *cand_src, *n_cand;  // [(L+1) * m_cap], [L+1]
   const __nv_bfloat16* x_all;                             // [L+1, m_cap, H] fresh rows of each layer
   const __nv_bfloat16* kept_qkv;                          // [L, m_cap, qkv_cols] QKV row of each candidate
   __nv_bfloat16* layer_in;                                // [L+1, T, H]
   __nv_bfloat16* qkv;                                     // [L, T, qkv_cols]
   uint8_t* self_stable;                                   // [L, T]
+  __nv_bfloat16* kv_hm;                                   // nullable: [L, 2, n_kv_heads, T, 128]
   GateConsts k;
 };
 
@@ -615,8 +616,53 @@ __global__ void __launch_bounds__(kRowThreads) k_promote_rows(const PromoteArgs 
   const char* qs = reinterpret_cast<const char*>(a.kept_qkv + cj * a.qkv_cols);
   char* qd = reinterpret_cast<char*>(a.qkv + ((int64_t)l * a.T + t) * a.qkv_cols);
   for (int jj = threadIdx.x; jj < a.qkv_cols / 8; jj += kRowThreads) stg16(qd + 16 * (int64_t)jj, ldg16(qs + 16 * (int64_t)jj));
+  if (a.kv_hm) {
+    // The same K and V columns into the head-major copy: 16-byte chunk c of
+    // head h of K (kv = 0) or V (kv = 1) is [l][kv][h][t][8c .. 8c + 7].
+    const int chunks = 2 * a.n_kv_heads * 16;
+    for (int jj = threadIdx.x; jj < chunks; jj += kRowThreads) {
+      const int kv = jj / (a.n_kv_heads * 16), h = (jj / 16) % a.n_kv_heads, c = jj % 16;
+      const int64_t off = ((((int64_t)l * 2 + kv) * a.n_kv_heads + h) * a.T + t) * 128 + 8 * c;
+      stg16(reinterpret_cast<char*>(a.kv_hm + off), ldg16(qs + 2 * (int64_t)a.q_cols + 16 * (int64_t)jj));
+    }
+  }
   const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, a.H, a.k, threadIdx.x, RowGroup{red});
   if (threadIdx.x == 0) a.self_stable[(int64_t)l * a.T + t] = o.stable;
+}
+
+// Head-major copy of a parent's keys and values: row t of layer l, K or V
+// (kv), head h goes to kv_hm[l][kv][h][t][0..127]. One CTA per (8 rows,
+// layer); each thread moves 16-byte chunks, reading whole rows in order.
+__global__ void __launch_bounds__(256) k_kv_headmajor(const __nv_bfloat16* __restrict__ qkv, int T, int q_cols,
+                                                      int qkv_cols, int n_kv_heads, __nv_bfloat16* __restrict__ kv_hm) {
+  const int l = blockIdx.y;
+  const int chunks = 2 * n_kv_heads * 16;  // per row
+  for (int r = 0; r < 8; ++r) {
+    const int t = blockIdx.x * 8 + r;
+    if (t >= T) return;
+    const char* src = reinterpret_cast<const char*>(qkv + ((int64_t)l * T + t) * qkv_cols + q_cols);
+    for (int jj = threadIdx.x; jj < chunks; jj += blockDim.x) {
+      const int kv = jj / (n_kv_heads * 16), h = (jj / 16) % n_kv_heads, c = jj % 16;
+      const int64_t off = ((((int64_t)l * 2 + kv) * n_kv_heads + h) * T + t) * 128 + 8 * c;
+      stg16(reinterpret_cast<char*>(kv_hm + off), ldg16(src + 16 * (int64_t)jj));
+    }
+  }
+}
+
+extern "C" int af_parent_kv_headmajor(const af_model_dims* dims, int64_t T, const void* qkv, void* kv_headmajor,
+                                      void* stream) {
+  AF_REQUIRE(dims && qkv && kv_headmajor, "af_parent_kv_headmajor: null pointer");
+  AF_REQUIRE(T > 0 && T <= (1 << 24), "af_parent_kv_headmajor: bad sequence length");
+  AF_REQUIRE(dims->head_dim == 128, "af_parent_kv_headmajor: head_dim must be 128");
+  AF_REQUIRE(((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(kv_headmajor)) & 15) == 0,
+             "af_parent_kv_headmajor: buffers must be 16-byte aligned");
+  AF_REQUIRE(dims->n_layers > 0 && dims->n_kv_heads > 0 && dims->n_heads > 0, "af_parent_kv_headmajor: bad dims");
+  const int q = (int)(dims->n_heads * 128), qkv_cols = q + 2 * (int)(dims->n_kv_heads * 128);
+  cudaStream_t s = as_stream(stream);
+  k_kv_headmajor<<<dim3((unsigned)((T + 7) / 8), (unsigned)dims->n_layers), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(qkv), (int)T, q, qkv_cols, (int)dims->n_kv_heads,
+      static_cast<__nv_bfloat16*>(kv_headmajor));
+  return check_launch("af_parent_kv_headmajor");
 }
 
 // Logits rows and logit row sums of the promoted child's last-layer divergent
@@ -1302,6 +1348,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.n_q_cap = M;
     ap.pk = pqkv_l + z.q;
     ap.pv = pqkv_l + z.q + z.kv;
+    ap.kv_hm = p->parent.kv_headmajor ? static_cast<const __nv_bfloat16*>(p->parent.kv_headmajor) + (int64_t)l * 2 * z.kv * T
+                                      : nullptr;
     ap.kv_ld = z.qkv;
     ap.T = T;
     ap.fresh_bits = w.bits;
@@ -1637,6 +1685,9 @@ extern "C" int af_fold_promote(void* plan, int64_t child, const int64_t* child_t
   a.L = z.L;
   a.m_cap = M;
   a.qkv_cols = z.qkv;
+  a.q_cols = z.q;
+  a.n_kv_heads = (int)p->model.dims.n_kv_heads;
+  a.kv_hm = static_cast<__nv_bfloat16*>(dst->kv_headmajor);
   a.cand_child = p->w.cand_child;
   a.cand_pos = p->w.cand_pos;
   a.cand_src = p->w.cand_src;

@@ -600,6 +600,21 @@ int make_tmap_bf16_tiled(CUtensorMap* map, const void* base, uint64_t rows, uint
   return AF_OK;
 }
 
+int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, uint64_t depth) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (!fn) return fail(AF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) & 15u) return fail(AF_ERR_ARG, "head-major K/V must be 16-byte aligned");
+  const cuuint64_t gdim[3] = {128, rows, depth};
+  const cuuint64_t gstride[2] = {256, rows * 256};  // bytes: row, matrix
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gdim, gstride, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AF_ERR_CUDA, "cuTensorMapEncodeTiled (heads) failed (" + std::to_string((int)r) + ")");
+  return AF_OK;
+}
+
 int gemm_ntok(int m_cap) {
   const int mt = (m_cap + 255) / 256;
   int nt = (m_cap + mt - 1) / mt;

@@ -237,5 +237,9 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 // (each 128 x 64 tile one contiguous 16 KB block): box = one tile, 128-byte
 // swizzle; tile (n_tile, k_block) sits at coordinate z = n_tile * (cols/64) + k_block.
 int make_tmap_bf16_tiled(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+// Map over `depth` contiguous [rows, 128] bf16 matrices (head-major K or V):
+// box 64 columns x 128 rows x 1 matrix, 128-byte swizzle; rows past `rows`
+// read as zeros.
+int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, uint64_t depth);
 
 }  // namespace af

@@ -55,7 +55,7 @@ class _Model(C.Structure):
 class _Parent(C.Structure):
     _fields_ = [
         ("seq", _i64), ("tokens", _vp), ("layer_in", _vp), ("qkv", _vp), ("logits", _vp),
-        ("self_stable", _vp), ("logit_row_sums", _vp),
+        ("self_stable", _vp), ("logit_row_sums", _vp), ("kv_headmajor", _vp),
     ]
 
 
@@ -92,6 +92,7 @@ _lib.SIGNATURES.update(
         "af_fold_set_timing": (_i32, [_vp, _i32]),
         "af_fold_get_timing": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32, C.POINTER(_i64)]),
         "af_fold_set_tensor_parallel": (_i32, [_vp, _i64, _i64, COLLECTIVE_FN, _vp]),
+        "af_parent_kv_headmajor": (_i32, [C.POINTER(_Dims), _i64, _vp, _vp, _vp]),
     }
 )
 
@@ -104,7 +105,7 @@ def _bind_late() -> C.CDLL:
     for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
                  "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy",
                  "af_fold_keep_kv", "af_fold_promote", "af_fold_set_child_cap",
-                 "af_fold_set_timing", "af_fold_get_timing", "af_fold_set_tensor_parallel"):
+                 "af_fold_set_timing", "af_fold_get_timing", "af_fold_set_tensor_parallel", "af_parent_kv_headmajor"):
         fn = getattr(lib, name)
         fn.restype, fn.argtypes = _lib.SIGNATURES[name]
     return lib
@@ -163,6 +164,12 @@ class ParentCache:
     tau: float
     # Bumped by contents_changed() whenever the arrays are rewritten in place.
     version: int = field(default=0, compare=False)
+    # [L, 2, n_kv_heads, T, 128] bf16: the K / V columns of qkv stored
+    # head-major, so the attention kernel reads one head's block of parent
+    # keys as one contiguous run (kv_headmajor() builds it; promotions keep
+    # it current). The buffer lives as long as the cache, so plans may hold it.
+    kv_hm: torch.Tensor | None = field(default=None, compare=False, repr=False)
+    _kv_hm_at: int = field(default=-1, compare=False, repr=False)
 
     @property
     def seq(self) -> int:
@@ -172,9 +179,30 @@ class ParentCache:
         """Host flags: layers where some parent row fails its own gate (one small copy)."""
         return (self.self_stable == 0).any(dim=1).to(torch.uint8).cpu().numpy()
 
-    def struct(self) -> _Parent:
+    def struct(self, model: "LLaDAModel | None" = None) -> _Parent:
+        """The C struct; with ``model`` (whose ``kv_headmajor`` is set) the head-major K / V are built or refreshed."""
+        hm = self.kv_headmajor(model) if model is not None and model.kv_headmajor else None
         return _Parent(self.seq, self.tokens.data_ptr(), self.layer_in.data_ptr(), self.qkv.data_ptr(),
-                       self.logits.data_ptr(), self.self_stable.data_ptr(), self.row_sums.data_ptr())
+                       self.logits.data_ptr(), self.self_stable.data_ptr(), self.row_sums.data_ptr(),
+                       hm.data_ptr() if hm is not None else None)
+
+    def kv_headmajor(self, model: "LLaDAModel") -> torch.Tensor:
+        """The head-major K / V of every layer, rebuilt in place (stream-ordered) when qkv changed since."""
+        d = model.dims
+        L, T = int(self.qkv.shape[0]), self.seq
+        if self.qkv.shape[2] != d.q_dim + 2 * d.kv_dim or L != d.n_layers:
+            raise ValueError(f"kv_headmajor: cache qkv {tuple(self.qkv.shape)} does not match the model")
+        shape = (L, 2, d.n_kv_heads, T, d.head_dim)
+        if self.kv_hm is None or tuple(self.kv_hm.shape) != shape:
+            self.kv_hm = torch.empty(shape, dtype=torch.bfloat16, device=self.qkv.device)
+            self._kv_hm_at = -1
+        if self._kv_hm_at != self.version:
+            lib = _bind_late()
+            with torch.cuda.device(self.qkv.device):
+                _lib.check(lib.af_parent_kv_headmajor(C.byref(model._cdims), T, self.qkv.data_ptr(), self.kv_hm.data_ptr(),
+                                                      _lib.stream_ptr(self.qkv.device)), "af_parent_kv_headmajor")
+            self._kv_hm_at = self.version
+        return self.kv_hm
 
     def tensors(self) -> list[torch.Tensor]:
         return [self.tokens, self.layer_in, self.qkv, self.logits, self.self_stable, self.row_sums]
@@ -292,7 +320,7 @@ class FoldPlan:
         nbytes = _i64()
         _lib.check(self.lib.af_fold_workspace_bytes(C.byref(model._cmodel.dims), C.byref(self._cfg), C.byref(nbytes)))
         self.workspace = torch.zeros(int(nbytes.value), dtype=torch.uint8, device=model.device)
-        self._pstruct = parent.struct()
+        self._pstruct = parent.struct(model)
         plan = _vp()
         _lib.check(self.lib.af_fold_plan_create(C.byref(model._cmodel), C.byref(self._pstruct), C.byref(self._cfg),
                                                 self.workspace.data_ptr(), self.workspace.numel(), C.byref(plan)))
@@ -349,6 +377,8 @@ class FoldPlan:
         where the parent fails its own gate changed, so the launch sequence
         does); otherwise the plan, and any graph captured from it, stays valid.
         """
+        if self._pstruct.kv_headmajor:
+            self.parent.kv_headmajor(self.model)  # same buffer, rebuilt from the rewritten qkv
         fresh = self.parent.self_stable_at(self.layer_taus)
         if fresh is not self.self_stable:
             self.self_stable.copy_(fresh)
@@ -419,7 +449,7 @@ class FoldPlan:
         elif into is not self.parent and into.seq != self.T:
             raise ValueError(f"promote: destination length {into.seq} differs from {self.T}")
         toks, logits = self.last_run
-        dst = into.struct()
+        dst = into.struct(self.model)
         _lib.check(self.lib.af_fold_promote(self._plan, int(child), toks.data_ptr(), logits.data_ptr(), C.byref(dst),
                                             _lib.stream_ptr(toks.device)), "af_fold_promote")
         if self.tau != into.tau:
@@ -430,6 +460,8 @@ class FoldPlan:
             into.self_stable.copy_(SimilarityGate(tau=self.tau)(x, x).to(torch.uint8))
             into.tau = float(self.tau)
         into.contents_changed()  # its token ids and self-gate rows are the child's now
+        if dst.kv_headmajor:
+            into._kv_hm_at = into.version  # the promotion wrote the head-major rows too
         return into
 
     def capture(self, child_tokens: torch.Tensor, logits: torch.Tensor, scores: torch.Tensor | None = None
@@ -497,6 +529,10 @@ class FoldPlan:
 
 class LLaDAModel(nn.Module):
     """LLaDA/Dream-architecture weights + native dense and folded passes (CUDA only)."""
+
+    # Parent caches keep a head-major copy of their keys and values for the
+    # folded pass's attention (False: it reads them from the row-major qkv).
+    kv_headmajor: bool = True
 
     def __init__(self, dims: ModelDims, embed, layers: Sequence[LLaDABlock], final_norm, lm_head, max_pos: int = 4096,
                  lm_head_tiled: bool = False) -> None:
@@ -597,7 +633,10 @@ class LLaDAModel(nn.Module):
         s = int(status.item())
         if s:
             raise TimeoutError(f"dense pass: device status {s:#x}") if s & 1 else RuntimeError(f"dense pass: device status {s:#x}")
-        return ParentCache(tokens, layer_in, qkv, logits, self_stable, row_sums, float(tau))
+        pc = ParentCache(tokens, layer_in, qkv, logits, self_stable, row_sums, float(tau))
+        if self.kv_headmajor:
+            pc.kv_headmajor(self)
+        return pc
 
     def forward(self, tokens: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
         """Plain (unfolded) logits [B, T, V] for tokens [B, T]: one dense pass per row."""

@@ -216,7 +216,17 @@ typedef struct {
   const void* logits;           /* [T, vocab] bf16 */
   const uint8_t* self_stable;   /* [n_layers, T] gate(parent row, parent row) */
   const float* logit_row_sums;  /* [T] fp32 sums of each logits row */
+  /* Nullable: [n_layers, 2, n_kv_heads, T, head_dim] bf16, the K (0) and V (1)
+   * columns of qkv stored head-major (af_parent_kv_headmajor), so one head's
+   * block of keys is one contiguous run of memory. The folded pass reads the
+   * parent's keys and values from here when it is set, and promotions keep it
+   * in step with qkv. */
+  void* kv_headmajor;
 } af_parent_cache;
+
+/* Builds af_parent_cache.kv_headmajor from qkv ([n_layers, T, q_dim + 2 kv_dim]);
+ * stream-ordered. No counterpart in the reference (a layout of the cache). */
+int af_parent_kv_headmajor(const af_model_dims* dims, int64_t T, const void* qkv, void* kv_headmajor, void* stream);
 
 /* Workspace of af_dense_forward for T tokens. */
 int af_dense_workspace_bytes(const af_model_dims* dims, int64_t T, int64_t* bytes);
