@@ -153,35 +153,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     }
   }
   pdl_wait();
-  const int n_q = p.n_q_dev ? min(*p.n_q_dev, p.n_q_cap) : p.n_q_cap;
-  if (q0 >= n_q) {  // uniform over a cluster (its CTAs share blockIdx.x)
-    // Nothing to compute; TMA writes into this CTA's shared memory land before it exits.
-    if (tid == 0 && kv_tma) {
-      volatile int no_abort = 0;
-      mbar_wait(barK, 0, &no_abort);
-      mbar_wait(barV, 0, &no_abort);
-    }
-    __syncthreads();
-    return;
-  }
-  const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
-  if (n_fb < n_fb_all && tid == 0 && p.fchild) {
-    // The window holds every candidate of this tile's children iff the
-    // candidates just outside it belong to other children (the list is
-    // ordered by child); otherwise keys would be missed: flag it.
-    const int qa = q0, qb = min(q0 + kTQ, n_q) - 1;
-    const int before = fb0 * kTK - 1, after = (fb0 + n_fb) * kTK;
-    const bool miss = (before >= 0 && before < n_f && p.fchild[before] == p.fchild[qa]) ||
-                      (after < n_f && p.fchild[after] == p.fchild[qb]);
-    if (miss && p.status) atomicOr(p.status, AF_STATUS_CAPACITY);
-  }
-  if (warp == 0) tmem_alloc(smem_u32(tmem_slot), 512);
   const bool c_tma = p.cand_tma != 0;
   if (c_tma && tid == 0) {
     // Candidate-row mode: the query tile (rows q0..q0+127 of the buffer) and
-    // this CTA's candidate key blocks, as soon as their producer is done.
-    // Rows past the valid counts are masked below (queries are not written,
-    // keys get zero weight).
+    // this CTA's candidate key blocks, as soon as their producer is done (they
+    // do not depend on the valid counts: rows past them are masked below,
+    // queries are not written and keys get zero weight).
     uint32_t kbytes = kOpB, vbytes = 0;
     for (int j = 0; j < nbl; ++j)
       if (b_lo + j >= n_pb) {
@@ -206,6 +183,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
         tma_load_2d(sV + j * kOpB + hf * kTileB, &tmC, barCV, p.fv_col + kvh * 128 + 64 * hf, y);
     }
   }
+  // Every per-row value read from global memory is requested here, in one
+  // round trip with the valid counts: the query row's child and output row,
+  // and the child of each candidate key of this CTA's candidate blocks.
+  const int qi = q0 + r;
+  const int child_ld = (p.qchild && qi < p.n_q_cap) ? p.qchild[qi] : -1;
+  const int orow_ld = qi < p.n_q_cap ? (p.out_rows ? p.out_rows[qi] : qi) : -1;
+  int fch[kMaxBlk];
+#pragma unroll
+  for (int j = 0; j < kMaxBlk; ++j) {
+    fch[j] = -1;
+    const int b = b_lo + j;
+    if (j < nbl && b >= n_pb && tid < kTK) {
+      const int jj = (fb0 + b - n_pb) * kTK + tid;
+      fch[j] = jj < p.n_f_cap ? (p.fchild ? p.fchild[jj] : -1) : -2;
+    }
+  }
+  const int n_q = p.n_q_dev ? min(*p.n_q_dev, p.n_q_cap) : p.n_q_cap;
+  const int n_f = p.fk ? (p.n_f_dev ? min(*p.n_f_dev, p.n_f_cap) : p.n_f_cap) : 0;
+  if (q0 >= n_q) {  // uniform over a cluster (its CTAs share blockIdx.x)
+    // Nothing to compute; TMA writes into this CTA's shared memory land before it exits.
+    if (tid == 0) {
+      volatile int no_abort = 0;
+      if (kv_tma) {
+        mbar_wait(barK, 0, &no_abort);
+        mbar_wait(barV, 0, &no_abort);
+      }
+      if (c_tma) {
+        mbar_wait(barC, 0, &no_abort);
+        mbar_wait(barCV, 0, &no_abort);
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tmem_slot), 512);
 
   // ---- operands (cp.async): whatever is not loaded by TMA ----
   if (!c_tma)
@@ -219,7 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     const bool parent_blk = b < n_pb;
     if (!parent_blk && tid < kTK) {
       const int jj = (fb0 + b - n_pb) * kTK + tid;
-      sF[j * kTK + tid] = jj >= n_f ? -2 : (p.fchild ? p.fchild[jj] : -1);
+      int f = -1;
+#pragma unroll
+      for (int jx = 0; jx < kMaxBlk; ++jx)
+        if (jx == j) f = fch[jx];
+      sF[j * kTK + tid] = jj >= n_f ? -2 : f;
     }
     if ((parent_blk && kv_tma) || (!parent_blk && c_tma)) continue;
     const int r0 = (parent_blk ? b : fb0 + b - n_pb) * kTK;
@@ -260,20 +276,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
       }
     tc_commit(barS);  // also when nothing was issued, so the waits below end
   }
+  if (n_fb < n_fb_all && tid == 0 && p.fchild) {
+    // The window holds every candidate of this tile's children iff the
+    // candidates just outside it belong to other children (the list is
+    // ordered by child); otherwise keys would be missed: flag it.
+    const int qa = q0, qb = min(q0 + kTQ, n_q) - 1;
+    const int before = fb0 * kTK - 1, after = (fb0 + n_fb) * kTK;
+    const bool miss = (before >= 0 && before < n_f && p.fchild[before] == p.fchild[qa]) ||
+                      (after < n_f && p.fchild[after] == p.fchild[qb]);
+    if (miss && p.status) atomicOr(p.status, AF_STATUS_CAPACITY);
+  }
 
   // ---- masked softmax: row r, key columns c0..c0+31 of every block ----
-  const bool row_ok = q0 + r < n_q;
-  const int child = (p.qchild && row_ok) ? p.qchild[q0 + r] : -1;
-  if (nbl > 0) {
-    volatile int no_abort = 0;
-    if (!mbar_wait(barS, 0, &no_abort)) *fail = 1;
-  }
-  const bool s_bad = __syncthreads_or(*fail);  // also: S is complete, Q's tiles are free for `red`
-  tc_fence_after();
-  float m = -INFINITY, l = 0.f;
+  // The masks are built while S is computed.
+  const bool row_ok = qi < n_q;
+  const int child = row_ok ? child_ld : -1;
   uint32_t vm[kMaxBlk];  // valid keys among this thread's 32 columns of each block
-  const float sc = p.scale_log2;
-  if (!s_bad) {
+  {
 #pragma unroll
     for (int j = 0; j < kMaxBlk; ++j) {
       if (j >= nbl) break;
@@ -293,6 +312,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
       }
       vm[j] = v;
     }
+  }
+  if (nbl > 0) {
+    volatile int no_abort = 0;
+    if (!mbar_wait(barS, 0, &no_abort)) *fail = 1;
+  }
+  const bool s_bad = __syncthreads_or(*fail);  // also: S is complete, Q's tiles are free for `red`
+  tc_fence_after();
+  // Output row of query row `tid` for the split combine (Q's tiles are free now).
+  int* s_orow = reinterpret_cast<int*>(gb + kOffQ + 8 * kTQ * 4);
+  if (ns > 1 && cg == 0) s_orow[r] = row_ok ? orow_ld : -1;
+  float m = -INFINITY, l = 0.f;
+  const float sc = p.scale_log2;
+  if (!s_bad) {
     auto sweep1 = [&](int j, const uint32_t* sv) {
       const uint32_t v = vm[j];
 #pragma unroll
@@ -396,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     for (int i = 0; i < 32; ++i) o[i] = 0u;
   }
   if (ns == 1) {
-    const int orow = row_ok ? (p.out_rows ? p.out_rows[q0 + r] : q0 + r) : -1;
+    const int orow = row_ok ? orow_ld : -1;
     if (orow >= 0 && !bad) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t)orow * p.out_ld + h * 128 + c0);
@@ -462,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
           acc.w += f * v.w;
         }
       }
-      const int orow = q0 + rr < n_q ? (p.out_rows ? p.out_rows[q0 + rr] : q0 + rr) : -1;
+      const int orow = s_orow[rr];
       if (orow >= 0 && !bad) {
         const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
         uint2 w;

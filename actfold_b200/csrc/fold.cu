@@ -213,9 +213,12 @@ __global__ void __launch_bounds__(256) k_embed_rows(const __nv_bfloat16* embed, 
 }
 
 // Rows of the per-row kernels below are spread over one CTA of kRowThreads
-// threads (H <= 4096 gives each thread at most two 16-byte vectors), so a
-// few hundred packed rows still occupy every SM.
-constexpr int kRowThreads = 256;
+// threads (H <= 4096 gives each thread one 16-byte vector, H <= 8192 two), so
+// a few hundred packed rows still occupy every SM. These kernels sit between
+// the projections of every layer, where their latency is on the critical
+// path: 512 threads give each thread the fewest elements (measured on B200:
+// 256-thread CTAs spent ~4 us of dependent arithmetic per 4096-wide row).
+constexpr int kRowThreads = 512;
 using RowGroup = CtaRows<kRowThreads>;
 
 template <int NV, class Rows = WarpRows>
@@ -272,8 +275,10 @@ struct PartialRows {
 };
 
 template <int NV>
-__device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row, int nvec, int tid, uint4 (&v)[NV]) {
-  const int64_t rrow = pr.res_rows ? pr.res_rows[row] : row;
+__device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row, int64_t rrow, int nvec, int tid,
+                                                  uint4 (&v)[NV]) {
+  // rrow: the residual row of `row` (pr.res_rows[row], or row), read by the
+  // caller together with its other indices.
   const char* rp = reinterpret_cast<const char*>(pr.res + rrow * (int64_t)(nvec * 8));
   const float* pp = pr.part + (int64_t)row * (nvec * 8);
   float acc[NV][8];
@@ -357,13 +362,14 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat1
   pdl_trigger();
   pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
-  const int i = blockIdx.x;
+  const int i = blockIdx.x;  // < n_cap: the index arrays are read before the count is known
+  const int rrow = pr.part && pr.res_rows ? pr.res_rows[i] : i;
   const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
   if (i >= n) return;
   const int nvec = H / 8;
   uint4 v[NV];
   if (pr.part)
-    load_row_partials<NV>(pr, i, nvec, threadIdx.x, v);
+    load_row_partials<NV>(pr, i, rrow, nvec, threadIdx.x, v);
   else
     load_row<NV, kRowThreads>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, threadIdx.x, v);
   rmsnorm_regs<NV>(v, nvec, H, w, eps, reinterpret_cast<char*>(out + (int64_t)i * H), threadIdx.x, RowGroup{red});
@@ -395,10 +401,11 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
   pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
   const int tid = threadIdx.x;
-  const int r = blockIdx.x;
+  const int r = blockIdx.x;  // < m_cap: the candidate arrays are read together with the count
+  const int t = g.cand_pos[r], src = g.cand_src[r];
+  const int rrow = g.fresh_part.res_rows && src >= 0 ? g.fresh_part.res_rows[src] : src;
   const int n = min(*g.n_cand, g.m_cap);
   if (r >= n) return;
-  const int t = g.cand_pos[r], src = g.cand_src[r];
   const int nvec = g.H / 8;
   const RowGroup rows{red};
   const char* prow = reinterpret_cast<const char*>(g.p_in + (int64_t)t * g.H);
@@ -406,10 +413,12 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
   uint4 hv[NV], pv[NV];
   load_row<NV, kRowThreads>(prow, nvec, tid, pv);
   if (src >= 0 && g.fresh_part.part)
-    load_row_partials<NV>(g.fresh_part, src, nvec, tid, hv);  // also stores the finished row into x_fresh
+    load_row_partials<NV>(g.fresh_part, src, rrow, nvec, tid, hv);  // also stores the finished row into x_fresh
   else
     load_row<NV, kRowThreads>(hrow, nvec, tid, hv);
-  const GateOut o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, tid, rows);
+  GateOut o;
+  if constexpr (METRIC == AF_METRIC_COSINE) o = gate_regs_bf16_cos<NV>(hv, pv, nvec, g.k, tid, rows);
+  else o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, tid, rows);
   if (tid == 0) g.stable[r] = g.force_div ? 0 : o.stable;
   char* xc = reinterpret_cast<char*>(g.xc + (int64_t)r * g.H);
 #pragma unroll
@@ -549,7 +558,7 @@ __global__ void __launch_bounds__(kRowThreads) k_self_gate(const __nv_bfloat16* 
   const int nvec = H / 8;
   uint4 v[NV];
   load_row<NV, kRowThreads>(reinterpret_cast<const char*>(x + (int64_t)t * H), nvec, threadIdx.x, v);
-  const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, H, k, threadIdx.x, RowGroup{red});
+  const GateOut o = gate_regs_bf16_cos<NV>(v, v, nvec, k, threadIdx.x, RowGroup{red});
   if (threadIdx.x == 0) self_stable[t] = o.stable;
 }
 
@@ -626,7 +635,7 @@ __global__ void __launch_bounds__(kRowThreads) k_promote_rows(const PromoteArgs 
       stg16(reinterpret_cast<char*>(a.kv_hm + off), ldg16(qs + 2 * (int64_t)a.q_cols + 16 * (int64_t)jj));
     }
   }
-  const GateOut o = gate_regs<AF_DTYPE_BF16, AF_METRIC_COSINE, NV>(v, v, nvec, a.H, a.k, threadIdx.x, RowGroup{red});
+  const GateOut o = gate_regs_bf16_cos<NV>(v, v, nvec, a.k, threadIdx.x, RowGroup{red});
   if (threadIdx.x == 0) a.self_stable[(int64_t)l * a.T + t] = o.stable;
 }
 
@@ -736,7 +745,7 @@ static bool pass_pdl() {
 #define AF_LAUNCH(KERNEL, GRID, BLOCK, SMEM, STREAM, ...) \
   launch_ex(KERNEL, dim3(GRID), dim3(BLOCK), (size_t)(SMEM), STREAM, pass_pdl(), dim3(1, 1, 1), __VA_ARGS__)
 
-// Per-row kernels on one CTA of kRowThreads threads per row: H <= 4096.
+// Per-row kernels on one CTA of kRowThreads threads per row: H <= 8192.
 #define AF_DISPATCH_ROWS(H, KERNEL, ROWS, STREAM, ...)                                   \
   do {                                                                                   \
     if ((H) / 8 <= kRowThreads) AF_LAUNCH(KERNEL<1>, (unsigned)(ROWS), kRowThreads, 0, STREAM, __VA_ARGS__); \
@@ -952,11 +961,23 @@ struct FoldWs {
   // Split-K partials of the O and down GEMMs ([S][m_cap][H] fp32, S = their
   // k-splits), finished by the next row kernel; null when neither splits.
   float* part;
-  int split_o, split_down;
-  int part_o, part_down;  // 1: that GEMM leaves its partials in `part`
+  int split_o, split_down, split_qkv;
+  int part_o, part_down, part_qkv;  // 1: that GEMM leaves its partials in `part`
   unsigned* bits0;        // [C, bits_ld] divergent rows of layer 0 (the early logits fill)
   uint8_t* later;         // [T] positions a layer >= 1 re-examines (the parent fails its own gate there)
 };
+
+// k-splits of the QKV projection when it leaves partials (tuning override
+// ACTFOLD_QKV_SPLITS: 0 for a cluster reduction in its own epilogue, 1 for
+// no split; else the partial-launch heuristic).
+static int qkv_partial_splits(const Sizes& z, int m_cap) {
+  static const int env = [] {
+    const char* e = getenv("ACTFOLD_QKV_SPLITS");
+    return e ? atoi(e) : -1;
+  }();
+  if (env >= 0) return std::min(env, 16);
+  return gemm_splits(z.qkv, z.H, m_cap, true);
+}
 
 static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool partial_always) {
   FoldWs w;
@@ -998,8 +1019,14 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool 
   w.part_down = partial_always || (split_d && !partials_off());
   w.split_o = w.part_o ? gemm_splits(z.H, z.q, m_cap, true) : 1;
   w.split_down = w.part_down ? gemm_splits(z.H, z.FF, m_cap, true) : 1;
+  // The QKV projection leaves its k-splits as partials too, finished (summed,
+  // rotated, stored) by k_gemm_finish before attention: a cluster reduction
+  // in its own epilogue costs more than that launch.
+  w.part_qkv = gemm_splits(z.qkv, z.H, m_cap) > 1 && !partials_off() && qkv_partial_splits(z, m_cap) > 1;
+  w.split_qkv = w.part_qkv ? qkv_partial_splits(z, m_cap) : 1;
   const int S = std::max(w.split_o, w.split_down);
-  w.part = (w.part_o || w.part_down) ? b.take<float>((int64_t)S * m_cap * z.H) : nullptr;
+  const int64_t per_row = std::max((int64_t)S * z.H, w.part_qkv ? (int64_t)w.split_qkv * z.qkv : 0);
+  w.part = (w.part_o || w.part_down || w.part_qkv) ? b.take<float>(per_row * m_cap) : nullptr;
   return w;
 }
 
@@ -1315,7 +1342,14 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     c.rope_cols = z.q + z.kv;
     c.tmap_w = &p->tm_qkv[l];
     c.tmap_x = &p->tx_A;
+    if (w.part_qkv) {
+      c.partial_out = w.part;
+      c.splits = w.split_qkv;
+    } else if (qkv_partial_splits(z, M) == 1) {
+      c.splits = 1;  // one CTA per weight tile, RoPE in its own epilogue
+    }
     AF_TIMED(FK_QKV, if ((st = gemm_run(c, s))) return st);
+    if (w.part_qkv) AF_TIMED(FK_QKV, if ((st = gemm_finish_run(c, w.split_qkv, s))) return st);
     if (fork_fill && ((l == 0 && early) || last)) {
       // After layer 0's compaction (a side task of this GEMM) the rows stable
       // for good are known; after the last layer's, every final-stable row is.

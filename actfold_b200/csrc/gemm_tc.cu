@@ -549,6 +549,51 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   }
 }
 
+// Rows finished from split-K partials: the epilogue of k_gemm_tc (RoPE,
+// residual or plain store) applied to the sum of the splits' fp32 partial
+// tiles, added in split order 0, 1, ... like the cluster reduction. One
+// thread per unit (row m, chunk pair c / c + 8 of a 128-column tile): 32 rows
+// of one tile per CTA. The partials and the row's indices are requested
+// together with the valid count (m < m_cap keeps every read in bounds).
+__global__ void __launch_bounds__(256) k_gemm_finish(const GemmDev p) {
+  pdl_trigger();
+  pdl_wait();
+  const int n0 = blockIdx.x * kTileN;
+  const int m = blockIdx.y * 32 + (int)(threadIdx.x >> 3), c = threadIdx.x & 7;
+  if (m >= p.m_cap) return;
+  const int pos = p.epi == EPI_ROPE ? p.positions[m] : 0;
+  const int orow = p.out_rows ? p.out_rows[m] : m;
+  const int rrow = p.epi == EPI_RESIDUAL && p.res_rows ? p.res_rows[m] : m;
+  const int M = p.m_dev ? min(*p.m_dev, p.m_cap) : p.m_cap;
+  const float* src = p.partial + (int64_t)m * p.n + n0 + 8 * c;
+  const int64_t split_stride = (int64_t)p.m_cap * p.n;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s0 = 0; s0 < p.splits; s0 += 4) {
+    float4 v[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (s0 + q < p.splits) {
+        const float4* t = reinterpret_cast<const float4*>(src + (s0 + q) * split_stride);
+        v[q][0] = t[0];
+        v[q][1] = t[1];
+        v[q][2] = t[16];
+        v[q][3] = t[17];
+      }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (s0 + q < p.splits) {
+        a[0] += v[q][0].x; a[1] += v[q][0].y; a[2] += v[q][0].z; a[3] += v[q][0].w;
+        a[4] += v[q][1].x; a[5] += v[q][1].y; a[6] += v[q][1].z; a[7] += v[q][1].w;
+        b[0] += v[q][2].x; b[1] += v[q][2].y; b[2] += v[q][2].z; b[3] += v[q][2].w;
+        b[4] += v[q][3].x; b[5] += v[q][3].y; b[6] += v[q][3].z; b[7] += v[q][3].w;
+      }
+  }
+  if (m >= M) return;
+  EpiOperands o;
+  epi_operands(p, n0, c, rrow, pos, o);
+  epi_pair(p, n0, c, orow, o, a, b);
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -770,6 +815,41 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
                             c.pdl != 0, dim3(1, partial ? 1 : g.splits, 1), *pw, *px, d);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_tc launch: ") + cudaGetErrorString(e));
   return check_launch("gemm_tc");
+}
+
+int gemm_finish_run(const GemmCall& c, int splits, cudaStream_t stream) {
+  AF_REQUIRE(c.partial_out && c.out && c.status, "gemm_finish: null pointer");
+  AF_REQUIRE(c.n > 0 && c.n % kTileN == 0 && c.m_cap > 0, "gemm_finish: bad shape");
+  AF_REQUIRE(splits >= 1 && splits <= kMaxPartialSplits, "gemm_finish: bad split count");
+  AF_REQUIRE(c.epi >= EPI_STORE && c.epi <= EPI_ROPE && c.epi != EPI_SWIGLU && !c.row_sums,
+             "gemm_finish: store, residual or RoPE epilogue without row sums");
+  AF_REQUIRE(c.epi != EPI_RESIDUAL || c.res, "gemm_finish: residual epilogue needs res");
+  AF_REQUIRE(c.epi != EPI_ROPE || (c.rope_cos && c.rope_sin && c.positions && c.head_dim == 128 && c.rope_cols % 128 == 0),
+             "gemm_finish: rope epilogue needs cos/sin/positions and head_dim 128");
+  GemmDev d{};
+  d.n = c.n;
+  d.k = c.k;
+  d.m_cap = c.m_cap;
+  d.m_dev = c.m_dev;
+  d.splits = splits;
+  d.epi = c.epi;
+  d.out = static_cast<__nv_bfloat16*>(c.out);
+  d.ldo = c.ldo;
+  d.out_rows = c.out_rows;
+  d.res = static_cast<const __nv_bfloat16*>(c.res);
+  d.ldr = c.ldr;
+  d.res_rows = c.res_rows;
+  d.rope_cos = c.rope_cos;
+  d.rope_sin = c.rope_sin;
+  d.positions = c.positions;
+  d.rope_cols = c.rope_cols;
+  d.half_dim = c.head_dim / 2;
+  d.status = c.status;
+  d.partial = c.partial_out;
+  cudaError_t e = launch_ex(k_gemm_finish, dim3(c.n / kTileN, (c.m_cap + 31) / 32, 1), dim3(256, 1, 1), 0, stream,
+                            c.pdl != 0, dim3(1, 1, 1), d);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_finish launch: ") + cudaGetErrorString(e));
+  return check_launch("gemm_finish");
 }
 
 }  // namespace af

@@ -58,5 +58,8 @@ int gemm_splits(int n, int k, int m_cap, bool partial = false);
 int gemm_ntok(int m_cap);
 // Launch (stream-ordered, no synchronisation).
 int gemm_run(const GemmCall& c, cudaStream_t stream);
+// The epilogue of a launch that left `splits` partials (c.partial_out):
+// sums them in split order and applies c's store / residual / RoPE epilogue.
+int gemm_finish_run(const GemmCall& c, int splits, cudaStream_t stream);
 
 }  // namespace af

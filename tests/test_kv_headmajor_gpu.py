@@ -7,7 +7,8 @@ has, so:
 
 * the copy equals the K / V columns of qkv exactly, after the parent pass and
   after a promotion rewrote rows of the cache;
-* the folded pass gives bit-identical logits, scores and stable masks whether
+* the folded pass gives bit-identical logits and stable masks (and scores
+  equal up to the order of their fp32 atomic row sums) whether
   attention reads the head-major copy or the row-major qkv (LLaDA tiny,
   Dream tiny with GQA, and 2 layers of the LLaDA-8B shapes at 8 children x
   1024 tokens).
@@ -64,8 +65,11 @@ def test_folded_pass_is_the_same_with_either_layout(name):
         del plan
     m.kv_headmajor = True
     m._plans = {}
-    for a, b in zip(out[True], out[False]):
-        assert torch.equal(a, b)
+    # Logits and masks bit for bit; scores are sums of fp32 row sums that the
+    # LM-head epilogue adds with atomics, so only their last bits may differ.
+    assert torch.equal(out[True][0], out[False][0])
+    assert torch.equal(out[True][2], out[False][2])
+    torch.testing.assert_close(out[True][1], out[False][1], rtol=1e-5, atol=0)
 
 
 def test_promotion_keeps_the_copy_current():
