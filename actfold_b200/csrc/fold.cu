@@ -1137,8 +1137,8 @@ struct FoldPlan {
 
 static int build_maps(FoldPlan* p) {
   const Sizes z = sizes_of(p->model.dims);
-  const int nt = gemm_ntok(p->m_cap);
-  p->ntok = nt;
+  const int nt = gemm_xbox(gemm_ntok(p->m_cap));  // token rows per box of the activation maps
+  p->ntok = gemm_ntok(p->m_cap);
   int st;
   p->tm_qkv.resize(z.L);
   p->tm_o.resize(z.L);

@@ -60,6 +60,7 @@ struct GemmDev {
   int has_side;  // CTA (0, 0, 0) runs `side` (the layer compaction) in its epilogue warps
   CompactArgs side;
   float* partial;  // split-K partials to global memory, reduced by the consumer (no cluster)
+  int xbox;        // token rows per TMA box (ntok or ntok / 2)
 };
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -195,6 +196,15 @@ __device__ __forceinline__ void epi_pair(const GemmDev& p, int n0, int c, int64_
   }
 }
 
+// kPair: the two CTAs of a 2-CTA cluster (adjacent weight tiles, same token
+// tile and k-range) run one cta_group::2 MMA of M = 256: each streams its own
+// 128 weight rows and HALF of the token tile, so a pair moves 3/4 of the
+// shared-memory bytes two single CTAs would for the same MMA work (the token
+// tile is as large as the weight tile at ~128 tokens). CTA 0 of the pair
+// issues the MMAs; every stage's TMA loads, from both CTAs, complete on CTA
+// 0's `full` barrier, and CTA 0's MMA commits arrive on both CTAs' `empty` and
+// accumulator barriers.
+template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmW,
                                                           const __grid_constant__ CUtensorMap tmX, const GemmDev p) {
   extern __shared__ uint8_t smem_raw[];
@@ -203,14 +213,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   // Grid x enumerates (weight tile, token tile) with the token tile fastest:
   // the CTAs that stream the same weight tile for different token tiles are
   // launched next to each other, so they run together and the second reads the
-  // tile from L2 instead of HBM.
-  const int mtile = blockIdx.x % p.m_tiles, wtile = blockIdx.x / p.m_tiles;
+  // tile from L2 instead of HBM. Pairs: x = 2 (weight pair, token tile) + rank.
+  const int prank = kPair ? (int)(blockIdx.x & 1) : 0;
+  const int xq = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int mtile = xq % p.m_tiles, wtile = kPair ? 2 * (xq / p.m_tiles) + prank : xq / p.m_tiles;
+  const bool leader = prank == 0;
   const int m0 = mtile * p.ntok;
   const int n0 = wtile * kTileN;
   const int kb0 = blockIdx.y * p.kb_per_split;
   const int nkb = min(p.kb_per_split, p.nkb - kb0);
   const int S = p.stages;
-  const uint32_t w_bytes = kTileN * kBlockK * 2, x_bytes = p.ntok * kBlockK * 2;
+  // This CTA's token rows per stage: the whole tile, or its half of it in a pair.
+  const int xrows = kPair ? p.xbox : p.ntok;
+  const uint32_t w_bytes = kTileN * kBlockK * 2, x_bytes = xrows * kBlockK * 2;
   const uint32_t stage_bytes = w_bytes + x_bytes;
 
   // 1024-byte aligned ring, then barriers and flags.
@@ -223,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 16);
   volatile int* issued_slot = reinterpret_cast<volatile int*>(gbase + S * stage_bytes + 16 * S + 24);
   const uint32_t recv_bar = bars + 16 * S + 32;  // split-K push: this CTA's receive slots are full
+  const uint32_t alloc_bar = bars + 16 * S + 40;  // pair: CTA 1's TMEM is allocated (CTA 0's barrier)
   // Per-token epilogue metadata (output row, residual row, RoPE position).
   int* s_orow = reinterpret_cast<int*>(gbase + S * stage_bytes + 16 * S + 64);
   int* s_rrow = s_orow + p.ntok;
@@ -231,22 +247,48 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const bool side_cta = p.has_side && blockIdx.x == 0 && blockIdx.y == 0;
 
   // Tiles start at different k-blocks (rotation by tile index) so concurrent CTAs
-  // do not all read the same activation lines at the same time.
-  const int rot = wtile % nkb;
+  // do not all read the same activation lines at the same time (a pair's two
+  // CTAs stream the same k-block at every step: rotation by pair index).
+  const int rot = (kPair ? wtile >> 1 : wtile) % nkb;
   auto kb_of = [&](int i) {
     int kb = i + rot;
     if (kb >= nkb) kb -= nkb;
     return kb + kb0;
   };
+  // Loads complete on `bar`: this CTA's barrier, or in a pair CTA 0's (a cluster address).
   auto load_w = [&](int i, uint32_t dst, uint32_t bar) {
-    if (p.w_tiled)
-      tma_load_3d(dst, &tmW, bar, 0, 0, wtile * p.nkb + kb_of(i));
-    else
-      tma_load_2d(dst, &tmW, bar, kb_of(i) * kBlockK, n0);
+    if constexpr (kPair) {
+      if (p.w_tiled)
+        tma_load_3d_pair(dst, &tmW, bar, 0, 0, wtile * p.nkb + kb_of(i));
+      else
+        tma_load_2d_pair(dst, &tmW, bar, kb_of(i) * kBlockK, n0);
+    } else {
+      if (p.w_tiled)
+        tma_load_3d(dst, &tmW, bar, 0, 0, wtile * p.nkb + kb_of(i));
+      else
+        tma_load_2d(dst, &tmW, bar, kb_of(i) * kBlockK, n0);
+    }
   };
+  auto load_x = [&](int i, uint32_t dst, uint32_t bar) {
+    if constexpr (kPair) {
+      tma_load_2d_pair(dst, &tmX, bar, kb_of(i) * kBlockK, m0 + prank * p.xbox);
+    } else {
+      for (int h = 0; h < p.ntok; h += p.xbox)
+        tma_load_2d(dst + (uint32_t)h * (kBlockK * 2), &tmX, bar, kb_of(i) * kBlockK, m0 + h);
+    }
+  };
+  // The barrier this CTA's loads of stage s complete on, and the bytes a
+  // stage's phase expects (both CTAs' in a pair; armed by CTA 0 only).
+  auto full_of = [&](int s) -> uint32_t {
+    const uint32_t b = bars + 8u * (uint32_t)s;
+    return kPair ? cluster_map(b, 0) : b;
+  };
+  const uint32_t w_expect = kPair ? 2 * w_bytes : w_bytes, x_expect = kPair ? 2 * x_bytes : x_bytes;
   // Stages whose weight tile is loaded before the dependency wait.
   const int npre = min(S, nkb);
 
+  uint32_t ncols = 32;
+  while ((int)ncols < p.ntok) ncols <<= 1;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
@@ -254,19 +296,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
     mbar_init(accb, 1);
     if (p.push) mbar_init(recv_bar, 1);
+    if (kPair) mbar_init(alloc_bar, 1);
     *abort_flag = 0;
     *issued_slot = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
+  }
+  // A pair's barriers exist in both CTAs before any load completes on CTA 0's.
+  if constexpr (kPair) cluster_sync_all();
+  if (threadIdx.x == 0) {
     // Weights never depend on the preceding kernel: the first ring stages are
     // filled with weight tiles, and the next k-blocks pulled into L2, while
     // that kernel may still be running. Each of these stages expects its
     // weight bytes now and is armed (arrive + activation bytes) after the wait,
     // so it cannot complete before its activation tile has landed.
     for (int i = 0; i < npre; ++i) {
-      mbar_expect_tx(full0 + 8 * i, w_bytes);
-      load_w(i, base + i * stage_bytes, full0 + 8 * i);
+      if (leader) mbar_expect_tx(full0 + 8 * i, w_expect);
+      load_w(i, base + i * stage_bytes, full_of(i));
     }
     for (int i = npre; i < min(nkb, 2 * S); ++i) {
       if (p.w_tiled)
@@ -281,26 +328,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
     M = p.m_cap;
   }
-  if (m0 >= M) {  // uniform over a cluster (all its CTAs share blockIdx.x)
+  if (m0 >= M) {  // uniform over a cluster (all its CTAs share the token tile)
     // No tokens for this tile (none at all for CTA (0, 0, 0)): the side task
     // still runs, with every thread of the CTA.
     if (side_cta) compact_rows<kThreads>(p.side, s_scan, threadIdx.x, 1);
-    // The early weight loads land before the CTA exits.
-    if (threadIdx.x == 0) {
+    // The early weight loads land before the CTA exits (a pair's on CTA 0's
+    // barriers: CTA 1 leaves after CTA 0 has seen them land).
+    if (threadIdx.x == 0 && leader) {
       volatile int no_abort = 0;
       for (int i = 0; i < npre; ++i) {
         mbar_arrive(full0 + 8 * i);
         mbar_wait(full0 + 8 * i, 0, &no_abort);
       }
     }
+    if constexpr (kPair) {
+      __syncwarp();
+      cluster_sync_all();
+    }
     return;
   }
   const int Mv = min(p.ntok, M - m0);
 
-  uint32_t ncols = 32;
-  while ((int)ncols < p.ntok) ncols <<= 1;
-
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), ncols);
+  if (warp == 1) {
+    if constexpr (kPair) {
+      // CTA 0's MMAs write this CTA's TMEM: CTA 1 reports its allocation.
+      tmem_alloc_pair(smem_u32(tmem_slot), ncols);
+      if (!leader && lane == 0) {
+        tc_fence_before();
+        mbar_arrive_cluster(cluster_map(alloc_bar, 0));
+      }
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), ncols);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -316,23 +376,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       const uint32_t ph = (i / S) & 1;
       const uint32_t st = base + s * stage_bytes;
       if (i < npre) {
-        mbar_arrive_expect_tx(full0 + 8 * s, x_bytes);  // weight tile already requested
+        if (leader) mbar_arrive_expect_tx(full0 + 8 * s, x_expect);  // weight tile already requested
       } else {
         if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) {
           atomicOr(p.status, AF_STATUS_TIMEOUT);
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(full0 + 8 * s, stage_bytes);
-        load_w(i, st, full0 + 8 * s);
+        if (leader) mbar_arrive_expect_tx(full0 + 8 * s, w_expect + x_expect);
+        load_w(i, st, full_of(s));
       }
-      tma_load_2d(st + w_bytes, &tmX, full0 + 8 * s, kb_of(i) * kBlockK, m0);
+      load_x(i, st + w_bytes, full_of(s));
     }
     *issued_slot = i;
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1 && lane == 0 && leader) {
     // ---------------- MMA issuer ----------------
-    const uint32_t idesc = idesc_bf16(kTileN, p.ntok);
-    for (int i = 0; i < nkb; ++i) {
+    const uint32_t idesc = idesc_bf16(kPair ? 2 * kTileN : kTileN, p.ntok);
+    bool ready = true;
+    if constexpr (kPair) {
+      ready = mbar_wait(alloc_bar, 0, abort_flag);
+      if (!ready) {
+        atomicOr(p.status, AF_STATUS_TIMEOUT);
+        *abort_flag = 1;
+      }
+      tc_fence_after();
+    }
+    for (int i = 0; i < nkb && ready; ++i) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1;
       if (!mbar_wait(full0 + 8 * s, ph, abort_flag)) {
@@ -343,12 +412,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       tc_fence_after();
       const uint32_t st = base + s * stage_bytes;
       const uint64_t adesc = sw128_desc(st), bdesc = sw128_desc(st + w_bytes);
+      if constexpr (kPair) {
 #pragma unroll
-      for (int kk = 0; kk < kBlockK / 16; ++kk)
-        tc_mma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
-      tc_commit(empty0 + 8 * s);
+        for (int kk = 0; kk < kBlockK / 16; ++kk)
+          tc_mma_bf16_pair(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        tc_commit_pair_both(empty0 + 8 * s);
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < kBlockK / 16; ++kk)
+          tc_mma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        tc_commit(empty0 + 8 * s);
+      }
     }
-    tc_commit(accb);
+    if constexpr (kPair) {
+      tc_commit_pair_both(accb);
+    } else {
+      tc_commit(accb);
+    }
   } else if (warp >= 2) {
     // ---------------- TMEM -> shared memory (128 threads, one tile row each) ----------------
     const int q = warp & 3;
@@ -536,16 +616,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     cluster_sync_all();
   }
 
-  if (threadIdx.x == 0 && *abort_flag) {
-    // Drain TMA loads that may still be in flight into the ring (bounded).
+  if (threadIdx.x == 0 && leader && *abort_flag) {
+    // Drain TMA loads that may still be in flight into the ring (bounded; a
+    // pair's loads all complete on CTA 0's barriers).
     const int issued = *issued_slot;
     volatile int no_abort = 0;
     for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(full0 + 8 * (i % S), (i / S) & 1, &no_abort);
   }
   __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, ncols);
+  if constexpr (kPair) {
+    // Neither CTA leaves while the other may still signal its barriers or
+    // read its shared memory (CTA 0's MMAs; CTA 1's loads onto CTA 0's barriers).
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, ncols);
+    }
+  } else {
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, ncols);
+    }
   }
 }
 
@@ -667,9 +759,21 @@ int gemm_ntok(int m_cap) {
   return nt < 16 ? 16 : nt;
 }
 
+int gemm_xbox(int ntok) { return ntok % 32 == 0 ? ntok / 2 : ntok; }
+
+// Paired-CTA launches (tuning override ACTFOLD_GEMM_PAIR=0 keeps single CTAs).
+static bool pair_off() {
+  static const bool off = [] {
+    const char* e = getenv("ACTFOLD_GEMM_PAIR");
+    return e && e[0] == '0';
+  }();
+  return off;
+}
+
 struct GemmShape {
   int ntok, m_tiles, n_tiles, nkb, splits, kb_per, stages, smem;
   int push;  // split-K partials pushed into the owners' shared memory (bulk copies)
+  int pair;  // CTA pairs (cta_group::2): adjacent weight tiles share one M = 256 MMA
 };
 
 // Tuning override of the k-splits of launches that leave partials (0: the heuristic).
@@ -687,7 +791,6 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   g.m_tiles = (m_cap + g.ntok - 1) / g.ntok;
   g.n_tiles = n / kTileN;
   g.nkb = k / kBlockK;
-  const int stage = kTileN * kBlockK * 2 + g.ntok * kBlockK * 2;
   static const int env_stages = [] {
     const char* e = getenv("ACTFOLD_GEMM_STAGES");  // tuning override of the ring depth
     return e ? atoi(e) : 0;
@@ -708,6 +811,11 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   if (!partial) splits = std::min(splits, kMaxSplits);
   g.kb_per = (g.nkb + splits - 1) / splits;
   g.splits = (g.nkb + g.kb_per - 1) / g.kb_per;
+  // CTA pairs need an even number of weight tiles, a token tile that halves
+  // into 16-row multiples, and no exchange between split CTAs (their cluster
+  // is the pair).
+  g.pair = !pair_off() && g.n_tiles % 2 == 0 && g.ntok % 32 == 0 && (g.splits == 1 || partial) ? 1 : 0;
+  const int stage = kTileN * kBlockK * 2 + (g.pair ? g.ntok / 2 : g.ntok) * kBlockK * 2;
   // A CTA streams at most (bytes its ring keeps in flight) / (load latency):
   // a launch whose CTAs all fit one per SM and stream long k-ranges (the down
   // projection) gets the deepest ring that fits; otherwise ~100 KB rings let
@@ -760,6 +868,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   GemmShape g = plan_shape(c.n, c.k, c.m_cap, c.splits, c.row_sums != nullptr, partial);
   AF_REQUIRE(!partial || (reinterpret_cast<uintptr_t>(c.partial_out) & 15u) == 0, "gemm: partial_out must be 16-byte aligned");
   if (partial) g.push = 0;  // no exchange between the splits: no receive slots in shared memory
+  AF_REQUIRE(!g.pair || g.splits == 1 || partial, "gemm: CTA pairs cannot exchange split-K partials");
   AF_REQUIRE(g.smem <= 227 * 1024, "gemm: shared memory budget exceeded");
 
   CUtensorMap tw, tx;
@@ -771,7 +880,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
     pw = &tw;
   }
   if (!px) {
-    int st = make_tmap_bf16(&tx, c.x, c.m_cap, c.k, c.ldx, g.ntok);
+    int st = make_tmap_bf16(&tx, c.x, c.m_cap, c.k, c.ldx, gemm_xbox(g.ntok));
     if (st) return st;
     px = &tx;
   }
@@ -806,13 +915,19 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   d.has_side = c.has_side;
   d.side = c.side;
   d.partial = partial ? c.partial_out : nullptr;
+  d.xbox = gemm_xbox(g.ntok);
 
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  cudaError_t e = launch_ex(k_gemm_tc, dim3(g.n_tiles * g.m_tiles, g.splits, 1), dim3(kThreads, 1, 1), (size_t)g.smem, stream,
-                            c.pdl != 0, dim3(1, partial ? 1 : g.splits, 1), *pw, *px, d);
+  // Tensor maps built elsewhere (c.tmap_x) use box rows gemm_xbox(ntok).
+  cudaError_t e =
+      g.pair ? launch_ex(k_gemm_tc<true>, dim3(g.n_tiles * g.m_tiles, g.splits, 1), dim3(kThreads, 1, 1), (size_t)g.smem,
+                         stream, c.pdl != 0, dim3(2, 1, 1), *pw, *px, d)
+             : launch_ex(k_gemm_tc<false>, dim3(g.n_tiles * g.m_tiles, g.splits, 1), dim3(kThreads, 1, 1), (size_t)g.smem,
+                         stream, c.pdl != 0, dim3(1, partial ? 1 : g.splits, 1), *pw, *px, d);
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_tc launch: ") + cudaGetErrorString(e));
   return check_launch("gemm_tc");
 }

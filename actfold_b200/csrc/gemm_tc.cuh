@@ -56,6 +56,9 @@ int gemm_splits(int n, int k, int m_cap, bool partial = false);
 
 // Token-tile width the kernel uses for a given row capacity.
 int gemm_ntok(int m_cap);
+// Token rows per TMA box of the activation operand: tensor maps passed in
+// GemmCall::tmap_x must be built with this box height for gemm_ntok(m_cap).
+int gemm_xbox(int ntok);
 // Launch (stream-ordered, no synchronisation).
 int gemm_run(const GemmCall& c, cudaStream_t stream);
 // The epilogue of a launch that left `splits` partials (c.partial_out):
