@@ -41,8 +41,8 @@ constexpr int kOffQ = 0;
 constexpr int kOffKP = kOffQ + kOpB;              // K_j, overwritten by P_j
 constexpr int kOffV = kOffKP + kMaxBlk * kOpB;
 constexpr int kOffF = kOffV + kMaxBlk * kOpB;      // child of each candidate key [3][128]
-constexpr int kOffBar = kOffF + kMaxBlk * kTK * 4;  // barS, barO, TMEM slot, fail flag, barK, barV
-constexpr int kSmemTc = kOffBar + 64 + 1024;        // + alignment slack
+constexpr int kOffBar = kOffF + kMaxBlk * kTK * 4;  // barS, barO, TMEM slot, fail flag, barK, barV, barC, barCV, barX
+constexpr int kSmemTc = kOffBar + 72 + 1024;        // + alignment slack
 
 // Byte offset of 16-byte chunk `ch` (0..7) of row `row` in a swizzled tile.
 __device__ __forceinline__ uint32_t sw_off(int row, int ch) { return (uint32_t)(row * 128 + ((ch ^ (row & 7)) << 4)); }
@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
   const uint32_t barS = base + kOffBar, barO = barS + 8, barK = barS + 32, barV = barS + 40;
   const uint32_t barC = barS + 48;   // candidate-row mode: query tile and candidate key blocks by TMA
   const uint32_t barCV = barS + 56;  // candidate-row mode: candidate value blocks by TMA
+  const uint32_t barX = barS + 64;   // key splits: the other splits' partial rows of this CTA's share have landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gb + kOffBar + 16);
   volatile int* fail = reinterpret_cast<volatile int*>(gb + kOffBar + 24);
 
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
     mbar_init(barV, 1);
     mbar_init(barC, 1);
     mbar_init(barCV, 1);
+    mbar_init(barX, 1);
     *fail = 0;
     fence_barrier_init();
     if (kv_tma) {
@@ -443,38 +445,55 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
       }
     }
   } else {
-    // Push: the V region of CTA k (idle once every CTA's P.V is done) receives, from every split s,
-    // the partial rows k owns: O rows [s][rows_per][kPoLd] f32, then (m, l)
-    // [s][rows_per]. Each thread stores its own row's 32 columns straight into
-    // the owner's shared memory (posted DSMEM stores, no round trips); after
-    // one cluster barrier every owner combines from its own shared memory.
-    constexpr int kPoLd = 132;  // padded row: conflict-free 16-byte accesses
+    // Each CTA stages its partial rows (O | m | l, fp32, padded rows) in its
+    // idle P region, then one thread sends CTA k the rows k owns with a bulk
+    // copy into k's idle V region (slot per source split), completing on k's
+    // barX. Owners combine from their own shared memory; a last cluster
+    // barrier keeps every CTA alive until the copies out of it are done.
+    constexpr int kPoLd = 132;  // padded row: 128 values, m, l, 2 spare; conflict-free 16-byte accesses
+    constexpr uint32_t kRowB = kPoLd * 4;
     const int rows_per = (kTQ + ns - 1) / ns;
-    float* po = reinterpret_cast<float*>(gb + kOffV);
-    float2* pml = reinterpret_cast<float2*>(gb + kOffV + ns * rows_per * kPoLd * 4);
-    const uint32_t po_s = smem_u32(po), pml_s = smem_u32(pml);
-    cluster_sync_all();  // every CTA's P.V is done: the V regions are free to receive
+    float* stg = reinterpret_cast<float*>(gb + kOffKP);   // [128][kPoLd] this split's partial rows
+    float* rcv = reinterpret_cast<float*>(gb + kOffV);    // [ns - 1][rows_per][kPoLd] the other splits' rows
+    const uint32_t stg_s = smem_u32(stg), rcv_s = smem_u32(rcv);
     {
-      const int owner = r / rows_per, lr = r - owner * rows_per;
-      const uint32_t dst = cluster_map(po_s + 4u * (uint32_t)((split * rows_per + lr) * kPoLd + c0), (uint32_t)owner);
+      float* row = stg + r * kPoLd;
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
-        st_cluster_f4(dst + 4u * i, make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]),
-                                                __uint_as_float(o[i + 2]), __uint_as_float(o[i + 3])));
-      if (cg == 0)
-        st_cluster_f2(cluster_map(pml_s + 8u * (uint32_t)(split * rows_per + lr), (uint32_t)owner),
-                      make_float2(bad ? -INFINITY : m, bad ? 0.f : l));
+        *reinterpret_cast<float4*>(row + c0 + i) = make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]),
+                                                               __uint_as_float(o[i + 2]), __uint_as_float(o[i + 3]));
+      if (cg == 0) *reinterpret_cast<float2*>(row + 128) = make_float2(bad ? -INFINITY : m, bad ? 0.f : l);
     }
-    cluster_sync_all();  // every partial has landed in its owner's shared memory
     const int rlo = split * rows_per, rhi = min(kTQ, rlo + rows_per);
-    for (int idx = tid; idx < (rhi - rlo) * 32; idx += kThreads) {
+    if (tid == 0) mbar_arrive_expect_tx(barX, (uint32_t)((ns - 1) * (rhi - rlo)) * kRowB);
+    fence_proxy_async();  // the staged rows are read by bulk copies (async proxy)
+    __syncthreads();
+    cluster_sync_all();  // every CTA's P.V is done: the V regions are free to receive
+    if (tid == 0) {
+      for (int k = 0; k < ns; ++k) {
+        const int klo = k * rows_per, khi = min(kTQ, klo + rows_per);
+        if (k == split || khi <= klo) continue;
+        const uint32_t slot = (uint32_t)(split < k ? split : split - 1);
+        bulk_copy_s2c(cluster_map(rcv_s + slot * (uint32_t)rows_per * kRowB, (uint32_t)k), stg_s + (uint32_t)klo * kRowB,
+                      (uint32_t)(khi - klo) * kRowB, cluster_map(barX, (uint32_t)k));
+      }
+    }
+    bool got = true;
+    {
+      volatile int no_abort = 0;
+      got = mbar_wait(barX, 0, &no_abort);
+    }
+    if (!got && tid == 0 && p.status) atomicOr(p.status, AF_STATUS_TIMEOUT);
+    for (int idx = tid; idx < (rhi - rlo) * 32 && got; idx += kThreads) {
       const int lr = idx / 32, c4 = idx % 32, rr = rlo + lr;
+      const float* src[8];
       float mk[8], lk[8];
       float mx = -INFINITY;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (k < ns) {
-          const float2 v = pml[k * rows_per + lr];
+          src[k] = k == split ? stg + rr * kPoLd : rcv + ((k < split ? k : k - 1) * rows_per + lr) * kPoLd;
+          const float2 v = *reinterpret_cast<const float2*>(src[k] + 128);
           mk[k] = v.x;
           lk[k] = v.y;
           mx = fmaxf(mx, v.x);
@@ -485,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (k < ns && mk[k] != -INFINITY) {
-          const float4 v = *reinterpret_cast<const float4*>(po + (k * rows_per + lr) * kPoLd + 4 * c4);
+          const float4 v = *reinterpret_cast<const float4*>(src[k] + 4 * c4);
           const float f = exp2f(mk[k] - mx);
           lsum += f * lk[k];
           acc.x += f * v.x;
@@ -503,6 +522,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention_tc(const __grid_const
         *reinterpret_cast<uint2*>(p.out + (int64_t)orow * p.out_ld + h * 128 + 4 * c4) = w;
       }
     }
+    __syncwarp();
+    cluster_sync_all();  // every CTA has received its rows: the copies out of this CTA are done
   }
   tc_fence_before();
   __syncthreads();
