@@ -276,9 +276,10 @@ struct PartialRows {
 
 template <int NV>
 __device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row, int64_t rrow, int nvec, int tid,
-                                                  uint4 (&v)[NV]) {
+                                                  uint4 (&v)[NV], bool store = true) {
   // rrow: the residual row of `row` (pr.res_rows[row], or row), read by the
-  // caller together with its other indices.
+  // caller together with its other indices. store = false: the caller stores
+  // the finished row (store_row) once it knows the row is the right one.
   const char* rp = reinterpret_cast<const char*>(pr.res + rrow * (int64_t)(nvec * 8));
   const float* pp = pr.part + (int64_t)row * (nvec * 8);
   float acc[NV][8];
@@ -327,7 +328,16 @@ __device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row
     for (int e = 0; e < 4; ++e)
       ow[e] = pack_bf16x2(__fadd_rn(r[2 * e], rnd<AF_DTYPE_BF16>(acc[i][2 * e])),
                           __fadd_rn(r[2 * e + 1], rnd<AF_DTYPE_BF16>(acc[i][2 * e + 1])));
-    stg16(reinterpret_cast<char*>(pr.store + (int64_t)row * (nvec * 8)) + 16 * (int64_t)j, v[i]);
+    if (store) stg16(reinterpret_cast<char*>(pr.store + (int64_t)row * (nvec * 8)) + 16 * (int64_t)j, v[i]);
+  }
+}
+
+template <int NV>
+__device__ __forceinline__ void store_row(__nv_bfloat16* dst, int nvec, int tid, const uint4 (&v)[NV]) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * kRowThreads + tid;
+    if (j < nvec) stg16(reinterpret_cast<char*>(dst) + 16 * (int64_t)j, v[i]);
   }
 }
 
@@ -360,17 +370,24 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat1
                                                               float eps, const int* n_dev, int n_cap,
                                                               __nv_bfloat16* out, const PartialRows pr) {
   pdl_trigger();
-  pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
   const int i = blockIdx.x;  // < n_cap: the index arrays are read before the count is known
-  const int rrow = pr.part && pr.res_rows ? pr.res_rows[i] : i;
-  const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
-  if (i >= n) return;
+  // The residual row index was written two or more kernels back and is
+  // usually in place before the wait: the row loads go out with it at once,
+  // and the index read again after the wait decides whether they stand (L2
+  // reads: no stale L1 line can answer either read).
+  const int rrow_e = pr.part && pr.res_rows ? min(max(__ldcg(pr.res_rows + i), 0), n_cap - 1) : i;
+  pdl_wait();
   const int nvec = H / 8;
   uint4 v[NV];
-  if (pr.part)
-    load_row_partials<NV>(pr, i, rrow, nvec, threadIdx.x, v);
-  else
+  if (pr.part) load_row_partials<NV>(pr, i, rrow_e, nvec, threadIdx.x, v, false);
+  const int rrow = pr.part && pr.res_rows ? __ldcg(pr.res_rows + i) : i;
+  const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
+  if (i >= n) return;
+  if (pr.part) {
+    if (rrow != rrow_e) load_row_partials<NV>(pr, i, rrow, nvec, threadIdx.x, v, false);
+    store_row<NV>(pr.store + (int64_t)i * H, nvec, threadIdx.x, v);
+  } else
     load_row<NV, kRowThreads>(reinterpret_cast<const char*>(in + (int64_t)i * H), nvec, threadIdx.x, v);
   rmsnorm_regs<NV>(v, nvec, H, w, eps, reinterpret_cast<char*>(out + (int64_t)i * H), threadIdx.x, RowGroup{red});
 }
@@ -380,7 +397,7 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat1
 // ----------------------------------------------------------------------------
 struct FoldGateArgs {
   const int* n_cand;
-  int m_cap, H;
+  int m_cap, H, T;
   const int* cand_pos;
   const int* cand_src;
   const __nv_bfloat16* x_fresh;   // fresh rows of this layer [m_cap, H]
@@ -398,24 +415,40 @@ struct FoldGateArgs {
 template <int METRIC, int NV>
 __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g) {
   pdl_trigger();
-  pdl_wait();
   __shared__ float red[2 * kRowThreads / 32];
   const int tid = threadIdx.x;
-  const int r = blockIdx.x;  // < m_cap: the candidate arrays are read together with the count
-  const int t = g.cand_pos[r], src = g.cand_src[r];
-  const int rrow = g.fresh_part.res_rows && src >= 0 ? g.fresh_part.res_rows[src] : src;
-  const int n = min(*g.n_cand, g.m_cap);
-  if (r >= n) return;
+  const int r = blockIdx.x;  // < m_cap: the candidate arrays are read before the count is known
   const int nvec = g.H / 8;
   const RowGroup rows{red};
-  const char* prow = reinterpret_cast<const char*>(g.p_in + (int64_t)t * g.H);
-  const char* hrow = src >= 0 ? reinterpret_cast<const char*>(g.x_fresh + (int64_t)src * g.H) : prow;
+  // This layer's candidate list was written two or more kernels back and is
+  // usually in place before the wait: the row loads go out with the indices
+  // read now, and the indices read again after the wait decide whether they
+  // stand (both reads from L2, so no stale L1 line answers the second).
+  const int t_e = min(max(__ldcg(g.cand_pos + r), 0), g.T - 1);
+  const int src_e = min(max(__ldcg(g.cand_src + r), -1), g.m_cap - 1);
   uint4 hv[NV], pv[NV];
-  load_row<NV, kRowThreads>(prow, nvec, tid, pv);
-  if (src >= 0 && g.fresh_part.part)
-    load_row_partials<NV>(g.fresh_part, src, rrow, nvec, tid, hv);  // also stores the finished row into x_fresh
-  else
-    load_row<NV, kRowThreads>(hrow, nvec, tid, hv);
+  // The parent's row is constant data: it is requested before the wait.
+  load_row<NV, kRowThreads>(reinterpret_cast<const char*>(g.p_in + (int64_t)t_e * g.H), nvec, tid, pv);
+  pdl_wait();
+  auto load_fresh = [&](int t, int src) {
+    if (src >= 0 && g.fresh_part.part) {
+      const int rrow = g.fresh_part.res_rows ? g.fresh_part.res_rows[src] : src;
+      load_row_partials<NV>(g.fresh_part, src, rrow, nvec, tid, hv, false);
+    } else if (src >= 0) {
+      load_row<NV, kRowThreads>(reinterpret_cast<const char*>(g.x_fresh + (int64_t)src * g.H), nvec, tid, hv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) hv[i] = pv[i];  // no fresh row: the parent's (as loaded for t)
+    }
+  };
+  load_fresh(t_e, src_e);
+  const int t = __ldcg(g.cand_pos + r), src = __ldcg(g.cand_src + r);
+  const int n = min(*g.n_cand, g.m_cap);
+  if (r >= n) return;
+  if (t != t_e) load_row<NV, kRowThreads>(reinterpret_cast<const char*>(g.p_in + (int64_t)t * g.H), nvec, tid, pv);
+  if (t != t_e || src != src_e) load_fresh(t, src);
+  // The finished fresh row (from the previous down GEMM's partials) is kept in x_fresh.
+  if (src >= 0 && g.fresh_part.part) store_row<NV>(g.fresh_part.store + (int64_t)src * g.H, nvec, tid, hv);
   GateOut o;
   if constexpr (METRIC == AF_METRIC_COSINE) o = gate_regs_bf16_cos<NV>(hv, pv, nvec, g.k, tid, rows);
   else o = gate_regs<AF_DTYPE_BF16, METRIC, NV>(hv, pv, nvec, g.H, g.k, tid, rows);
@@ -1270,6 +1303,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     g.n_cand = nc;
     g.m_cap = M;
     g.H = z.H;
+    g.T = T;
     g.cand_pos = cp;
     g.cand_src = cs;
     g.x_fresh = x_l;

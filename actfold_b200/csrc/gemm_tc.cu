@@ -323,6 +323,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
   }
   pdl_wait();
+  // The activation tiles of the pre-filled stages go out at once: they need
+  // no valid count (rows past it are never stored), so the count's round
+  // trip overlaps them.
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < npre; ++i) {
+      if (leader) mbar_arrive_expect_tx(full0 + 8 * i, x_expect);  // weight tile already requested
+      load_x(i, base + i * stage_bytes + w_bytes, full_of(i));
+    }
+  }
   int M = p.m_dev ? *p.m_dev : p.m_cap;
   if (M > p.m_cap) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicOr(p.status, AF_STATUS_CAPACITY);
@@ -332,14 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     // No tokens for this tile (none at all for CTA (0, 0, 0)): the side task
     // still runs, with every thread of the CTA.
     if (side_cta) compact_rows<kThreads>(p.side, s_scan, threadIdx.x, 1);
-    // The early weight loads land before the CTA exits (a pair's on CTA 0's
+    // The early loads land before the CTA exits (a pair's on CTA 0's
     // barriers: CTA 1 leaves after CTA 0 has seen them land).
     if (threadIdx.x == 0 && leader) {
       volatile int no_abort = 0;
-      for (int i = 0; i < npre; ++i) {
-        mbar_arrive(full0 + 8 * i);
-        mbar_wait(full0 + 8 * i, 0, &no_abort);
-      }
+      for (int i = 0; i < npre; ++i) mbar_wait(full0 + 8 * i, 0, &no_abort);
     }
     if constexpr (kPair) {
       __syncwarp();
@@ -370,22 +376,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
-    int i = 0;
+    int i = npre;  // stages 0..npre-1 are fully requested already
     for (; i < nkb; ++i) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1;
       const uint32_t st = base + s * stage_bytes;
-      if (i < npre) {
-        if (leader) mbar_arrive_expect_tx(full0 + 8 * s, x_expect);  // weight tile already requested
-      } else {
-        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) {
-          atomicOr(p.status, AF_STATUS_TIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        if (leader) mbar_arrive_expect_tx(full0 + 8 * s, w_expect + x_expect);
-        load_w(i, st, full_of(s));
+      if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag)) {
+        atomicOr(p.status, AF_STATUS_TIMEOUT);
+        *abort_flag = 1;
+        break;
       }
+      if (leader) mbar_arrive_expect_tx(full0 + 8 * s, w_expect + x_expect);
+      load_w(i, st, full_of(s));
       load_x(i, st + w_bytes, full_of(s));
     }
     *issued_slot = i;
