@@ -50,10 +50,12 @@ __global__ void __launch_bounds__(256) k_gate_vec(const GateParams p) {
 // kGateRowThreads threads per row, at most two vectors per thread per tensor,
 // and block reductions. With a warp per row such rows keep up to 128 values
 // per lane in registers and add them in one dependent chain, which caps the
-// kernel far below HBM speed (one CTA per SM, latency bound). The folded
-// pass's gates group a row's threads the same way (512), so both reduce in
-// the same order and give the same bits.
-constexpr int kGateRowThreads = 512;
+// kernel far below HBM speed (one CTA per SM, latency bound). 256 threads
+// (two vectors each at H = 4096) keep enough CTAs resident per SM for the
+// broadcast kernel's streaming; the folded pass's in-pass gates use
+// 512-thread rows instead (their latency, not their bandwidth, is what
+// counts there), so the two may add a row's squares in different orders.
+constexpr int kGateRowThreads = 256;
 
 template <int DT, int METRIC, int NV>
 __global__ void __launch_bounds__(kGateRowThreads) k_gate_row(const GateParams p) {
