@@ -138,7 +138,7 @@ class ActFoldVerificationEngine:
         if self.use_graphs:
             plan = self.model.plan(pc, Cn, m_cap, self.gate.tau, self.gate.metric)
             plan.set_child_cap(child_cap)
-            gkey = (id(plan), child_cap)
+            gkey = (id(plan), child_cap, plan.keeps_kv)
             entry = self._graphs.get(gkey)
             if entry is None or entry[1] is not plan or entry[2] is not bufs:
                 if len(self._graphs) >= 8:

@@ -114,6 +114,34 @@ def test_promote_in_place_reuses_the_plan(chain, golden):
     assert torch.equal(lg2[G:], pc.logits[None].expand(n - G, -1, -1))
 
 
+def test_engine_verifies_against_a_cache_promoted_in_place(chain, golden):
+    """verify_tokens -> plan.promote(k, into=the engine's parent cache) -> verify_tokens on the promoted branch.
+
+    The promotion rewrites the cache's token ids and self-gate rows on the
+    device; the engine must see the new ids (not a stale host copy) when it
+    matches the branch and sizes the next plan, and verify the grandchildren
+    against the promoted child like the oracle's chain.
+    """
+    from actfold_b200.core import SimilarityGate
+    from actfold_b200.speculative import ActFoldVerificationEngine, Branch
+
+    m = chain["model"]
+    tau, k = SPEC["tau"], chain["k"]
+    eng = ActFoldVerificationEngine(m, gate=SimilarityGate(tau=tau), use_graphs=True)
+    pb = Branch("p", None, torch.from_numpy(chain["parent"])[None])
+    kids = torch.from_numpy(chain["children"]).pin_memory()
+    res = eng.verify_tokens(pb, kids)
+    res["plan"].keep_kv()
+    res = eng.verify_tokens(pb, kids)  # recaptured: this run keeps its QKV rows
+    pc = eng.parent_cache(pb)
+    res["plan"].promote(k, into=pc)
+    kb = Branch("p", None, torch.from_numpy(chain["children"][k])[None])
+    assert eng.parent_cache(kb) is pc  # matched on the promoted ids, no new dense pass
+    res2 = eng.verify_tokens(kb, torch.from_numpy(chain["grand"]).pin_memory())
+    torch.cuda.synchronize()
+    _check_grand(res2["plan"].stable_masks().cpu().numpy(), res2["logits"], chain, golden)
+
+
 def test_folded_model_chains_through_a_verified_child(chain, golden):
     from actfold_b200.core import ActivationCache, FoldedModel, SimilarityGate
 
