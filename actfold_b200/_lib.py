@@ -25,6 +25,7 @@ _i64, _i32, _f32, _vp = C.c_int64, C.c_int, C.c_float, C.c_void_p
 # name -> (restype, argtypes); must match include/actfold_b200.h
 SIGNATURES: dict[str, tuple] = {
     "af_version": (C.c_char_p, []),
+    "af_set_attention_kernel": (_i32, [_i32]),
     "af_last_error_string": (C.c_char_p, []),
     "af_gate": (
         _i32,

@@ -372,7 +372,7 @@ static int attention_splits(const AttnParams& p) {
 
 bool attention_uses_tc(const AttnParams& p) {
   const char* impl = std::getenv("ACTFOLD_ATTN_IMPL");
-  return !(impl && impl[0] == 'm') && attention_tc_splits(p) > 0;
+  return !(impl && impl[0] == 'm') && (attention_fa_ok(p) || attention_tc_splits(p) > 0);
 }
 
 int attention_run(const AttnParams& p, cudaStream_t s) {
@@ -386,6 +386,7 @@ int attention_run(const AttnParams& p, cudaStream_t s) {
   // 3 blocks each); ACTFOLD_ATTN_IMPL=mma selects this mma.sync kernel instead.
   const char* impl = std::getenv("ACTFOLD_ATTN_IMPL");
   if (!(impl && impl[0] == 'm')) {
+    if (attention_fa_ok(p)) return attention_fa_run(p, s);
     const int ns_tc = attention_tc_splits(p);
     if (ns_tc > 0) return attention_tc_run(p, ns_tc, s);
   }

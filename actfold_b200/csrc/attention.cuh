@@ -55,7 +55,15 @@ int attention_run(const AttnParams& p, cudaStream_t s);
 // tcgen05 kernel (attention_tc.cu): key splits for `p` (0: shape not supported) and launch.
 int attention_tc_splits(const AttnParams& p);
 int attention_tc_run(const AttnParams& p, int splits, cudaStream_t s);
-// Whether attention_run takes the tcgen05 kernel for `p`.
+// Whether attention_run takes a tcgen05 kernel for `p`.
 bool attention_uses_tc(const AttnParams& p);
+// Flash-style tcgen05 kernel (attention_fa.cu): one CTA per query tile and
+// head over every key block, for contiguous query rows (candidate keys, if
+// any, in candidate-row mode).
+bool attention_fa_ok(const AttnParams& p);
+int attention_fa_run(const AttnParams& p, cudaStream_t s);
+// Cached tensor map of a parent's K or V: [T keys, cols] of a row-major
+// buffer with row stride ld, or head-major [-cols heads][T][128] when cols < 0.
+int attention_kv_tmap(CUtensorMap* map, const __nv_bfloat16* base, int T, int cols, int64_t ld);
 
 }  // namespace af

@@ -555,7 +555,7 @@ int attention_tc_splits(const AttnParams& p) {
 // of a row-major buffer with row stride ld, or head-major [heads][T][128]
 // when cols < 0), reused across passes: the parent cache keeps its buffers
 // for its lifetime.
-static int kv_tmap(CUtensorMap* map, const __nv_bfloat16* base, int T, int cols, int64_t ld) {
+int attention_kv_tmap(CUtensorMap* map, const __nv_bfloat16* base, int T, int cols, int64_t ld) {
   struct Entry {
     const void* base;
     int T, cols;
@@ -598,12 +598,12 @@ int attention_tc_run(const AttnParams& p, int ns, cudaStream_t s) {
   }
   if (p.kv_static && p.kv_hm) {
     const __nv_bfloat16* vbase = p.kv_hm + (int64_t)p.n_kv_heads * p.T * 128;
-    if (int st = kv_tmap(&tk, p.kv_hm, p.T, -p.n_kv_heads, 0)) return st;
-    if (int st = kv_tmap(&tv, vbase, p.T, -p.n_kv_heads, 0)) return st;
+    if (int st = attention_kv_tmap(&tk, p.kv_hm, p.T, -p.n_kv_heads, 0)) return st;
+    if (int st = attention_kv_tmap(&tv, vbase, p.T, -p.n_kv_heads, 0)) return st;
   } else if (p.kv_static) {
     const int cols = p.n_kv_heads * 128;
-    if (int st = kv_tmap(&tk, p.pk, p.T, cols, p.kv_ld)) return st;
-    if (int st = kv_tmap(&tv, p.pv, p.T, cols, p.kv_ld)) return st;
+    if (int st = attention_kv_tmap(&tk, p.pk, p.T, cols, p.kv_ld)) return st;
+    if (int st = attention_kv_tmap(&tv, p.pv, p.T, cols, p.kv_ld)) return st;
   }
   cudaError_t e = launch_ex(k_attention_tc, dim3((p.n_q_cap + kTQ - 1) / kTQ, p.n_heads, ns), dim3(kThreads, 1, 1),
                             (size_t)kSmemTc, s, p.pdl != 0, dim3(1, 1, ns), tk, tv, tc, p);

@@ -1441,6 +1441,8 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     ap.cand_win = p->child_cap > 0 ? 2 * ((p->child_cap - 1 + 127) / 128) + 1 : 0;
     AttnParams probe = ap;
     probe.cand_tma = 1;
+    probe.qsrc = nullptr;
+    probe.tmap_c = &p->tx_qkv;
     if (attention_uses_tc(probe)) {
       // Candidate-row mode: every candidate row is a query (the query tile is
       // 128 rows whatever the divergent count), so the queries and the

@@ -157,10 +157,13 @@ int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_d
  * fresh_bits[qchild[i] * bits_ld] is set, plus candidate rows j of fk/fv with
  * fchild[j] == qchild[i]. Valid query / candidate counts are read from
  * n_q_dev / n_f_dev (nullable -> caps). head_dim must be 128; GQA when
- * n_kv_heads < n_heads. Up to 24 blocks of 128 keys (parent + candidates) run
- * on tcgen05 tensor cores (128 query rows per CTA, key splits combined in a
- * thread-block cluster); larger shapes use an mma.sync kernel. status
- * (nullable) receives AF_STATUS_TIMEOUT if a bounded wait ran out.
+ * n_kv_heads < n_heads. Runs on tcgen05 tensor cores: key splits combined in
+ * a thread-block cluster (up to 24 blocks of 128 keys), or one CTA per query
+ * tile and head streaming every key block with an online softmax (contiguous
+ * queries: qsrc null, no candidate keys; chosen when those CTAs fill the GPU,
+ * or when the sequence is too long for key splits). Gathered queries over more
+ * than 24 key blocks use an mma.sync kernel. status (nullable) receives
+ * AF_STATUS_TIMEOUT if a bounded wait ran out.
  */
 int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsrc, const int32_t* qchild,
                       const int32_t* n_q_dev, int64_t n_q_cap, const void* pk, const void* pv,
@@ -169,6 +172,13 @@ int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsrc, const in
                       const int32_t* n_f_dev, int64_t n_f_cap, void* out, int64_t out_ld,
                       int n_heads, int n_kv_heads, int head_dim, float scale, uint32_t* status,
                       void* stream);
+
+/* Attention kernel choice for later calls (process-wide; no counterpart in
+ * the reference): AF_ATTN_AUTO picks per shape as above, AF_ATTN_STREAM
+ * takes the streaming (one CTA per query tile and head) kernel wherever it
+ * applies, AF_ATTN_SPLIT never takes it. Returns AF_ERR_ARG for other values. */
+enum { AF_ATTN_AUTO = 0, AF_ATTN_STREAM = 1, AF_ATTN_SPLIT = 2 };
+int af_set_attention_kernel(int kind);
 
 /* ------------------------------------------------------------------------
  * Native folded verification of LLaDA / Dream-architecture models.

@@ -2,8 +2,9 @@
 
 Tolerance: the kernel feeds bf16 probabilities to the tensor cores, so the
 max error is bounded at 2e-2 of the output scale. Each case runs on the
-tcgen05 kernel (the default for up to 24 key blocks) and on the mma.sync
-kernel (ACTFOLD_ATTN_IMPL=mma).
+tcgen05 kernels as chosen by shape, on the streaming tcgen05 kernel where it
+applies (af_set_attention_kernel), and on the mma.sync kernel
+(ACTFOLD_ATTN_IMPL=mma).
 """
 
 from __future__ import annotations
@@ -31,10 +32,17 @@ def _err(a, b):
     return float((a.float() - b.float()).abs().max() / b.float().abs().max())
 
 
-@pytest.fixture(params=["tc", "mma"])
+@pytest.fixture(params=["tc", "stream", "mma"])
 def impl(request, monkeypatch):
-    monkeypatch.setenv("ACTFOLD_ATTN_IMPL", request.param)
-    return request.param
+    """tcgen05 kernels with the shape-based choice, the streaming kernel forced
+    wherever it applies (contiguous queries, no candidate keys), and mma.sync."""
+    from actfold_b200 import _lib
+
+    lib = _lib.load()
+    monkeypatch.setenv("ACTFOLD_ATTN_IMPL", "mma" if request.param == "mma" else "tc")
+    _lib.check(lib.af_set_attention_kernel(1 if request.param == "stream" else 0))
+    yield request.param
+    _lib.check(lib.af_set_attention_kernel(0))
 
 
 @pytest.mark.parametrize("T,n_q,heads,kv", [(64, 64, 2, 2), (1024, 1024, 4, 4), (200, 37, 4, 1), (512, 130, 8, 2),

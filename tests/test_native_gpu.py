@@ -73,7 +73,7 @@ def tiny(request):
     return dict(dims=dims, spec=spec, gname=gname, w=w, parent=parent, children=children, model=model, ref_par=ref_par, ref=ref)
 
 
-def test_parent_pass_matches_oracle(tiny):
+def test_parent_pass_matches_oracle(tiny, attn_kernel):
     m = tiny["model"]
     pc = m.parent_pass(torch.from_numpy(tiny["parent"]).cuda(), tau=tiny["spec"]["tau"])
     torch.cuda.synchronize()
@@ -89,7 +89,20 @@ def test_parent_pass_matches_oracle(tiny):
     np.testing.assert_allclose(pc.row_sums.cpu().numpy(), lg.sum(-1), rtol=1e-3, atol=1e-2)
 
 
-def test_folded_children_match_oracle_and_reference(tiny, golden):
+@pytest.fixture(params=["auto", "stream"])
+def attn_kernel(request):
+    """Each folded-pass parity case also runs with the streaming attention kernel
+    (one CTA per query tile and head, online softmax) forced wherever it applies."""
+    from actfold_b200 import _lib
+
+    lib = _lib.load()
+    kind = {"auto": 0, "stream": 1}[request.param]
+    _lib.check(lib.af_set_attention_kernel(kind))
+    yield request.param
+    _lib.check(lib.af_set_attention_kernel(0))
+
+
+def test_folded_children_match_oracle_and_reference(tiny, golden, attn_kernel):
     m = tiny["model"]
     spec = tiny["spec"]
     pc = m.parent_pass(torch.from_numpy(tiny["parent"]).cuda(), tau=spec["tau"])
