@@ -1066,7 +1066,7 @@ static FoldWs carve_fold(Bump& b, const Sizes& z, int C, int T, int m_cap, bool 
 // Kernel classes of a folded pass (per-class CUDA-event timing).
 enum FoldKind {
   FK_SETUP = 0, FK_GATE, FK_COMPACT, FK_QKV, FK_ATTN, FK_O, FK_NORM, FK_GATEUP, FK_DOWN, FK_LM, FK_FILL, FK_SCORES,
-  FK_COUNT
+  FK_FINISH, FK_COUNT
 };
 
 // Optional CUDA-event brackets around each launch of a pass, on the pass's stream.
@@ -1383,7 +1383,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
       c.splits = 1;  // one CTA per weight tile, RoPE in its own epilogue
     }
     AF_TIMED(FK_QKV, if ((st = gemm_run(c, s))) return st);
-    if (w.part_qkv) AF_TIMED(FK_QKV, if ((st = gemm_finish_run(c, w.split_qkv, s))) return st);
+    if (w.part_qkv) AF_TIMED(FK_FINISH, if ((st = gemm_finish_run(c, w.split_qkv, s))) return st);
     if (fork_fill && ((l == 0 && early) || last)) {
       // After layer 0's compaction (a side task of this GEMM) the rows stable
       // for good are known; after the last layer's, every final-stable row is.

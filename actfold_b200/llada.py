@@ -97,7 +97,7 @@ _lib.SIGNATURES.update(
 )
 
 KERNEL_CLASSES = ("setup", "gate", "compact", "gemm_qkv", "attention", "gemm_o", "rmsnorm", "gemm_gateup",
-                  "gemm_down", "gemm_lm_head", "logits_fill", "scores")
+                  "gemm_down", "gemm_lm_head", "logits_fill", "scores", "qkv_finish")
 
 
 def _bind_late() -> C.CDLL:

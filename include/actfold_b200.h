@@ -393,7 +393,8 @@ int af_fold_promote(void* plan, int64_t child, const int64_t* child_tokens, cons
  * Per-kernel-class CUDA-event timing of af_fold_run, recorded on the pass's
  * stream when enabled. Classes: 0 candidates/embedding, 1 gate, 2 compaction,
  * 3 QKV GEMM, 4 attention, 5 O GEMM, 6 RMSNorm, 7 gate/up GEMM, 8 down GEMM,
- * 9 LM-head GEMM, 10 parent-logit fill, 11 scores. af_fold_get_timing
+ * 9 LM-head GEMM, 10 parent-logit fill, 11 scores, 12 QKV rows finished from
+ * the QKV GEMM's split partials. af_fold_get_timing
  * synchronizes on the last event, returns the accumulated milliseconds and
  * launch counts per class (then resets them) and the number of kernel
  * launches of the last run. No counterpart in the reference (measurement).
