@@ -272,7 +272,60 @@ struct PartialRows {
   const __nv_bfloat16* res;        // residual rows [.., H]
   const int* res_rows;             // nullable: residual row of row i
   __nv_bfloat16* store;            // the finished rows are written here (row i)
+  // Peer-memory sums (af_fold_set_peer_sum): the S slices are the ranks'
+  // sums, stored here by k_sum_push on every rank; they are read once
+  // peer_flags[0..S) have reached this rank's launch count of that sum
+  // (*peer_ctr / peer_grid). Null: no wait.
+  const unsigned* peer_flags;
+  const unsigned long long* peer_ctr;
+  unsigned peer_grid;
+  unsigned* status;
 };
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr unsigned long long kPeerWaitNs = 5000000000ull;  // bound of one wait on the other ranks' sums
+
+// Thread 0 waits until every rank's sum of this launch is in place, then the
+// CTA goes on. A wait that runs out ORs AF_STATUS_TIMEOUT into the status
+// word, and later waits of the pass see the bit and do not wait again (the
+// rows are then wrong, and the host raises on the status).
+__device__ __forceinline__ void peer_rows_wait(const PartialRows& pr) {
+  if (!pr.peer_flags) return;
+  if (threadIdx.x == 0) {
+    const unsigned expect = (unsigned)(__ldcg(pr.peer_ctr) / pr.peer_grid);
+    if (!(__ldcg(pr.status) & AF_STATUS_TIMEOUT)) {
+      const unsigned long long t0 = global_ns();
+      for (int q = 0; q < pr.nsplit; ++q) {
+        bool late = false;
+        while ((int)(ld_acquire_sys(pr.peer_flags + q) - expect) < 0) {
+          if (global_ns() - t0 > kPeerWaitNs) {
+            atomicOr(pr.status, AF_STATUS_TIMEOUT);
+            late = true;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (late) break;
+      }
+    }
+  }
+  __syncthreads();
+}
 
 template <int NV>
 __device__ __forceinline__ void load_row_partials(const PartialRows& pr, int row, int64_t rrow, int nvec, int tid,
@@ -363,6 +416,47 @@ __global__ void __launch_bounds__(256) k_sum_splits(float* part, int64_t stride,
   }
 }
 
+// Peer-memory cross-rank sum, producer side: this rank's k-splits added in
+// order and stored into its slot of every rank's exchange buffer; when the
+// launch's last CTA is done, each rank's flag for this rank is raised to the
+// launch count. Every thread fences its stores at system scope before its CTA
+// counts itself in, so the flag orders after every CTA's stores.
+constexpr int kMaxRanks = 8;
+struct PeerPush {
+  float* dst[kMaxRanks];       // rank q's slot for this rank's sum
+  unsigned* flag[kMaxRanks];   // rank q's flag for this rank's sum
+  unsigned long long* ctr;     // this rank's CTA count of this sum (grows by the grid size per launch)
+  int world;
+};
+
+__global__ void __launch_bounds__(256) k_sum_push(const float* part, int64_t stride, int nsplit, int64_t n4,
+                                                  const int* rows_dev, int64_t row_len4, const PeerPush pp) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t lim = rows_dev ? min(n4, (int64_t)(*rows_dev) * row_len4) : n4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < lim; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float4 v = reinterpret_cast<const float4*>(part + sp * stride)[i];
+      a.x += v.x;
+      a.y += v.y;
+      a.z += v.z;
+      a.w += v.w;
+    }
+    for (int q = 0; q < pp.world; ++q) reinterpret_cast<float4*>(pp.dst[q])[i] = a;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long done = atomicAdd(pp.ctr, 1ull) + 1ull;
+    if (done % gridDim.x == 0) {
+      const unsigned seq = (unsigned)(done / gridDim.x);
+      __threadfence_system();
+      for (int q = 0; q < pp.world; ++q) st_release_sys(pp.flag[q], seq);
+    }
+  }
+}
+
 // out[i] = rmsnorm(in[i]) * w for i < n (rows strided by H); one CTA per row.
 // With pr.part, row i is first finished from its split-K partials (and stored).
 template <int NV>
@@ -380,6 +474,7 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat1
   pdl_wait();
   const int nvec = H / 8;
   uint4 v[NV];
+  if (pr.part) peer_rows_wait(pr);
   if (pr.part) load_row_partials<NV>(pr, i, rrow_e, nvec, threadIdx.x, v, false);
   const int rrow = pr.part && pr.res_rows ? __ldcg(pr.res_rows + i) : i;
   const int n = n_dev ? min(*n_dev, n_cap) : n_cap;
@@ -430,6 +525,7 @@ __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g)
   // The parent's row is constant data: it is requested before the wait.
   load_row<NV, kRowThreads>(reinterpret_cast<const char*>(g.p_in + (int64_t)t_e * g.H), nvec, tid, pv);
   pdl_wait();
+  if (g.fresh_part.part) peer_rows_wait(g.fresh_part);
   auto load_fresh = [&](int t, int src) {
     if (src >= 0 && g.fresh_part.part) {
       const int rrow = g.fresh_part.res_rows ? g.fresh_part.res_rows[src] : src;
@@ -1161,6 +1257,10 @@ struct FoldPlan {
   af_collective_fn coll = nullptr;
   void* coll_user = nullptr;
   int64_t embed_rows = 0, vocab_total = 0;
+  // Peer-memory sums (af_fold_set_peer_sum): this rank, the number of ranks
+  // (0: sums through the hook) and each rank's exchange buffer as mapped here.
+  int peer_rank = 0, peer_world = 0;
+  char* exch[kMaxRanks] = {};
   ~FoldPlan() {
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
@@ -1208,11 +1308,64 @@ static int collective(FoldPlan* p, int kind, int layer, void* data, int64_t coun
   return AF_OK;
 }
 
+// Exchange buffer of the peer-memory sums, per rank: the ranks' sums of the O
+// and down projections [2][world][m_cap][H] fp32, then the flags
+// [2][kMaxRanks] u32 (flag q of a sum: rank q's launch count of it, raised by
+// rank q), then this rank's CTA counters [2] u64.
+static int64_t peer_flags_off(const FoldPlan* p, int world) {
+  const int64_t recv = 2 * (int64_t)world * p->m_cap * sizes_of(p->model.dims).H * 4;
+  return (recv + 255) / 256 * 256;
+}
+static int64_t peer_bytes(const FoldPlan* p, int world) { return peer_flags_off(p, world) + 256; }
+static float* peer_slot(const FoldPlan* p, char* ex, int kind, int q) {
+  return reinterpret_cast<float*>(ex) + ((int64_t)kind * p->peer_world + q) * p->m_cap * sizes_of(p->model.dims).H;
+}
+static unsigned* peer_flag(const FoldPlan* p, char* ex, int kind, int q) {
+  return reinterpret_cast<unsigned*>(ex + peer_flags_off(p, p->peer_world)) + kind * kMaxRanks + q;
+}
+static unsigned long long* peer_ctr(const FoldPlan* p, int kind) {
+  return reinterpret_cast<unsigned long long*>(p->exch[p->peer_rank] + peer_flags_off(p, p->peer_world) + 64) + kind;
+}
+static unsigned peer_grid() { return (unsigned)(2 * sm_count()); }
+
+// Where the rows of an O / down projection are finished from: this rank's
+// k-splits (one GPU), the hook's in-place sum (one slice), or the ranks' sums
+// in every rank's exchange buffer (peer-memory sums, added in rank order).
+static void tp_partials(const FoldPlan* p, int kind, int local_splits, PartialRows& pr) {
+  if (!p->coll) {
+    pr.nsplit = local_splits;
+  } else if (!p->peer_world) {
+    pr.nsplit = 1;
+  } else {
+    char* own = p->exch[p->peer_rank];
+    pr.part = peer_slot(p, own, kind, 0);
+    pr.nsplit = p->peer_world;
+    pr.peer_flags = peer_flag(p, own, kind, 0);
+    pr.peer_ctr = peer_ctr(p, kind);
+    pr.peer_grid = peer_grid();
+    pr.status = p->w.status;
+  }
+}
+
 // Tensor parallel: this rank's k-splits of an O / down projection added into
-// the first slice, then that slice summed over the ranks by the hook.
+// the first slice, then that slice summed over the ranks by the hook; or, with
+// peer-memory sums, added and stored into every rank's exchange buffer.
 static int cross_rank_sum(FoldPlan* p, int kind, int layer, int nsplit, const int* rows_dev, cudaStream_t s) {
   const Sizes z = sizes_of(p->model.dims);
   const int64_t n = (int64_t)p->m_cap * z.H;
+  if (p->peer_world) {
+    PeerPush pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.world = p->peer_world;
+    for (int q = 0; q < p->peer_world; ++q) {
+      pp.dst[q] = peer_slot(p, p->exch[q], kind, p->peer_rank);
+      pp.flag[q] = peer_flag(p, p->exch[q], kind, p->peer_rank);
+    }
+    pp.ctr = peer_ctr(p, kind);
+    AF_TIMED(FK_NORM, AF_LAUNCH(k_sum_push, peer_grid(), 256, 0, s, (const float*)p->w.part, n, nsplit, n / 4,
+                                rows_dev, (int64_t)z.H / 4, pp));
+    return AF_OK;
+  }
   if (nsplit > 1)
     AF_TIMED(FK_NORM, AF_LAUNCH(k_sum_splits, (unsigned)(2 * sm_count()), 256, 0, s, p->w.part, n, nsplit, n / 4,
                                 rows_dev, (int64_t)z.H / 4));
@@ -1318,9 +1471,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
       // split-K partials: finish them here (residual = that layer's h1).
       g.fresh_part.part = w.part;
       g.fresh_part.split_stride = (int64_t)M * z.H;
-      g.fresh_part.nsplit = p->coll ? 1 : w.split_down;  // tensor parallel: already added up
       g.fresh_part.res = w.h1;
       g.fresh_part.store = x_l;
+      tp_partials(p, AF_COLL_DOWN, w.split_down, g.fresh_part);
     }
     g.stable = w.stable;
     g.xc = w.xc;
@@ -1484,10 +1637,10 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
     if (w.part_o) {  // h1 = xc + O, finished from the O GEMM's partials
       pr_o.part = w.part;
       pr_o.split_stride = (int64_t)M * z.H;
-      pr_o.nsplit = p->coll ? 1 : w.split_o;
       pr_o.res = w.xc;
       pr_o.res_rows = dcand;
       pr_o.store = w.h1;
+      tp_partials(p, AF_COLL_O, w.split_o, pr_o);
     }
     AF_TIMED(FK_NORM, AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, M, s, w.h1, static_cast<const __nv_bfloat16*>(lw.ffn_norm),
                                        z.H, eps, nd, M, w.bn, pr_o));
@@ -1558,9 +1711,9 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   if (w.part_down) {  // the last layer's outputs, finished from its down GEMM's partials
     pr_f.part = w.part;
     pr_f.split_stride = (int64_t)M * z.H;
-    pr_f.nsplit = p->coll ? 1 : w.split_down;
     pr_f.res = w.h1;
     pr_f.store = const_cast<__nv_bfloat16*>(x_final);
+    tp_partials(p, AF_COLL_DOWN, w.split_down, pr_f);
   }
   AF_TIMED(FK_NORM, AF_DISPATCH_ROWS(z.H, k_rmsnorm_rows, M, s, x_final,
                                      static_cast<const __nv_bfloat16*>(p->model.final_norm), z.H, eps, nd_last, M, w.A,
@@ -1715,6 +1868,27 @@ extern "C" int af_fold_set_tensor_parallel(void* plan, int64_t embed_rows, int64
   p->coll_user = user;
   p->embed_rows = embed_rows;
   p->vocab_total = vocab_total;
+  return AF_OK;
+}
+
+extern "C" int af_fold_peer_bytes(void* plan, int32_t world, int64_t* bytes) {
+  AF_REQUIRE(plan && bytes, "af_fold_peer_bytes: null pointer");
+  AF_REQUIRE(world >= 1 && world <= kMaxRanks, "af_fold_peer_bytes: world must be 1..8");
+  *bytes = peer_bytes(static_cast<FoldPlan*>(plan), world);
+  return AF_OK;
+}
+
+extern "C" int af_fold_set_peer_sum(void* plan, int32_t rank, int32_t world, void* const* exchange) {
+  AF_REQUIRE(plan && exchange, "af_fold_set_peer_sum: null pointer");
+  FoldPlan* p = static_cast<FoldPlan*>(plan);
+  AF_REQUIRE(p->coll, "af_fold_set_peer_sum: call af_fold_set_tensor_parallel first");
+  AF_REQUIRE(world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world, "af_fold_set_peer_sum: bad rank / world");
+  for (int q = 0; q < world; ++q)
+    AF_REQUIRE(exchange[q] && !(reinterpret_cast<uintptr_t>(exchange[q]) & 255u),
+               "af_fold_set_peer_sum: exchange buffers must be non-null and 256-byte aligned");
+  p->peer_rank = rank;
+  p->peer_world = world;
+  for (int q = 0; q < kMaxRanks; ++q) p->exch[q] = q < world ? static_cast<char*>(exchange[q]) : nullptr;
   return AF_OK;
 }
 

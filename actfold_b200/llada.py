@@ -93,6 +93,11 @@ _lib.SIGNATURES.update(
         "af_fold_get_timing": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32, C.POINTER(_i64)]),
         "af_fold_set_tensor_parallel": (_i32, [_vp, _i64, _i64, COLLECTIVE_FN, _vp]),
         "af_parent_kv_headmajor": (_i32, [C.POINTER(_Dims), _i64, _vp, _vp, _vp]),
+        "af_fold_peer_bytes": (_i32, [_vp, _i32, C.POINTER(_i64)]),
+        "af_fold_set_peer_sum": (_i32, [_vp, _i32, _i32, C.POINTER(_vp)]),
+        "af_ipc_export": (_i32, [_vp, _vp, C.POINTER(_i64)]),
+        "af_ipc_import": (_i32, [_vp, _i64, C.POINTER(_vp), C.POINTER(_vp)]),
+        "af_ipc_close": (_i32, [_vp]),
     }
 )
 
@@ -105,7 +110,8 @@ def _bind_late() -> C.CDLL:
     for name in ("af_dense_workspace_bytes", "af_dense_forward", "af_fold_workspace_bytes", "af_fold_plan_create",
                  "af_fold_run", "af_fold_get_outputs", "af_fold_materialize", "af_fold_plan_destroy",
                  "af_fold_keep_kv", "af_fold_promote", "af_fold_set_child_cap",
-                 "af_fold_set_timing", "af_fold_get_timing", "af_fold_set_tensor_parallel", "af_parent_kv_headmajor"):
+                 "af_fold_set_timing", "af_fold_get_timing", "af_fold_set_tensor_parallel", "af_parent_kv_headmajor",
+                 "af_fold_peer_bytes", "af_fold_set_peer_sum", "af_ipc_export", "af_ipc_import", "af_ipc_close"):
         fn = getattr(lib, name)
         fn.restype, fn.argtypes = _lib.SIGNATURES[name]
     return lib
@@ -361,6 +367,22 @@ class FoldPlan:
                    "af_fold_set_tensor_parallel")
 
     collective_error = None
+
+    def peer_bytes(self, world: int) -> int:
+        """Bytes of one rank's exchange buffer for peer-memory sums over ``world`` ranks."""
+        n = _i64()
+        _lib.check(self.lib.af_fold_peer_bytes(self._plan, int(world), C.byref(n)), "af_fold_peer_bytes")
+        return int(n.value)
+
+    def set_peer_sum(self, rank: int, world: int, exchange_ptrs) -> None:
+        """Route the O / down sums through the ranks' exchange buffers (``exchange_ptrs[q]``: rank q's, as mapped here).
+
+        Every buffer must be zero-filled on every rank before any rank runs
+        the plan; after ``set_tensor_parallel``.
+        """
+        arr = (_vp * int(world))(*[int(x) for x in exchange_ptrs])
+        _lib.check(self.lib.af_fold_set_peer_sum(self._plan, int(rank), int(world), arr), "af_fold_set_peer_sum")
+        self._exchange_ptrs = arr
 
     def workspace_view(self, ptr: int, n: int, dtype: torch.dtype) -> torch.Tensor:
         """``n`` elements of ``dtype`` at device address ``ptr`` inside this plan's workspace."""

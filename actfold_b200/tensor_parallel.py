@@ -16,10 +16,18 @@ rank holds a slice of each layer instead (Megatron-style):
 Every rank runs the same folded pass on its slices (``af_fold_set_tensor_parallel``):
 gate decisions, compaction and norms are computed redundantly on identical
 data; the O and down projections leave fp32 partial sums that are added over
-the ranks (one all-reduce each per layer, before the row kernel that adds the
-residual), and the fresh logits' row sums are added after the LM head so the
-scores are means over the whole vocabulary. Each rank's logits are its
-vocabulary slice of the full [C, T, V] logits.
+the ranks before the row kernel that adds the residual, and the fresh logits'
+row sums are added after the LM head so the scores are means over the whole
+vocabulary. Each rank's logits are its vocabulary slice of the full [C, T, V]
+logits.
+
+The O and down sums (two per layer) go through peer memory by default
+(``sums="peer"``): every rank maps the other ranks' exchange buffers (CUDA IPC
+over NVLink), a kernel after each projection stores this rank's sum into every
+rank's buffer and raises a flag there, and the row kernel that consumes the
+sum waits for the flags (bounded) and adds the ranks' slices in rank order.
+``sums="nccl"`` runs an NCCL all-reduce per sum instead. The row sums after the
+LM head (one per pass) use ``torch.distributed.all_reduce`` in both modes.
 
 The parent cache is whole on every rank apart from the per-head K/V columns
 and the logits, which are sliced the same way (``shard_parent_cache``).
@@ -105,16 +113,20 @@ class TensorParallelVerifier:
     split the weights (NCCL for CUDA tensors).
     """
 
-    def __init__(self, model: LLaDAModel, group=None) -> None:
+    def __init__(self, model: LLaDAModel, group=None, sums: str = "peer") -> None:
         import torch.distributed as dist
 
+        if sums not in ("peer", "nccl"):
+            raise ValueError(f"sums must be 'peer' or 'nccl', not {sums!r}")
         self.dist = dist
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.sums = sums if self.world > 1 else "nccl"  # one rank: the sums are the identity
         self.full = model
         self.local = shard_model(model, self.rank, self.world)
         self._plans: dict = {}
+        self._exchanges: list[PeerExchange] = []
 
     def shard_parent(self, pc: ParentCache) -> ParentCache:
         return shard_parent_cache(pc, self.full.dims, self.rank, self.world)
@@ -131,6 +143,11 @@ class TensorParallelVerifier:
         if p is None:
             p = FoldPlan(self.local, pc_local, C, m_cap, tau, partial_always=True)
             p.set_tensor_parallel(self.full.dims.vocab, self.full.dims.vocab, self._sum)
+            if self.sums == "peer":  # every rank makes its plan in the same call, so the exchange is collective
+                ex = PeerExchange(p.peer_bytes(self.world), self.local.device, self.group)
+                p.set_peer_sum(self.rank, self.world, ex.ptrs)
+                p.peer_exchange = ex  # this rank's buffer lives as long as the plan
+                self._exchanges.append(ex)
             self._plans = {key: p}
         p.set_child_cap(child_cap)
         return p
@@ -146,6 +163,101 @@ class TensorParallelVerifier:
         plan.run(child_tokens, logits, scores)
         return logits, plan
 
+    def release(self) -> None:
+        """Unmap the other ranks' exchange buffers of every plan made so far.
 
-__all__ = ["TensorParallelVerifier", "shard_block", "shard_dims", "shard_model", "shard_parent_cache", "split_range",
+        Collective: every rank calls it, with no pass in flight; plans (and
+        graphs captured from them) made by this verifier must not run after it.
+        """
+        for ex in self._exchanges:
+            ex.close()
+        self._exchanges = []
+        self._plans = {}
+
+
+# Mappings of other processes' allocations, shared by every exchange that
+# lands in the same allocation (an allocation is mapped once per process):
+# handle bytes -> [mapping base, users].
+_IPC_MAPS: dict[bytes, list] = {}
+
+
+class PeerExchange:
+    """This rank's zero-filled exchange buffer and the other ranks' buffers mapped into this process (CUDA IPC).
+
+    Collective over ``group``: the handles are all-gathered, every rank maps
+    the others' buffers, and a barrier after the zero fill makes sure that no
+    rank's first store reaches a buffer that is still being cleared.
+    """
+
+    def __init__(self, nbytes: int, device: torch.device, group=None) -> None:
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from actfold_b200 import _lib
+        from actfold_b200.llada import _bind_late
+
+        self.lib = _bind_late()
+        self.group = group
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        self.closed = False
+        self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+        own = (self.buf.data_ptr() + 255) // 256 * 256
+        handle = (C.c_char * 64)()
+        off = C.c_int64()
+        _lib.check(self.lib.af_ipc_export(C.c_void_p(own), handle, C.byref(off)), "af_ipc_export")
+        entries: list = [None] * world
+        dist.all_gather_object(entries, (bytes(handle.raw), int(off.value)), group=group)
+        self.ptrs: list[int] = []
+        self._bases: list[bytes] = []  # handles of the mappings this exchange uses
+        err = None
+        try:
+            for q, (h, o) in enumerate(entries):
+                if q == rank:
+                    self.ptrs.append(own)
+                    continue
+                m = _IPC_MAPS.get(h)
+                if m is None:
+                    ptr, base = C.c_void_p(), C.c_void_p()
+                    _lib.check(self.lib.af_ipc_import(C.create_string_buffer(h, 64), 0, C.byref(ptr), C.byref(base)),
+                               "af_ipc_import")
+                    m = _IPC_MAPS[h] = [int(base.value), 0]
+                m[1] += 1
+                self._bases.append(h)
+                self.ptrs.append(m[0] + int(o))
+        except Exception as exc:  # reported on every rank below, so that no rank runs with a partial mapping
+            err = exc
+        oks: list = [None] * world
+        dist.all_gather_object(oks, err is None, group=group)
+        if not all(oks):
+            self._unmap()
+            self.closed = True
+            raise err or RuntimeError("peer-memory sums: another rank could not map the exchange buffers")
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers (collective; this rank's own buffer stays allocated)."""
+        import torch.distributed as dist
+
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.buf.device)
+        dist.barrier(group=self.group)  # no rank still stores into a buffer that is about to be unmapped
+        self._unmap()
+        self.closed = True
+
+    def _unmap(self) -> None:
+        from actfold_b200 import _lib
+
+        for h in self._bases:
+            m = _IPC_MAPS[h]
+            m[1] -= 1
+            if m[1] == 0:
+                del _IPC_MAPS[h]
+                _lib.check(self.lib.af_ipc_close(m[0]), "af_ipc_close")
+        self._bases = []
+
+
+__all__ = ["PeerExchange", "TensorParallelVerifier", "shard_block", "shard_dims", "shard_model", "shard_parent_cache", "split_range",
            "round_capacity"]

@@ -74,7 +74,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None, help="override layer count (small profiling captures only)")
     ap.add_argument("--tp", action="store_true",
                     help="tensor parallel: every rank verifies the same children (--global-children, default "
-                         "--children) with its slice of the weights; cross-rank sums over NCCL inside the pass")
+                         "--children) with its slice of the weights; cross-rank sums inside the pass")
+    ap.add_argument("--tp-sums", choices=("peer", "nccl"), default="peer",
+                    help="with --tp: the per-layer O / down sums through peer memory (default) or NCCL all-reduces")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch the pass kernel by kernel instead of replaying its CUDA graph")
     ap.add_argument("--block-decoding", action="store_true",
@@ -436,7 +438,7 @@ def run_tensor_parallel(a, rank: int, world: int, local_rank: int) -> None:
     pc = model.parent_pass(torch.from_numpy(parent_np).to(dev), tau=a.tau)  # whole weights on every rank: no broadcast
     torch.cuda.synchronize()
     parent_ms = (time.perf_counter() - t0) * 1e3
-    tp = TensorParallelVerifier(model)
+    tp = TensorParallelVerifier(model, sums=a.tp_sums)
     pcl = tp.shard_parent(pc)
     ct = torch.from_numpy(children_np).to(dev)
     scores = torch.empty((C,), dtype=torch.float32, device=dev)
@@ -486,8 +488,9 @@ def run_tensor_parallel(a, rank: int, world: int, local_rank: int) -> None:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,0.02) weights drawn on the GPU, seeded token ids",
-            "config": dict(config_dict(a, world), parallelism=f"tensor parallel over {world} GPUs (heads, FFN and "
-                                                             f"vocabulary split; NCCL all-reduce after O and down)"),
+            "config": dict(config_dict(a, world), children_per_gpu=C, parallelism=(
+                f"tensor parallel over {world} GPUs (heads, FFN and vocabulary split; O and down sums "
+                + ("through peer memory" if tp.sums == "peer" else "by NCCL all-reduce") + ")")),
             "gpu_launches": int(per_run * a.steps),
             "clocks": clocks,
             "parent_pass_ms": parent_ms,
@@ -496,6 +499,7 @@ def run_tensor_parallel(a, rank: int, world: int, local_rank: int) -> None:
         }
         print(json.dumps(line), flush=True)
     graph = None  # a graph holding NCCL calls is released before the process group
+    tp.release()
     del plan, tp
     torch.cuda.synchronize()
     dist.barrier()

@@ -365,6 +365,37 @@ int af_fold_set_tensor_parallel(void* plan, int64_t embed_rows, int64_t vocab_to
                                 void* user);
 
 /*
+ * Peer-memory sums for a tensor-parallel plan (ranks on one node, GPUs with
+ * peer access over NVLink). With it the AF_COLL_O and AF_COLL_DOWN sums no
+ * longer go through the hook: after each of those projections one kernel adds
+ * this rank's k-splits and stores the fp32 sum into a slot of EVERY rank's
+ * exchange buffer (its own through local stores, the others' through peer
+ * stores), then raises a flag in each; the kernel that consumes the sum waits
+ * (bounded, AF_STATUS_TIMEOUT after about 5 s) until every rank's flag for that
+ * launch is up and adds the slots in rank order, so every rank finishes the
+ * same rows bit for bit. The hook still carries AF_COLL_ROWSUM.
+ *
+ * af_fold_peer_bytes: bytes of one rank's exchange buffer for `world` ranks.
+ * af_fold_set_peer_sum: exchange[q] (q < world <= 8) is rank q's exchange
+ *   buffer as this process addresses it (exchange[rank] its own), 256-byte
+ *   aligned; every buffer must be zero-filled, and the fill complete on every
+ *   rank, before any rank runs the plan. Needs af_fold_set_tensor_parallel
+ *   first. Host-side setting: make it before capturing a run.
+ * af_ipc_export / af_ipc_import / af_ipc_close: CUDA IPC of a device address
+ *   inside any cudaMalloc allocation (a caching allocator's block included):
+ *   export writes the 64-byte handle of the enclosing allocation and the
+ *   address's offset in it; import maps a handle exported by another process
+ *   of this node (peer access enabled on first use) and returns the mapped
+ *   address of the same byte (`ptr`) and the mapping's base, which close
+ *   unmaps.
+ */
+int af_fold_peer_bytes(void* plan, int32_t world, int64_t* bytes);
+int af_fold_set_peer_sum(void* plan, int32_t rank, int32_t world, void* const* exchange);
+int af_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int af_ipc_import(const void* handle, int64_t offset, void** ptr, void** base);
+int af_ipc_close(void* base);
+
+/*
  * Promotion of a verified child to a parent. Replaces the child branch's own
  * ActivationCache entries, which the reference writes after every merge
  * (_store_activations, actfold/core/folded_transformer.py:190-199 and
