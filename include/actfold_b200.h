@@ -161,9 +161,10 @@ int af_linear_bf16(const void* x, int64_t ldx, int64_t m_cap, const int32_t* m_d
  * a thread-block cluster (up to 24 blocks of 128 keys), or one CTA per query
  * tile and head streaming every key block with an online softmax (contiguous
  * queries: qsrc null, no candidate keys; chosen when those CTAs fill the GPU,
- * or when the sequence is too long for key splits). Gathered queries over more
- * than 24 key blocks use an mma.sync kernel. status (nullable) receives
- * AF_STATUS_TIMEOUT if a bounded wait ran out.
+ * or when the sequence is too long for key splits). Gathered queries or
+ * candidate keys over more than 24 key blocks are refused with AF_ERR_ARG
+ * before any launch. status (nullable) receives AF_STATUS_TIMEOUT if a
+ * bounded wait ran out.
  */
 int af_attention_bf16(const void* q, int64_t q_ld, const int32_t* qsrc, const int32_t* qchild,
                       const int32_t* n_q_dev, int64_t n_q_cap, const void* pk, const void* pv,

@@ -2,9 +2,8 @@
 
 Tolerance: the kernel feeds bf16 probabilities to the tensor cores, so the
 max error is bounded at 2e-2 of the output scale. Each case runs on the
-tcgen05 kernels as chosen by shape, on the streaming tcgen05 kernel where it
-applies (af_set_attention_kernel), and on the mma.sync kernel
-(ACTFOLD_ATTN_IMPL=mma).
+tcgen05 kernels as chosen by shape, and on the streaming tcgen05 kernel where
+it applies (af_set_attention_kernel).
 """
 
 from __future__ import annotations
@@ -32,14 +31,13 @@ def _err(a, b):
     return float((a.float() - b.float()).abs().max() / b.float().abs().max())
 
 
-@pytest.fixture(params=["tc", "stream", "mma"])
-def impl(request, monkeypatch):
-    """tcgen05 kernels with the shape-based choice, the streaming kernel forced
-    wherever it applies (contiguous queries, no candidate keys), and mma.sync."""
+@pytest.fixture(params=["tc", "stream"])
+def impl(request):
+    """tcgen05 kernels with the shape-based choice, and the streaming kernel
+    forced wherever it applies (contiguous queries, no candidate keys)."""
     from actfold_b200 import _lib
 
     lib = _lib.load()
-    monkeypatch.setenv("ACTFOLD_ATTN_IMPL", "mma" if request.param == "mma" else "tc")
     _lib.check(lib.af_set_attention_kernel(1 if request.param == "stream" else 0))
     yield request.param
     _lib.check(lib.af_set_attention_kernel(0))
@@ -116,15 +114,12 @@ def test_fresh_key_overrides(kv, impl):
     assert (out2[4:] == 0).all()
 
 
-@pytest.mark.parametrize("splits", [1, 2, 4, 8])
 @pytest.mark.parametrize("T", [300, 1024])
-def test_key_splits_over_a_cluster(splits, T, monkeypatch, impl):
-    """Every key-split count gives the unsplit result: 8 splits of a 300-key
-    case leave some CTAs without key blocks, 70 queries leave the second query
-    block partly empty, and a dynamic query count cuts it further."""
+def test_key_splits_over_a_cluster(T, impl):
+    """Key splits combined over a cluster give the reference result: 70 queries
+    leave the query tile partly empty, and a dynamic query count cuts it further."""
     from actfold_b200.kernels import attention
 
-    monkeypatch.setenv("ACTFOLD_ATTN_SPLITS", str(splits))  # mma.sync kernel; tcgen05 picks its own
     heads, kv = 4, 2
     fresh = {0: [1, 64, T - 1], 1: [0, 127, 128], 2: list(range(10, 30)), 3: [T // 2]}
     nc = sum(len(v) for v in fresh.values())
@@ -154,3 +149,17 @@ def test_fold_shape_many_children_and_timeout_status(impl):
     torch.cuda.synchronize()
     st.check_status()
     assert _err(out, ref) <= 2e-2
+
+
+def test_unsupported_shape_is_refused_before_launch():
+    """Gathered queries over more than 24 key blocks fit neither tcgen05 kernel: the call raises ValueError (AF_ERR_ARG,
+    checked on the host before any launch) instead of running anything."""
+    from actfold_b200.kernels import attention
+
+    T, heads = 25 * 128, 2
+    q = torch.zeros(4, heads * 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(T, heads * 128, device="cuda", dtype=torch.bfloat16)
+    qsrc = torch.tensor([3, 2, 1, 0], dtype=torch.int32, device="cuda")
+    with pytest.raises(ValueError, match="24 key blocks"):
+        attention(q, k, k, heads, heads, qsrc=qsrc)
+    torch.cuda.synchronize()
