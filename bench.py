@@ -75,8 +75,9 @@ def parse_args():
     ap.add_argument("--tp", action="store_true",
                     help="tensor parallel: every rank verifies the same children (--global-children, default "
                          "--children) with its slice of the weights; cross-rank sums inside the pass")
-    ap.add_argument("--tp-sums", choices=("peer", "nccl"), default="peer",
-                    help="with --tp: the per-layer O / down sums through peer memory (default) or NCCL all-reduces")
+    ap.add_argument("--tp-sums", choices=("auto", "peer", "nccl"), default="auto",
+                    help="with --tp: the per-layer O / down sums through peer memory or NCCL all-reduces "
+                         "(auto: peer memory on 2 GPUs, NCCL on more)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch the pass kernel by kernel instead of replaying its CUDA graph")
     ap.add_argument("--block-decoding", action="store_true",

@@ -1,6 +1,6 @@
-"""The tensor-parallel folded pass on 2 GPUs against the one-GPU pass (skipped with fewer GPUs).
+"""The tensor-parallel folded pass on 2 to 8 GPUs against the one-GPU pass (skipped with fewer than 2).
 
-Two NCCL ranks each hold a slice of the weights (actfold_b200.tensor_parallel)
+The NCCL ranks each hold a slice of the weights (actfold_b200.tensor_parallel)
 and verify the same children; rank r's logits are its vocabulary slice. Each
 rank also runs the one-GPU pass with the whole model and compares:
 
@@ -10,8 +10,8 @@ rank also runs the one-GPU pass with the whole model and compares:
 * its logits slice: relative error <= 2e-2 of the scale, cosine >= 0.999;
 * scores (means over the whole vocabulary) within 2e-2 of the logits' scale.
 
-Shapes: the tiny LLaDA block, and 2 layers of the LLaDA-8B shapes (8 children
-x 1024 tokens, d = 16). Both ways of adding the O / down sums over the ranks
+Shapes: the tiny LLaDA block on 2 GPUs, and 2 layers of the LLaDA-8B shapes
+(8 children x 1024 tokens, d = 16) on every GPU of the box (2, 4 or 8). Both ways of adding the O / down sums over the ranks
 run: through peer memory (the default) and through NCCL all-reduces. The ranks run as child processes (NCCL_NVLS_ENABLE=0)
 with a 120 s process-group timeout.
 """
@@ -104,18 +104,20 @@ def test_tensor_parallel_pass_matches_one_gpu(name, sums):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, sums, q)) for r in range(2)]
+    # The tiny model has 2 heads; the LLaDA-8B layers split over every GPU of the box (2, 4 or 8).
+    world = 2 if name == "tiny" else max(w for w in (2, 4, 8) if w <= torch.cuda.device_count())
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, sums, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
-    for _ in range(2):
+    for _ in range(world):
         rank, msg = q.get(timeout=600)
         out[rank] = msg
     for p in procs:
         p.join(timeout=120)
         if p.is_alive():
             p.kill()
-    assert out == {0: "ok", 1: "ok"}, out
+    assert out == {r: "ok" for r in range(world)}, out
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
