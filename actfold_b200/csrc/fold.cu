@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_rows(const __nv_bfloat1
                                                               float eps, const int* n_dev, int n_cap,
                                                               __nv_bfloat16* out, const PartialRows pr) {
   pdl_trigger();
-  __shared__ float red[2 * kRowThreads / 32];
+  __shared__ __align__(16) float red[2 * kRowThreads / 32];
   const int i = blockIdx.x;  // < n_cap: the index arrays are read before the count is known
   // The residual row index was written two or more kernels back and is
   // usually in place before the wait: the row loads go out with it at once,
@@ -510,7 +510,7 @@ struct FoldGateArgs {
 template <int METRIC, int NV>
 __global__ void __launch_bounds__(kRowThreads) k_fold_gate(const FoldGateArgs g) {
   pdl_trigger();
-  __shared__ float red[2 * kRowThreads / 32];
+  __shared__ __align__(16) float red[2 * kRowThreads / 32];
   const int tid = threadIdx.x;
   const int r = blockIdx.x;  // < m_cap: the candidate arrays are read before the count is known
   const int nvec = g.H / 8;
@@ -681,7 +681,7 @@ __global__ void __launch_bounds__(kRowThreads) k_self_gate(const __nv_bfloat16* 
                                                            uint8_t* self_stable) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float red[2 * kRowThreads / 32];
+  __shared__ __align__(16) float red[2 * kRowThreads / 32];
   const int t = blockIdx.x;
   if (t >= T) return;
   const int nvec = H / 8;
@@ -733,7 +733,7 @@ template <int NV>
 __global__ void __launch_bounds__(kRowThreads) k_promote_rows(const PromoteArgs a) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float red[2 * kRowThreads / 32];
+  __shared__ __align__(16) float red[2 * kRowThreads / 32];
   const int j = blockIdx.x, l = blockIdx.y;
   if (j >= min(a.n_cand[l], a.m_cap)) return;
   const int64_t cj = (int64_t)l * a.m_cap + j;

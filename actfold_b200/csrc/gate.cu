@@ -16,6 +16,7 @@
 // fp32 product lies within 4 ulp of a bf16 rounding midpoint, so the bf16
 // result equals bf16(fp32(x / n)) exactly.
 #include "gate_row.cuh"
+#include "tc_common.cuh"
 
 namespace af {
 
@@ -33,6 +34,7 @@ struct GateParams {
 
 template <int DT, int METRIC, int NV>
 __global__ void __launch_bounds__(256) k_gate_vec(const GateParams p) {
+  pdl_trigger();  // the compaction kernel may launch now; it waits for this grid
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
@@ -59,7 +61,8 @@ constexpr int kGateRowThreads = 256;
 
 template <int DT, int METRIC, int NV>
 __global__ void __launch_bounds__(kGateRowThreads) k_gate_row(const GateParams p) {
-  __shared__ float red[2 * kGateRowThreads / 32];
+  pdl_trigger();  // the compaction kernel may launch now; it waits for this grid
+  __shared__ __align__(16) float red[2 * kGateRowThreads / 32];
   const int64_t row = blockIdx.x;
   if (row >= p.rows) return;
   const int64_t b = row / p.T, t = row - b * p.T;
@@ -80,15 +83,45 @@ __global__ void __launch_bounds__(kGateRowThreads) k_gate_row(const GateParams p
 // bf16 cosine gate of children against ONE parent row per position (parent
 // batch stride 0, the cached parent broadcast over the children): CTA
 // (t, chunk) takes position t for kBcastChildren children. The parent row is
-// loaded and normalised once; each child's row is loaded while the previous
-// child's row is reduced, so the CTA streams rows instead of waiting on one.
-// Same per-thread summation order as gate_regs_bf16_cos: the same bits.
+// loaded and normalised once (kept as bf16x2 words). The children's rows
+// stream through a ring of kBcastRing shared-memory slots filled by bulk
+// copies (one per row, completing on the slot's mbarrier), so up to
+// kBcastRing rows per CTA are in flight whatever the register budget.
+//
+// The per-element chain runs on packed pairs, so the instruction count per
+// element roughly halves (the kernel was bound by instruction issue): x^2
+// sums and x * (1/n) as fp32x2 FMA / MUL, the two quotients rounded to bf16 by
+// one cvt.rn.bf16x2, both products y_c * y_p by one mul.rn.bf16x2, and the
+// products added into two fp32 accumulators (even and odd elements) by one
+// fp32x2 add. The rounding points are the reference's: a product of two bf16
+// values is exact in fp32, so rounding it once to bf16 equals rnd(fp32
+// product); x * (1/n) rounds to the same bf16 as x / n (rcp_for_bf16_quot)
+// except where x / n is an fp32 subnormal, and such products (and any
+// product below 2^-126) are too small to change a similarity sum of normal
+// size. Only the order of the fp32 additions differs from the reference's
+// (whose order is ATen's), as it does for every other gate kernel here.
 constexpr int kBcastChildren = 8;
+constexpr int kBcastRing = 4;
+// 128 threads per row: with the packed chain the block reductions and the
+// per-row steps (square root, reciprocal, ring wait, outputs) are a large
+// share of the instructions, and 32 elements per thread halve it against 256
+// threads (the kernel is bound by instruction issue).
+constexpr int kBcastThreads = 128;
+
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
 
 template <int NV>
-__global__ void __launch_bounds__(kGateRowThreads) k_gate_bcast(const GateParams p) {
-  constexpr int G = kGateRowThreads;
-  __shared__ float red[2 * G / 32];
+__global__ void __launch_bounds__(kBcastThreads) k_gate_bcast(const GateParams p) {
+  pdl_trigger();  // the compaction kernel may launch now; it waits for this grid
+  constexpr int G = kBcastThreads;
+  extern __shared__ __align__(128) uint4 ring[];  // [kBcastRing][nvec] child rows
+  __shared__ __align__(16) float red[2 * G / 32];
+  __shared__ __align__(8) uint64_t full[kBcastRing];
+  __shared__ volatile int fail;
   const CtaRows<G> rows{red};
   const int tid = threadIdx.x;
   const int64_t t = blockIdx.x;
@@ -96,71 +129,91 @@ __global__ void __launch_bounds__(kGateRowThreads) k_gate_bcast(const GateParams
   const int64_t b0 = (int64_t)blockIdx.y * kBcastChildren;
   const int64_t b1 = min(B, b0 + kBcastChildren);
   if (t >= p.T || b0 >= B) return;
-  uint4 pv[NV], cv[NV], nv[NV];
-  load_row<NV, G>(p.parent + t * p.p_ts, p.nvec, tid, pv);
-  load_row<NV, G>(p.child + b0 * p.c_bs + t * p.c_ts, p.nvec, tid, cv);
-  // Parent: norm and normalised values, once.
-  float yp[NV][8];
-  float sp = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    unpack<AF_DTYPE_BF16>(pv[i], yp[i]);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sp = fmaf(yp[i][e], yp[i][e], sp);
+  const int nb = (int)(b1 - b0);
+  const uint32_t row_bytes = (uint32_t)p.nvec * 16u;
+  auto issue = [&](int k) {  // child b0 + k into slot k % kBcastRing (thread 0)
+    const uint32_t bar = smem_u32(&full[k % kBcastRing]);
+    mbar_arrive_expect_tx(bar, row_bytes);
+    bulk_load_g2s(smem_u32(ring + (k % kBcastRing) * p.nvec), p.child + (b0 + k) * p.c_bs + t * p.c_ts, row_bytes,
+                  bar);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kBcastRing; ++s) mbar_init(smem_u32(&full[s]), 1);
+    fail = 0;
+    fence_barrier_init();
+    for (int k = 0; k < min(kBcastRing, nb); ++k) issue(k);
   }
-  sp = rows.sum(sp);
-  float np = rnd<AF_DTYPE_BF16>(__fsqrt_rn(sp));
-  np = np < p.k.eps_r ? p.k.eps_r : np;  // clamp_min keeps NaN
-  const float rp = __frcp_rn(np);
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float2 y = __bfloat1622float2(
-          __floats2bfloat162_rn(quot_bf16(yp[i][e], np, rp), quot_bf16(yp[i][e + 1], np, rp)));
-      yp[i][e] = y.x;
-      yp[i][e + 1] = y.y;
-    }
-  for (int64_t b = b0; b < b1; ++b) {
-    if (b + 1 < b1) load_row<NV, G>(p.child + (b + 1) * p.c_bs + t * p.c_ts, p.nvec, tid, nv);
-    float fc[NV][8];
-    float sc = 0.f;
+  uint4 pv[NV];
+  load_row<NV, G>(p.parent + t * p.p_ts, p.nvec, tid, pv);
+  // Parent: norm and normalised values (bf16x2 words), once.
+  uint32_t yp[NV][4];
+  {
+    float fp[NV][8];
+    float sp = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      unpack<AF_DTYPE_BF16>(cv[i], fc[i]);
+      unpack<AF_DTYPE_BF16>(pv[i], fp[i]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sc = fmaf(fc[i][e], fc[i][e], sc);
+      for (int e = 0; e < 8; ++e) sp = fmaf(fp[i][e], fp[i][e], sp);
     }
-    sc = rows.sum(sc);
-    float nc = rnd<AF_DTYPE_BF16>(__fsqrt_rn(sc));
+    sp = rows.sum(sp);  // its barriers also publish the ring's barrier set-up
+    float np = rnd<AF_DTYPE_BF16>(__fsqrt_rn(sp));
+    np = np < p.k.eps_r ? p.k.eps_r : np;  // clamp_min keeps NaN
+    const float rp = __frcp_rn(np);
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; e += 2)
+        yp[i][e / 2] = bf2_round(f2_pack(quot_bf16(fp[i][e], np, rp), quot_bf16(fp[i][e + 1], np, rp)));
+  }
+  for (int k = 0; k < nb; ++k) {
+    const int slot = k % kBcastRing;
+    const bool landed = mbar_wait(smem_u32(&full[slot]), (uint32_t)(k / kBcastRing) & 1u, &fail);
+    if (!landed) fail = 1;  // bounded wait ran out: this row's outputs are marked invalid below
+    uint64_t xc[NV][4];
+    uint64_t sc2 = 0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * G + tid;
+      const uint4 v = j < p.nvec ? ring[slot * p.nvec + j] : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        xc[i][e] = bf2_widen(w[e]);
+        sc2 = f2_fma(xc[i][e], xc[i][e], sc2);
+      }
+    }
+    // After this sum's barriers every thread has read the slot: refill it.
+    float nc = sqrt_to_bf16(rows.sum(f2_lo(sc2) + f2_hi(sc2)));
+    if (tid == 0 && k + kBcastRing < nb && !fail) {
+      fence_proxy_async_smem();
+      issue(k + kBcastRing);
+    }
     nc = nc < p.k.eps_r ? p.k.eps_r : nc;  // clamp_min keeps NaN
-    const float rc = __frcp_rn(nc);
-    float s = 0.f;
+    const float rc = rcp_for_bf16_quot(nc);
+    const uint64_t rc2 = f2_pack(rc, rc);
+    uint64_t s2 = 0;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       if (i * G + tid >= p.nvec) continue;
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const float2 yc = __bfloat1622float2(
-            __floats2bfloat162_rn(quot_bf16(fc[i][e], nc, rc), quot_bf16(fc[i][e + 1], nc, rc)));
-        const float2 pr =
-            __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(yc.x, yp[i][e]), __fmul_rn(yc.y, yp[i][e + 1])));
-        s = __fadd_rn(s, pr.x);
-        s = __fadd_rn(s, pr.y);
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t yc = bf2_round(f2_mul(xc[i][e], rc2));
+        s2 = f2_add(s2, bf2_widen(bf2_mul(yc, yp[i][e])));
       }
     }
-    const float sim = rnd<AF_DTYPE_BF16>(rows.sum(s));
+    const float sim = rnd<AF_DTYPE_BF16>(rows.sum(f2_lo(s2) + f2_hi(s2)));
     if (tid == 0) {
-      p.mask[b * p.m_bs + t] = sim > p.k.tau_r ? 1 : 0;
-      if (p.sim) p.sim[b * p.T + t] = sim;
+      const int64_t b = b0 + k;
+      p.mask[b * p.m_bs + t] = (!fail && sim > p.k.tau_r) ? 1 : 0;
+      if (p.sim) p.sim[b * p.T + t] = fail ? __int_as_float(0x7fc00000) : sim;
     }
-#pragma unroll
-    for (int i = 0; i < NV; ++i) cv[i] = nv[i];
   }
 }
 
 template <int DT, int METRIC>
 __global__ void __launch_bounds__(256) k_gate_scalar(const GateParams p) {
+  pdl_trigger();  // the compaction kernel may launch now; it waits for this grid
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= p.rows) return;
@@ -181,6 +234,7 @@ __global__ void __launch_bounds__(1024) k_compact(const uint8_t* __restrict__ ma
                                                   int64_t idx_bs, int32_t* __restrict__ div_count) {
   __shared__ int warp_tot[32];
   __shared__ int chunk_base[2];
+  pdl_wait();  // launched as a programmatic dependent of the gate kernel: its masks are complete past this
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   int base_d = 0, base_s = 0;
@@ -236,13 +290,15 @@ static int launch_gate(const GateParams& p, bool vec, cudaStream_t s) {
     return check_launch("af_gate(scalar)");
   }
   if constexpr (DT == AF_DTYPE_BF16 && METRIC == AF_METRIC_COSINE) {
-    if (p.p_bs == 0 && p.nvec > 64 && p.nvec <= 2 * kGateRowThreads) {
+    if (p.p_bs == 0 && p.nvec > 64 && p.nvec <= 4 * kBcastThreads) {
       const int64_t B = p.rows / p.T;
       if (p.T > 0x7fffffff) return fail(AF_ERR_ARG, "af_gate: seq too large");
       const dim3 grid((unsigned)p.T, (unsigned)ceil_div(B, (int64_t)kBcastChildren));
       if (grid.y > 65535) return fail(AF_ERR_ARG, "af_gate: batch too large");
-      if (p.nvec <= kGateRowThreads) k_gate_bcast<1><<<grid, kGateRowThreads, 0, s>>>(p);
-      else k_gate_bcast<2><<<grid, kGateRowThreads, 0, s>>>(p);
+      const size_t ring_bytes = (size_t)kBcastRing * p.nvec * 16;  // <= 32 KB: no opt-in needed
+      if (p.nvec <= kBcastThreads) k_gate_bcast<1><<<grid, kBcastThreads, ring_bytes, s>>>(p);
+      else if (p.nvec <= 2 * kBcastThreads) k_gate_bcast<2><<<grid, kBcastThreads, ring_bytes, s>>>(p);
+      else k_gate_bcast<4><<<grid, kBcastThreads, ring_bytes, s>>>(p);
       return check_launch("af_gate(broadcast)");
     }
   }
@@ -322,7 +378,11 @@ extern "C" int af_gate(const void* child, int64_t child_bstride, int64_t child_t
   const bool vec = (align % 16) == 0 && p.nvec <= 16 * 32;
   int st = gate_launch(p, dtype, metric, vec, s);
   if (st != AF_OK || !div_idx) return st;
-  k_compact<<<(unsigned)batch, 1024, 0, s>>>(stable_mask, mask_bstride, seq, stable_idx, div_idx, idx_bstride,
-                                              div_count);
+  // Programmatic dependent launch: the compaction's CTAs are set up while the
+  // gate's last CTAs run, and wait for the gate grid inside the kernel.
+  const cudaError_t e = launch_ex(k_compact, dim3((unsigned)batch), dim3(1024), 0, s, true, dim3(1, 1, 1),
+                                  (const uint8_t*)stable_mask, mask_bstride, (int64_t)seq, stable_idx, div_idx,
+                                  idx_bstride, div_count);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("af_gate: compact launch: ") + cudaGetErrorString(e));
   return check_launch("af_gate(compact)");
 }

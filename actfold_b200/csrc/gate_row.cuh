@@ -103,10 +103,17 @@ struct CtaRows {
     a = x;
     b = y;
   }
+  // One value: the same warp sums and the same order of the cross-warp adds
+  // as sum2's first value, with half its shuffles and shared-memory reads.
   __device__ __forceinline__ float sum(float v) const {
-    float z = 0.f;
-    sum2(v, z);
-    return v;
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float x = 0.f;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) x += red[i];
+    __syncthreads();
+    return x;
   }
 };
 
@@ -251,6 +258,67 @@ __device__ __forceinline__ float quot_bf16(float x, float n, float r) {
   float y = __fmul_rn(x, r);
   if (fabsf(y) < 0x1p-125f) y = __fdiv_rn(x, n);
   return y;  // rounded to bf16 by the caller
+}
+
+// Packed pair arithmetic (sm_100): two fp32 lanes in one 64-bit register
+// (element 0 in the low half) and bf16x2 words (element 0 in the low half).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// bf16x2 word of rnd(lo), rnd(hi) (round to nearest even).
+__device__ __forceinline__ uint32_t bf2_round(uint64_t v) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(f2_hi(v)), "f"(f2_lo(v)));
+  return r;
+}
+// Both products of two bf16x2 words, each rounded once to bf16.
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// A bf16x2 word as two fp32 lanes (exact).
+__device__ __forceinline__ uint64_t bf2_widen(uint32_t w) { return f2_pack(bf16_lo(w), bf16_hi(w)); }
+
+// rnd_bf16(sqrt(x)) for x >= 0: the approximate square root (within a few
+// fp32 ulp), and the IEEE one only where the approximation lies within 8 ulp
+// of a bf16 rounding midpoint, so the bf16 result is that of the exact root.
+__device__ __forceinline__ float sqrt_to_bf16(float x) {
+  float s;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(s) : "f"(x));
+  const int low = (int)(__float_as_uint(s) & 0xffffu) - 0x8000;
+  if (low >= -8 && low <= 8) s = __fsqrt_rn(x);
+  return rnd<AF_DTYPE_BF16>(s);
+}
+
+// 1 / n for a bf16 n > 0, for the quotients x * (1/n) of bf16 values: the
+// approximate reciprocal is within 2^-22 of 1/n, and every exact quotient of
+// two bf16 values that is not an fp32 subnormal lies at least 2^-17 (relative)
+// from a bf16 rounding midpoint (quot_bf16), so x * (1/n) still rounds to the
+// bf16 value of x / n.
+__device__ __forceinline__ float rcp_for_bf16_quot(float n) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(n));
+  return r;
 }
 
 // gate_regs<bf16, cosine> with the same per-thread order of every fp32 sum, so
