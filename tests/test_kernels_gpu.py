@@ -90,6 +90,45 @@ def test_gate_broadcast_parent_kernel(B, H):
     assert ((sim_b == ora.sim) | (np.isnan(sim_b) & np.isnan(ora.sim))).mean() >= 0.999
 
 
+def test_gate_broadcast_extreme_magnitudes_match_oracle():
+    """The broadcast kernel's packed chain (x * approximate 1/n, one bf16 rounding per product) against the
+    oracle's exact chain on rows built to reach its edges: bf16 subnormal elements beside normal ones (their
+    quotients are fp32 subnormals), a row of subnormals only (norm clamped to eps), zero elements and rows,
+    rows whose squares overflow fp32 (norm inf), and a NaN element. Masks and similarity bits equal the
+    oracle's on every row."""
+    from actfold_b200.core import SimilarityGate
+    from oracle.numerics import round_bf16
+
+    B, T, H = 8, 16, 4096
+    rng = np.random.default_rng(7)
+    parent = rng.standard_normal((1, T, H), dtype=np.float32)
+    child = np.repeat(parent, B, axis=0) + np.float32(0.05) * rng.standard_normal((B, T, H), dtype=np.float32)
+    sub = np.float32(2.0 ** -133)  # smallest bf16 subnormal
+    child[0, 0, ::7] = sub
+    child[0, 1, ::3] = -sub
+    child[1, 2] = sub * rng.integers(1, 100, H).astype(np.float32)  # subnormals only
+    child[2, 3] = 0.0
+    child[2, 4, ::2] = 0.0
+    child[3, 5] *= np.float32(2.0 ** 70)  # squares overflow fp32
+    child[4, 6, 100] = np.nan
+    parent[0, 7, ::5] = sub  # the parent row itself holds subnormals
+    child = round_bf16(child)
+    parent = round_bf16(parent)
+    sg = SimilarityGate(tau=0.95)
+    tp = torch.from_numpy(parent).to(torch.bfloat16).cuda().expand(B, T, H)  # batch stride 0: broadcast kernel
+    tc = torch.from_numpy(child).to(torch.bfloat16).cuda()
+    sim = sg.similarity(tc, tp).cpu().numpy()
+    mask = sg(tc, tp).cpu().numpy()
+    ora = gate(child, np.broadcast_to(parent, child.shape), 0.95, "cosine", 1e-8, "bf16")
+    same = (sim.view(np.uint32) == ora.sim.view(np.uint32)) | (np.isnan(sim) & np.isnan(ora.sim))
+    edges = [(0, 0), (0, 1), (1, 2), (2, 3), (2, 4), (3, 5), (4, 6)] + [(b, 7) for b in range(B)]
+    assert all(same[e] for e in edges), [e for e in edges if not same[e]]
+    # Ordinary rows: the fp32 sums run in another order than the oracle's, which can move a similarity
+    # across a bf16 rounding boundary only rarely.
+    assert same.mean() >= 0.99, same.mean()
+    assert not ((mask != ora.mask) & ~exempt_rows(ora)).any()
+
+
 @pytest.mark.parametrize("H", [4096, 3584, 100])
 def test_gate_large_and_odd_hidden(H):
     from actfold_b200.core import SimilarityGate
