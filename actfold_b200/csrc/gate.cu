@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kGateRowThreads) k_gate_row(const GateParams p
 // size. Only the order of the fp32 additions differs from the reference's
 // (whose order is ATen's), as it does for every other gate kernel here.
 constexpr int kBcastChildren = 8;
-constexpr int kBcastRing = 4;
+constexpr int kBcastRing = 3;
 // 128 threads per row: with the packed chain the block reductions and the
 // per-row steps (square root, reciprocal, ring wait, outputs) are a large
 // share of the instructions, and 32 elements per thread halve it against 256
@@ -295,7 +295,7 @@ static int launch_gate(const GateParams& p, bool vec, cudaStream_t s) {
       if (p.T > 0x7fffffff) return fail(AF_ERR_ARG, "af_gate: seq too large");
       const dim3 grid((unsigned)p.T, (unsigned)ceil_div(B, (int64_t)kBcastChildren));
       if (grid.y > 65535) return fail(AF_ERR_ARG, "af_gate: batch too large");
-      const size_t ring_bytes = (size_t)kBcastRing * p.nvec * 16;  // <= 32 KB: no opt-in needed
+      const size_t ring_bytes = (size_t)kBcastRing * p.nvec * 16;  // <= 24 KB: eight CTAs per SM
       if (p.nvec <= kBcastThreads) k_gate_bcast<1><<<grid, kBcastThreads, ring_bytes, s>>>(p);
       else if (p.nvec <= 2 * kBcastThreads) k_gate_bcast<2><<<grid, kBcastThreads, ring_bytes, s>>>(p);
       else k_gate_bcast<4><<<grid, kBcastThreads, ring_bytes, s>>>(p);
