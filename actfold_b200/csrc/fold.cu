@@ -1238,7 +1238,7 @@ struct FoldPlan {
   FoldWs w;
   int ntok;
   std::vector<CUtensorMap> tm_qkv, tm_o, tm_gu, tm_down;
-  CUtensorMap tm_lm, tx_A, tx_att, tx_bn, tx_f, tx_qkv;
+  CUtensorMap tm_lm, tx_A, tx_Alm, tx_att, tx_bn, tx_f, tx_qkv;  // tx_Alm: w.A for the LM head
   KernelTimer tk;
   int64_t last_launches = 0;
   // Side stream of the pass: the logits fill of stable rows runs there from the
@@ -1270,8 +1270,10 @@ struct FoldPlan {
 
 static int build_maps(FoldPlan* p) {
   const Sizes z = sizes_of(p->model.dims);
-  const int nt = gemm_xbox(gemm_ntok(p->m_cap));  // token rows per box of the activation maps
-  p->ntok = gemm_ntok(p->m_cap);
+  // Token rows per box of each activation map: those of the token tile of the
+  // GEMM that reads it (w.A feeds QKV and the LM head: one map each).
+  auto nt = [&](int n) { return gemm_xbox(gemm_ntok(p->m_cap, n)); };
+  p->ntok = gemm_ntok(p->m_cap, z.qkv);
   int st;
   p->tm_qkv.resize(z.L);
   p->tm_o.resize(z.L);
@@ -1285,11 +1287,12 @@ static int build_maps(FoldPlan* p) {
     if ((st = make_tmap_bf16_tiled(&p->tm_down[l], lw.w_down, z.H, z.FF))) return st;
   }
   if ((st = make_tmap_bf16_tiled(&p->tm_lm, p->model.lm_head, z.V, z.H))) return st;
-  if ((st = make_tmap_bf16(&p->tx_A, p->w.A, p->m_cap, z.H, z.H, nt))) return st;
-  if ((st = make_tmap_bf16(&p->tx_att, p->w.att, p->m_cap, z.q, z.q, nt))) return st;
-  if ((st = make_tmap_bf16(&p->tx_bn, p->w.bn, p->m_cap, z.H, z.H, nt))) return st;
+  if ((st = make_tmap_bf16(&p->tx_A, p->w.A, p->m_cap, z.H, z.H, nt(z.qkv)))) return st;
+  if ((st = make_tmap_bf16(&p->tx_Alm, p->w.A, p->m_cap, z.H, z.H, nt(z.V)))) return st;
+  if ((st = make_tmap_bf16(&p->tx_att, p->w.att, p->m_cap, z.q, z.q, nt(z.H)))) return st;
+  if ((st = make_tmap_bf16(&p->tx_bn, p->w.bn, p->m_cap, z.H, z.H, nt(2 * z.FF)))) return st;
   if ((st = make_tmap_bf16(&p->tx_qkv, p->w.qkv, p->m_cap, z.qkv, z.qkv, 128))) return st;
-  if ((st = make_tmap_bf16(&p->tx_f, p->w.f, p->m_cap, z.FF, z.FF, nt))) return st;
+  if ((st = make_tmap_bf16(&p->tx_f, p->w.f, p->m_cap, z.FF, z.FF, nt(z.H)))) return st;
   return AF_OK;
 }
 
@@ -1732,7 +1735,7 @@ static int fold_run(FoldPlan* p, const int64_t* ctok, __nv_bfloat16* logits, flo
   c.out_rows = pos_last;
   c.row_sums = w.row_sums;
   c.tmap_w = &p->tm_lm;
-  c.tmap_x = &p->tx_A;
+  c.tmap_x = &p->tx_Alm;
   AF_TIMED(FK_LM, if ((st = gemm_run(c, s))) return st);
   if (p->coll && (st = collective(p, AF_COLL_ROWSUM, L - 1, w.row_sums, (int64_t)C * T, s))) return st;
   if (fork_fill) {

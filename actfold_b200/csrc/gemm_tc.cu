@@ -38,6 +38,7 @@ constexpr int kTileN = 128;   // weight rows per CTA (MMA M)
 constexpr int kThreads = 192;
 constexpr int kMaxSplits = 8; // portable cluster size
 constexpr int kMaxPartialSplits = 16;  // launches that leave partials need no cluster
+constexpr int kEpiTok = 256;            // tokens staged per epilogue chunk (wide token tiles take two)
 
 struct GemmDev {
   int n, k, m_cap, ntok, n_tiles, m_tiles, nkb, kb_per_split, splits, stages;
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const int nkb = min(p.kb_per_split, p.nkb - kb0);
   const int S = p.stages;
   // This CTA's token rows per stage: the whole tile, or its half of it in a pair.
-  const int xrows = kPair ? p.xbox : p.ntok;
+  const int xrows = kPair ? p.ntok / 2 : p.ntok;
   const uint32_t w_bytes = kTileN * kBlockK * 2, x_bytes = xrows * kBlockK * 2;
   const uint32_t stage_bytes = w_bytes + x_bytes;
 
@@ -271,7 +272,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   };
   auto load_x = [&](int i, uint32_t dst, uint32_t bar) {
     if constexpr (kPair) {
-      tma_load_2d_pair(dst, &tmX, bar, kb_of(i) * kBlockK, m0 + prank * p.xbox);
+      // Box h of CTA r holds tokens m0 + (2h + r) * xbox: the pair's MMA h
+      // (one box of each CTA) then covers tokens [2h * xbox, (2h + 2) * xbox).
+      for (int h = 0; 2 * h * p.xbox < p.ntok; ++h)
+        tma_load_2d_pair(dst + (uint32_t)(h * p.xbox) * (kBlockK * 2), &tmX, bar, kb_of(i) * kBlockK,
+                         m0 + (2 * h + prank) * p.xbox);
     } else {
       for (int h = 0; h < p.ntok; h += p.xbox)
         tma_load_2d(dst + (uint32_t)h * (kBlockK * 2), &tmX, bar, kb_of(i) * kBlockK, m0 + h);
@@ -393,7 +398,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     *issued_slot = i;
   } else if (warp == 1 && lane == 0 && leader) {
     // ---------------- MMA issuer ----------------
-    const uint32_t idesc = idesc_bf16(kPair ? 2 * kTileN : kTileN, p.ntok);
+    // Token tiles wider than 256 run as 256-token MMAs side by side in TMEM.
+    const int nsub = p.ntok > 256 ? p.ntok / 256 : 1;
+    const uint32_t sub_b = (uint32_t)(kPair ? p.xbox : 256) * (kBlockK * 2);  // B bytes per sub-MMA per CTA
+    const uint32_t idesc = idesc_bf16(kPair ? 2 * kTileN : kTileN, p.ntok > 256 ? 256 : p.ntok);
     bool ready = true;
     if constexpr (kPair) {
       ready = mbar_wait(alloc_bar, 0, abort_flag);
@@ -413,16 +421,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       }
       tc_fence_after();
       const uint32_t st = base + s * stage_bytes;
-      const uint64_t adesc = sw128_desc(st), bdesc = sw128_desc(st + w_bytes);
+      const uint64_t adesc = sw128_desc(st);
       if constexpr (kPair) {
+        for (int h = 0; h < nsub; ++h) {
+          const uint64_t bdesc = sw128_desc(st + w_bytes + (uint32_t)h * sub_b);
 #pragma unroll
-        for (int kk = 0; kk < kBlockK / 16; ++kk)
-          tc_mma_bf16_pair(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBlockK / 16; ++kk)
+            tc_mma_bf16_pair(tmem + (uint32_t)(256 * h), adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                             (i | kk) != 0 ? 1u : 0u);
+        }
         tc_commit_pair_both(empty0 + 8 * s);
       } else {
+        for (int h = 0; h < nsub; ++h) {
+          const uint64_t bdesc = sw128_desc(st + w_bytes + (uint32_t)h * sub_b);
 #pragma unroll
-        for (int kk = 0; kk < kBlockK / 16; ++kk)
-          tc_mma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBlockK / 16; ++kk)
+            tc_mma_bf16(tmem + (uint32_t)(256 * h), adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        }
         tc_commit(empty0 + 8 * s);
       }
     }
@@ -467,61 +482,69 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       *abort_flag = 1;
     }
     tc_fence_after();
-    if (!*abort_flag) {
-      // Thread r holds tile row r (TMEM lane) across the token columns; the
-      // token-major staging makes a warp's 32 stores one contiguous line.
-      const int nchunk = (Mv + 15) / 16;
-      for (int c = 0; c < nchunk; ++c) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(16 * c), v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) tile[(16 * c + j) * kLdt + r] = v[j];
-      }
-      if (p.push) fence_proxy_async_smem();  // the staged rows are read by bulk copies (async proxy)
-    }
   }
+  // Tokens [t0, t0 + kEpiTok) of the accumulator into `tile` (warps 2-5):
+  // thread r holds tile row r (TMEM lane) across the token columns; the
+  // token-major staging makes a warp's 32 stores one contiguous line.
+  auto stage = [&](int t0) {
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    const int nchunk = (min(kEpiTok, Mv - t0) + 15) / 16;
+    for (int c = 0; c < nchunk; ++c) {
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(t0 + 16 * c), v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) tile[(16 * c + j) * kLdt + r] = v[j];
+    }
+    if (p.push) fence_proxy_async_smem();  // the staged rows are read by bulk copies (async proxy)
+  };
+  if (warp >= 2 && !*abort_flag) stage(0);
   __syncthreads();
   const bool ok = !*abort_flag;
 
-  if (p.partial) {
-    // ---------------- split j's fp32 partial rows to global memory ----------------
-    // Row m of this tile: 128 features = 512 contiguous bytes, one warp-wide
-    // 16-byte store per lane; the consumer sums the splits.
-    if (ok) {
-      float* dst = p.partial + ((int64_t)blockIdx.y * p.m_cap + m0) * p.n + n0;
-      for (int idx = threadIdx.x; idx < Mv * 32; idx += kThreads) {
-        const int m = idx >> 5, c4 = idx & 31;
-        *reinterpret_cast<float4*>(dst + (int64_t)m * p.n + 4 * c4) =
-            *reinterpret_cast<const float4*>(tile + m * kLdt + 4 * c4);
+  if (p.partial || p.splits == 1) {
+   // Wide token tiles are staged and stored kEpiTok tokens at a time (token
+   // m of the tile is row m - t0 of the staged chunk).
+   for (int t0 = 0;;) {
+    const int tn = min(kEpiTok, Mv - t0);
+    if (p.partial) {
+      // ---------------- split j's fp32 partial rows to global memory ----------------
+      // Row m of this tile: 128 features = 512 contiguous bytes, one warp-wide
+      // 16-byte store per lane; the consumer sums the splits.
+      if (ok) {
+        float* dst = p.partial + ((int64_t)blockIdx.y * p.m_cap + m0) * p.n + n0;
+        for (int idx = threadIdx.x; idx < tn * 32; idx += kThreads) {
+          const int m = t0 + (idx >> 5), c4 = idx & 31;
+          *reinterpret_cast<float4*>(dst + (int64_t)m * p.n + 4 * c4) =
+              *reinterpret_cast<const float4*>(tile + (m - t0) * kLdt + 4 * c4);
+        }
       }
-    }
-  } else if (p.splits == 1) {
-    if (ok && p.epi == EPI_SWIGLU) {
+    } else if (ok && p.epi == EPI_SWIGLU) {
       // ---------------- SwiGLU: one unit per (token, gate chunk), all threads ----------------
-      const int total = Mv * 8;
+      const int total = tn * 8;
       for (int u = threadIdx.x; u < total; u += kThreads) {
-        const int m = u >> 3, r0 = 8 * (u & 7);
+        const int m = t0 + (u >> 3), r0 = 8 * (u & 7);
         float a[8], b[8];
-        load8(tile + m * kLdt + r0, a);
-        load8(tile + m * kLdt + r0 + 64, b);
+        load8(tile + (m - t0) * kLdt + r0, a);
+        load8(tile + (m - t0) * kLdt + r0 + 64, b);
         epi_swiglu(p, n0, r0, s_orow[m], a, b);
       }
     } else if (ok) {
       // ---------------- units (token m, chunk pair c / c + 8), warp-uniform loop ----------------
       // Lanes 8k..8k+7 of a warp cover the 8 units of one token, so the logit
       // row sums reduce over groups of 8 lanes.
-      const int total = Mv * 8;
+      const int total = tn * 8;
       for (int base_u = warp * 32; base_u < total; base_u += kThreads) {
         const int u = base_u + lane;
         const bool valid = u < total;
-        const int m = u >> 3, c = u & 7;
+        const int m = t0 + (u >> 3), c = u & 7;
         float rs = 0.f;
         if (valid) {
           EpiOperands o;
           epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
           float a[8], b[8];
-          load8(tile + m * kLdt + 8 * c, a);
-          load8(tile + m * kLdt + 8 * c + 64, b);
+          load8(tile + (m - t0) * kLdt + 8 * c, a);
+          load8(tile + (m - t0) * kLdt + 8 * c + 64, b);
           if (p.epi == EPI_STORE) {
             rs = epi_store(p, n0, 8 * c, s_orow[m], a);
             rs += epi_store(p, n0, 8 * c + 64, s_orow[m], b);
@@ -537,6 +560,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
         }
       }
     }
+    t0 += kEpiTok;
+    if (t0 >= Mv) break;
+    __syncthreads();  // every thread is done with the staged chunk
+    if (warp >= 2 && ok) stage(t0);
+    __syncthreads();
+   }
   } else {
     // ---------------- cluster split-K reduction ----------------
     // CTA j owns tokens [tlo, thi) and sums their units (token m, chunk pair
@@ -754,14 +783,30 @@ int make_tmap_bf16_heads(CUtensorMap* map, const void* base, uint64_t rows, uint
   return AF_OK;
 }
 
-int gemm_ntok(int m_cap) {
+// Row capacities that are multiples of 512 (>= 1024) take 512-token tiles
+// where their (weight tile, token tile) CTAs fill at least two waves of one
+// CTA per SM: two 256-token MMAs per stage, staged and stored 256 tokens at a
+// time, so every weight and activation byte loaded into shared memory feeds
+// twice the MMA work of a 256-token tile (measured on B200 at 1024 rows:
+// gate/up -21 %, LM head -15 %; fewer CTAs, e.g. QKV's 192, lose more to the
+// partly filled last wave than they gain). ACTFOLD_GEMM_WIDE=0 turns it off.
+static bool gemm_wide() {
+  static const bool on = [] {
+    const char* e = getenv("ACTFOLD_GEMM_WIDE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+int gemm_ntok(int m_cap, int n) {
+  if (gemm_wide() && m_cap >= 1024 && m_cap % 512 == 0 && (n / kTileN) * (m_cap / 512) >= 2 * sm_count()) return 512;
   const int mt = (m_cap + 255) / 256;
   int nt = (m_cap + mt - 1) / mt;
   nt = (nt + 15) / 16 * 16;
   return nt < 16 ? 16 : nt;
 }
 
-int gemm_xbox(int ntok) { return ntok % 32 == 0 ? ntok / 2 : ntok; }
+int gemm_xbox(int ntok) { return ntok > 256 ? 128 : (ntok % 32 == 0 ? ntok / 2 : ntok); }
 
 // Paired-CTA launches (tuning override ACTFOLD_GEMM_PAIR=0 keeps single CTAs).
 static bool pair_off() {
@@ -789,7 +834,7 @@ static int env_partial_splits() {
 
 static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_sums, bool partial = false) {
   GemmShape g;
-  g.ntok = gemm_ntok(m_cap);
+  g.ntok = gemm_ntok(m_cap, n);
   g.m_tiles = (m_cap + g.ntok - 1) / g.ntok;
   g.n_tiles = n / kTileN;
   g.nkb = k / kBlockK;
@@ -811,6 +856,7 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   if (partial) splits = std::min(splits, kMaxPartialSplits);
   if (row_sums) splits = 1;
   if (!partial) splits = std::min(splits, kMaxSplits);
+  if (g.ntok > 256 && !partial) splits = 1;  // a wide tile's epilogue has no cluster reduction
   g.kb_per = (g.nkb + splits - 1) / splits;
   g.splits = (g.nkb + g.kb_per - 1) / g.kb_per;
   // CTA pairs need an even number of weight tiles, a token tile that halves
@@ -822,11 +868,11 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   // a launch whose CTAs all fit one per SM and stream long k-ranges (the down
   // projection) gets the deepest ring that fits; otherwise ~100 KB rings let
   // two CTAs share an SM.
-  const bool one_per_sm = tiles * g.splits <= sm_count() && g.kb_per >= 24;
+  const bool one_per_sm = (tiles * g.splits <= sm_count() && g.kb_per >= 24) || g.ntok > 256;
   int st = (one_per_sm ? 220 * 1024 : 100 * 1024) / stage;
   if (env_stages > 0) st = env_stages;
   st = std::max(2, std::min(16, st));
-  const int tile_bytes = g.ntok * kLdt * 4;  // fp32 staging of the accumulator
+  const int tile_bytes = std::min(g.ntok, kEpiTok) * kLdt * 4;  // fp32 staging of the accumulator (one chunk)
   while (st * stage < tile_bytes) ++st;
   // Ring + alignment slack + barriers/flags + per-token metadata (3 ints per
   // token) + the side task's 32-int scan buffer.
@@ -871,6 +917,7 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
   AF_REQUIRE(!partial || (reinterpret_cast<uintptr_t>(c.partial_out) & 15u) == 0, "gemm: partial_out must be 16-byte aligned");
   if (partial) g.push = 0;  // no exchange between the splits: no receive slots in shared memory
   AF_REQUIRE(!g.pair || g.splits == 1 || partial, "gemm: CTA pairs cannot exchange split-K partials");
+  AF_REQUIRE(g.ntok <= 256 || g.splits == 1 || partial, "gemm: wide token tiles need one split or partials");
   AF_REQUIRE(g.smem <= 227 * 1024, "gemm: shared memory budget exceeded");
 
   CUtensorMap tw, tx;

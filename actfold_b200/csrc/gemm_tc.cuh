@@ -54,10 +54,10 @@ struct GemmCall {
 // k-splits a launch of this shape uses (1: no split); `partial`: one that leaves partials.
 int gemm_splits(int n, int k, int m_cap, bool partial = false);
 
-// Token-tile width the kernel uses for a given row capacity.
-int gemm_ntok(int m_cap);
+// Token-tile width the kernel uses for a given row capacity and output width n.
+int gemm_ntok(int m_cap, int n);
 // Token rows per TMA box of the activation operand: tensor maps passed in
-// GemmCall::tmap_x must be built with this box height for gemm_ntok(m_cap).
+// GemmCall::tmap_x must be built with this box height for gemm_ntok(m_cap, n).
 int gemm_xbox(int ntok);
 // Launch (stream-ordered, no synchronisation).
 int gemm_run(const GemmCall& c, cudaStream_t stream);

@@ -150,3 +150,30 @@ def test_linear_tiled_weights(ws, splits):
     assert _rel(out_g, ref_g) <= 2e-2
     torch.cuda.synchronize()
     ws.check_status()
+
+
+@pytest.mark.parametrize("m,valid", [(1024, 1024), (1536, 1100)])
+def test_linear_many_tokens_wide_weights(ws, m, valid):
+    """Row capacities of 512-token multiples over an output wide enough to fill the GPU with (weight tile,
+    token tile) CTAs (the shape that takes 512-token tiles when they are enabled): plain store with a
+    dynamic valid count (rows past it untouched) and the SwiGLU epilogue."""
+    from actfold_b200.kernels import EPI_SWIGLU, linear, tile_weight
+
+    n = 24576
+    g = torch.Generator(device="cuda").manual_seed(m)
+    x = torch.randn(m, 4096, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, 4096, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    wt = tile_weight(w)
+    m_dev = torch.tensor([valid], dtype=torch.int32, device="cuda")
+    out = torch.full((m, n), 7.0, dtype=torch.bfloat16, device="cuda")
+    linear(x, wt, ws, out=out, m_dev=m_dev, w_tiled=True, n=n)
+    ref = (x.float() @ w.float().T).to(torch.bfloat16)
+    assert _rel(out[:valid], ref[:valid]) <= 1e-2
+    assert (out[valid:] == 7.0).all()
+    out_g = linear(x, wt, ws, epilogue=EPI_SWIGLU, w_tiled=True, n=n)
+    r = ref.float().view(m, n // 128, 2, 64)
+    gate, up = r[:, :, 0].reshape(m, n // 2), r[:, :, 1].reshape(m, n // 2)
+    ref_g = (gate / (1 + torch.exp(-gate)) * up).to(torch.bfloat16)
+    assert _rel(out_g, ref_g) <= 2e-2
+    torch.cuda.synchronize()
+    ws.check_status()
