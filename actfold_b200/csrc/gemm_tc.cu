@@ -845,7 +845,14 @@ static GemmShape plan_shape(int n, int k, int m_cap, int want_splits, bool row_s
   const int tiles = g.n_tiles * g.m_tiles;
   int splits = want_splits;
   if (splits <= 0 && partial && env_partial_splits() > 0) splits = env_partial_splits();
-  if (splits <= 0) {
+  if (splits <= 0 && partial && g.ntok >= 256) {
+    // Tensor-bound token tiles leaving partials: at most one CTA per SM.
+    // Every split adds a partial slice that the next row kernel reads, and at
+    // 512 rows two splits of the O / down projections beat three and four
+    // (measured on B200: d = 64 at 512 tokens 12.08 -> 11.3 ms, 32 children
+    // 13.7 -> 13.2 ms; one split 12.7 ms).
+    splits = std::max(1, std::min(4, sm_count() / tiles));
+  } else if (splits <= 0) {
     // About 4/3 CTAs per SM, at most 4 splits: measured on B200 for the
     // LLaDA/Dream projections, more and shorter split CTAs lose more to their
     // ramp-up and cluster reduction than they gain in parallel streams.
