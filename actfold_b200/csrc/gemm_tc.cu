@@ -205,7 +205,9 @@ __device__ __forceinline__ void epi_pair(const GemmDev& p, int n0, int c, int64_
 // issues the MMAs; every stage's TMA loads, from both CTAs, complete on CTA
 // 0's `full` barrier, and CTA 0's MMA commits arrive on both CTAs' `empty` and
 // accumulator barriers.
-template <bool kPair>
+// kWide: 512-token tiles (two 256-token MMAs per stage, epilogue in 256-token
+// chunks); the narrow instantiation is the 256-token kernel unchanged.
+template <bool kPair, bool kWide>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmW,
                                                           const __grid_constant__ CUtensorMap tmX, const GemmDev p) {
   extern __shared__ uint8_t smem_raw[];
@@ -225,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
   const int nkb = min(p.kb_per_split, p.nkb - kb0);
   const int S = p.stages;
   // This CTA's token rows per stage: the whole tile, or its half of it in a pair.
-  const int xrows = kPair ? p.ntok / 2 : p.ntok;
+  const int xrows = kPair ? (kWide ? p.ntok / 2 : p.xbox) : p.ntok;
   const uint32_t w_bytes = kTileN * kBlockK * 2, x_bytes = xrows * kBlockK * 2;
   const uint32_t stage_bytes = w_bytes + x_bytes;
 
@@ -271,12 +273,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
   };
   auto load_x = [&](int i, uint32_t dst, uint32_t bar) {
-    if constexpr (kPair) {
+    if constexpr (kPair && kWide) {
       // Box h of CTA r holds tokens m0 + (2h + r) * xbox: the pair's MMA h
       // (one box of each CTA) then covers tokens [2h * xbox, (2h + 2) * xbox).
       for (int h = 0; 2 * h * p.xbox < p.ntok; ++h)
         tma_load_2d_pair(dst + (uint32_t)(h * p.xbox) * (kBlockK * 2), &tmX, bar, kb_of(i) * kBlockK,
                          m0 + (2 * h + prank) * p.xbox);
+    } else if constexpr (kPair) {
+      tma_load_2d_pair(dst, &tmX, bar, kb_of(i) * kBlockK, m0 + prank * p.xbox);
     } else {
       for (int h = 0; h < p.ntok; h += p.xbox)
         tma_load_2d(dst + (uint32_t)h * (kBlockK * 2), &tmX, bar, kb_of(i) * kBlockK, m0 + h);
@@ -398,10 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     *issued_slot = i;
   } else if (warp == 1 && lane == 0 && leader) {
     // ---------------- MMA issuer ----------------
-    // Token tiles wider than 256 run as 256-token MMAs side by side in TMEM.
-    const int nsub = p.ntok > 256 ? p.ntok / 256 : 1;
+    // Wide token tiles run as 256-token MMAs side by side in TMEM.
+    const int nsub = kWide ? p.ntok / 256 : 1;
     const uint32_t sub_b = (uint32_t)(kPair ? p.xbox : 256) * (kBlockK * 2);  // B bytes per sub-MMA per CTA
-    const uint32_t idesc = idesc_bf16(kPair ? 2 * kTileN : kTileN, p.ntok > 256 ? 256 : p.ntok);
+    const uint32_t idesc = idesc_bf16(kPair ? 2 * kTileN : kTileN, kWide ? 256 : p.ntok);
     bool ready = true;
     if constexpr (kPair) {
       ready = mbar_wait(alloc_bar, 0, abort_flag);
@@ -422,7 +426,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       tc_fence_after();
       const uint32_t st = base + s * stage_bytes;
       const uint64_t adesc = sw128_desc(st);
-      if constexpr (kPair) {
+      if constexpr (!kWide) {
+        const uint64_t bdesc = sw128_desc(st + w_bytes);
+        if constexpr (kPair) {
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk)
+            tc_mma_bf16_pair(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+          tc_commit_pair_both(empty0 + 8 * s);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk)
+            tc_mma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+          tc_commit(empty0 + 8 * s);
+        }
+      } else if constexpr (kPair) {
         for (int h = 0; h < nsub; ++h) {
           const uint64_t bdesc = sw128_desc(st + w_bytes + (uint32_t)h * sub_b);
 #pragma unroll
@@ -482,8 +499,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
       *abort_flag = 1;
     }
     tc_fence_after();
+    if constexpr (!kWide) {
+      if (!*abort_flag) {
+        // Thread r holds tile row r (TMEM lane) across the token columns; the
+        // token-major staging makes a warp's 32 stores one contiguous line.
+        const int nchunk = (Mv + 15) / 16;
+        for (int c = 0; c < nchunk; ++c) {
+          float v[16];
+          tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(16 * c), v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) tile[(16 * c + j) * kLdt + r] = v[j];
+        }
+        if (p.push) fence_proxy_async_smem();  // the staged rows are read by bulk copies (async proxy)
+      }
+    }
   }
-  // Tokens [t0, t0 + kEpiTok) of the accumulator into `tile` (warps 2-5):
+  // Wide tiles: tokens [t0, t0 + kEpiTok) of the accumulator into `tile` (warps 2-5):
   // thread r holds tile row r (TMEM lane) across the token columns; the
   // token-major staging makes a warp's 32 stores one contiguous line.
   auto stage = [&](int t0) {
@@ -498,153 +529,214 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_tc(const __grid_constant__
     }
     if (p.push) fence_proxy_async_smem();  // the staged rows are read by bulk copies (async proxy)
   };
-  if (warp >= 2 && !*abort_flag) stage(0);
+  if constexpr (kWide) {
+    if (warp >= 2 && !*abort_flag) stage(0);
+  }
   __syncthreads();
   const bool ok = !*abort_flag;
 
-  if (p.partial || p.splits == 1) {
-   // Wide token tiles are staged and stored kEpiTok tokens at a time (token
-   // m of the tile is row m - t0 of the staged chunk).
-   for (int t0 = 0;;) {
-    const int tn = min(kEpiTok, Mv - t0);
+  if constexpr (!kWide) {
     if (p.partial) {
       // ---------------- split j's fp32 partial rows to global memory ----------------
       // Row m of this tile: 128 features = 512 contiguous bytes, one warp-wide
       // 16-byte store per lane; the consumer sums the splits.
       if (ok) {
         float* dst = p.partial + ((int64_t)blockIdx.y * p.m_cap + m0) * p.n + n0;
-        for (int idx = threadIdx.x; idx < tn * 32; idx += kThreads) {
-          const int m = t0 + (idx >> 5), c4 = idx & 31;
+        for (int idx = threadIdx.x; idx < Mv * 32; idx += kThreads) {
+          const int m = idx >> 5, c4 = idx & 31;
           *reinterpret_cast<float4*>(dst + (int64_t)m * p.n + 4 * c4) =
-              *reinterpret_cast<const float4*>(tile + (m - t0) * kLdt + 4 * c4);
+              *reinterpret_cast<const float4*>(tile + m * kLdt + 4 * c4);
         }
       }
-    } else if (ok && p.epi == EPI_SWIGLU) {
-      // ---------------- SwiGLU: one unit per (token, gate chunk), all threads ----------------
-      const int total = tn * 8;
-      for (int u = threadIdx.x; u < total; u += kThreads) {
-        const int m = t0 + (u >> 3), r0 = 8 * (u & 7);
-        float a[8], b[8];
-        load8(tile + (m - t0) * kLdt + r0, a);
-        load8(tile + (m - t0) * kLdt + r0 + 64, b);
-        epi_swiglu(p, n0, r0, s_orow[m], a, b);
-      }
-    } else if (ok) {
-      // ---------------- units (token m, chunk pair c / c + 8), warp-uniform loop ----------------
-      // Lanes 8k..8k+7 of a warp cover the 8 units of one token, so the logit
-      // row sums reduce over groups of 8 lanes.
-      const int total = tn * 8;
-      for (int base_u = warp * 32; base_u < total; base_u += kThreads) {
-        const int u = base_u + lane;
-        const bool valid = u < total;
-        const int m = t0 + (u >> 3), c = u & 7;
-        float rs = 0.f;
-        if (valid) {
-          EpiOperands o;
-          epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
+    } else if (p.splits == 1) {
+      if (ok && p.epi == EPI_SWIGLU) {
+        // ---------------- SwiGLU: one unit per (token, gate chunk), all threads ----------------
+        const int total = Mv * 8;
+        for (int u = threadIdx.x; u < total; u += kThreads) {
+          const int m = u >> 3, r0 = 8 * (u & 7);
           float a[8], b[8];
-          load8(tile + (m - t0) * kLdt + 8 * c, a);
-          load8(tile + (m - t0) * kLdt + 8 * c + 64, b);
-          if (p.epi == EPI_STORE) {
-            rs = epi_store(p, n0, 8 * c, s_orow[m], a);
-            rs += epi_store(p, n0, 8 * c + 64, s_orow[m], b);
-          } else {
-            epi_pair(p, n0, c, s_orow[m], o, a, b);
+          load8(tile + m * kLdt + r0, a);
+          load8(tile + m * kLdt + r0 + 64, b);
+          epi_swiglu(p, n0, r0, s_orow[m], a, b);
+        }
+      } else if (ok) {
+        // ---------------- units (token m, chunk pair c / c + 8), warp-uniform loop ----------------
+        // Lanes 8k..8k+7 of a warp cover the 8 units of one token, so the logit
+        // row sums reduce over groups of 8 lanes.
+        const int total = Mv * 8;
+        for (int base_u = warp * 32; base_u < total; base_u += kThreads) {
+          const int u = base_u + lane;
+          const bool valid = u < total;
+          const int m = u >> 3, c = u & 7;
+          float rs = 0.f;
+          if (valid) {
+            EpiOperands o;
+            epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
+            float a[8], b[8];
+            load8(tile + m * kLdt + 8 * c, a);
+            load8(tile + m * kLdt + 8 * c + 64, b);
+            if (p.epi == EPI_STORE) {
+              rs = epi_store(p, n0, 8 * c, s_orow[m], a);
+              rs += epi_store(p, n0, 8 * c + 64, s_orow[m], b);
+            } else {
+              epi_pair(p, n0, c, s_orow[m], o, a, b);
+            }
+          }
+          if (p.row_sums) {
+            rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+            if (valid && (lane & 7) == 0) atomicAdd(p.row_sums + s_orow[m], rs);
           }
         }
-        if (p.row_sums) {
-          rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-          rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-          rs += __shfl_xor_sync(0xffffffffu, rs, 4);
-          if (valid && (lane & 7) == 0) atomicAdd(p.row_sums + s_orow[m], rs);
-        }
       }
-    }
-    t0 += kEpiTok;
-    if (t0 >= Mv) break;
-    __syncthreads();  // every thread is done with the staged chunk
-    if (warp >= 2 && ok) stage(t0);
-    __syncthreads();
-   }
-  } else {
-    // ---------------- cluster split-K reduction ----------------
-    // CTA j owns tokens [tlo, thi) and sums their units (token m, chunk pair
-    // c / c + 8: rows 8c..8c+7 and their partners 64+8c..64+8c+7) over every
-    // CTA of the cluster in a fixed source order. The other CTAs' partial rows
-    // of those tokens are either pushed into this CTA's receive slots by bulk
-    // copies (push) or read from their shared memory (pull); the sums are the
-    // same. Per unit the global operands are requested first, then every
-    // source's partials (up to 4 in flight), so their latencies overlap.
-    const int j = blockIdx.y, Sp = p.splits;
-    const int tlo = (j * Mv) / Sp, thi = ((j + 1) * Mv) / Sp;
-    const int lo = tlo * 8, hi = thi * 8;
-    const uint32_t row_b = kLdt * 4;
-    const uint32_t recv_off = (uint32_t)(p.ntok * kLdt * 4);
-    const uint32_t slot_b = (uint32_t)xch_slot_bytes(p.ntok, Sp);
-    if (p.push && threadIdx.x == 0)
-      mbar_arrive_expect_tx(recv_bar, (uint32_t)((Sp - 1) * (thi - tlo)) * row_b);
-    __syncwarp();
-    cluster_sync_all();  // every partial tile is staged, every receive barrier armed, every ring idle
-    bool got = true;
-    if (p.push) {
-      if (threadIdx.x == 0)
-        for (int k = 0; k < Sp; ++k) {
-          const int klo = (k * Mv) / Sp, khi = ((k + 1) * Mv) / Sp;
-          if (k == j || khi <= klo) continue;
-          const uint32_t dst = cluster_map(base + recv_off + (uint32_t)(j < k ? j : j - 1) * slot_b, (uint32_t)k);
-          bulk_copy_s2c(dst, base + (uint32_t)klo * row_b, (uint32_t)(khi - klo) * row_b, cluster_map(recv_bar, (uint32_t)k));
-        }
-      volatile int no_abort = 0;
-      got = mbar_wait(recv_bar, 0, &no_abort);
-      if (!got && threadIdx.x == 0) atomicOr(p.status, AF_STATUS_TIMEOUT);
-    }
-    if (ok && got) {
-      for (int u = lo + threadIdx.x; u < hi; u += kThreads) {
-        const int m = u >> 3, c = u & 7;
-        EpiOperands o;
-        epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
-        const uint32_t oa = base + (uint32_t)((m * kLdt + 8 * c) * 4);
-        const uint32_t ob = oa + 64 * 4;
-        float sa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, sb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int s0 = 0; s0 < Sp; s0 += 4) {
-          float4 v[4][4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (s0 + q < Sp) {
-              const int src = s0 + q;
-              if (p.push) {
-                const float* t = src == j ? tile + m * kLdt + 8 * c
-                                          : reinterpret_cast<const float*>(gbase + recv_off + (src < j ? src : src - 1) * slot_b +
-                                                                           (m - tlo) * row_b) + 8 * c;
-                v[q][0] = *reinterpret_cast<const float4*>(t);
-                v[q][1] = *reinterpret_cast<const float4*>(t + 4);
-                v[q][2] = *reinterpret_cast<const float4*>(t + 64);
-                v[q][3] = *reinterpret_cast<const float4*>(t + 68);
-              } else {
-                v[q][0] = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
-                v[q][1] = ld_cluster_f4(cluster_map(oa + 16, (uint32_t)src));
-                v[q][2] = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
-                v[q][3] = ld_cluster_f4(cluster_map(ob + 16, (uint32_t)src));
+    } else {
+      // ---------------- cluster split-K reduction ----------------
+      // CTA j owns tokens [tlo, thi) and sums their units (token m, chunk pair
+      // c / c + 8: rows 8c..8c+7 and their partners 64+8c..64+8c+7) over every
+      // CTA of the cluster in a fixed source order. The other CTAs' partial rows
+      // of those tokens are either pushed into this CTA's receive slots by bulk
+      // copies (push) or read from their shared memory (pull); the sums are the
+      // same. Per unit the global operands are requested first, then every
+      // source's partials (up to 4 in flight), so their latencies overlap.
+      const int j = blockIdx.y, Sp = p.splits;
+      const int tlo = (j * Mv) / Sp, thi = ((j + 1) * Mv) / Sp;
+      const int lo = tlo * 8, hi = thi * 8;
+      const uint32_t row_b = kLdt * 4;
+      const uint32_t recv_off = (uint32_t)(p.ntok * kLdt * 4);
+      const uint32_t slot_b = (uint32_t)xch_slot_bytes(p.ntok, Sp);
+      if (p.push && threadIdx.x == 0)
+        mbar_arrive_expect_tx(recv_bar, (uint32_t)((Sp - 1) * (thi - tlo)) * row_b);
+      __syncwarp();
+      cluster_sync_all();  // every partial tile is staged, every receive barrier armed, every ring idle
+      bool got = true;
+      if (p.push) {
+        if (threadIdx.x == 0)
+          for (int k = 0; k < Sp; ++k) {
+            const int klo = (k * Mv) / Sp, khi = ((k + 1) * Mv) / Sp;
+            if (k == j || khi <= klo) continue;
+            const uint32_t dst = cluster_map(base + recv_off + (uint32_t)(j < k ? j : j - 1) * slot_b, (uint32_t)k);
+            bulk_copy_s2c(dst, base + (uint32_t)klo * row_b, (uint32_t)(khi - klo) * row_b, cluster_map(recv_bar, (uint32_t)k));
+          }
+        volatile int no_abort = 0;
+        got = mbar_wait(recv_bar, 0, &no_abort);
+        if (!got && threadIdx.x == 0) atomicOr(p.status, AF_STATUS_TIMEOUT);
+      }
+      if (ok && got) {
+        for (int u = lo + threadIdx.x; u < hi; u += kThreads) {
+          const int m = u >> 3, c = u & 7;
+          EpiOperands o;
+          epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
+          const uint32_t oa = base + (uint32_t)((m * kLdt + 8 * c) * 4);
+          const uint32_t ob = oa + 64 * 4;
+          float sa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, sb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int s0 = 0; s0 < Sp; s0 += 4) {
+            float4 v[4][4];
+  #pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (s0 + q < Sp) {
+                const int src = s0 + q;
+                if (p.push) {
+                  const float* t = src == j ? tile + m * kLdt + 8 * c
+                                            : reinterpret_cast<const float*>(gbase + recv_off + (src < j ? src : src - 1) * slot_b +
+                                                                             (m - tlo) * row_b) + 8 * c;
+                  v[q][0] = *reinterpret_cast<const float4*>(t);
+                  v[q][1] = *reinterpret_cast<const float4*>(t + 4);
+                  v[q][2] = *reinterpret_cast<const float4*>(t + 64);
+                  v[q][3] = *reinterpret_cast<const float4*>(t + 68);
+                } else {
+                  v[q][0] = ld_cluster_f4(cluster_map(oa, (uint32_t)src));
+                  v[q][1] = ld_cluster_f4(cluster_map(oa + 16, (uint32_t)src));
+                  v[q][2] = ld_cluster_f4(cluster_map(ob, (uint32_t)src));
+                  v[q][3] = ld_cluster_f4(cluster_map(ob + 16, (uint32_t)src));
+                }
+              }
+            }
+  #pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (s0 + q < Sp) {
+                sa[0] += v[q][0].x; sa[1] += v[q][0].y; sa[2] += v[q][0].z; sa[3] += v[q][0].w;
+                sa[4] += v[q][1].x; sa[5] += v[q][1].y; sa[6] += v[q][1].z; sa[7] += v[q][1].w;
+                sb[0] += v[q][2].x; sb[1] += v[q][2].y; sb[2] += v[q][2].z; sb[3] += v[q][2].w;
+                sb[4] += v[q][3].x; sb[5] += v[q][3].y; sb[6] += v[q][3].z; sb[7] += v[q][3].w;
               }
             }
           }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (s0 + q < Sp) {
-              sa[0] += v[q][0].x; sa[1] += v[q][0].y; sa[2] += v[q][0].z; sa[3] += v[q][0].w;
-              sa[4] += v[q][1].x; sa[5] += v[q][1].y; sa[6] += v[q][1].z; sa[7] += v[q][1].w;
-              sb[0] += v[q][2].x; sb[1] += v[q][2].y; sb[2] += v[q][2].z; sb[3] += v[q][2].w;
-              sb[4] += v[q][3].x; sb[5] += v[q][3].y; sb[6] += v[q][3].z; sb[7] += v[q][3].w;
-            }
+          epi_pair(p, n0, c, s_orow[m], o, sa, sb);
+        }
+      }
+      __syncwarp();
+      // Pull: peers may still read this CTA's partial tile until here. Push:
+      // every CTA has received its slots, so this CTA's outgoing copies are done.
+      cluster_sync_all();
+    }
+  } else {
+    // A wide tile's launch has one split or leaves partials (no cluster reduction).
+    if (p.partial || p.splits == 1) {
+     // Wide token tiles are staged and stored kEpiTok tokens at a time (token
+     // m of the tile is row m - t0 of the staged chunk).
+     for (int t0 = 0;;) {
+      const int tn = min(kEpiTok, Mv - t0);
+      if (p.partial) {
+        // ---------------- split j's fp32 partial rows to global memory ----------------
+        // Row m of this tile: 128 features = 512 contiguous bytes, one warp-wide
+        // 16-byte store per lane; the consumer sums the splits.
+        if (ok) {
+          float* dst = p.partial + ((int64_t)blockIdx.y * p.m_cap + m0) * p.n + n0;
+          for (int idx = threadIdx.x; idx < tn * 32; idx += kThreads) {
+            const int m = t0 + (idx >> 5), c4 = idx & 31;
+            *reinterpret_cast<float4*>(dst + (int64_t)m * p.n + 4 * c4) =
+                *reinterpret_cast<const float4*>(tile + (m - t0) * kLdt + 4 * c4);
           }
         }
-        epi_pair(p, n0, c, s_orow[m], o, sa, sb);
+      } else if (ok && p.epi == EPI_SWIGLU) {
+        // ---------------- SwiGLU: one unit per (token, gate chunk), all threads ----------------
+        const int total = tn * 8;
+        for (int u = threadIdx.x; u < total; u += kThreads) {
+          const int m = t0 + (u >> 3), r0 = 8 * (u & 7);
+          float a[8], b[8];
+          load8(tile + (m - t0) * kLdt + r0, a);
+          load8(tile + (m - t0) * kLdt + r0 + 64, b);
+          epi_swiglu(p, n0, r0, s_orow[m], a, b);
+        }
+      } else if (ok) {
+        // ---------------- units (token m, chunk pair c / c + 8), warp-uniform loop ----------------
+        // Lanes 8k..8k+7 of a warp cover the 8 units of one token, so the logit
+        // row sums reduce over groups of 8 lanes.
+        const int total = tn * 8;
+        for (int base_u = warp * 32; base_u < total; base_u += kThreads) {
+          const int u = base_u + lane;
+          const bool valid = u < total;
+          const int m = t0 + (u >> 3), c = u & 7;
+          float rs = 0.f;
+          if (valid) {
+            EpiOperands o;
+            epi_operands(p, n0, c, p.epi == EPI_RESIDUAL ? s_rrow[m] : 0, p.epi == EPI_ROPE ? s_pos[m] : 0, o);
+            float a[8], b[8];
+            load8(tile + (m - t0) * kLdt + 8 * c, a);
+            load8(tile + (m - t0) * kLdt + 8 * c + 64, b);
+            if (p.epi == EPI_STORE) {
+              rs = epi_store(p, n0, 8 * c, s_orow[m], a);
+              rs += epi_store(p, n0, 8 * c + 64, s_orow[m], b);
+            } else {
+              epi_pair(p, n0, c, s_orow[m], o, a, b);
+            }
+          }
+          if (p.row_sums) {
+            rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+            if (valid && (lane & 7) == 0) atomicAdd(p.row_sums + s_orow[m], rs);
+          }
+        }
       }
+      t0 += kEpiTok;
+      if (t0 >= Mv) break;
+      __syncthreads();  // every thread is done with the staged chunk
+      if (warp >= 2 && ok) stage(t0);
+      __syncthreads();
+     }
     }
-    __syncwarp();
-    // Pull: peers may still read this CTA's partial tile until here. Push:
-    // every CTA has received its slots, so this CTA's outgoing copies are done.
-    cluster_sync_all();
   }
 
   if (threadIdx.x == 0 && leader && *abort_flag) {
@@ -975,15 +1067,20 @@ int gemm_run(const GemmCall& c, cudaStream_t stream) {
 
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(k_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_tc<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   // Tensor maps built elsewhere (c.tmap_x) use box rows gemm_xbox(ntok).
+  const dim3 grid(g.n_tiles * g.m_tiles, g.splits, 1), block(kThreads, 1, 1);
+  const dim3 cl_pair(2, 1, 1), cl_one(1, partial ? 1 : g.splits, 1);
+  const bool wide = g.ntok > 256;
   cudaError_t e =
-      g.pair ? launch_ex(k_gemm_tc<true>, dim3(g.n_tiles * g.m_tiles, g.splits, 1), dim3(kThreads, 1, 1), (size_t)g.smem,
-                         stream, c.pdl != 0, dim3(2, 1, 1), *pw, *px, d)
-             : launch_ex(k_gemm_tc<false>, dim3(g.n_tiles * g.m_tiles, g.splits, 1), dim3(kThreads, 1, 1), (size_t)g.smem,
-                         stream, c.pdl != 0, dim3(1, partial ? 1 : g.splits, 1), *pw, *px, d);
+      g.pair ? (wide ? launch_ex(k_gemm_tc<true, true>, grid, block, (size_t)g.smem, stream, c.pdl != 0, cl_pair, *pw, *px, d)
+                     : launch_ex(k_gemm_tc<true, false>, grid, block, (size_t)g.smem, stream, c.pdl != 0, cl_pair, *pw, *px, d))
+             : (wide ? launch_ex(k_gemm_tc<false, true>, grid, block, (size_t)g.smem, stream, c.pdl != 0, cl_one, *pw, *px, d)
+                     : launch_ex(k_gemm_tc<false, false>, grid, block, (size_t)g.smem, stream, c.pdl != 0, cl_one, *pw, *px, d));
   if (e != cudaSuccess) return fail(AF_ERR_CUDA, std::string("gemm_tc launch: ") + cudaGetErrorString(e));
   return check_launch("gemm_tc");
 }
